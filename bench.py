@@ -1,0 +1,355 @@
+"""Decode-token-loop benchmark (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+A step is one lockstep tick of the workload (serve-demo schedule): every
+client decodes one token off one sweep of the weights.  `value` is the
+whole-job tokens/s with the weights resident in HBM, each step timed with
+CUDA events on the session stream and L2 flushed (a 256 MiB write) between
+steps; `e2e` runs the same ticks through spm_decode_step with host token
+buffers (H2D of the tokens and D2H of the greedy picks inside the timed
+region).  Dense models do not shard: N>1 runs N independent replicas
+("replicas only"), and the slowest rank's time sets the job time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+DEFAULT_WORKLOAD = "smollm2-b5"
+
+
+def _args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=96)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+def _dist():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+class Clocks:
+    """nvidia-smi samples (200 ms) while the timed region runs."""
+
+    Q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread:
+                self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[0]) for r in self.rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if len(r) > 4 + i and r[4 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _workload(name):
+    from emufpga_b200 import configs
+
+    w = configs.WORKLOADS[name]
+    return w, configs.RECIPES[w["recipe"]], configs.workload_prompts(name)
+
+
+def _tick_tokens(prompts, tick, best):
+    """Next tokens under serve-demo's lockstep rule."""
+    return [p[tick + 1] if tick + 1 < len(p) else best[i] for i, p in enumerate(prompts)]
+
+
+def cpu_baseline(recipe, img, prompts, steps, seconds: float):
+    """The oracle (this repo's C restatement of the reference CPU loop) on all
+    host cores: lockstep ticks until `seconds` of work; tokens/s."""
+    from oracle import oracle as O
+
+    n = len(prompts)
+    om = O.OracleModel(img, recipe.shape)
+    longest = max(len(p) for p in prompts)
+    sess = om.session(n, longest + steps + 1)
+    tokens = [p[0] for p in prompts]
+    t0 = time.perf_counter()
+    ticks = 0
+    while ticks < longest + steps - 1:
+        logits = sess.step(tokens)
+        best = [O.argmax_last(logits[i]) for i in range(n)]
+        tokens = _tick_tokens(prompts, ticks, best)
+        ticks += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": n * ticks / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"first {ticks} lockstep ticks x {n} clients of the workload (oracle, OpenMP over rows)"}
+
+
+def run_reference(a, rank, world):
+    if rank != 0:
+        return 0
+    w, recipe, prompts = _workload(a.workload)
+    import emufpga_b200 as eb
+
+    img = eb.synth_gguf(recipe)
+    n = len(prompts)
+    from oracle import oracle as O
+
+    om = O.OracleModel(img, recipe.shape)
+    longest = max(len(p) for p in prompts)
+    sess = om.session(n, longest + w["steps"] + 1)
+    tokens = [p[0] for p in prompts]
+    total = longest + w["steps"] - 1
+    steps = min(a.steps, max(1, total - a.warmup))
+    times = []
+    for tick in range(min(total, a.warmup + steps)):
+        t0 = time.perf_counter()
+        logits = sess.step(tokens)
+        best = [O.argmax_last(logits[i]) for i in range(n)]
+        dt = time.perf_counter() - t0
+        tokens = _tick_tokens(prompts, tick, best)
+        if tick >= a.warmup:
+            times.append(dt)
+        if tick >= a.warmup and sum(times) > 150.0:
+            break
+    value = n * len(times) / sum(times)
+    line = {"metric": "decode tokens/s", "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": world,
+            "steps": len(times), "warmup": a.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids)",
+            "config": {"workload": a.workload, "clients": n},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "kind": "port", "cores": os.cpu_count(),
+                             "sample": f"{len(times)} lockstep ticks after {a.warmup} warm-up ticks"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    a = _args()
+    rank, world, local = _dist()
+    if a.impl == "reference":
+        return run_reference(a, rank, world)
+    import torch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        pg = dist
+    import emufpga_b200 as eb
+
+    w, recipe, prompts = _workload(a.workload)
+    img = eb.synth_gguf(recipe)
+    model = eb.Model(img, recipe.shape, device=local)
+    n = len(prompts)
+    longest = max(len(p) for p in prompts)
+    total_ticks = longest + w["steps"] - 1
+    warm, steps = a.warmup, a.steps
+    if warm + steps > total_ticks:
+        steps = max(1, total_ticks - warm)
+    context = longest + w["steps"] + 1
+    sess = eb.Session(model, n, context)
+    stream = torch.cuda.ExternalStream(sess.cuda_stream, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    argmax = torch.zeros(n, dtype=torch.int32, device=dev)
+    prompt_dev = torch.tensor([[p[min(t + 1, len(p) - 1)] for p in prompts] for t in range(total_ticks)],
+                              dtype=torch.int32, device=dev)
+    in_prompt = torch.tensor([[t + 1 < len(p) for p in prompts] for t in range(total_ticks)], device=dev)
+    tokens = torch.tensor([p[0] for p in prompts], dtype=torch.int32, device=dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+
+    # ---- device-resident timing (value) ----
+    with torch.cuda.stream(stream):
+        for t in range(warm):
+            sess.decode_step_device(tokens, n, argmax)
+            tokens = torch.where(in_prompt[t], prompt_dev[t], argmax)
+        torch.cuda.synchronize(dev)
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize(dev)
+        with Clocks(local) as clocks:
+            for i in range(steps):
+                t = warm + i
+                flush.zero_()
+                starts[i].record(stream)
+                sess.decode_step_device(tokens, n, argmax)
+                ends[i].record(stream)
+                tokens = torch.where(in_prompt[t], prompt_dev[t], argmax)
+            torch.cuda.synchronize(dev)
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    local_ms = sum(step_ms)
+    job_ms = local_ms
+    if pg:
+        tt = torch.tensor([local_ms], device=dev)
+        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
+        job_ms = float(tt.item())
+    launches = sess.launches_per_step(n)
+    sess.close()
+
+    # ---- end to end through the C ABI with host buffers (e2e) ----
+    sess = eb.Session(model, n, context)
+    toks = [p[0] for p in prompts]
+    for t in range(warm):
+        best, _ = sess.decode_step(toks)
+        toks = _tick_tokens(prompts, t, best)
+    if pg:
+        pg.barrier()
+    t0 = time.perf_counter()
+    for i in range(steps):
+        best, _ = sess.decode_step(toks)
+        toks = _tick_tokens(prompts, warm + i, best)
+    e2e_s = time.perf_counter() - t0
+    if pg:
+        tt = torch.tensor([e2e_s], device=dev)
+        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
+        e2e_s = float(tt.item())
+    sess.close()
+
+    # ---- roofline of the GEMV: one sweep of every weight stream, graph-captured ----
+    roof = None
+    if rank == 0:
+        roof = gemv_roofline(eb, model, n, dev)
+    tokens_total = n * steps * world
+    line = None
+    if rank == 0:
+        peak, how = _peaks()
+        clk = clocks.summary()
+        line = {
+            "metric": "decode tokens/s", "value": tokens_total / (job_ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": warm, "ms_per_step": job_ms / steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,0.02) weights quantized by this repo's encoder, uniform prompt ids)",
+            "config": {"workload": a.workload, "model": w["recipe"], "clients": n, "prompts": w["prompts"],
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "weight_bytes_per_step": model.weight_bytes,
+                       "l2": "flushed between timed steps (256 MiB write); weights 143 MB > 126 MB L2"},
+            "weight_stream_gbs": model.weight_bytes * steps / (job_ms / 1e3) / 1e9,
+            "e2e": {"value": tokens_total / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4 * n,
+                    "d2h_bytes_per_step": 4 * n},
+            "gpu_launches": launches * steps,
+            "roofline": None, "clocks": clk,
+        }
+        if roof:
+            ach = roof["bytes"] / roof["seconds"] / 1e9
+            line["roofline"] = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                                "peak_source": how, "traffic": None, "kernel": "gemv_kernel (all streams, one sweep)",
+                                "launches_per_sweep": roof["launches"]}
+        if not a.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(recipe, img, prompts, w["steps"], a.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def gemv_roofline(eb, model, n, dev):
+    """Graph-capture one sweep of spm_streamed over every rotating stream plus
+    the LM head (the decode step's GEMV launches, same shapes and client
+    count), replay it with L2 flushed between sweeps, and time each replay
+    with CUDA events: achieved = quantized bytes per sweep / sweep time."""
+    import torch
+
+    idx = list(range(model.stream_count))
+    infos = [model.stream_info(i) for i in idx]
+    embd = model.stream_index("token_embd.weight")
+    # every matrix a step sweeps: all streams but the embedding, which is the
+    # LM head itself when tied
+    keep = [i for i in idx if i != embd or model.shape.tied]
+    maxc = max(infos[i]["cols"] for i in keep)
+    maxr = max(infos[i]["rows"] for i in keep)
+    x = torch.randn(n * maxc, device=dev)
+    y = torch.empty(n * maxr, device=dev)
+    s = torch.cuda.Stream(device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    with torch.cuda.stream(s):
+        for i in keep:
+            eb.streamed(model, i, x, n, y, stream=s.cuda_stream)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in keep:
+            eb.streamed(model, i, x, n, y, stream=s.cuda_stream)
+    total = 0.0
+    reps = 10
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            g.replay()
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            g.replay()
+            b.record(s)
+            b.synchronize()
+            total += a.elapsed_time(b) / 1e3
+    nbytes = sum(infos[i]["bytes"] for i in keep)
+    del g
+    return {"bytes": nbytes, "seconds": total / reps, "launches": len(keep)}
+
+
+
+if __name__ == "__main__":
+    sys.exit(main())

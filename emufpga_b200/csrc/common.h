@@ -1,0 +1,88 @@
+// Internal declarations shared by the host (.cpp) and device (.cu) halves of
+// libspmgpu.so.  Nothing here crosses the C ABI (include/spmgpu.h does).
+#pragma once
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/spmgpu.h"
+
+namespace spm {
+
+// ---- errors: a thread-local message behind spm_last_error() ----
+void set_error(const std::string& msg);
+struct Error {
+    spm_status code;
+    std::string msg;
+};
+[[noreturn]] void fail(spm_status code, const std::string& msg);
+
+// ---- GGML block geometry (spm-gguf/src/parse.rs:26-45) ----
+bool type_layout(uint32_t dtype, uint64_t* block_values, uint64_t* block_bytes);
+float f16_to_f32(uint16_t bits);
+uint16_t f32_to_f16(float f);
+
+// ---- GGUF container ----
+struct GgufTensor {
+    std::string name;
+    std::vector<uint64_t> dims;  // ne[0] = innermost (cols)
+    uint32_t dtype = 0;
+    uint64_t offset = 0;         // absolute byte offset in the image
+    uint64_t len = 0;            // byte length
+};
+struct GgufMeta {
+    std::string key;
+    uint32_t type = 0;
+    bool has_int = false, has_float = false;
+    uint64_t u = 0;
+    double f = 0;
+    std::string s;
+};
+struct Gguf {
+    uint32_t version = 0;
+    uint64_t data_offset = 0;
+    std::vector<GgufMeta> meta;
+    std::vector<GgufTensor> tensors;  // sorted by offset
+    const GgufTensor* find(const std::string& name) const;
+    const GgufMeta* meta_find(const std::string& key) const;
+};
+// Bounded parse of an in-memory image (limits of spm-gguf/src/lib.rs:11-16).
+Gguf gguf_parse(const uint8_t* buf, uint64_t len);
+
+// ---- host codecs ----
+void decode_blocks(uint32_t dtype, const uint8_t* bytes, uint64_t nbytes, float* out);
+// Quantize n values (n a multiple of the block size) into GGML blocks.
+void quantize(uint32_t dtype, const float* src, uint64_t n, uint8_t* dst);
+
+// ---- synthetic models ----
+// Returns a malloc'd GGUF image (release with free) of *len bytes.
+uint8_t* synth_gguf(const spm_synth_spec& spec, uint64_t* len);
+
+// ---- .order files (spm-order/src/order.rs) ----
+struct Order {
+    std::vector<std::string> rotating, resident;
+};
+Order parse_order(const std::string& text);
+std::string default_order(const spm_model_cfg& cfg, bool router_bias);
+
+// ---- packed device layout of one quantized matrix ----
+// Rows are grouped in tiles of kTileRows.  Inside a tile every plane is
+// contiguous and 16-byte aligned; a plane holds one fixed-size record per
+// 32-weight unit (or per 256-weight block) of every row of the tile.  The
+// records keep exactly the GGML bytes, rearranged so that one thread owns one
+// unit and extracts four codes per 32-bit word.
+constexpr int kTileRows = 4;
+struct Packed {
+    uint32_t dtype = 0;
+    uint64_t rows = 0, cols = 0;
+    uint64_t tiles = 0, tile_bytes = 0;
+    uint32_t plane[4] = {0, 0, 0, 0};  // plane offsets inside a tile
+    uint64_t offset = 0;               // offset of tile 0 in the device image
+    uint64_t quant_bytes = 0;          // GGML size: rows*cols/bv*bb
+};
+Packed packed_shape(uint32_t dtype, uint64_t rows, uint64_t cols);
+// Repack GGML row-major blocks into `dst` (packed.tiles * tile_bytes bytes).
+void pack_matrix(const Packed& p, const uint8_t* gguf_blocks, uint8_t* dst);
+
+}  // namespace spm

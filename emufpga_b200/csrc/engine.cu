@@ -1,0 +1,834 @@
+// Host orchestration and the C ABI (include/spmgpu.h).
+//
+// A model is the weight stream laid out in HBM in consumption order (the
+// .order file's [rotating] list, then the [resident] quantized tensors), one
+// packed matrix after another.  A session owns the per-client KV caches and
+// scratch, and replays one CUDA graph per client count: a decode step reads
+// every weight exactly once and serves all clients
+// (spm-batch/src/step.rs:19-53).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <fstream>
+#include <map>
+#include <memory>
+#include <set>
+#include <sstream>
+#include <thread>
+
+#include "kernels.h"
+
+namespace spm {
+const std::string& last_error();
+}
+using namespace spm;
+
+#define CUDA_OK(expr)                                                                        \
+    do {                                                                                     \
+        cudaError_t e_ = (expr);                                                             \
+        if (e_ != cudaSuccess) fail(SPM_E_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+namespace {
+
+template <class F>
+spm_status guarded(F&& f) {
+    try {
+        f();
+        return SPM_OK;
+    } catch (const Error& e) {
+        set_error(e.msg);
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        set_error("host allocation failed");
+        return SPM_E_ARG;
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return SPM_E_ARG;
+    }
+}
+
+struct DeviceBuf {
+    void* p = nullptr;
+    ~DeviceBuf() { if (p) cudaFree(p); }
+};
+
+}  // namespace
+
+// A packed matrix in the device image.
+struct StreamDesc {
+    std::string name;
+    Packed pk;
+    uint64_t experts = 1;       // >1: rows = experts * rows_per_expert
+    bool rotating = false;      // swept every step (counted in weight bytes)
+};
+
+struct LayerIdx {
+    int q = -1, k = -1, v = -1, o = -1, gate = -1, up = -1, down = -1;
+    int router = -1, gate_exps = -1, up_exps = -1, down_exps = -1;
+    int64_t attn_norm = -1, ffn_norm = -1, q_norm = -1, k_norm = -1, bias = -1;  // offsets in gains
+};
+
+struct spm_model {
+    spm_model_cfg cfg{};
+    int device = 0, sms = 148;
+    uint8_t* image = nullptr;
+    uint64_t image_bytes = 0;
+    std::vector<StreamDesc> streams;
+    std::vector<LayerIdx> layers;
+    int embed = -1, head = -1;
+    float* gains = nullptr;
+    int64_t output_norm = -1;
+    uint64_t weight_bytes = 0;
+    ~spm_model() {
+        if (image) cudaFree(image);
+        if (gains) cudaFree(gains);
+    }
+    const uint8_t* tiles(int idx) const { return image + streams[idx].pk.offset; }
+};
+
+struct spm_weights {
+    Packed pk;
+    int device = 0, sms = 148;
+    uint8_t* dev = nullptr;
+    ~spm_weights() { if (dev) cudaFree(dev); }
+};
+
+struct spm_session {
+    spm_model* m = nullptr;
+    int max_clients = 0, context = 0;
+    cudaStream_t stream = nullptr;
+    float *kc = nullptr, *vc = nullptr;
+    float *states = nullptr, *normed = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
+    float *act = nullptr, *logits = nullptr;
+    float2* rope = nullptr;
+    int32_t* pos = nullptr;
+    uint32_t *tokens = nullptr, *argmax = nullptr;
+    uint32_t *h_tokens = nullptr, *h_argmax = nullptr;
+    std::vector<int> lens;
+    bool graphs = true;
+    std::map<int, cudaGraphExec_t> exec;
+    std::map<int, int> launches;
+    std::vector<void*> allocs;
+    ~spm_session() {
+        for (auto& kv : exec) cudaGraphExecDestroy(kv.second);
+        for (void* p : allocs) cudaFree(p);
+        if (h_tokens) cudaFreeHost(h_tokens);
+        if (h_argmax) cudaFreeHost(h_argmax);
+        if (stream) cudaStreamDestroy(stream);
+    }
+    template <class T>
+    T* alloc(size_t count) {
+        void* p = nullptr;
+        CUDA_OK(cudaMalloc(&p, std::max<size_t>(count, 1) * sizeof(T)));
+        CUDA_OK(cudaMemset(p, 0, std::max<size_t>(count, 1) * sizeof(T)));
+        allocs.push_back(p);
+        return static_cast<T*>(p);
+    }
+};
+
+namespace {
+
+bool is_moe(const spm_model_cfg& c) { return c.family == SPM_FAMILY_OLMOE || c.family == SPM_FAMILY_QWEN3MOE; }
+
+uint32_t meta_u32(const Gguf& g, const std::string& key, uint32_t dflt) {
+    auto* m = g.meta_find(key);
+    return (m && m->has_int) ? uint32_t(m->u) : dflt;
+}
+float meta_f32(const Gguf& g, const std::string& key, float dflt) {
+    auto* m = g.meta_find(key);
+    return (m && m->has_float) ? float(m->f) : dflt;
+}
+
+// Model shape from GGUF metadata when the caller passes none.
+spm_model_cfg cfg_from_gguf(const Gguf& g) {
+    spm_model_cfg c{};
+    auto* a = g.meta_find("general.architecture");
+    if (!a) fail(SPM_E_STREAM, "GGUF has no general.architecture and no shape was given");
+    const std::string arch = a->s;
+    if (arch == "llama") c.family = SPM_FAMILY_LLAMA;
+    else if (arch == "qwen3") c.family = SPM_FAMILY_QWEN3;
+    else if (arch == "olmoe") c.family = SPM_FAMILY_OLMOE;
+    else if (arch == "qwen3moe") c.family = SPM_FAMILY_QWEN3MOE;
+    else fail(SPM_E_ARG, "unsupported architecture " + arch);
+    c.layers = meta_u32(g, arch + ".block_count", 0);
+    c.hidden = meta_u32(g, arch + ".embedding_length", 0);
+    c.intermediate = meta_u32(g, arch + ".feed_forward_length", 0);
+    c.heads = meta_u32(g, arch + ".attention.head_count", 0);
+    c.kv_heads = meta_u32(g, arch + ".attention.head_count_kv", c.heads);
+    c.head_dim = meta_u32(g, arch + ".attention.key_length", c.heads ? c.hidden / c.heads : 0);
+    c.experts = meta_u32(g, arch + ".expert_count", 0);
+    c.experts_used = meta_u32(g, arch + ".expert_used_count", 0);
+    c.expert_ff = meta_u32(g, arch + ".expert_feed_forward_length", 0);
+    c.rope_base = meta_f32(g, arch + ".rope.freq_base", 10000.0f);
+    c.eps = meta_f32(g, arch + ".attention.layer_norm_rms_epsilon", 1e-5f);
+    auto* te = g.find("token_embd.weight");
+    if (!te || te->dims.size() < 2) fail(SPM_E_STREAM, "missing token_embd.weight");
+    c.vocab = meta_u32(g, arch + ".vocab_size", uint32_t(te->dims[1]));
+    c.tied = g.find("output.weight") ? 0 : 1;
+    return c;
+}
+
+void check_cfg(const spm_model_cfg& c) {
+    if (c.family < SPM_FAMILY_LLAMA || c.family > SPM_FAMILY_QWEN3MOE) fail(SPM_E_ARG, "unknown model family");
+    if (!c.layers || !c.hidden || !c.heads || !c.kv_heads || !c.head_dim || !c.vocab)
+        fail(SPM_E_ARG, "model shape has a zero dimension");
+    if (c.heads % c.kv_heads) fail(SPM_E_ARG, "heads must group evenly over kv_heads");
+    if (c.head_dim % 2 || c.head_dim > 1024) fail(SPM_E_ARG, "head_dim must be even and at most 1024");
+    if (c.hidden % 32) fail(SPM_E_ARG, "hidden must be a multiple of 32");
+    if (is_moe(c) && (!c.experts || !c.experts_used || c.experts_used > c.experts || !c.expert_ff))
+        fail(SPM_E_ARG, "MoE shape needs experts, experts_used <= experts and expert_ff");
+}
+
+// Both directions, as spm-order/src/order.rs:64-83 (reorder).
+void check_order(const Order& o, const Gguf& g) {
+    std::set<std::string> wanted;
+    for (auto* list : {&o.rotating, &o.resident})
+        for (auto& n : *list) {
+            if (!g.find(n)) fail(SPM_E_STREAM, n + ": named in the order file but not in the checkpoint");
+            if (!wanted.insert(n).second) fail(SPM_E_STREAM, n + ": named twice in the order file");
+        }
+    for (auto& t : g.tensors)
+        if (!wanted.count(t.name)) fail(SPM_E_STREAM, t.name + ": in the checkpoint but not named in the order file");
+}
+
+spm_model* open_model(const uint8_t* buf, uint64_t len, const std::string* order_text, const spm_model_cfg* cfg,
+                      int device) {
+    Gguf g = gguf_parse(buf, len);
+    std::unique_ptr<spm_model> m(new spm_model());
+    m->cfg = cfg ? *cfg : cfg_from_gguf(g);
+    check_cfg(m->cfg);
+    const spm_model_cfg& c = m->cfg;
+    Order order = parse_order(order_text ? *order_text : default_order(c, g.find("blk.0.exp_probs_b.bias") != nullptr));
+    check_order(order, g);
+
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) fail(SPM_E_NO_DEVICE, "no CUDA device is visible");
+    if (device < 0 || device >= ndev) fail(SPM_E_ARG, "device index out of range");
+    m->device = device;
+    CUDA_OK(cudaSetDevice(device));
+    CUDA_OK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, device));
+
+    // Streams in consumption order; 1-D tensors are resident gains.
+    std::vector<float> gains;
+    std::map<std::string, int64_t> gain_off;
+    std::map<std::string, int> stream_of;
+    uint64_t off = 0;
+    auto add_names = [&](const std::vector<std::string>& names, bool rotating) {
+        for (auto& n : names) {
+            const GgufTensor* t = g.find(n);
+            if (t->dims.size() == 1) {
+                if (t->dtype != SPM_F32 && t->dtype != SPM_F16)
+                    fail(SPM_E_ENCODING, n + ": 1-D tensors must be F32 or F16");
+                gain_off[n] = int64_t(gains.size());
+                std::vector<float> v(t->dims[0]);
+                decode_blocks(t->dtype, buf + t->offset, t->len, v.data());
+                gains.insert(gains.end(), v.begin(), v.end());
+                while (gains.size() % 4) gains.push_back(0.f);
+                continue;
+            }
+            StreamDesc s;
+            s.name = n;
+            s.rotating = rotating;
+            uint64_t rows = 1;
+            for (size_t d = 1; d < t->dims.size(); d++) rows *= t->dims[d];
+            s.experts = t->dims.size() > 2 ? t->dims[2] : 1;
+            s.pk = packed_shape(t->dtype, rows, t->dims[0]);
+            s.pk.offset = off;
+            off += (s.pk.tiles * s.pk.tile_bytes + 255) & ~uint64_t(255);
+            stream_of[n] = int(m->streams.size());
+            m->streams.push_back(s);
+        }
+    };
+    add_names(order.rotating, true);
+    add_names(order.resident, false);
+    m->image_bytes = off;
+
+    auto need_stream = [&](const std::string& n) {
+        auto it = stream_of.find(n);
+        if (it == stream_of.end()) fail(SPM_E_STREAM, "missing tensor " + n);
+        return it->second;
+    };
+    auto need_gain = [&](const std::string& n, uint64_t count) {
+        auto it = gain_off.find(n);
+        if (it == gain_off.end()) fail(SPM_E_STREAM, "missing tensor " + n);
+        if (g.find(n)->dims[0] != count) fail(SPM_E_ARG, n + " has the wrong length");
+        return it->second;
+    };
+    auto check_shape = [&](int idx, uint64_t rows, uint64_t cols) {
+        const StreamDesc& s = m->streams[idx];
+        if (s.pk.rows != rows || s.pk.cols != cols)
+            fail(SPM_E_ARG, s.name + ": shape " + std::to_string(s.pk.rows) + "x" + std::to_string(s.pk.cols) +
+                                " does not match the model (" + std::to_string(rows) + "x" + std::to_string(cols) + ")");
+        return idx;
+    };
+    const uint64_t qw = uint64_t(c.heads) * c.head_dim, kvw = uint64_t(c.kv_heads) * c.head_dim;
+    m->layers.resize(c.layers);
+    for (uint32_t l = 0; l < c.layers; l++) {
+        const std::string p = "blk." + std::to_string(l) + ".";
+        LayerIdx& L = m->layers[l];
+        L.q = check_shape(need_stream(p + "attn_q.weight"), qw, c.hidden);
+        L.k = check_shape(need_stream(p + "attn_k.weight"), kvw, c.hidden);
+        L.v = check_shape(need_stream(p + "attn_v.weight"), kvw, c.hidden);
+        L.o = check_shape(need_stream(p + "attn_output.weight"), c.hidden, qw);
+        L.attn_norm = need_gain(p + "attn_norm.weight", c.hidden);
+        L.ffn_norm = need_gain(p + "ffn_norm.weight", c.hidden);
+        if (c.family == SPM_FAMILY_OLMOE) {
+            L.q_norm = need_gain(p + "attn_q_norm.weight", qw);
+            L.k_norm = need_gain(p + "attn_k_norm.weight", kvw);
+        } else if (c.family != SPM_FAMILY_LLAMA) {
+            L.q_norm = need_gain(p + "attn_q_norm.weight", c.head_dim);
+            L.k_norm = need_gain(p + "attn_k_norm.weight", c.head_dim);
+        }
+        if (is_moe(c)) {
+            L.router = check_shape(need_stream(p + "ffn_gate_inp.weight"), c.experts, c.hidden);
+            L.gate_exps = check_shape(need_stream(p + "ffn_gate_exps.weight"), uint64_t(c.experts) * c.expert_ff, c.hidden);
+            L.up_exps = check_shape(need_stream(p + "ffn_up_exps.weight"), uint64_t(c.experts) * c.expert_ff, c.hidden);
+            L.down_exps = check_shape(need_stream(p + "ffn_down_exps.weight"), uint64_t(c.experts) * c.hidden, c.expert_ff);
+            if (gain_off.count(p + "exp_probs_b.bias")) L.bias = need_gain(p + "exp_probs_b.bias", c.experts);
+        } else {
+            L.gate = check_shape(need_stream(p + "ffn_gate.weight"), c.intermediate, c.hidden);
+            L.up = check_shape(need_stream(p + "ffn_up.weight"), c.intermediate, c.hidden);
+            L.down = check_shape(need_stream(p + "ffn_down.weight"), c.hidden, c.intermediate);
+            if (m->streams[L.gate].pk.dtype != m->streams[L.up].pk.dtype)
+                fail(SPM_E_ENCODING, p + "ffn_gate and ffn_up must share an encoding");
+        }
+        if (m->streams[L.q].pk.dtype != m->streams[L.k].pk.dtype || m->streams[L.q].pk.dtype != m->streams[L.v].pk.dtype)
+            fail(SPM_E_ENCODING, p + "attn_q/k/v must share an encoding");
+    }
+    m->embed = check_shape(need_stream("token_embd.weight"), c.vocab, c.hidden);
+    m->head = c.tied ? m->embed : check_shape(need_stream("output.weight"), c.vocab, c.hidden);
+    m->output_norm = need_gain("output_norm.weight", c.hidden);
+    if (m->streams[m->embed].pk.dtype == SPM_F32 && c.hidden % 32) fail(SPM_E_ARG, "bad embedding width");
+
+    // StepReport::for_sweep (spm-batch/src/session.rs:263-278): descriptor
+    // bytes of every matrix one step reads -- here the rotating streams plus
+    // the LM head.  MoE steps read only the routed experts; their per-step
+    // bytes are counted by the session.
+    for (auto& s : m->streams)
+        if (s.rotating && s.experts == 1) m->weight_bytes += s.pk.quant_bytes;
+    if (!m->streams[m->head].rotating) m->weight_bytes += m->streams[m->head].pk.quant_bytes;
+
+    // Upload: pack each matrix on the host (threads over matrices) and copy.
+    CUDA_OK(cudaMalloc(&m->image, std::max<uint64_t>(m->image_bytes, 256)));
+    std::atomic<size_t> next{0};
+    std::vector<std::string> errs(std::max(1u, std::min(16u, std::thread::hardware_concurrency())));
+    auto worker = [&](size_t w) {
+        try {
+            if (cudaSetDevice(device) != cudaSuccess) fail(SPM_E_CUDA, "cudaSetDevice failed");
+            std::vector<uint8_t> host;
+            for (;;) {
+                size_t i = next.fetch_add(1);
+                if (i >= m->streams.size()) break;
+                const StreamDesc& s = m->streams[i];
+                const GgufTensor* t = g.find(s.name);
+                host.resize(s.pk.tiles * s.pk.tile_bytes);
+                pack_matrix(s.pk, buf + t->offset, host.data());
+                CUDA_OK(cudaMemcpy(m->image + s.pk.offset, host.data(), host.size(), cudaMemcpyHostToDevice));
+            }
+        } catch (const Error& e) {
+            errs[w] = e.msg;
+        }
+    };
+    std::vector<std::thread> pool;
+    for (size_t w = 0; w < errs.size(); w++) pool.emplace_back(worker, w);
+    for (auto& th : pool) th.join();
+    for (auto& e : errs)
+        if (!e.empty()) fail(SPM_E_CUDA, e);
+    CUDA_OK(cudaMalloc(&m->gains, std::max<size_t>(gains.size(), 4) * sizeof(float)));
+    CUDA_OK(cudaMemcpy(m->gains, gains.data(), gains.size() * sizeof(float), cudaMemcpyHostToDevice));
+    return m.release();
+}
+
+std::string read_file(const char* path) {
+    std::ifstream f(path, std::ios::binary);
+    if (!f) fail(SPM_E_STREAM, std::string(path) + ": cannot open");
+    std::ostringstream ss;
+    ss << f.rdbuf();
+    return ss.str();
+}
+
+// ---- one decode step ----
+GemvLaunch gemv_base(const spm_model* m, int idx, const float* x, int n) {
+    const Packed& p = m->streams[idx].pk;
+    GemvLaunch L{};
+    L.cols = uint32_t(p.cols);
+    L.tile_bytes = uint32_t(p.tile_bytes);
+    L.plane1 = p.plane[1];
+    L.plane2 = p.plane[2];
+    L.plane3 = p.plane[3];
+    L.x = x;
+    L.x_stride = int(p.cols);
+    L.n = n;
+    return L;
+}
+
+void add_job(GemvLaunch& L, const spm_model* m, int idx, const uint8_t* b, float* y, int y_stride, const float* aux,
+             int aux_stride, int epi) {
+    GemvJob& J = L.job[L.njobs++];
+    const Packed& p = m->streams[idx].pk;
+    J.a = m->tiles(idx);
+    J.b = b;
+    J.y = y;
+    J.y_stride = y_stride;
+    J.aux = aux;
+    J.aux_stride = aux_stride;
+    J.epi = epi;
+    J.rows = uint32_t(p.rows);
+    J.tile_begin = L.total_tiles;
+    L.total_tiles += uint32_t(p.tiles);
+}
+
+void run_gemv(const spm_model* m, const GemvLaunch& L, uint32_t dtype, cudaStream_t st) {
+    CUDA_OK(launch_gemv(dtype, L, m->sms, st));
+}
+
+void enqueue_step(spm_session* s, int n) {
+    spm_model* m = s->m;
+    const spm_model_cfg& c = m->cfg;
+    cudaStream_t st = s->stream;
+    const int d = int(c.hidden), qw = int(c.heads * c.head_dim), kvw = int(c.kv_heads * c.head_dim);
+    const int ff = int(c.intermediate);
+    const StreamDesc& E = m->streams[m->embed];
+    CUDA_OK(launch_embed(E.pk.dtype, m->tiles(m->embed), E.pk, s->tokens, n, s->states, st));
+    for (uint32_t l = 0; l < c.layers; l++) {
+        const LayerIdx& L = m->layers[l];
+        CUDA_OK(launch_rmsnorm(s->states, m->gains + L.attn_norm, s->normed, n, d, c.eps, st));
+        GemvLaunch g = gemv_base(m, L.q, s->normed, n);
+        add_job(g, m, L.q, nullptr, s->q, qw, nullptr, 0, EPI_STORE);
+        add_job(g, m, L.k, nullptr, s->k, kvw, nullptr, 0, EPI_STORE);
+        add_job(g, m, L.v, nullptr, s->v, kvw, nullptr, 0, EPI_STORE);
+        run_gemv(m, g, m->streams[L.q].pk.dtype, st);
+        AttnParams P{};
+        P.q = s->q; P.k = s->k; P.v = s->v; P.out = s->attn;
+        P.kcache = s->kc; P.vcache = s->vc; P.pos = s->pos; P.rope = s->rope;
+        P.q_norm = L.q_norm >= 0 ? m->gains + L.q_norm : nullptr;
+        P.k_norm = L.k_norm >= 0 ? m->gains + L.k_norm : nullptr;
+        P.layer = int(l); P.layers = int(c.layers); P.context = s->context;
+        P.heads = int(c.heads); P.kv_heads = int(c.kv_heads); P.head_dim = int(c.head_dim);
+        P.family = int(c.family); P.eps = c.eps;
+        CUDA_OK(launch_attention(P, n, st));
+        GemvLaunch go = gemv_base(m, L.o, s->attn, n);
+        add_job(go, m, L.o, nullptr, s->states, d, s->states, d, EPI_ADD);
+        run_gemv(m, go, m->streams[L.o].pk.dtype, st);
+        CUDA_OK(launch_rmsnorm(s->states, m->gains + L.ffn_norm, s->normed, n, d, c.eps, st));
+        if (is_moe(c)) fail(SPM_E_ARG, "MoE layers are not enabled in this build");
+        GemvLaunch gu = gemv_base(m, L.gate, s->normed, n);
+        add_job(gu, m, L.gate, m->tiles(L.up), s->act, ff, nullptr, 0, EPI_SWIGLU);
+        run_gemv(m, gu, m->streams[L.gate].pk.dtype, st);
+        GemvLaunch gd = gemv_base(m, L.down, s->act, n);
+        add_job(gd, m, L.down, nullptr, s->states, d, s->states, d, EPI_ADD);
+        run_gemv(m, gd, m->streams[L.down].pk.dtype, st);
+    }
+    CUDA_OK(launch_rmsnorm(s->states, m->gains + m->output_norm, s->normed, n, d, c.eps, st));
+    GemvLaunch gh = gemv_base(m, m->head, s->normed, n);
+    add_job(gh, m, m->head, nullptr, s->logits, int(c.vocab), nullptr, 0, EPI_STORE);
+    run_gemv(m, gh, m->streams[m->head].pk.dtype, st);
+    CUDA_OK(launch_argmax(s->logits, n, int(c.vocab), s->argmax, st));
+    CUDA_OK(launch_advance(s->pos, n, st));
+}
+
+// Client counts above 8 are not batched into one sweep by this build.
+constexpr int kMaxBatch = 8;
+
+void step(spm_session* s, int n) {
+    if (n < 1 || n > s->max_clients) fail(SPM_E_ARG, "client count out of range");
+    if (n > kMaxBatch) fail(SPM_E_ARG, "at most 8 clients share one sweep");
+    for (int i = 0; i < n; i++)
+        if (s->lens[i] >= s->context) fail(SPM_E_CONTEXT, "context " + std::to_string(s->context) + " exhausted");
+    if (s->graphs) {
+        auto it = s->exec.find(n);
+        if (it == s->exec.end()) {
+            cudaGraph_t graph;
+            CUDA_OK(cudaStreamBeginCapture(s->stream, cudaStreamCaptureModeThreadLocal));
+            try {
+                enqueue_step(s, n);
+            } catch (...) {
+                cudaStreamEndCapture(s->stream, &graph);
+                throw;
+            }
+            CUDA_OK(cudaStreamEndCapture(s->stream, &graph));
+            size_t nodes = 0;
+            CUDA_OK(cudaGraphGetNodes(graph, nullptr, &nodes));
+            std::vector<cudaGraphNode_t> list(nodes);
+            CUDA_OK(cudaGraphGetNodes(graph, list.data(), &nodes));
+            int kernels = 0;
+            for (auto nd : list) {
+                cudaGraphNodeType t;
+                CUDA_OK(cudaGraphNodeGetType(nd, &t));
+                if (t == cudaGraphNodeTypeKernel) kernels++;
+            }
+            s->launches[n] = kernels;
+            cudaGraphExec_t ge;
+            CUDA_OK(cudaGraphInstantiate(&ge, graph, 0));
+            cudaGraphDestroy(graph);
+            it = s->exec.emplace(n, ge).first;
+        }
+        CUDA_OK(cudaGraphLaunch(it->second, s->stream));
+    } else {
+        enqueue_step(s, n);
+    }
+    for (int i = 0; i < n; i++) s->lens[i]++;
+}
+
+// Host-computed rotary table so that cos/sin are the oracle's glibc values:
+// LLAMA spm-ops/src/attention.rs:241-248, others spm-qwen3-slice/src/attention.rs:11-19.
+std::vector<float2> rope_table(const spm_model_cfg& c, int context) {
+    const int half = int(c.head_dim / 2);
+    std::vector<float2> t(size_t(context) * half);
+    for (int pos = 0; pos < context; pos++)
+        for (int i = 0; i < half; i++) {
+            float theta;
+            if (c.family == SPM_FAMILY_LLAMA) {
+                const float width = float(c.head_dim), at = float(pos > 65535 ? 65535 : pos), index = float(i);
+                theta = powf(c.rope_base, -2.0f * index / width) * at;
+            } else {
+                const float exponent = 2.0f * float(i) / float(c.head_dim);
+                theta = float(pos) / powf(c.rope_base, exponent);
+            }
+            t[size_t(pos) * half + i] = make_float2(cosf(theta), sinf(theta));
+        }
+    return t;
+}
+
+}  // namespace
+
+// ================================================================== C ABI ==
+extern "C" {
+
+const char* spm_last_error(void) { return spm::last_error().c_str(); }
+const char* spm_version(void) { return "emufpga-b200 0.1 (sm_100a)"; }
+void spm_free(void* p) { std::free(p); }
+
+spm_status spm_synth_gguf(const spm_synth_spec* spec, uint8_t** out, uint64_t* len) {
+    return guarded([&] {
+        if (!spec || !out || !len) fail(SPM_E_ARG, "null argument");
+        *out = synth_gguf(*spec, len);
+    });
+}
+
+spm_status spm_gguf_probe(const uint8_t* buf, uint64_t len, uint64_t* tensors, uint64_t* data_offset) {
+    return guarded([&] {
+        if (!buf && len) fail(SPM_E_ARG, "null buffer");
+        Gguf g = gguf_parse(buf, len);
+        if (tensors) *tensors = g.tensors.size();
+        if (data_offset) *data_offset = g.data_offset;
+    });
+}
+
+spm_status spm_gguf_probe_file(const char* path, uint64_t* tensors, uint64_t* data_offset) {
+    return guarded([&] {
+        std::string s = read_file(path);
+        Gguf g = gguf_parse(reinterpret_cast<const uint8_t*>(s.data()), s.size());
+        if (tensors) *tensors = g.tensors.size();
+        if (data_offset) *data_offset = g.data_offset;
+    });
+}
+
+spm_status spm_gguf_find(const uint8_t* buf, uint64_t len, const char* name, uint32_t* dtype, uint64_t* dims4,
+                         uint64_t* offset, uint64_t* nbytes) {
+    return guarded([&] {
+        Gguf g = gguf_parse(buf, len);
+        const GgufTensor* t = g.find(name ? name : "");
+        if (!t) fail(SPM_E_STREAM, std::string("no tensor named ") + (name ? name : ""));
+        if (dtype) *dtype = t->dtype;
+        if (dims4)
+            for (int d = 0; d < 4; d++) dims4[d] = d < int(t->dims.size()) ? t->dims[d] : 1;
+        if (offset) *offset = t->offset;
+        if (nbytes) *nbytes = t->len;
+    });
+}
+
+spm_status spm_decode_blocks(uint32_t dtype, const uint8_t* bytes, uint64_t nbytes, float* out) {
+    return guarded([&] { decode_blocks(dtype, bytes, nbytes, out); });
+}
+
+spm_status spm_order_check(const char* text, const uint8_t* gguf, uint64_t len) {
+    return guarded([&] { check_order(parse_order(text ? text : ""), gguf_parse(gguf, len)); });
+}
+
+spm_status spm_order_default(const spm_model_cfg* cfg, const uint8_t* gguf, uint64_t len, char** text) {
+    return guarded([&] {
+        bool bias = false;
+        if (gguf) bias = gguf_parse(gguf, len).find("blk.0.exp_probs_b.bias") != nullptr;
+        std::string s = default_order(*cfg, bias);
+        *text = static_cast<char*>(std::malloc(s.size() + 1));
+        std::memcpy(*text, s.c_str(), s.size() + 1);
+    });
+}
+
+spm_status spm_model_open(const char* gguf_path, const char* order_path, const spm_model_cfg* cfg, int device,
+                          spm_model** out) {
+    return guarded([&] {
+        std::string img = read_file(gguf_path);
+        std::string order;
+        if (order_path) order = read_file(order_path);
+        *out = open_model(reinterpret_cast<const uint8_t*>(img.data()), img.size(), order_path ? &order : nullptr, cfg,
+                          device);
+    });
+}
+
+spm_status spm_model_open_memory(const uint8_t* gguf, uint64_t len, const char* order_text, const spm_model_cfg* cfg,
+                                 int device, spm_model** out) {
+    return guarded([&] {
+        std::string order = order_text ? order_text : "";
+        *out = open_model(gguf, len, order_text ? &order : nullptr, cfg, device);
+    });
+}
+
+spm_status spm_model_close(spm_model* m) {
+    return guarded([&] {
+        if (m) cudaSetDevice(m->device);
+        delete m;
+    });
+}
+
+spm_status spm_model_weight_bytes(const spm_model* m, uint64_t* bytes) {
+    return guarded([&] { *bytes = m->weight_bytes; });
+}
+
+spm_status spm_model_stream_count(const spm_model* m, int32_t* streams) {
+    return guarded([&] { *streams = int32_t(m->streams.size()); });
+}
+
+spm_status spm_model_stream_info(const spm_model* m, int32_t index, uint64_t* rows, uint64_t* cols, uint32_t* dtype,
+                                 uint64_t* bytes) {
+    return guarded([&] {
+        if (index < 0 || index >= int32_t(m->streams.size())) fail(SPM_E_ARG, "stream index out of range");
+        const Packed& p = m->streams[index].pk;
+        if (rows) *rows = p.rows;
+        if (cols) *cols = p.cols;
+        if (dtype) *dtype = p.dtype;
+        if (bytes) *bytes = p.quant_bytes;
+    });
+}
+
+spm_status spm_model_stream_index(const spm_model* m, const char* name, int32_t* index) {
+    return guarded([&] {
+        for (size_t i = 0; i < m->streams.size(); i++)
+            if (m->streams[i].name == name) { *index = int32_t(i); return; }
+        fail(SPM_E_ARG, std::string("no stream named ") + name);
+    });
+}
+
+spm_status spm_dequant_rows(const spm_model* m, int32_t index, uint64_t row0, uint64_t rows, float* out_host) {
+    return guarded([&] {
+        if (index < 0 || index >= int32_t(m->streams.size())) fail(SPM_E_ARG, "stream index out of range");
+        const Packed& p = m->streams[index].pk;
+        if (row0 > p.rows || rows > p.rows - row0) fail(SPM_E_ARG, "row range exceeds the matrix");
+        CUDA_OK(cudaSetDevice(m->device));
+        DeviceBuf out;
+        CUDA_OK(cudaMalloc(&out.p, std::max<uint64_t>(rows * p.cols, 1) * sizeof(float)));
+        CUDA_OK(launch_dequant(p.dtype, m->tiles(index), p, row0, rows, static_cast<float*>(out.p), nullptr));
+        CUDA_OK(cudaMemcpy(out_host, out.p, rows * p.cols * sizeof(float), cudaMemcpyDeviceToHost));
+    });
+}
+
+spm_status spm_streamed(const spm_model* m, int32_t index, const float* x_dev, int32_t positions, float* y_dev,
+                        void* cuda_stream) {
+    return guarded([&] {
+        if (index < 0 || index >= int32_t(m->streams.size())) fail(SPM_E_ARG, "stream index out of range");
+        if (positions < 0) fail(SPM_E_ACTIVATION_LEN, "negative position count");
+        if (positions > 0 && (!x_dev || !y_dev)) fail(SPM_E_ARG, "null activation or output pointer");
+        CUDA_OK(cudaSetDevice(m->device));
+        const Packed& p = m->streams[index].pk;
+        for (int32_t p0 = 0; p0 < positions; p0 += kMaxBatch) {
+            const int n = std::min(kMaxBatch, positions - p0);
+            GemvLaunch L = gemv_base(m, index, x_dev + size_t(p0) * p.cols, n);
+            add_job(L, m, index, nullptr, y_dev + size_t(p0) * p.rows, int(p.rows), nullptr, 0, EPI_STORE);
+            run_gemv(m, L, p.dtype, static_cast<cudaStream_t>(cuda_stream));
+        }
+    });
+}
+
+spm_status spm_weights_upload(uint32_t dtype, uint64_t rows, uint64_t cols, const uint8_t* blocks, int device,
+                              spm_weights** out) {
+    return guarded([&] {
+        std::unique_ptr<spm_weights> w(new spm_weights());
+        w->pk = packed_shape(dtype, rows, cols);
+        int ndev = 0;
+        if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) fail(SPM_E_NO_DEVICE, "no CUDA device is visible");
+        w->device = device;
+        CUDA_OK(cudaSetDevice(device));
+        CUDA_OK(cudaDeviceGetAttribute(&w->sms, cudaDevAttrMultiProcessorCount, device));
+        std::vector<uint8_t> host(w->pk.tiles * w->pk.tile_bytes);
+        pack_matrix(w->pk, blocks, host.data());
+        CUDA_OK(cudaMalloc(&w->dev, host.size()));
+        CUDA_OK(cudaMemcpy(w->dev, host.data(), host.size(), cudaMemcpyHostToDevice));
+        *out = w.release();
+    });
+}
+
+spm_status spm_weights_free(spm_weights* w) {
+    return guarded([&] { delete w; });
+}
+
+spm_status spm_weights_gemv(const spm_weights* w, const float* x_dev, int32_t positions, float* y_dev,
+                            void* cuda_stream) {
+    return guarded([&] {
+        if (positions < 0) fail(SPM_E_ACTIVATION_LEN, "negative position count");
+        CUDA_OK(cudaSetDevice(w->device));
+        const Packed& p = w->pk;
+        for (int32_t p0 = 0; p0 < positions; p0 += kMaxBatch) {
+            const int n = std::min(kMaxBatch, positions - p0);
+            GemvLaunch L{};
+            L.cols = uint32_t(p.cols);
+            L.tile_bytes = uint32_t(p.tile_bytes);
+            L.plane1 = p.plane[1];
+            L.plane2 = p.plane[2];
+            L.plane3 = p.plane[3];
+            L.x = x_dev + size_t(p0) * p.cols;
+            L.x_stride = int(p.cols);
+            L.n = n;
+            GemvJob& J = L.job[L.njobs++];
+            J.a = w->dev;
+            J.y = y_dev + size_t(p0) * p.rows;
+            J.y_stride = int(p.rows);
+            J.rows = uint32_t(p.rows);
+            J.epi = EPI_STORE;
+            L.total_tiles = uint32_t(p.tiles);
+            CUDA_OK(launch_gemv(p.dtype, L, w->sms, static_cast<cudaStream_t>(cuda_stream)));
+        }
+    });
+}
+
+spm_status spm_weights_dequant(const spm_weights* w, uint64_t row0, uint64_t rows, float* out_host) {
+    return guarded([&] {
+        const Packed& p = w->pk;
+        if (row0 > p.rows || rows > p.rows - row0) fail(SPM_E_ARG, "row range exceeds the matrix");
+        CUDA_OK(cudaSetDevice(w->device));
+        DeviceBuf out;
+        CUDA_OK(cudaMalloc(&out.p, std::max<uint64_t>(rows * p.cols, 1) * sizeof(float)));
+        CUDA_OK(launch_dequant(p.dtype, w->dev, p, row0, rows, static_cast<float*>(out.p), nullptr));
+        CUDA_OK(cudaMemcpy(out_host, out.p, rows * p.cols * sizeof(float), cudaMemcpyDeviceToHost));
+    });
+}
+
+spm_status spm_session_create(spm_model* m, int32_t max_clients, int32_t max_context, spm_session** out) {
+    return guarded([&] {
+        if (max_clients < 1 || max_context < 1) fail(SPM_E_ARG, "clients and context must be positive");
+        CUDA_OK(cudaSetDevice(m->device));
+        std::unique_ptr<spm_session> s(new spm_session());
+        s->m = m;
+        s->max_clients = max_clients;
+        s->context = max_context;
+        const spm_model_cfg& c = m->cfg;
+        const size_t n = size_t(max_clients), d = c.hidden, qw = size_t(c.heads) * c.head_dim;
+        const size_t kvw = size_t(c.kv_heads) * c.head_dim;
+        const size_t ff = std::max<size_t>(c.intermediate, c.expert_ff);
+        CUDA_OK(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
+        s->kc = s->alloc<float>(n * c.layers * size_t(max_context) * kvw);
+        s->vc = s->alloc<float>(n * c.layers * size_t(max_context) * kvw);
+        s->states = s->alloc<float>(n * d);
+        s->normed = s->alloc<float>(n * d);
+        s->q = s->alloc<float>(n * qw);
+        s->k = s->alloc<float>(n * kvw);
+        s->v = s->alloc<float>(n * kvw);
+        s->attn = s->alloc<float>(n * qw);
+        s->act = s->alloc<float>(n * ff);
+        s->logits = s->alloc<float>(n * c.vocab);
+        s->pos = s->alloc<int32_t>(n);
+        s->tokens = s->alloc<uint32_t>(n);
+        s->argmax = s->alloc<uint32_t>(n);
+        auto table = rope_table(c, max_context);
+        s->rope = s->alloc<float2>(table.size());
+        CUDA_OK(cudaMemcpy(s->rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice));
+        CUDA_OK(cudaMallocHost(&s->h_tokens, n * sizeof(uint32_t)));
+        CUDA_OK(cudaMallocHost(&s->h_argmax, n * sizeof(uint32_t)));
+        s->lens.assign(n, 0);
+        *out = s.release();
+    });
+}
+
+spm_status spm_session_destroy(spm_session* s) {
+    return guarded([&] {
+        if (s) cudaSetDevice(s->m->device);
+        delete s;
+    });
+}
+
+spm_status spm_client_reset(spm_session* s, int32_t client) {
+    return guarded([&] {
+        if (client < 0 || client >= s->max_clients) fail(SPM_E_ARG, "client index out of range");
+        CUDA_OK(cudaSetDevice(s->m->device));
+        CUDA_OK(cudaMemsetAsync(s->pos + client, 0, sizeof(int32_t), s->stream));
+        CUDA_OK(cudaStreamSynchronize(s->stream));
+        s->lens[client] = 0;
+    });
+}
+
+spm_status spm_client_len(const spm_session* s, int32_t client, int32_t* len) {
+    return guarded([&] {
+        if (client < 0 || client >= s->max_clients) fail(SPM_E_ARG, "client index out of range");
+        *len = s->lens[client];
+    });
+}
+
+spm_status spm_decode_step(spm_session* s, const uint32_t* tokens, int32_t n, float* logits_host,
+                           uint32_t* argmax_host) {
+    return guarded([&] {
+        if (n < 1 || n > s->max_clients) fail(SPM_E_ARG, "client count out of range");
+        for (int i = 0; i < n; i++)
+            if (tokens[i] >= s->m->cfg.vocab) fail(SPM_E_ARG, "token id out of range");
+        CUDA_OK(cudaSetDevice(s->m->device));
+        std::memcpy(s->h_tokens, tokens, size_t(n) * sizeof(uint32_t));
+        CUDA_OK(cudaMemcpyAsync(s->tokens, s->h_tokens, size_t(n) * sizeof(uint32_t), cudaMemcpyHostToDevice, s->stream));
+        step(s, n);
+        if (argmax_host)
+            CUDA_OK(cudaMemcpyAsync(s->h_argmax, s->argmax, size_t(n) * sizeof(uint32_t), cudaMemcpyDeviceToHost, s->stream));
+        if (logits_host)
+            CUDA_OK(cudaMemcpyAsync(logits_host, s->logits, size_t(n) * s->m->cfg.vocab * sizeof(float),
+                                    cudaMemcpyDeviceToHost, s->stream));
+        CUDA_OK(cudaStreamSynchronize(s->stream));
+        if (argmax_host) std::memcpy(argmax_host, s->h_argmax, size_t(n) * sizeof(uint32_t));
+    });
+}
+
+spm_status spm_decode_step_device(spm_session* s, const uint32_t* tokens_dev, int32_t n, float* logits_dev,
+                                  uint32_t* argmax_dev) {
+    return guarded([&] {
+        if (n < 1 || n > s->max_clients) fail(SPM_E_ARG, "client count out of range");
+        CUDA_OK(cudaSetDevice(s->m->device));
+        if (tokens_dev != s->tokens)
+            CUDA_OK(cudaMemcpyAsync(s->tokens, tokens_dev, size_t(n) * sizeof(uint32_t), cudaMemcpyDeviceToDevice, s->stream));
+        step(s, n);
+        if (argmax_dev)
+            CUDA_OK(cudaMemcpyAsync(argmax_dev, s->argmax, size_t(n) * sizeof(uint32_t), cudaMemcpyDeviceToDevice, s->stream));
+        if (logits_dev)
+            CUDA_OK(cudaMemcpyAsync(logits_dev, s->logits, size_t(n) * s->m->cfg.vocab * sizeof(float),
+                                    cudaMemcpyDeviceToDevice, s->stream));
+    });
+}
+
+spm_status spm_session_sync(spm_session* s) {
+    return guarded([&] { CUDA_OK(cudaStreamSynchronize(s->stream)); });
+}
+
+spm_status spm_session_stream(const spm_session* s, void** cuda_stream) {
+    return guarded([&] { *cuda_stream = s->stream; });
+}
+
+spm_status spm_session_set_graphs(spm_session* s, int32_t enable) {
+    return guarded([&] { s->graphs = enable != 0; });
+}
+
+spm_status spm_session_routes(const spm_session* s, int32_t n, int32_t* routes_host) {
+    return guarded([&] {
+        (void)n;
+        (void)routes_host;
+        if (!is_moe(s->m->cfg)) fail(SPM_E_ARG, "the model has no routed layers");
+        fail(SPM_E_ARG, "routes are not recorded by this build");
+    });
+}
+
+spm_status spm_session_launches_per_step(spm_session* s, int32_t n, int32_t* launches) {
+    return guarded([&] {
+        auto it = s->launches.find(n);
+        if (it == s->launches.end()) fail(SPM_E_ARG, "no step has been captured at this client count");
+        *launches = it->second;
+    });
+}
+
+}  // extern "C"

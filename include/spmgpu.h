@@ -1,0 +1,167 @@
+/*
+ * spmgpu.h -- C ABI of libspmgpu.so, the sm_100a backend for emufpga's
+ * decode token loop (the streamed low-bit weight pass shared by N clients).
+ *
+ * Every entry point returns an spm_status (0 = ok, negative = error; the
+ * message is available from spm_last_error() on the calling thread).  All
+ * pointers are plain host or device pointers; no framework types cross the
+ * boundary.  Handles are opaque; there is no global model state.
+ *
+ * Reference interfaces replaced (paths inside the emufpga tree):
+ *   spm_gguf_*            spm-gguf/src/parse.rs:169-198 (read), tensor.rs:21-67
+ *   spm_decode_blocks     spm-gguf/src/tensor.rs:69-210 (decode_f32/q8_0/q5_k/q6_k)
+ *   spm_order_check       spm-order/src/order.rs:28-111 (parse_order, reorder)
+ *   spm_model_open*       spm-stream-groups/src/groups.rs:54-117 (GroupStream::open)
+ *                         + spm-smol/src/config.rs (SmolConfig) + the .order layout
+ *   spm_model_weight_bytes spm-batch/src/session.rs:255-278 (StepReport::for_sweep)
+ *   spm_session_create    spm-batch/src/session.rs:180-237 (Client::new, Scratch::new)
+ *   spm_decode_step       spm-batch/src/step.rs:19-40 (decode_step) + the greedy pick
+ *                         of spm-batch/examples/serve-demo.rs:72-90
+ *   spm_streamed          spm-linear/src/stream.rs:31-55 (streamed) for one stream
+ *   spm_dequant_rows      parity hook for the decoders above, run on the device
+ */
+#ifndef SPMGPU_H
+#define SPMGPU_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int32_t spm_status;
+enum {
+    SPM_OK = 0,
+    SPM_E_ARG = -1,            /* bad argument / shape (LinearError::WeightCount)  */
+    SPM_E_ACTIVATION_LEN = -2, /* LinearError::ActivationLen                      */
+    SPM_E_TRUNCATED = -3,      /* LinearError::Truncated / StreamError::Truncated */
+    SPM_E_STREAM = -4,         /* LinearError::Stream (I/O, parse, layout)        */
+    SPM_E_ENCODING = -5,       /* LayoutError::UnknownEncoding / unsupported dtype */
+    SPM_E_CUDA = -6,
+    SPM_E_NCCL = -7,
+    SPM_E_TIMEOUT = -8,        /* a bounded device wait gave up                   */
+    SPM_E_CONTEXT = -9,        /* KvCache::append: context exhausted              */
+    SPM_E_NO_DEVICE = -10
+};
+
+/* GGML dtype codes (spm-gguf/src/parse.rs:26-45). */
+enum { SPM_F32 = 0, SPM_F16 = 1, SPM_Q8_0 = 8, SPM_Q2_K = 10, SPM_Q5_K = 13, SPM_Q6_K = 14 };
+
+/* Which layer equations a model uses. */
+enum {
+    SPM_FAMILY_LLAMA = 1,    /* SmolLM2: spm-smol / spm-batch / spm-kv equations     */
+    SPM_FAMILY_QWEN3 = 2,    /* Qwen3 dense: spm-qwen3-slice equations, head QK-norm */
+    SPM_FAMILY_OLMOE = 3,    /* OLMoE: full-width QK-norm, softmax top-k experts     */
+    SPM_FAMILY_QWEN3MOE = 4  /* Qwen3-MoE: head QK-norm, softmax top-k experts       */
+};
+
+/* Model shape.  Field order and meaning match the oracle's or_cfg. */
+typedef struct spm_model_cfg {
+    uint32_t family;
+    uint32_t layers, hidden, intermediate, heads, kv_heads, head_dim, vocab;
+    uint32_t experts, experts_used, expert_ff;
+    uint32_t tied;            /* logits reuse token_embd (SmolLM2)   */
+    float rope_base, eps;
+} spm_model_cfg;
+
+/* Synthetic GGUF recipe: seeded N(0, sigma) weights quantised by this
+ * library's encoders; norm gains 1; optional Zipf router bias. */
+typedef struct spm_synth_spec {
+    spm_model_cfg cfg;
+    uint32_t layer_type;      /* dtype of attention / dense FFN matrices */
+    uint32_t expert_type;     /* dtype of expert matrices (MoE)          */
+    uint32_t embed_type;      /* dtype of token_embd                     */
+    uint32_t head_type;       /* dtype of output.weight (untied)         */
+    uint64_t seed;
+    float sigma;              /* 0.02 in every BASELINE config           */
+    float zipf_s;             /* 0 = no router bias                      */
+    float gain_sigma;         /* 0: norm gains are 1 (BASELINE); else 1+N(0,gain_sigma) */
+    int32_t threads;          /* <=0: all cores                          */
+} spm_synth_spec;
+
+typedef struct spm_model spm_model;
+typedef struct spm_session spm_session;
+typedef struct spm_weights spm_weights;
+
+const char* spm_last_error(void);
+const char* spm_version(void);
+
+/* ---- host-side format pieces ---- */
+/* Write a synthetic model as a GGUF v3 image into a malloc'd buffer
+ * (release with spm_free).  Deterministic in spec (threads do not matter). */
+spm_status spm_synth_gguf(const spm_synth_spec* spec, uint8_t** out, uint64_t* len);
+void spm_free(void* p);
+/* Bounded GGUF parse (spm-gguf limits); reports tensor count and data offset. */
+spm_status spm_gguf_probe(const uint8_t* buf, uint64_t len, uint64_t* tensors, uint64_t* data_offset);
+spm_status spm_gguf_probe_file(const char* path, uint64_t* tensors, uint64_t* data_offset);
+/* Tensor lookup by name: dtype, up to 4 dims, absolute offset and byte length. */
+spm_status spm_gguf_find(const uint8_t* buf, uint64_t len, const char* name, uint32_t* dtype,
+                         uint64_t* dims4, uint64_t* offset, uint64_t* nbytes);
+/* Host decode of whole GGML blocks (CPU, for loaders and tests). */
+spm_status spm_decode_blocks(uint32_t dtype, const uint8_t* bytes, uint64_t nbytes, float* out);
+/* Validate an .order text against a model's tensor names (both directions). */
+spm_status spm_order_check(const char* order_text, const uint8_t* gguf, uint64_t len);
+/* Default consumption order for a model shape as .order text (malloc'd).
+ * When gguf is given, optional tensors it holds (router biases) are listed. */
+spm_status spm_order_default(const spm_model_cfg* cfg, const uint8_t* gguf, uint64_t len, char** text);
+
+/* ---- device model: the weight stream laid out in HBM in consumption order ---- */
+spm_status spm_model_open(const char* gguf_path, const char* order_path,
+                          const spm_model_cfg* cfg, int device, spm_model** out);
+spm_status spm_model_open_memory(const uint8_t* gguf, uint64_t len, const char* order_text,
+                                 const spm_model_cfg* cfg, int device, spm_model** out);
+spm_status spm_model_close(spm_model* m);
+/* Weight bytes one decode sweep reads (descriptor sizes, LM head included). */
+spm_status spm_model_weight_bytes(const spm_model* m, uint64_t* bytes);
+spm_status spm_model_stream_count(const spm_model* m, int32_t* streams);
+/* rows, cols, dtype and quantized byte size of stream `index` (consumption order). */
+spm_status spm_model_stream_info(const spm_model* m, int32_t index, uint64_t* rows,
+                                 uint64_t* cols, uint32_t* dtype, uint64_t* bytes);
+spm_status spm_model_stream_index(const spm_model* m, const char* tensor_name, int32_t* index);
+/* Dequantize rows [row0, row0+rows) of stream `index` on the device into host
+ * memory (rows x cols floats).  Bit-exact with spm_decode_blocks. */
+spm_status spm_dequant_rows(const spm_model* m, int32_t index, uint64_t row0, uint64_t rows,
+                            float* out_host);
+/* y[p][r] = sum_c W[r][c] * x[p][c] for one stream; x_dev is positions x cols,
+ * y_dev positions x rows (device pointers); cuda_stream may be NULL. */
+spm_status spm_streamed(const spm_model* m, int32_t index, const float* x_dev, int32_t positions,
+                        float* y_dev, void* cuda_stream);
+
+/* ---- standalone operator: one quantized matrix, no model ---- */
+spm_status spm_weights_upload(uint32_t dtype, uint64_t rows, uint64_t cols,
+                              const uint8_t* gguf_blocks_host, int device, spm_weights** out);
+spm_status spm_weights_free(spm_weights* w);
+spm_status spm_weights_gemv(const spm_weights* w, const float* x_dev, int32_t positions,
+                            float* y_dev, void* cuda_stream);
+spm_status spm_weights_dequant(const spm_weights* w, uint64_t row0, uint64_t rows, float* out_host);
+
+/* ---- sessions: N clients, one weight sweep per step ---- */
+spm_status spm_session_create(spm_model* m, int32_t max_clients, int32_t max_context,
+                              spm_session** out);
+spm_status spm_session_destroy(spm_session* s);
+/* Empty client `client`'s KV cache (position 0). */
+spm_status spm_client_reset(spm_session* s, int32_t client);
+spm_status spm_client_len(const spm_session* s, int32_t client, int32_t* len);
+/* One decode step for clients 0..n-1: tokens (host) in, greedy argmax (host,
+ * last index on ties) out; logits (host, n x vocab) optional. */
+spm_status spm_decode_step(spm_session* s, const uint32_t* tokens, int32_t n, float* logits_host,
+                           uint32_t* argmax_host);
+/* Same step on device buffers (no host copies): tokens_dev n uint32,
+ * argmax_dev n uint32, logits_dev n x vocab (may be NULL). Enqueued on the
+ * session stream; use spm_session_sync to wait. */
+spm_status spm_decode_step_device(spm_session* s, const uint32_t* tokens_dev, int32_t n,
+                                  float* logits_dev, uint32_t* argmax_dev);
+spm_status spm_session_sync(spm_session* s);
+/* The session's CUDA stream (cudaStream_t as void*). */
+spm_status spm_session_stream(const spm_session* s, void** cuda_stream);
+/* Capture steps as a CUDA graph per client count (1) or launch eagerly (0). */
+spm_status spm_session_set_graphs(spm_session* s, int32_t enable);
+/* Routes of the last step (MoE): layers x n x experts_used expert ids. */
+spm_status spm_session_routes(const spm_session* s, int32_t n, int32_t* routes_host);
+/* Kernel launches issued by one step at client count n (graph nodes). */
+spm_status spm_session_launches_per_step(spm_session* s, int32_t n, int32_t* launches);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

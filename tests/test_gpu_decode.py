@@ -1,0 +1,178 @@
+"""The whole token loop on the device against the oracle's CPU token loop.
+
+Bars: greedy tokens identical over the run; logits within
+max|delta| <= 1e-3 * max|logit| (fp32 accumulation); weight bytes per step
+independent of the client count; batched clients get what they get alone.
+"""
+import numpy as np
+import pytest
+
+import emufpga_b200 as eb
+from emufpga_b200 import configs
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-3
+DENSE = ["llama-q8_0", "llama-q6_k", "qwen3-q6_k", "qwen3-q5_k", "qwen3-q2_k"]
+
+
+def logits_close(got, want):
+    bound = LOGIT_TOL * float(np.abs(want).max())
+    return float(np.abs(got - want).max()) <= bound
+
+
+@pytest.fixture(scope="module")
+def models():
+    cache = {}
+
+    def get(name):
+        if name not in cache:
+            r = configs.TINY[name]
+            img = eb.synth_gguf(r)
+            cache[name] = (r, img, eb.Model(img, r.shape), O.OracleModel(img, r.shape))
+        return cache[name]
+
+    yield get
+    for r, img, m, om in cache.values():
+        m.close()
+
+
+@pytest.mark.parametrize("name", DENSE)
+def test_stepwise_logits_match_the_oracle(cuda, models, name):
+    # Teacher-forced: both sides see the same token every step.
+    r, img, m, om = models(name)
+    n, steps = 3, 6
+    sess = eb.Session(m, n, 16)
+    osess = om.session(n, 16)
+    for step in range(steps):
+        toks = [(step * 37 + i * 11) % r.shape.vocab for i in range(n)]
+        best, got = sess.decode_step(toks, want_logits=True)
+        want = osess.step(toks)
+        assert logits_close(got, want), (step, float(np.abs(got - want).max()), float(np.abs(want).max()))
+        assert best == [O.argmax_last(want[i]) for i in range(n)]
+    sess.close()
+
+
+@pytest.mark.parametrize("name", DENSE)
+def test_greedy_serving_matches_the_oracle(cuda, models, name):
+    r, img, m, om = models(name)
+    prompts = [configs.prompt_tokens(11, i, ln, r.shape.vocab) for i, ln in enumerate([3, 5, 8])]
+    want, wl = om.serve(prompts, 10)
+    got, gl = eb.serve(m, prompts, 10, want_logits=True)
+    assert got == want
+    assert logits_close(gl, wl)
+
+
+def test_batched_clients_get_what_they_get_alone(cuda, models):
+    # spm-batch/tests/batching.rs:128-145 on the device
+    r, img, m, om = models("qwen3-q6_k")
+    prompts = [configs.prompt_tokens(5, i, ln, r.shape.vocab) for i, ln in enumerate([2, 4, 6, 3, 5])]
+    together, _ = eb.serve(m, prompts, 6)
+    longest = max(len(p) for p in prompts)
+    for i, p in enumerate(prompts):
+        alone, _ = eb.serve(m, [p], 6 + longest - len(p))
+        assert alone[0] == together[i]
+
+
+def test_weight_bytes_do_not_depend_on_client_count(cuda, models):
+    # spm-batch/tests/batching.rs:147-217: bytes per sweep come from the
+    # descriptors, not from the clients.
+    r, img, m, om = models("llama-q8_0")
+    s = r.shape
+    per_layer = 2 * s.hidden * s.q_width + 2 * s.hidden * s.kv_width + 3 * s.hidden * s.intermediate
+    expect = (s.layers * per_layer + s.vocab * s.hidden) * 34 // 32
+    assert m.weight_bytes == expect
+    for n in (1, 2, 5):
+        sess = eb.Session(m, n, 8)
+        sess.decode_step([1] * n)
+        assert m.weight_bytes == expect
+        sess.close()
+
+
+def test_context_exhaustion_is_an_error_not_a_fault(cuda, models):
+    r, img, m, om = models("llama-q8_0")
+    sess = eb.Session(m, 1, 3)
+    for _ in range(3):
+        sess.decode_step([1])
+    with pytest.raises(eb.SpmError) as e:
+        sess.decode_step([1])
+    assert e.value.name == "SPM_E_CONTEXT"
+    sess.reset(0)
+    assert sess.length(0) == 0
+    sess.decode_step([1])
+    sess.close()
+
+
+def test_graph_and_eager_steps_agree_bit_for_bit(cuda, models):
+    r, img, m, om = models("qwen3-q5_k")
+    a = eb.Session(m, 2, 8, graphs=True)
+    b = eb.Session(m, 2, 8, graphs=False)
+    for t in range(4):
+        _, la = a.decode_step([t, t + 1], want_logits=True)
+        _, lb = b.decode_step([t, t + 1], want_logits=True)
+        assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+    assert a.launches_per_step(2) > 0
+
+
+def test_bad_token_is_refused(cuda, models):
+    r, img, m, om = models("llama-q8_0")
+    sess = eb.Session(m, 1, 4)
+    with pytest.raises(eb.SpmError):
+        sess.decode_step([r.shape.vocab])
+    sess.close()
+
+
+# ---- BASELINE shapes ----
+def test_smollm2_b5_full_run_matches_the_oracle(cuda):
+    """Config 2 (SmolLM2 Q8_0, 5 clients, prompts 16/24/32/48/64, 128 greedy
+    tokens each, lockstep): every greedy token identical over the full run."""
+    w = configs.WORKLOADS["smollm2-b5"]
+    r = configs.RECIPES[w["recipe"]]
+    img = eb.synth_gguf(r)
+    prompts = configs.workload_prompts("smollm2-b5")
+    om = O.OracleModel(img, r.shape)
+    want, wl = om.serve(prompts, w["steps"])
+    m = eb.Model(img, r.shape)
+    got, gl = eb.serve(m, prompts, w["steps"], want_logits=True)
+    m.close()
+    assert [len(g) for g in got] == [len(x) for x in want]
+    assert got == want
+    assert logits_close(gl, wl)
+
+
+def test_smollm2_b1_full_run_matches_the_oracle(cuda):
+    """Config 1 (SmolLM2 Q8_0, one 32-token prompt, 64 greedy tokens)."""
+    w = configs.WORKLOADS["smollm2-b1"]
+    r = configs.RECIPES[w["recipe"]]
+    img = eb.synth_gguf(r)
+    prompts = configs.workload_prompts("smollm2-b1")
+    want, wl = O.OracleModel(img, r.shape).serve(prompts, w["steps"])
+    m = eb.Model(img, r.shape)
+    got, gl = eb.serve(m, prompts, w["steps"], want_logits=True)
+    m.close()
+    assert got == want
+    assert logits_close(gl, wl)
+
+
+def test_qwen3_8b_shape_two_layers_matches_the_oracle(cuda):
+    """Qwen3-8B dimensions (hidden 4096, ffn 12288, 32/8 heads of 128, vocab
+    151936, Q6_K) with 2 of its 36 layers: stepwise logits and tokens."""
+    base = configs.RECIPES["qwen3-8b-q6_k"]
+    import dataclasses
+
+    r = base.replace(shape=dataclasses.replace(base.shape, layers=2))
+    img = eb.synth_gguf(r)
+    om = O.OracleModel(img, r.shape)
+    m = eb.Model(img, r.shape)
+    n = 4
+    sess = eb.Session(m, n, 8)
+    osess = om.session(n, 8)
+    for step in range(3):
+        toks = configs.prompt_tokens(3 + step, 0, n, r.shape.vocab)
+        best, got = sess.decode_step(toks, want_logits=True)
+        want = osess.step(toks)
+        assert logits_close(got, want)
+        assert best == [O.argmax_last(want[i]) for i in range(n)]
+    sess.close()
+    m.close()
