@@ -1,0 +1,112 @@
+// Device helpers shared by the kernels: loads, exact conversions, bulk copies
+// into shared memory, mbarriers with bounded waits, programmatic dependent
+// launch.
+#pragma once
+#include <cuda_fp16.h>
+
+#include "kernels.h"
+
+namespace spm {
+namespace dev {
+
+// ---- global loads ----
+__device__ __forceinline__ float4 ldx4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+
+// ---- shared loads by 32-bit shared address ----
+__device__ __forceinline__ uint32_t saddr(const void* p) { return uint32_t(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
+    return r;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
+    uint2 r;
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(a));
+    return r;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t r;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(a));
+    return r;
+}
+__device__ __forceinline__ uint32_t lds16(uint32_t a) {
+    unsigned short r;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(r) : "r"(a));
+    return r;
+}
+
+// Exact half -> float.
+__device__ __forceinline__ float h2f(uint32_t bits) {
+    return __half2float(__ushort_as_half((unsigned short)(bits & 0xffff)));
+}
+// 2^23 + (byte B of w), exactly; subtracting a constant recovers the code.
+template <int B>
+__device__ __forceinline__ float bytef(uint32_t w) {
+    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | B));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ---- time, errors ----
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s: then give up and flag
+__device__ __forceinline__ void flag(int32_t* status, int32_t code) {
+    if (status) atomicCAS(status, 0, code);
+}
+
+// ---- mbarriers (CTA scope) ----
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(saddr(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Waits for phase `parity` to complete; false after kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+    if (mbar_try(b, parity)) return true;
+    const uint64_t t0 = now_ns();
+    while (!mbar_try(b, parity))
+        if (now_ns() - t0 > kWaitLimitNs) return false;
+    return true;
+}
+// One bulk copy global -> shared (no multicast), completing on `bar`.
+// Source, destination and size must be multiples of 16 bytes.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     saddr(dst)),
+                 "l"(src), "r"(bytes), "r"(saddr(bar))
+                 : "memory");
+}
+
+// ---- programmatic dependent launch ----
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Named barrier among the first `threads` threads (id 1; 0 is __syncthreads).
+__device__ __forceinline__ void bar_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+}  // namespace dev
+}  // namespace spm

@@ -96,6 +96,10 @@ struct spm_weights {
     ~spm_weights() { if (dev) cudaFree(dev); }
 };
 
+// Upper bound on the CTAs of any GEMV launch (2 per SM) and so on the
+// sum-of-squares parts one launch writes.
+constexpr int kMaxParts = 2 * 1024;
+
 struct spm_session {
     spm_model* m = nullptr;
     int max_clients = 0, context = 0;
@@ -107,8 +111,13 @@ struct spm_session {
     int32_t* pos = nullptr;
     uint32_t *tokens = nullptr, *argmax = nullptr;
     uint32_t *h_tokens = nullptr, *h_argmax = nullptr;
+    float* sumsq = nullptr;            // two [kMaxParts][8] partial sum-of-squares buffers
+    float* attn_scratch = nullptr;
+    int32_t* attn_counters = nullptr;
+    int32_t* status = nullptr;         // device error word of bounded waits
+    int32_t* h_status = nullptr;
     std::vector<int> lens;
-    bool graphs = true;
+    bool graphs = true, pdl = true;
     std::map<int, cudaGraphExec_t> exec;
     std::map<int, int> launches;
     std::vector<void*> allocs;
@@ -117,6 +126,7 @@ struct spm_session {
         for (void* p : allocs) cudaFree(p);
         if (h_tokens) cudaFreeHost(h_tokens);
         if (h_argmax) cudaFreeHost(h_argmax);
+        if (h_status) cudaFreeHost(h_status);
         if (stream) cudaStreamDestroy(stream);
     }
     template <class T>
@@ -381,53 +391,92 @@ void add_job(GemvLaunch& L, const spm_model* m, int idx, const uint8_t* b, float
     L.total_tiles += uint32_t(p.tiles);
 }
 
-void run_gemv(const spm_model* m, const GemvLaunch& L, uint32_t dtype, cudaStream_t st) {
-    CUDA_OK(launch_gemv(dtype, L, m->sms, st));
+// Launches a GEMV; returns its grid size (the number of sum-of-squares parts
+// an EPI_ADD launch writes).
+int run_gemv(const spm_model* m, GemvLaunch L, uint32_t dtype, cudaStream_t st, bool pdl) {
+    int grid = 0;
+    CUDA_OK(launch_gemv(dtype, L, m->sms, st, pdl, &grid));
+    return grid;
 }
 
+// One decode step (spm-batch/src/step.rs:19-53), one kernel per streamed op:
+//   embed -> per layer [norm+QKV] [attention] [O+residual] [norm+gate/up+SwiGLU]
+//   [down+residual] -> [final norm + LM head] -> argmax -> positions += 1.
+// The RMSNorms are fused into the GEMV that consumes them: the residual-add
+// epilogues (and the embedding) write per-CTA sums of squares, which the next
+// GEMV reduces in a fixed order before normalising its activations on load.
 void enqueue_step(spm_session* s, int n) {
     spm_model* m = s->m;
     const spm_model_cfg& c = m->cfg;
     cudaStream_t st = s->stream;
+    const bool pdl = s->pdl;
     const int d = int(c.hidden), qw = int(c.heads * c.head_dim), kvw = int(c.kv_heads * c.head_dim);
     const int ff = int(c.intermediate);
     const StreamDesc& E = m->streams[m->embed];
-    CUDA_OK(launch_embed(E.pk.dtype, m->tiles(m->embed), E.pk, s->tokens, n, s->states, st));
+    float* part[2] = {s->sumsq, s->sumsq + kMaxParts * 8};
+    CUDA_OK(launch_embed(E.pk.dtype, m->tiles(m->embed), E.pk, s->tokens, n, s->states, part[0], st, false));
+    int parts = n;
+    auto norm_in = [&](GemvLaunch& g, int64_t gain, int which) {
+        g.gain = m->gains + gain;
+        g.sumsq = part[which];
+        g.sumsq_parts = parts;
+        g.eps = c.eps;
+    };
     for (uint32_t l = 0; l < c.layers; l++) {
         const LayerIdx& L = m->layers[l];
-        CUDA_OK(launch_rmsnorm(s->states, m->gains + L.attn_norm, s->normed, n, d, c.eps, st));
-        GemvLaunch g = gemv_base(m, L.q, s->normed, n);
+        GemvLaunch g = gemv_base(m, L.q, s->states, n);
+        g.status = s->status;
+        norm_in(g, L.attn_norm, 0);
         add_job(g, m, L.q, nullptr, s->q, qw, nullptr, 0, EPI_STORE);
         add_job(g, m, L.k, nullptr, s->k, kvw, nullptr, 0, EPI_STORE);
         add_job(g, m, L.v, nullptr, s->v, kvw, nullptr, 0, EPI_STORE);
-        run_gemv(m, g, m->streams[L.q].pk.dtype, st);
+        run_gemv(m, g, m->streams[L.q].pk.dtype, st, pdl);
         AttnParams P{};
         P.q = s->q; P.k = s->k; P.v = s->v; P.out = s->attn;
         P.kcache = s->kc; P.vcache = s->vc; P.pos = s->pos; P.rope = s->rope;
+        P.scratch = s->attn_scratch; P.counters = s->attn_counters;
         P.q_norm = L.q_norm >= 0 ? m->gains + L.q_norm : nullptr;
         P.k_norm = L.k_norm >= 0 ? m->gains + L.k_norm : nullptr;
         P.layer = int(l); P.layers = int(c.layers); P.context = s->context;
         P.heads = int(c.heads); P.kv_heads = int(c.kv_heads); P.head_dim = int(c.head_dim);
         P.family = int(c.family); P.eps = c.eps;
-        CUDA_OK(launch_attention(P, n, st));
+        CUDA_OK(launch_attention(P, n, st, pdl));
         GemvLaunch go = gemv_base(m, L.o, s->attn, n);
+        go.status = s->status;
+        go.sumsq_out = part[1];
         add_job(go, m, L.o, nullptr, s->states, d, s->states, d, EPI_ADD);
-        run_gemv(m, go, m->streams[L.o].pk.dtype, st);
-        CUDA_OK(launch_rmsnorm(s->states, m->gains + L.ffn_norm, s->normed, n, d, c.eps, st));
+        parts = run_gemv(m, go, m->streams[L.o].pk.dtype, st, pdl);
         if (is_moe(c)) fail(SPM_E_ARG, "MoE layers are not enabled in this build");
-        GemvLaunch gu = gemv_base(m, L.gate, s->normed, n);
+        GemvLaunch gu = gemv_base(m, L.gate, s->states, n);
+        gu.status = s->status;
+        norm_in(gu, L.ffn_norm, 1);
         add_job(gu, m, L.gate, m->tiles(L.up), s->act, ff, nullptr, 0, EPI_SWIGLU);
-        run_gemv(m, gu, m->streams[L.gate].pk.dtype, st);
+        run_gemv(m, gu, m->streams[L.gate].pk.dtype, st, pdl);
         GemvLaunch gd = gemv_base(m, L.down, s->act, n);
+        gd.status = s->status;
+        gd.sumsq_out = part[0];
         add_job(gd, m, L.down, nullptr, s->states, d, s->states, d, EPI_ADD);
-        run_gemv(m, gd, m->streams[L.down].pk.dtype, st);
+        parts = run_gemv(m, gd, m->streams[L.down].pk.dtype, st, pdl);
     }
-    CUDA_OK(launch_rmsnorm(s->states, m->gains + m->output_norm, s->normed, n, d, c.eps, st));
-    GemvLaunch gh = gemv_base(m, m->head, s->normed, n);
+    GemvLaunch gh = gemv_base(m, m->head, s->states, n);
+    gh.status = s->status;
+    norm_in(gh, m->output_norm, 0);
     add_job(gh, m, m->head, nullptr, s->logits, int(c.vocab), nullptr, 0, EPI_STORE);
-    run_gemv(m, gh, m->streams[m->head].pk.dtype, st);
-    CUDA_OK(launch_argmax(s->logits, n, int(c.vocab), s->argmax, st));
-    CUDA_OK(launch_advance(s->pos, n, st));
+    run_gemv(m, gh, m->streams[m->head].pk.dtype, st, pdl);
+    CUDA_OK(launch_argmax(s->logits, n, int(c.vocab), s->argmax, st, pdl));
+    CUDA_OK(launch_advance(s->pos, n, st, pdl));
+}
+
+// A bounded device wait that gave up leaves a code in the status word; the
+// step's outputs are then not trustworthy.  The word is cleared after reporting.
+void check_status(spm_session* s) {
+    if (*s->h_status) {
+        const int code = *s->h_status;
+        *s->h_status = 0;
+        cudaMemsetAsync(s->status, 0, sizeof(int32_t), s->stream);
+        cudaStreamSynchronize(s->stream);
+        fail(SPM_E_TIMEOUT, "a device wait gave up (code " + std::to_string(code) + ")");
+    }
 }
 
 // Client counts above 8 are not batched into one sweep by this build.
@@ -638,7 +687,7 @@ spm_status spm_streamed(const spm_model* m, int32_t index, const float* x_dev, i
             const int n = std::min(kMaxBatch, positions - p0);
             GemvLaunch L = gemv_base(m, index, x_dev + size_t(p0) * p.cols, n);
             add_job(L, m, index, nullptr, y_dev + size_t(p0) * p.rows, int(p.rows), nullptr, 0, EPI_STORE);
-            run_gemv(m, L, p.dtype, static_cast<cudaStream_t>(cuda_stream));
+            run_gemv(m, L, p.dtype, static_cast<cudaStream_t>(cuda_stream), false);
         }
     });
 }
@@ -689,7 +738,7 @@ spm_status spm_weights_gemv(const spm_weights* w, const float* x_dev, int32_t po
             J.rows = uint32_t(p.rows);
             J.epi = EPI_STORE;
             L.total_tiles = uint32_t(p.tiles);
-            CUDA_OK(launch_gemv(p.dtype, L, w->sms, static_cast<cudaStream_t>(cuda_stream)));
+            CUDA_OK(launch_gemv(p.dtype, L, w->sms, static_cast<cudaStream_t>(cuda_stream), false));
         }
     });
 }
@@ -732,11 +781,19 @@ spm_status spm_session_create(spm_model* m, int32_t max_clients, int32_t max_con
         s->pos = s->alloc<int32_t>(n);
         s->tokens = s->alloc<uint32_t>(n);
         s->argmax = s->alloc<uint32_t>(n);
+        s->sumsq = s->alloc<float>(2 * size_t(kMaxParts) * 8);
+        s->status = s->alloc<int32_t>(1);
+        const size_t chunks = (size_t(max_context) + kAttnChunk - 1) / kAttnChunk;
+        const size_t group = c.heads / c.kv_heads;
+        if (group * c.head_dim > 1024) fail(SPM_E_ARG, "attention supports at most 1024 query values per kv head");
+        s->attn_scratch = s->alloc<float>(n * c.kv_heads * chunks * group * (c.head_dim + 2));
+        s->attn_counters = s->alloc<int32_t>(n * c.kv_heads);
         auto table = rope_table(c, max_context);
         s->rope = s->alloc<float2>(table.size());
         CUDA_OK(cudaMemcpy(s->rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice));
         CUDA_OK(cudaMallocHost(&s->h_tokens, n * sizeof(uint32_t)));
         CUDA_OK(cudaMallocHost(&s->h_argmax, n * sizeof(uint32_t)));
+        CUDA_OK(cudaMallocHost(&s->h_status, sizeof(int32_t)));
         s->lens.assign(n, 0);
         *out = s.release();
     });
@@ -781,7 +838,9 @@ spm_status spm_decode_step(spm_session* s, const uint32_t* tokens, int32_t n, fl
         if (logits_host)
             CUDA_OK(cudaMemcpyAsync(logits_host, s->logits, size_t(n) * s->m->cfg.vocab * sizeof(float),
                                     cudaMemcpyDeviceToHost, s->stream));
+        CUDA_OK(cudaMemcpyAsync(s->h_status, s->status, sizeof(int32_t), cudaMemcpyDeviceToHost, s->stream));
         CUDA_OK(cudaStreamSynchronize(s->stream));
+        check_status(s);
         if (argmax_host) std::memcpy(argmax_host, s->h_argmax, size_t(n) * sizeof(uint32_t));
     });
 }
@@ -803,7 +862,11 @@ spm_status spm_decode_step_device(spm_session* s, const uint32_t* tokens_dev, in
 }
 
 spm_status spm_session_sync(spm_session* s) {
-    return guarded([&] { CUDA_OK(cudaStreamSynchronize(s->stream)); });
+    return guarded([&] {
+        CUDA_OK(cudaMemcpyAsync(s->h_status, s->status, sizeof(int32_t), cudaMemcpyDeviceToHost, s->stream));
+        CUDA_OK(cudaStreamSynchronize(s->stream));
+        check_status(s);
+    });
 }
 
 spm_status spm_session_stream(const spm_session* s, void** cuda_stream) {

@@ -1,0 +1,9 @@
+// Streaming GEMV instantiations for one block type (see gemv_impl.cuh).
+#include "gemv_impl.cuh"
+
+namespace spm {
+namespace gemv {
+template cudaError_t launch_enc<SPM_Q2_K>(const GemvLaunch&, bool, int, size_t, cudaStream_t, bool);
+template int occupancy_enc<SPM_Q2_K>(const GemvLaunch&, bool, size_t);
+}  // namespace gemv
+}  // namespace spm

@@ -1,452 +1,11 @@
-// sm_100a kernels of the decode token loop.
-//
-// The GEMV is the hot path: it streams one packed weight matrix (host_pack.cpp
-// layout) from HBM exactly once and applies every weight to all N clients'
-// activations while it is in registers -- the reference's "one weight,
-// every position" schedule (spm-linear/src/resident.rs:120-137) mapped onto
-// warps.  Each thread owns one 32-weight unit per pass; codes become floats
-// with a byte permute into the mantissa of 2^23 (exact), the 16- or
-// 32-weight sub-block sums are taken against the activations, and the block
-// scale is applied once per sub-block:
-//     sum_c w_c x_c = (d*sc) * sum_c q_c x_c  [- (dmin*m) * sum_c x_c]
-// which is the reference dot product regrouped (the weights themselves are
-// decoded bit-exactly by the dequant kernel below; only the order of the
-// fp32 additions differs from the reference FMA chain).
-#include <cuda_fp16.h>
-
-#include "kernels.h"
+// sm_100a kernels of the decode token loop besides the GEMV (gemv.cu):
+// exact dequantization (parity hook and embedding lookup), attention over the
+// device KV cache, greedy selection, position bookkeeping.
+#include "device.cuh"
 
 namespace spm {
 namespace {
-
-constexpr int kWarps = 8;
-
-__device__ __forceinline__ uint4 ldw4(const uint8_t* p) {
-    uint4 r;
-    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-        : "l"(p));
-    return r;
-}
-__device__ __forceinline__ uint2 ldw2(const uint8_t* p) {
-    uint2 r;
-    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
-    return r;
-}
-__device__ __forceinline__ uint32_t ldw1(const uint8_t* p) {
-    uint32_t r;
-    asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
-    return r;
-}
-__device__ __forceinline__ uint32_t ldu16(const uint8_t* p) {
-    unsigned short r;
-    asm("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
-    return r;
-}
-__device__ __forceinline__ float4 ldx4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
-
-// Exact half -> float.
-__device__ __forceinline__ float h2f(uint32_t bits) { return __half2float(__ushort_as_half((unsigned short)(bits & 0xffff))); }
-
-// 2^23 + (byte b of w), exactly; subtracting a constant recovers the code.
-template <int B>
-__device__ __forceinline__ float bytef(uint32_t w) {
-    return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | B));
-}
-
-template <int T>
-__device__ __forceinline__ uint32_t word(const uint4& v) {
-    return T == 0 ? v.x : T == 1 ? v.y : T == 2 ? v.z : v.w;
-}
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-template <int NC>
-__device__ __forceinline__ void dot4(float (&s)[NC], float f0, float f1, float f2, float f3, const float4 (&x)[NC]) {
-#pragma unroll
-    for (int c = 0; c < NC; c++) {
-        s[c] = fmaf(f0, x[c].x, s[c]);
-        s[c] = fmaf(f1, x[c].y, s[c]);
-        s[c] = fmaf(f2, x[c].z, s[c]);
-        s[c] = fmaf(f3, x[c].w, s[c]);
-    }
-}
-
-// Row `rt` of the tile that virtual row v reads (paired gate/up launches read
-// matrix b for v >= RR).
-template <int RR>
-__device__ __forceinline__ const uint8_t* vtile(const uint8_t* ta, const uint8_t* tb, int v) {
-    return v < RR ? ta : tb;
-}
-
-// ---------------------------------------------------------------- Q8_0 ----
-template <int NC, int VR, int RR>
-__device__ __forceinline__ void unit_q8_0(const uint8_t* ta, const uint8_t* tb, int r0, uint32_t u,
-                                          const GemvLaunch& L, float (&acc)[VR][NC]) {
-    const uint32_t U = L.cols >> 5;
-    uint4 q0[VR], q1[VR];
-    float d[VR];
-#pragma unroll
-    for (int v = 0; v < VR; v++) {
-        const uint8_t* t = vtile<RR>(ta, tb, v);
-        const size_t unit = size_t(r0 + v % RR) * U + u;
-        q0[v] = ldw4(t + unit * 32);
-        q1[v] = ldw4(t + unit * 32 + 16);
-        d[v] = h2f(ldu16(t + L.plane1 + unit * 2));
-    }
-    const float* xb = L.x + 32 * size_t(u);
-    float s[VR][NC];
-#pragma unroll
-    for (int v = 0; v < VR; v++)
-#pragma unroll
-        for (int c = 0; c < NC; c++) s[v][c] = 0.f;
-#pragma unroll
-    for (int t = 0; t < 8; t++) {
-        float4 x[NC];
-#pragma unroll
-        for (int c = 0; c < NC; c++) x[c] = ldx4(xb + size_t(c) * L.x_stride + 4 * t);
-#pragma unroll
-        for (int v = 0; v < VR; v++) {
-            uint32_t w = (t < 4 ? (t == 0 ? q0[v].x : t == 1 ? q0[v].y : t == 2 ? q0[v].z : q0[v].w)
-                                : (t == 4 ? q1[v].x : t == 5 ? q1[v].y : t == 6 ? q1[v].z : q1[v].w)) ^
-                         0x80808080u;
-            const float k = 8388736.0f;  // 2^23 + 128: (u8 ^ 0x80) - 128 == int8
-            dot4<NC>(s[v], bytef<0>(w) - k, bytef<1>(w) - k, bytef<2>(w) - k, bytef<3>(w) - k, x);
-        }
-    }
-#pragma unroll
-    for (int v = 0; v < VR; v++)
-#pragma unroll
-        for (int c = 0; c < NC; c++) acc[v][c] = fmaf(d[v], s[v][c], acc[v][c]);
-}
-
-// ---------------------------------------------------------------- Q6_K ----
-template <int NC, int VR, int RR>
-__device__ __forceinline__ void unit_q6_k(const uint8_t* ta, const uint8_t* tb, int r0, uint32_t u,
-                                          const GemvLaunch& L, float (&acc)[VR][NC]) {
-    const uint32_t U = L.cols >> 5, B = L.cols >> 8;
-    uint4 ql[VR];
-    uint2 qh[VR];
-    float dsa[VR], dsb[VR];
-#pragma unroll
-    for (int v = 0; v < VR; v++) {
-        const uint8_t* t = vtile<RR>(ta, tb, v);
-        const size_t row = size_t(r0 + v % RR), unit = row * U + u;
-        ql[v] = ldw4(t + unit * 16);
-        qh[v] = ldw2(t + L.plane1 + unit * 8);
-        const uint32_t sc = ldu16(t + L.plane2 + unit * 2);
-        const float d = h2f(ldu16(t + L.plane3 + (row * B + (u >> 3)) * 2));
-        dsa[v] = d * float(int8_t(sc & 0xff));
-        dsb[v] = d * float(int8_t(sc >> 8));
-    }
-    const float* xb = L.x + 32 * size_t(u);
-    float sa[VR][NC], sb[VR][NC];
-#pragma unroll
-    for (int v = 0; v < VR; v++)
-#pragma unroll
-        for (int c = 0; c < NC; c++) sa[v][c] = sb[v][c] = 0.f;
-#pragma unroll
-    for (int t = 0; t < 4; t++) {
-        float4 xa[NC], xc[NC];
-#pragma unroll
-        for (int c = 0; c < NC; c++) {
-            xa[c] = ldx4(xb + size_t(c) * L.x_stride + 4 * t);
-            xc[c] = ldx4(xb + size_t(c) * L.x_stride + 16 + 4 * t);
-        }
-#pragma unroll
-        for (int v = 0; v < VR; v++) {
-            const uint32_t w = t == 0 ? ql[v].x : t == 1 ? ql[v].y : t == 2 ? ql[v].z : ql[v].w;
-            const uint32_t ha = (t < 2 ? qh[v].x << (4 - 2 * t) : qh[v].x >> (2 * t - 4)) & 0x30303030u;
-            const uint32_t hb = (t < 2 ? qh[v].y << (4 - 2 * t) : qh[v].y >> (2 * t - 4)) & 0x30303030u;
-            const uint32_t qa = (w & 0x0F0F0F0Fu) | ha;
-            const uint32_t qb = ((w >> 4) & 0x0F0F0F0Fu) | hb;
-            const float k = 8388640.0f;  // 2^23 + 32
-            dot4<NC>(sa[v], bytef<0>(qa) - k, bytef<1>(qa) - k, bytef<2>(qa) - k, bytef<3>(qa) - k, xa);
-            dot4<NC>(sb[v], bytef<0>(qb) - k, bytef<1>(qb) - k, bytef<2>(qb) - k, bytef<3>(qb) - k, xc);
-        }
-    }
-#pragma unroll
-    for (int v = 0; v < VR; v++)
-#pragma unroll
-        for (int c = 0; c < NC; c++) {
-            acc[v][c] = fmaf(dsa[v], sa[v][c], acc[v][c]);
-            acc[v][c] = fmaf(dsb[v], sb[v][c], acc[v][c]);
-        }
-}
-
-// ---------------------------------------------------------------- Q5_K ----
-__device__ __forceinline__ uint32_t sbyte(const uint4& m, int k) {  // scales byte k (0..11)
-    const uint32_t w = k < 4 ? m.y : k < 8 ? m.z : m.w;
-    return (w >> (8 * (k & 3))) & 0xffu;
-}
-
-template <int NC, int VR, int RR>
-__device__ __forceinline__ void unit_q5_k(const uint8_t* ta, const uint8_t* tb, int r0, uint32_t u,
-                                          const GemvLaunch& L, float (&acc)[VR][NC]) {
-    const uint32_t U = L.cols >> 5, B = L.cols >> 8;
-    const int j = int(u & 7);
-    uint4 qs[VR];
-    uint32_t qh[VR];
-    float ds[VR], dm[VR];
-#pragma unroll
-    for (int v = 0; v < VR; v++) {
-        const uint8_t* t = vtile<RR>(ta, tb, v);
-        const size_t row = size_t(r0 + v % RR), unit = row * U + u;
-        const uint4 m = ldw4(t + (row * B + (u >> 3)) * 16);
-        qs[v] = ldw4(t + L.plane1 + unit * 16);
-        qh[v] = ldw1(t + L.plane2 + unit * 4);
-        uint32_t sc, mn;
-        if (j < 4) {
-            sc = sbyte(m, j) & 63;
-            mn = sbyte(m, j + 4) & 63;
-        } else {
-            sc = (sbyte(m, j + 4) & 15) | ((sbyte(m, j - 4) >> 6) << 4);
-            mn = (sbyte(m, j + 4) >> 4) | ((sbyte(m, j) >> 6) << 4);
-        }
-        ds[v] = h2f(m.x) * float(sc);
-        dm[v] = h2f(m.x >> 16) * float(mn);
-    }
-    const float* xb = L.x + 32 * size_t(u);
-    float s[VR][NC], xs[NC];
-#pragma unroll
-    for (int c = 0; c < NC; c++) xs[c] = 0.f;
-#pragma unroll
-    for (int v = 0; v < VR; v++)
-#pragma unroll
-        for (int c = 0; c < NC; c++) s[v][c] = 0.f;
-#pragma unroll
-    for (int t = 0; t < 4; t++) {
-        float4 xa[NC], xc[NC];
-#pragma unroll
-        for (int c = 0; c < NC; c++) {
-            xa[c] = ldx4(xb + size_t(c) * L.x_stride + 4 * t);
-            xc[c] = ldx4(xb + size_t(c) * L.x_stride + 16 + 4 * t);
-            xs[c] += (xa[c].x + xa[c].y) + (xa[c].z + xa[c].w) + ((xc[c].x + xc[c].y) + (xc[c].z + xc[c].w));
-        }
-#pragma unroll
-        for (int v = 0; v < VR; v++) {
-            const uint32_t w = t == 0 ? qs[v].x : t == 1 ? qs[v].y : t == 2 ? qs[v].z : qs[v].w;
-            const uint32_t spa = (((qh[v] >> (4 * t)) & 0xfu) * 0x02040810u) & 0x10101010u;
-            const uint32_t spb = (((qh[v] >> (16 + 4 * t)) & 0xfu) * 0x02040810u) & 0x10101010u;
-            const uint32_t qa = (w & 0x0F0F0F0Fu) | spa;
-            const uint32_t qb = ((w >> 4) & 0x0F0F0F0Fu) | spb;
-            const float k = 8388608.0f;
-            dot4<NC>(s[v], bytef<0>(qa) - k, bytef<1>(qa) - k, bytef<2>(qa) - k, bytef<3>(qa) - k, xa);
-            dot4<NC>(s[v], bytef<0>(qb) - k, bytef<1>(qb) - k, bytef<2>(qb) - k, bytef<3>(qb) - k, xc);
-        }
-    }
-#pragma unroll
-    for (int v = 0; v < VR; v++)
-#pragma unroll
-        for (int c = 0; c < NC; c++) acc[v][c] = fmaf(-dm[v], xs[c], fmaf(ds[v], s[v][c], acc[v][c]));
-}
-
-// ---------------------------------------------------------------- Q2_K ----
-template <int NC, int VR, int RR>
-__device__ __forceinline__ void unit_q2_k(const uint8_t* ta, const uint8_t* tb, int r0, uint32_t u,
-                                          const GemvLaunch& L, float (&acc)[VR][NC]) {
-    const uint32_t U = L.cols >> 5, B = L.cols >> 8;
-    uint2 qs[VR];
-    float dl[VR][2], ml[VR][2];
-#pragma unroll
-    for (int v = 0; v < VR; v++) {
-        const uint8_t* t = vtile<RR>(ta, tb, v);
-        const size_t row = size_t(r0 + v % RR), unit = row * U + u;
-        qs[v] = ldw2(t + unit * 8);
-        const uint32_t sc = ldu16(t + L.plane1 + unit * 2);
-        const uint32_t dd = ldw1(t + L.plane2 + (row * B + (u >> 3)) * 4);
-        const float d = h2f(dd), dmin = h2f(dd >> 16);
-        dl[v][0] = d * float(sc & 15);
-        ml[v][0] = dmin * float((sc >> 4) & 15);
-        dl[v][1] = d * float((sc >> 8) & 15);
-        ml[v][1] = dmin * float((sc >> 12) & 15);
-    }
-    const float* xb = L.x + 32 * size_t(u);
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        float s[VR][NC], xs[NC];
-#pragma unroll
-        for (int c = 0; c < NC; c++) xs[c] = 0.f;
-#pragma unroll
-        for (int v = 0; v < VR; v++)
-#pragma unroll
-            for (int c = 0; c < NC; c++) s[v][c] = 0.f;
-#pragma unroll
-        for (int t = 0; t < 4; t++) {
-            float4 x[NC];
-#pragma unroll
-            for (int c = 0; c < NC; c++) {
-                x[c] = ldx4(xb + size_t(c) * L.x_stride + 16 * h + 4 * t);
-                xs[c] += (x[c].x + x[c].y) + (x[c].z + x[c].w);
-            }
-#pragma unroll
-            for (int v = 0; v < VR; v++) {
-                const uint32_t q = ((h == 0 ? qs[v].x : qs[v].y) >> (2 * t)) & 0x03030303u;
-                const float k = 8388608.0f;
-                dot4<NC>(s[v], bytef<0>(q) - k, bytef<1>(q) - k, bytef<2>(q) - k, bytef<3>(q) - k, x);
-            }
-        }
-#pragma unroll
-        for (int v = 0; v < VR; v++)
-#pragma unroll
-            for (int c = 0; c < NC; c++) acc[v][c] = fmaf(-ml[v][h], xs[c], fmaf(dl[v][h], s[v][c], acc[v][c]));
-    }
-}
-
-// ----------------------------------------------------------------- F32 ----
-template <int NC, int VR, int RR>
-__device__ __forceinline__ void unit_f32(const uint8_t* ta, const uint8_t* tb, int r0, uint32_t u,
-                                         const GemvLaunch& L, float (&acc)[VR][NC]) {
-    const float* xb = L.x + 32 * size_t(u);
-#pragma unroll
-    for (int t = 0; t < 8; t++) {
-        float4 x[NC];
-#pragma unroll
-        for (int c = 0; c < NC; c++) x[c] = ldx4(xb + size_t(c) * L.x_stride + 4 * t);
-#pragma unroll
-        for (int v = 0; v < VR; v++) {
-            const uint8_t* tl = vtile<RR>(ta, tb, v);
-            const uint4 w = ldw4(tl + (size_t(r0 + v % RR) * L.cols + 32 * size_t(u) + 4 * t) * 4);
-            dot4<NC>(acc[v], __uint_as_float(w.x), __uint_as_float(w.y), __uint_as_float(w.z),
-                     __uint_as_float(w.w), x);
-        }
-    }
-}
-
-template <int ENC, int NC, int VR, int RR>
-__device__ __forceinline__ void unit_dot(const uint8_t* ta, const uint8_t* tb, int r0, uint32_t u,
-                                         const GemvLaunch& L, float (&acc)[VR][NC]) {
-    if constexpr (ENC == SPM_Q8_0) unit_q8_0<NC, VR, RR>(ta, tb, r0, u, L, acc);
-    else if constexpr (ENC == SPM_Q6_K) unit_q6_k<NC, VR, RR>(ta, tb, r0, u, L, acc);
-    else if constexpr (ENC == SPM_Q5_K) unit_q5_k<NC, VR, RR>(ta, tb, r0, u, L, acc);
-    else if constexpr (ENC == SPM_Q2_K) unit_q2_k<NC, VR, RR>(ta, tb, r0, u, L, acc);
-    else unit_f32<NC, VR, RR>(ta, tb, r0, u, L, acc);
-}
-
-__device__ __forceinline__ float silu_mul(float g, float u) { return __fdiv_rn(g, 1.0f + expf(-g)) * u; }
-
-// A CTA of 8 warps takes 8/KS tiles at a time; KS warps share a tile, each
-// summing every KS-th run of 32 units, and their partial sums are added in a
-// fixed order (deterministic).
-template <int ENC, int NC, int VR, bool DUAL, int KS>
-__global__ void __launch_bounds__(kWarps * 32) gemv_kernel(const __grid_constant__ GemvLaunch L) {
-    constexpr int RR = DUAL ? VR / 2 : VR;
-    constexpr int TPC = kWarps / KS;  // tiles per CTA pass
-    __shared__ float part[kWarps][VR][NC];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int slot = warp / KS, ks = warp % KS;
-    const uint32_t U = L.cols >> 5;
-    for (uint32_t base = blockIdx.x * TPC; base < L.total_tiles; base += gridDim.x * TPC) {
-        const uint32_t g = base + slot;
-        const bool active = g < L.total_tiles;
-        GemvJob J = L.job[0];
-        if (L.njobs > 1 && g >= L.job[1].tile_begin) J = L.job[1];
-        if (L.njobs > 2 && g >= L.job[2].tile_begin) J = L.job[2];
-        if (L.njobs > 3 && g >= L.job[3].tile_begin) J = L.job[3];
-        const uint32_t tile = g - J.tile_begin;
-        const uint8_t* ta = J.a + size_t(tile) * L.tile_bytes;
-        const uint8_t* tb = DUAL ? J.b + size_t(tile) * L.tile_bytes : nullptr;
-#pragma unroll 1
-        for (int r0 = 0; r0 < kTileRows; r0 += RR) {
-            float acc[VR][NC];
-#pragma unroll
-            for (int v = 0; v < VR; v++)
-#pragma unroll
-                for (int c = 0; c < NC; c++) acc[v][c] = 0.f;
-            if (active) {
-#pragma unroll 1
-                for (uint32_t u = uint32_t(ks) * 32 + lane; u < U; u += 32 * KS)
-                    unit_dot<ENC, NC, VR, RR>(ta, tb, r0, u, L, acc);
-            }
-#pragma unroll
-            for (int v = 0; v < VR; v++)
-#pragma unroll
-                for (int c = 0; c < NC; c++) acc[v][c] = warp_sum(acc[v][c]);
-            if constexpr (KS > 1) {
-                if (lane == 0) {
-#pragma unroll
-                    for (int v = 0; v < VR; v++)
-#pragma unroll
-                        for (int c = 0; c < NC; c++) part[warp][v][c] = acc[v][c];
-                }
-                __syncthreads();
-                if (ks == 0) {
-#pragma unroll
-                    for (int v = 0; v < VR; v++)
-#pragma unroll
-                        for (int c = 0; c < NC; c++) {
-                            float t = part[warp][v][c];
-#pragma unroll
-                            for (int k = 1; k < KS; k++) t += part[warp + k][v][c];
-                            acc[v][c] = t;
-                        }
-                }
-                __syncthreads();
-            }
-            if (active && ks == 0) {
-#pragma unroll
-                for (int v = 0; v < RR; v++) {
-                    const uint32_t row = tile * kTileRows + r0 + v;
-                    if (row >= J.rows) continue;
-#pragma unroll
-                    for (int c = 0; c < NC; c++) {
-                        if (lane != ((v * NC + c) & 31)) continue;
-                        float r = acc[v][c];
-                        if constexpr (DUAL) r = silu_mul(acc[v][c], acc[v + RR][c]);
-                        if (J.epi == EPI_ADD) r = J.aux[size_t(c) * J.aux_stride + row] + r;
-                        J.y[size_t(c) * J.y_stride + row] = r;
-                    }
-                }
-            }
-        }
-    }
-}
-
-template <int ENC, int NC, int VR, bool DUAL>
-cudaError_t launch_ks(const GemvLaunch& L, int sms, cudaStream_t s) {
-    // Enough warps in flight to cover HBM latency: split K when tiles are few.
-    const uint32_t U = L.cols >> 5;
-    int ks = 1;
-    while (ks < 8 && uint64_t(L.total_tiles) * ks < uint64_t(sms) * 48 && U >= 64u * ks) ks *= 2;
-    const uint32_t tpc = kWarps / ks;
-    uint32_t grid = (L.total_tiles + tpc - 1) / tpc;
-    const uint32_t cap = uint32_t(sms) * 16;
-    if (grid > cap) grid = cap;
-    if (grid == 0) return cudaSuccess;
-    switch (ks) {
-        case 1: gemv_kernel<ENC, NC, VR, DUAL, 1><<<grid, kWarps * 32, 0, s>>>(L); break;
-        case 2: gemv_kernel<ENC, NC, VR, DUAL, 2><<<grid, kWarps * 32, 0, s>>>(L); break;
-        case 4: gemv_kernel<ENC, NC, VR, DUAL, 4><<<grid, kWarps * 32, 0, s>>>(L); break;
-        default: gemv_kernel<ENC, NC, VR, DUAL, 8><<<grid, kWarps * 32, 0, s>>>(L); break;
-    }
-    return cudaGetLastError();
-}
-
-template <int ENC, int NC>
-cudaError_t launch_nc(const GemvLaunch& L, bool dual, int sms, cudaStream_t s) {
-    constexpr int VR = NC <= 4 ? 4 : 2;
-    if (dual) return launch_ks<ENC, NC, VR, true>(L, sms, s);
-    return launch_ks<ENC, NC, VR, false>(L, sms, s);
-}
-
-template <int ENC>
-cudaError_t launch_enc(const GemvLaunch& L, bool dual, int sms, cudaStream_t s) {
-    switch (L.n) {
-        case 1: return launch_nc<ENC, 1>(L, dual, sms, s);
-        case 2: return launch_nc<ENC, 2>(L, dual, sms, s);
-        case 3: return launch_nc<ENC, 3>(L, dual, sms, s);
-        case 4: return launch_nc<ENC, 4>(L, dual, sms, s);
-        case 5: return launch_nc<ENC, 5>(L, dual, sms, s);
-        case 6: return launch_nc<ENC, 6>(L, dual, sms, s);
-        case 7: return launch_nc<ENC, 7>(L, dual, sms, s);
-        case 8: return launch_nc<ENC, 8>(L, dual, sms, s);
-        default: return cudaErrorInvalidValue;
-    }
-}
+using namespace dev;
 
 // ---------------------------------------------------------------- decode ----
 // Exact dequantization of unit u of a packed row, in the reference's
@@ -517,6 +76,7 @@ __device__ void dequant_unit(uint32_t dtype, const uint8_t* tile, const Packed& 
     }
 }
 
+
 __global__ void dequant_kernel(uint32_t dtype, const uint8_t* tiles, const Packed p, uint64_t row0, uint64_t rows,
                                float* out) {
     const uint32_t U = uint32_t(p.cols >> 5);
@@ -529,15 +89,6 @@ __global__ void dequant_kernel(uint32_t dtype, const uint8_t* tiles, const Packe
     }
 }
 
-__global__ void embed_kernel(uint32_t dtype, const uint8_t* tiles, const Packed p, const uint32_t* tokens,
-                             float* out) {
-    const uint32_t U = uint32_t(p.cols >> 5);
-    const uint64_t r = tokens[blockIdx.x];
-    for (uint32_t u = threadIdx.x; u < U; u += blockDim.x)
-        dequant_unit(dtype, tiles + (r / kTileRows) * p.tile_bytes, p, uint32_t(r % kTileRows), u,
-                     out + size_t(blockIdx.x) * p.cols + 32 * size_t(u));
-}
-
 // ------------------------------------------------------------ reductions ----
 template <int NT>
 __device__ float block_sum(float v, float* red) {
@@ -545,14 +96,13 @@ __device__ float block_sum(float v, float* red) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     if (lane == 0) red[w] = v;
     __syncthreads();
-    float t = 0.f;
     if (threadIdx.x < 32) {
-        t = threadIdx.x < NT / 32 ? red[threadIdx.x] : 0.f;
+        float t = threadIdx.x < NT / 32 ? red[threadIdx.x] : 0.f;
         t = warp_sum(t);
         if (threadIdx.x == 0) red[32] = t;
     }
     __syncthreads();
-    t = red[32];
+    const float t = red[32];
     __syncthreads();
     return t;
 }
@@ -576,17 +126,28 @@ __device__ float block_max(float v, float* red) {
     return t;
 }
 
-// RMSNorm: x * (1/sqrt(mean(x^2) + eps)) * g (spm-smol-ops/src/norm.rs:12-21,
-// spm-qwen3-slice/src/math.rs:1-10; both round the same way).
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const float* x, const float* g, float* out, int width, float eps) {
+// Embedding gather (spm-batch/src/step.rs:27-30): decode the token's row,
+// exactly; also the row's sum of squares for the first layer's fused norm.
+__global__ void __launch_bounds__(128) embed_kernel(uint32_t dtype, const uint8_t* tiles, const Packed p,
+                                                    const uint32_t* tokens, float* out, float* sumsq) {
     __shared__ float red[33];
-    const float* xr = x + size_t(blockIdx.x) * width;
+    pdl_wait();
+    const uint32_t U = uint32_t(p.cols >> 5);
+    const uint64_t r = tokens[blockIdx.x];
+    float* o = out + size_t(blockIdx.x) * p.cols;
     float ss = 0.f;
-    for (int i = threadIdx.x; i < width; i += 256) ss = fmaf(xr[i], xr[i], ss);
-    ss = block_sum<256>(ss, red);
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(width)), eps)));
-    for (int i = threadIdx.x; i < width; i += 256)
-        out[size_t(blockIdx.x) * width + i] = __fmul_rn(__fmul_rn(xr[i], scale), g[i]);
+    for (uint32_t u = threadIdx.x; u < U; u += blockDim.x) {
+        float w[32];
+        dequant_unit(dtype, tiles + (r / kTileRows) * p.tile_bytes, p, uint32_t(r % kTileRows), u, w);
+#pragma unroll
+        for (int l = 0; l < 32; l++) {
+            o[32 * size_t(u) + l] = w[l];
+            ss = fmaf(w[l], w[l], ss);
+        }
+    }
+    ss = block_sum<128>(ss, red);
+    pdl_trigger();
+    if (threadIdx.x < 8) sumsq[blockIdx.x * 8 + threadIdx.x] = threadIdx.x == blockIdx.x ? ss : 0.f;
 }
 
 // Greedy selection: largest logit, LAST index among equals
@@ -594,6 +155,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* x, const floa
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int vocab, uint32_t* out) {
     __shared__ float sv[32];
     __shared__ int si[32];
+    pdl_wait();
     const float* row = logits + size_t(blockIdx.x) * vocab;
     float bv = -INFINITY;
     int bi = -1;
@@ -610,6 +172,7 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int v
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     if (lane == 0) { sv[w] = bv; si[w] = bi; }
     __syncthreads();
+    pdl_trigger();
     if (w == 0) {
         bv = sv[lane];
         bi = si[lane];
@@ -624,16 +187,26 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int v
 }
 
 __global__ void advance_kernel(int32_t* pos, int n) {
+    pdl_wait();
+    pdl_trigger();
     if (threadIdx.x < n) pos[threadIdx.x] += 1;
 }
 
 // ------------------------------------------------------------- attention ----
-// One CTA per (kv head, client): QK-norm, RoPE at the client's position from
-// the host-computed table, KV append, then each query head of the group
-// attends over positions 0..pos (the diagonal included).
-//   LLAMA  : spm-kv/src/attend.rs:37-94   (dot*(1/sqrt hd), fma value chain)
-//   others : spm-qwen3-slice/src/attention.rs:11-79 (dot/sqrt hd, mul+add values)
-constexpr int kAttnThreads = 128;
+// Grid (kv head, client, position chunk of kChunk).  Every CTA applies the
+// QK-norm and RoPE (host-computed cos/sin table) to its group's queries and
+// the new key; the CTA whose chunk holds the new position appends k, v to the
+// cache (spm-kv/src/cache.rs:49-58).  Each CTA scores its positions for all
+// query heads of the group (keys staged in shared memory, shared by the
+// group), forms its chunk's softmax partials (max, sum, unnormalised value
+// sum), and the last CTA of a (kv head, client) to finish combines the chunks
+// in chunk order.  The scores, the mask (diagonal included) and the GQA head
+// mapping are the reference's:
+//   LLAMA  : spm-kv/src/attend.rs:37-94   (dot * (1/sqrt hd))
+//   others : spm-qwen3-slice/src/attention.rs:36-79 (dot / sqrt hd), with
+//            per-head (Qwen3) or full-width (OLMoE) QK RMSNorm.
+constexpr int kAttnThreads = 256;
+constexpr int kSub = 64;  // positions staged per pass
 
 __device__ __forceinline__ void rope_pair(float& x, float& y, float c, float s, bool llama) {
     if (llama) {  // spm-ops/src/attention.rs:249-251
@@ -650,25 +223,29 @@ __device__ __forceinline__ void rope_pair(float& x, float& y, float c, float s, 
 }
 
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParams P) {
-    extern __shared__ float sm[];
-    const int kvh = blockIdx.x, i = blockIdx.y;
+    extern __shared__ __align__(16) float sm[];
+    const int kvh = blockIdx.x, i = blockIdx.y, chunk = blockIdx.z, S = gridDim.z;
     const int hd = P.head_dim, group = P.heads / P.kv_heads;
-    const int qw = P.heads * hd, kvw = P.kv_heads * hd;
+    const int qw = P.heads * hd, kvw = P.kv_heads * hd, ld = hd + 4;
     const bool llama = P.family == SPM_FAMILY_LLAMA;
-    float* qs = sm;                   // group * hd
-    float* ks = qs + group * hd;      // hd
-    float* scores = ks + hd;          // context
-    float* red = scores + P.context;  // 33
+    float* qs = sm;                         // group * hd
+    float* kn = qs + group * hd;            // hd (new key)
+    float* vn = kn + hd;                    // hd (new value)
+    float* kv = vn + hd;                    // kSub * ld (staged keys, then values)
+    float* sc = kv + kSub * ld;             // group * kChunk scores
+    float* red = sc + group * kAttnChunk;   // 64
+    pdl_wait();
     const int pos = P.pos[i];
+    const int p0 = chunk * kAttnChunk;
+    const int p1 = min(pos + 1, p0 + kAttnChunk);
     const float* qg = P.q + size_t(i) * qw + size_t(kvh) * group * hd;
-    const float* kg = P.k + size_t(i) * kvw + size_t(kvh) * hd;
-    const float* vg = P.v + size_t(i) * kvw + size_t(kvh) * hd;
     for (int t = threadIdx.x; t < group * hd; t += kAttnThreads) qs[t] = qg[t];
-    for (int t = threadIdx.x; t < hd; t += kAttnThreads) ks[t] = kg[t];
+    for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
+        kn[t] = P.k[size_t(i) * kvw + size_t(kvh) * hd + t];
+        vn[t] = P.v[size_t(i) * kvw + size_t(kvh) * hd + t];
+    }
     __syncthreads();
-    // ---- QK-norm ----
     if (P.family == SPM_FAMILY_OLMOE) {
-        // Full-width RMSNorm of the whole q and k projections.
         float sq = 0.f, sk = 0.f;
         for (int t = threadIdx.x; t < qw; t += kAttnThreads) sq = fmaf(P.q[size_t(i) * qw + t], P.q[size_t(i) * qw + t], sq);
         for (int t = threadIdx.x; t < kvw; t += kAttnThreads) sk = fmaf(P.k[size_t(i) * kvw + t], P.k[size_t(i) * kvw + t], sk);
@@ -678,110 +255,212 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         const float sck = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sk, float(kvw)), P.eps)));
         for (int t = threadIdx.x; t < group * hd; t += kAttnThreads)
             qs[t] = __fmul_rn(__fmul_rn(qs[t], scq), P.q_norm[kvh * group * hd + t]);
-        for (int t = threadIdx.x; t < hd; t += kAttnThreads)
-            ks[t] = __fmul_rn(__fmul_rn(ks[t], sck), P.k_norm[kvh * hd + t]);
+        for (int t = threadIdx.x; t < hd; t += kAttnThreads) kn[t] = __fmul_rn(__fmul_rn(kn[t], sck), P.k_norm[kvh * hd + t]);
         __syncthreads();
     } else if (!llama) {
-        // Per-head RMSNorm (spm-qwen3-slice/src/attention.rs:27-34).
-        for (int h = 0; h <= group; h++) {
-            float* x = h < group ? qs + h * hd : ks;
+        // per-head RMSNorm, one warp per head (spm-qwen3-slice/src/attention.rs:27-34)
+        const int lane = threadIdx.x & 31;
+        for (int h = threadIdx.x >> 5; h <= group; h += kAttnThreads / 32) {
+            float* x = h < group ? qs + h * hd : kn;
             const float* g = h < group ? P.q_norm : P.k_norm;
             float ss = 0.f;
-            for (int t = threadIdx.x; t < hd; t += kAttnThreads) ss = fmaf(x[t], x[t], ss);
-            ss = block_sum<kAttnThreads>(ss, red);
-            const float sc = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(hd)), P.eps)));
-            for (int t = threadIdx.x; t < hd; t += kAttnThreads) x[t] = __fmul_rn(__fmul_rn(x[t], sc), g[t]);
-            __syncthreads();
+            for (int t = lane; t < hd; t += 32) ss = fmaf(x[t], x[t], ss);
+            ss = warp_sum(ss);
+            const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(hd)), P.eps)));
+            __syncwarp();
+            for (int t = lane; t < hd; t += 32) x[t] = __fmul_rn(__fmul_rn(x[t], s), g[t]);
         }
+        __syncthreads();
     }
-    // ---- RoPE (half-split pairs i, i + hd/2) ----
     const int half = hd / 2;
     const float2* rt = P.rope + size_t(pos) * half;
     for (int t = threadIdx.x; t < (group + 1) * half; t += kAttnThreads) {
         const int h = t / half, j = t % half;
-        float* x = h < group ? qs + h * hd : ks;
+        float* x = h < group ? qs + h * hd : kn;
         const float2 cs = rt[j];
         rope_pair(x[j], x[j + half], cs.x, cs.y, llama);
     }
     __syncthreads();
-    // ---- KV append (spm-kv/src/cache.rs:49-58) ----
-    const size_t layer_base = (size_t(i) * P.layers + P.layer) * P.context * size_t(kvw) + size_t(kvh) * hd;
-    float* kc = P.kcache + layer_base;
-    float* vc = P.vcache + layer_base;
-    for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
-        kc[size_t(pos) * kvw + t] = ks[t];
-        vc[size_t(pos) * kvw + t] = vg[t];
-    }
+    const size_t base = (size_t(i) * P.layers + P.layer) * P.context * size_t(kvw) + size_t(kvh) * hd;
+    float* kc = P.kcache + base;
+    float* vc = P.vcache + base;
+    if (pos >= p0 && pos < p0 + kAttnChunk)
+        for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
+            kc[size_t(pos) * kvw + t] = kn[t];
+            vc[size_t(pos) * kvw + t] = vn[t];
+        }
     __syncthreads();
-    const int positions = pos + 1;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(float(hd)));
     const float denom = __fsqrt_rn(float(hd));
-    for (int h = 0; h < group; h++) {
-        const float* q = qs + h * hd;
-        for (int p = warp; p < positions; p += kAttnThreads / 32) {
-            const float* kp = kc + size_t(p) * kvw;
+    const int npos = max(0, p1 - p0);
+    // ---- scores for this chunk, all heads of the group ----
+    for (int b0 = 0; b0 < npos; b0 += kSub) {
+        const int nb = min(kSub, npos - b0);
+        for (int t = threadIdx.x; t < nb * (hd / 4); t += kAttnThreads) {
+            const int p = t / (hd / 4), c4 = t % (hd / 4);
+            const float4 v = *reinterpret_cast<const float4*>(kc + size_t(p0 + b0 + p) * kvw + 4 * c4);
+            *reinterpret_cast<float4*>(kv + p * ld + 4 * c4) = v;
+        }
+        __syncthreads();
+        for (int t = threadIdx.x; t < nb * group; t += kAttnThreads) {
+            const int p = t % nb, h = t / nb;
+            const float* q = qs + h * hd;
+            const float* k = kv + p * ld;
             float d = 0.f;
-            for (int t = lane; t < hd; t += 32) d = fmaf(q[t], kp[t], d);
-            d = warp_sum(d);
-            if (lane == 0) scores[p] = llama ? __fmul_rn(d, scale) : __fdiv_rn(d, denom);
-        }
-        __syncthreads();
-        float mx = -INFINITY;
-        for (int p = threadIdx.x; p < positions; p += kAttnThreads) mx = fmaxf(mx, scores[p]);
-        mx = block_max<kAttnThreads>(mx, red);
-        float tot = 0.f;
-        for (int p = threadIdx.x; p < positions; p += kAttnThreads) {
-            const float e = expf(scores[p] - mx);
-            scores[p] = e;
-            tot += e;
-        }
-        tot = block_sum<kAttnThreads>(tot, red);
-        for (int p = threadIdx.x; p < positions; p += kAttnThreads) scores[p] = __fdiv_rn(scores[p], tot);
-        __syncthreads();
-        float* o = P.out + size_t(i) * qw + (size_t(kvh) * group + h) * hd;
-        for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
-            float a = 0.f;
-            for (int p = 0; p < positions; p++) {
-                const float v = vc[size_t(p) * kvw + t];
-                a = llama ? __fmaf_rn(scores[p], v, a) : __fadd_rn(a, __fmul_rn(v, scores[p]));
+            for (int c = 0; c < hd; c += 4) {
+                const float4 kk = *reinterpret_cast<const float4*>(k + c);
+                d = fmaf(q[c], kk.x, d);
+                d = fmaf(q[c + 1], kk.y, d);
+                d = fmaf(q[c + 2], kk.z, d);
+                d = fmaf(q[c + 3], kk.w, d);
             }
-            o[t] = a;
+            sc[h * kAttnChunk + b0 + p] = llama ? __fmul_rn(d, scale) : __fdiv_rn(d, denom);
         }
         __syncthreads();
+    }
+    // ---- chunk softmax partials per head (one warp per head): m, l ----
+    float* part = P.scratch + ((size_t(i) * P.kv_heads + kvh) * S + chunk) * group * (hd + 2);
+    float* ml = red;  // [group][2]: max, sum of exp
+    {
+        const int lane = threadIdx.x & 31;
+        for (int h = threadIdx.x >> 5; h < group; h += kAttnThreads / 32) {
+            float mx = -INFINITY;
+            for (int p = lane; p < npos; p += 32) mx = fmaxf(mx, sc[h * kAttnChunk + p]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            float tot = 0.f;
+            for (int p = lane; p < npos; p += 32) {
+                const float e = expf(sc[h * kAttnChunk + p] - mx);
+                sc[h * kAttnChunk + p] = e;
+                tot += e;
+            }
+            tot = warp_sum(tot);
+            if (lane == 0) {
+                ml[2 * h] = mx;
+                ml[2 * h + 1] = tot;
+            }
+        }
+    }
+    __syncthreads();
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // (head, dim) pairs t, t+256, ... (group*hd <= 1024)
+    for (int b0 = 0; b0 < npos; b0 += kSub) {
+        const int nb = min(kSub, npos - b0);
+        for (int t = threadIdx.x; t < nb * (hd / 4); t += kAttnThreads) {
+            const int p = t / (hd / 4), c4 = t % (hd / 4);
+            *reinterpret_cast<float4*>(kv + p * ld + 4 * c4) =
+                *reinterpret_cast<const float4*>(vc + size_t(p0 + b0 + p) * kvw + 4 * c4);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const int t = threadIdx.x + r * kAttnThreads;
+            if (t < group * hd) {
+                const int h = t / hd, dd = t % hd;
+                float a = acc[r];
+                for (int p = 0; p < nb; p++) a = fmaf(sc[h * kAttnChunk + b0 + p], kv[p * ld + dd], a);
+                acc[r] = a;
+            }
+        }
+        __syncthreads();
+    }
+    if (S == 1) {
+        // the whole prefix is in this CTA: finish here (no partials)
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const int t = threadIdx.x + r * kAttnThreads;
+            if (t < group * hd) {
+                const int h = t / hd, dd = t % hd;
+                P.out[size_t(i) * qw + (size_t(kvh) * group + h) * hd + dd] = __fdiv_rn(acc[r], ml[2 * h + 1]);
+            }
+        }
+        pdl_trigger();
+        return;
+    }
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        const int t = threadIdx.x + r * kAttnThreads;
+        if (t < group * hd) part[(t / hd) * (hd + 2) + (t % hd)] = acc[r];
+    }
+    if (threadIdx.x < group) {
+        part[threadIdx.x * (hd + 2) + hd] = ml[2 * threadIdx.x];
+        part[threadIdx.x * (hd + 2) + hd + 1] = ml[2 * threadIdx.x + 1];
+    }
+    // ---- the last chunk CTA of this (kv head, client) combines ----
+    __shared__ int last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int* ctr = P.counters + i * P.kv_heads + kvh;
+        last = atomicAdd(ctr, 1) == S - 1;
+        if (last) *ctr = 0;
+    }
+    __syncthreads();
+    pdl_trigger();
+    if (!last) return;
+    __threadfence();
+    const float* parts = P.scratch + (size_t(i) * P.kv_heads + kvh) * S * group * (hd + 2);
+    for (int t = threadIdx.x; t < group * hd; t += kAttnThreads) {
+        const int h = t / hd, dd = t % hd;
+        float M = -INFINITY;
+        for (int s = 0; s < S; s++) M = fmaxf(M, __ldcg(parts + (size_t(s) * group + h) * (hd + 2) + hd));
+        float Lsum = 0.f, O = 0.f;
+        for (int s = 0; s < S; s++) {
+            const float* ps = parts + (size_t(s) * group + h) * (hd + 2);
+            const float m = __ldcg(ps + hd);
+            if (m == -INFINITY) continue;
+            const float w = expf(m - M);
+            Lsum = fmaf(__ldcg(ps + hd + 1), w, Lsum);
+            O = fmaf(__ldcg(ps + dd), w, O);
+        }
+        P.out[size_t(i) * qw + (size_t(kvh) * group + h) * hd + dd] = __fdiv_rn(O, Lsum);
     }
 }
 
 }  // namespace
 
-cudaError_t launch_gemv(uint32_t dtype, const GemvLaunch& L, int sms, cudaStream_t s) {
-    const bool dual = L.job[0].b != nullptr;
-    switch (dtype) {
-        case SPM_Q8_0: return launch_enc<SPM_Q8_0>(L, dual, sms, s);
-        case SPM_Q6_K: return launch_enc<SPM_Q6_K>(L, dual, sms, s);
-        case SPM_Q5_K: return launch_enc<SPM_Q5_K>(L, dual, sms, s);
-        case SPM_Q2_K: return launch_enc<SPM_Q2_K>(L, dual, sms, s);
-        case SPM_F32: return launch_enc<SPM_F32>(L, dual, sms, s);
-        default: return cudaErrorInvalidValue;
-    }
-}
-
-cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t s) {
+size_t attention_smem(const AttnParams& P) {
     const int group = P.heads / P.kv_heads;
-    const size_t smem = (size_t(group) * P.head_dim + P.head_dim + P.context + 33) * sizeof(float);
-    attention_kernel<<<dim3(P.kv_heads, n), kAttnThreads, smem, s>>>(P);
-    return cudaGetLastError();
+    return (size_t(group) * P.head_dim + 2 * P.head_dim + size_t(kSub) * (P.head_dim + 4) + size_t(group) * kAttnChunk +
+            64) * sizeof(float);
 }
 
-cudaError_t launch_rmsnorm(const float* x, const float* g, float* out, int n, int width, float eps, cudaStream_t s) {
-    rmsnorm_kernel<<<n, 256, 0, s>>>(x, g, out, width, eps);
-    return cudaGetLastError();
+static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                              void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t s, bool pdl) {
+    const size_t smem = attention_smem(P);
+    static int configured_for = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (smem > 48 * 1024 && configured_for != dev) {
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        if (e != cudaSuccess) return e;
+        configured_for = dev;
+    }
+    const int chunks = (P.context + kAttnChunk - 1) / kAttnChunk;
+    AttnParams p = P;
+    void* args[] = {&p};
+    return launch_pdl(reinterpret_cast<const void*>(attention_kernel), dim3(P.kv_heads, n, chunks),
+                      dim3(kAttnThreads), smem, s, pdl, args);
 }
 
 cudaError_t launch_embed(uint32_t dtype, const uint8_t* tiles, const Packed& p, const uint32_t* tokens, int n,
-                         float* out, cudaStream_t s) {
-    embed_kernel<<<n, 128, 0, s>>>(dtype, tiles, p, tokens, out);
-    return cudaGetLastError();
+                         float* out, float* sumsq, cudaStream_t s, bool pdl) {
+    Packed pk = p;
+    void* args[] = {&dtype, &tiles, &pk, &tokens, &out, &sumsq};
+    return launch_pdl(reinterpret_cast<const void*>(embed_kernel), dim3(n), dim3(128), 0, s, pdl, args);
 }
 
 cudaError_t launch_dequant(uint32_t dtype, const uint8_t* tiles, const Packed& p, uint64_t row0, uint64_t rows,
@@ -794,14 +473,14 @@ cudaError_t launch_dequant(uint32_t dtype, const uint8_t* tiles, const Packed& p
     return cudaGetLastError();
 }
 
-cudaError_t launch_argmax(const float* logits, int n, int vocab, uint32_t* out, cudaStream_t s) {
-    argmax_kernel<<<n, 1024, 0, s>>>(logits, vocab, out);
-    return cudaGetLastError();
+cudaError_t launch_argmax(const float* logits, int n, int vocab, uint32_t* out, cudaStream_t s, bool pdl) {
+    void* args[] = {&logits, &vocab, &out};
+    return launch_pdl(reinterpret_cast<const void*>(argmax_kernel), dim3(n), dim3(1024), 0, s, pdl, args);
 }
 
-cudaError_t launch_advance(int32_t* pos, int n, cudaStream_t s) {
-    advance_kernel<<<1, 32, 0, s>>>(pos, n);
-    return cudaGetLastError();
+cudaError_t launch_advance(int32_t* pos, int n, cudaStream_t s, bool pdl) {
+    void* args[] = {&pos, &n};
+    return launch_pdl(reinterpret_cast<const void*>(advance_kernel), dim3(1), dim3(32), 0, s, pdl, args);
 }
 
 }  // namespace spm

@@ -28,9 +28,33 @@ struct GemvLaunch {
     uint32_t cols, tile_bytes, plane1, plane2, plane3;
     const float* x;       // x[p * x_stride + col]
     int32_t x_stride, n;
+    // Fused RMSNorm of x when gain != nullptr: x_hat = (x * s_p) * gain, with
+    // s_p = 1/sqrt(sum_k sumsq[k*8+p] / cols + eps) over the producer's parts.
+    const float* gain;
+    const float* sumsq;
+    int32_t sumsq_parts;
+    float eps;
+    float* sumsq_out;     // EPI_ADD: per-CTA sum of squares of the rows written, [grid][8]
+    int32_t* status;      // device error word: a bounded wait that gave up sets it
+    int32_t slots;        // shared-memory ring slots (set by gemv_geometry)
+    int32_t consumers;    // consuming warps (set by gemv_geometry)
+    int32_t c0;           // index of client 0 of this launch in the sum-of-squares arrays
 };
 
-cudaError_t launch_gemv(uint32_t dtype, const GemvLaunch& L, int sms, cudaStream_t stream);
+// Grid, ring slots and dynamic shared memory of a streaming GEMV launch.
+struct GemvGeometry {
+    int grid, slots, consumers;
+    size_t smem;
+};
+GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms);
+// `pdl`: launch with programmatic stream serialization (prefetch of the
+// weights overlaps the previous kernel; activations are read after it ends).
+// `grid_out` receives the grid size (= sum-of-squares parts written by EPI_ADD).
+cudaError_t launch_gemv(uint32_t dtype, GemvLaunch L, int sms, cudaStream_t stream, bool pdl, int* grid_out = nullptr);
+
+// Positions per attention CTA; a (kv head, client) is split over
+// ceil(context / kAttnChunk) CTAs whose softmax partials are combined.
+constexpr int kAttnChunk = 256;
 
 struct AttnParams {
     const float *q, *k, *v;        // [n][q_width], [n][kv_width]
@@ -39,21 +63,23 @@ struct AttnParams {
     const int32_t* pos;            // [n] position of the token being decoded
     const float2* rope;            // [context][head_dim/2] (cos, sin)
     const float *q_norm, *k_norm;  // QK-norm gains or nullptr
+    float* scratch;                // [n][kv_heads][chunks][group][head_dim + 2] partials
+    int32_t* counters;             // [n][kv_heads], zero between launches
     int32_t layer, layers, context, heads, kv_heads, head_dim, family;
     float eps;
 };
-cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t stream);
+size_t attention_smem(const AttnParams& P);
+cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t stream, bool pdl);
 
-cudaError_t launch_rmsnorm(const float* x, const float* gain, float* out, int n, int width, float eps,
-                           cudaStream_t stream);
 // Gather-and-decode one packed row per client (embedding lookup).
+// Also writes sumsq_out[i*8 + c] = (i == c) ? sum of squares of row i : 0.
 cudaError_t launch_embed(uint32_t dtype, const uint8_t* tiles, const Packed& p, const uint32_t* tokens, int n,
-                         float* out, cudaStream_t stream);
+                         float* out, float* sumsq_out, cudaStream_t stream, bool pdl);
 // Decode rows [row0, row0+rows) into out (rows x cols floats), exact.
 cudaError_t launch_dequant(uint32_t dtype, const uint8_t* tiles, const Packed& p, uint64_t row0, uint64_t rows,
                            float* out, cudaStream_t stream);
 // Greedy pick per client over logits [n][vocab]: largest value, last index on ties.
-cudaError_t launch_argmax(const float* logits, int n, int vocab, uint32_t* out, cudaStream_t stream);
-cudaError_t launch_advance(int32_t* pos, int n, cudaStream_t stream);
+cudaError_t launch_argmax(const float* logits, int n, int vocab, uint32_t* out, cudaStream_t stream, bool pdl);
+cudaError_t launch_advance(int32_t* pos, int n, cudaStream_t stream, bool pdl);
 
 }  // namespace spm

@@ -176,3 +176,21 @@ def test_qwen3_8b_shape_two_layers_matches_the_oracle(cuda):
         assert best == [O.argmax_last(want[i]) for i in range(n)]
     sess.close()
     m.close()
+
+
+@pytest.mark.parametrize("name", ["llama-q8_0", "qwen3-q6_k"])
+def test_long_context_attention_matches_the_oracle(cuda, models, name):
+    # past kAttnChunk (256) positions the attention splits a client's prefix
+    # over several CTAs and combines their softmax partials
+    r, img, m, om = models(name)
+    n, steps = 2, 600
+    sess = eb.Session(m, n, steps)
+    osess = om.session(n, steps)
+    for step in range(steps):
+        toks = [(step * 13 + i * 7) % r.shape.vocab for i in range(n)]
+        best, got = sess.decode_step(toks, want_logits=step % 50 == 49)
+        want = osess.step(toks)
+        if got is not None:
+            assert logits_close(got, want), step
+        assert best == [O.argmax_last(want[i]) for i in range(n)], step
+    sess.close()

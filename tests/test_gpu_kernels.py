@@ -139,3 +139,11 @@ def test_streamed_one_stream_of_a_model(cuda):
     assert np.all(np.abs(yd.cpu().numpy() - want) <= 1e-5 * scale)
     # the model's dequant of that stream is the reference decode, bit for bit
     assert np.array_equal(bits(m.dequant_rows(idx, 0, info["rows"])), bits(dense))
+
+
+@pytest.mark.parametrize("rows,cols,positions", [(8192, 4096, 4), (2048, 12288, 1), (4096, 4096, 3)])
+def test_gemv_reuses_ring_slots(cuda, rows, cols, positions):
+    # enough tiles per CTA that every shared-memory ring slot is refilled
+    # several times (slot counts of 2, 4 and 8 with 2 or 4 consuming warps)
+    got, want, scale = gemv_case(cuda, O.Q6_K, rows, cols, positions, seed=rows + cols)
+    assert np.all(np.abs(got - want) <= 1e-5 * scale)
