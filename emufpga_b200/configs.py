@@ -112,6 +112,8 @@ TINY = {
                          gain_sigma=0.1),
     "olmoe-q6_k": Recipe(Shape(OLMOE, 2, 256, 0, 4, 4, 64, 128, experts=8, experts_used=2, expert_ff=256),
                          Q6_K, Q6_K, Q6_K, expert_type=Q6_K, seed=12, zipf_s=1.1, gain_sigma=0.1),
+    "olmoe-q2_k": Recipe(Shape(OLMOE, 2, 256, 0, 4, 4, 64, 128, experts=8, experts_used=2, expert_ff=256),
+                         Q6_K, Q6_K, Q6_K, expert_type=Q2_K, seed=14, zipf_s=1.1, gain_sigma=0.1),
     "qwen3moe-q5_k": Recipe(Shape(QWEN3MOE, 2, 256, 0, 4, 2, 64, 128, experts=8, experts_used=2, expert_ff=256,
                                   rope_base=1e6, eps=1e-6), Q5_K, Q5_K, Q5_K, expert_type=Q5_K, seed=13, zipf_s=1.1,
                             gain_sigma=0.1),

@@ -19,6 +19,7 @@
 #include <thread>
 
 #include "kernels.h"
+#include "moe.h"
 
 namespace spm {
 const std::string& last_error();
@@ -112,6 +113,10 @@ struct spm_session {
     uint32_t *tokens = nullptr, *argmax = nullptr;
     uint32_t *h_tokens = nullptr, *h_argmax = nullptr;
     float* sumsq = nullptr;            // two [kMaxParts][8] partial sum-of-squares buffers
+    // routed feed-forward: router logits, one plan per layer, expert activations / outputs
+    float *moe_logits = nullptr, *moe_act = nullptr, *moe_out = nullptr;
+    MoePlan* plans = nullptr;
+    int moe_max_active = 0;
     float* attn_scratch = nullptr;
     int32_t* attn_counters = nullptr;
     int32_t* status = nullptr;         // device error word of bounded waits
@@ -446,7 +451,43 @@ void enqueue_step(spm_session* s, int n) {
         go.sumsq_out = part[1];
         add_job(go, m, L.o, nullptr, s->states, d, s->states, d, EPI_ADD);
         parts = run_gemv(m, go, m->streams[L.o].pk.dtype, st, pdl);
-        if (is_moe(c)) fail(SPM_E_ARG, "MoE layers are not enabled in this build");
+        if (is_moe(c)) {
+            // routed feed-forward (spm-granite-moe/src/layout.rs:188-333)
+            const int E = int(c.experts), K = int(c.experts_used), eff = int(c.expert_ff);
+            GemvLaunch gr = gemv_base(m, L.router, s->states, n);
+            gr.status = s->status;
+            norm_in(gr, L.ffn_norm, 1);
+            add_job(gr, m, L.router, nullptr, s->moe_logits, E, nullptr, 0, EPI_STORE);
+            run_gemv(m, gr, m->streams[L.router].pk.dtype, st, pdl);
+            MoePlan* plan = s->plans + l;
+            CUDA_OK(launch_route(s->moe_logits, L.bias >= 0 ? m->gains + L.bias : nullptr, n, E, K, plan, st, pdl));
+            const int chunks_gu = std::max(1, std::min(eff / kTileRows, (2 * m->sms + s->moe_max_active - 1) / s->moe_max_active));
+            GemvLaunch ge = gemv_base(m, L.gate_exps, s->states, kMoeMaxClients);
+            ge.status = s->status;
+            norm_in(ge, L.ffn_norm, 1);
+            add_job(ge, m, L.gate_exps, m->tiles(L.up_exps), s->moe_act, eff, nullptr, 0, EPI_SWIGLU);
+            ge.plan = plan;
+            ge.expert_max = s->moe_max_active;
+            ge.expert_chunks = chunks_gu;
+            ge.expert_tiles = uint32_t(eff / kTileRows);
+            ge.total_tiles = ge.expert_tiles;
+            ge.xmode = 0;
+            run_gemv(m, ge, m->streams[L.gate_exps].pk.dtype, st, pdl);
+            const int chunks_d = std::max(1, std::min(d / kTileRows, (2 * m->sms + s->moe_max_active - 1) / s->moe_max_active));
+            GemvLaunch gx = gemv_base(m, L.down_exps, s->moe_act, kMoeMaxClients);
+            gx.status = s->status;
+            add_job(gx, m, L.down_exps, nullptr, s->moe_out, d, nullptr, 0, EPI_STORE);
+            gx.plan = plan;
+            gx.expert_max = s->moe_max_active;
+            gx.expert_chunks = chunks_d;
+            gx.expert_tiles = uint32_t(d / kTileRows);
+            gx.total_tiles = gx.expert_tiles;
+            gx.xmode = 1;
+            run_gemv(m, gx, m->streams[L.down_exps].pk.dtype, st, pdl);
+            CUDA_OK(launch_combine(plan, s->moe_out, d, s->states, d, n, K, part[0], st, pdl));
+            parts = n;
+            continue;
+        }
         GemvLaunch gu = gemv_base(m, L.gate, s->states, n);
         gu.status = s->status;
         norm_in(gu, L.ffn_norm, 1);
@@ -788,6 +829,16 @@ spm_status spm_session_create(spm_model* m, int32_t max_clients, int32_t max_con
         if (group * c.head_dim > 1024) fail(SPM_E_ARG, "attention supports at most 1024 query values per kv head");
         s->attn_scratch = s->alloc<float>(n * c.kv_heads * chunks * group * (c.head_dim + 2));
         s->attn_counters = s->alloc<int32_t>(n * c.kv_heads);
+        if (is_moe(c)) {
+            if (c.experts > uint32_t(kMoeMaxExperts) || c.experts_used > uint32_t(kMoeMaxUsed))
+                fail(SPM_E_ARG, "at most 256 experts and 8 routed per token");
+            if (c.expert_ff % kTileRows || c.hidden % kTileRows) fail(SPM_E_ARG, "expert rows must be whole tiles");
+            s->moe_max_active = int(std::min<size_t>(c.experts, std::min<size_t>(n, kMoeMaxClients) * c.experts_used));
+            s->moe_logits = s->alloc<float>(n * c.experts);
+            s->plans = s->alloc<MoePlan>(c.layers);
+            s->moe_act = s->alloc<float>(size_t(s->moe_max_active) * kMoeMaxClients * c.expert_ff);
+            s->moe_out = s->alloc<float>(size_t(s->moe_max_active) * kMoeMaxClients * c.hidden);
+        }
         auto table = rope_table(c, max_context);
         s->rope = s->alloc<float2>(table.size());
         CUDA_OK(cudaMemcpy(s->rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice));
@@ -879,10 +930,15 @@ spm_status spm_session_set_graphs(spm_session* s, int32_t enable) {
 
 spm_status spm_session_routes(const spm_session* s, int32_t n, int32_t* routes_host) {
     return guarded([&] {
-        (void)n;
-        (void)routes_host;
-        if (!is_moe(s->m->cfg)) fail(SPM_E_ARG, "the model has no routed layers");
-        fail(SPM_E_ARG, "routes are not recorded by this build");
+        const spm_model_cfg& c = s->m->cfg;
+        if (!is_moe(c)) fail(SPM_E_ARG, "the model has no routed layers");
+        if (n < 1 || n > s->max_clients || n > kMoeMaxClients) fail(SPM_E_ARG, "client count out of range");
+        std::vector<MoePlan> plans(c.layers);
+        CUDA_OK(cudaMemcpy(plans.data(), s->plans, c.layers * sizeof(MoePlan), cudaMemcpyDeviceToHost));
+        for (uint32_t l = 0; l < c.layers; l++)
+            for (int i = 0; i < n; i++)
+                for (uint32_t j = 0; j < c.experts_used; j++)
+                    routes_host[(size_t(l) * n + i) * c.experts_used + j] = plans[l].route[i][j];
     });
 }
 

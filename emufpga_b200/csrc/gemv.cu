@@ -43,35 +43,47 @@ static GemvGeometry geometry_resident(uint32_t dtype, const GemvLaunch& L, bool 
     return g;
 }
 
-GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms) {
+// Ring slots and shared memory for CTAs that each own about `per` tiles.
+static GemvGeometry ring_geometry(const GemvLaunch& L, bool dual, int per) {
     GemvGeometry g{};
     const size_t slot = size_t(L.tile_bytes) * (dual ? 2 : 1);
     const size_t xb = x_stage_bytes(L);
     // Two CTAs per SM when ring + activations fit in half the SM's shared
     // memory (the next kernel's CTAs can then start prefetching beside them).
     size_t ring = kRingBytes;
-    int per_sm = 2;
-    if (xb + ring > kHalfSm) {
-        ring = xb + kRingMin <= kHalfSm ? kHalfSm - xb : kSmemMax - xb;
-        if (xb + kRingMin > kHalfSm) per_sm = 1;
-    }
+    if (xb + ring > kHalfSm) ring = xb + kRingMin <= kHalfSm ? kHalfSm - xb : kSmemMax - xb;
     if (ring > kRingBytes) ring = kRingBytes;
     int slots = int(ring / slot);
     if (slots > kMaxSlots) slots = kMaxSlots;
-    if (slots < 1) slots = 1;
-    const uint32_t gcap = uint32_t(sms) * per_sm;
-    g.grid = int(L.total_tiles < gcap ? L.total_tiles : gcap);
-    const int per = g.grid ? int((L.total_tiles + g.grid - 1) / g.grid) : 1;
     if (slots > per) slots = per;
+    if (slots < 1) slots = 1;
     g.slots = slots;
     g.consumers = kConsumers;
     g.smem = slot * size_t(slots) + xb;
     return g;
 }
 
+GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms) {
+    const size_t xb = x_stage_bytes(L);
+    const int per_sm = xb + kRingMin <= kHalfSm ? 2 : 1;
+    const uint32_t gcap = uint32_t(sms) * per_sm;
+    const int grid = int(L.total_tiles < gcap ? L.total_tiles : gcap);
+    const int per = grid ? int((L.total_tiles + grid - 1) / grid) : 1;
+    GemvGeometry g = ring_geometry(L, dual, per);
+    g.grid = grid;
+    return g;
+}
+
 static cudaError_t launch_one(uint32_t dtype, GemvLaunch L, int sms, cudaStream_t s, bool pdl, int grid) {
     const bool dual = L.job[0].b != nullptr;
-    GemvGeometry g = geometry_resident(dtype, L, dual, sms);
+    GemvGeometry g;
+    if (L.plan) {
+        // expert mode: a CTA owns 1/expert_chunks of one active expert's tiles
+        g = ring_geometry(L, dual, int((L.expert_tiles + L.expert_chunks - 1) / L.expert_chunks));
+        g.grid = L.expert_max * L.expert_chunks;
+    } else {
+        g = geometry_resident(dtype, L, dual, sms);
+    }
     if (grid > 0 && grid < g.grid) g.grid = grid;  // more tiles per CTA; the ring stays valid
     L.slots = g.slots;
     L.consumers = g.consumers;
@@ -92,6 +104,7 @@ cudaError_t launch_gemv(uint32_t dtype, GemvLaunch L, int sms, cudaStream_t s, b
     if (L.n < 1 || L.n > 8 || (L.cols & 31)) return cudaErrorInvalidValue;
     const size_t slot = size_t(L.tile_bytes) * (dual ? 2 : 1);
     if (slot + size_t(L.cols) * 4 + (L.cols / 16) * 4 > kSmemMax) return cudaErrorInvalidValue;
+    if (L.plan && slot + x_stage_bytes(L) > kSmemMax) return cudaErrorInvalidValue;
     if (slot + x_stage_bytes(L) > kSmemMax) {
         // The clients' activations do not fit beside one tile: one launch per
         // half of the clients (the weights are read twice), on a common grid

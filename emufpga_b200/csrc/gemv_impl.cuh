@@ -29,6 +29,7 @@
 // read the activations only after griddepcontrol.wait.
 #pragma once
 #include "device.cuh"
+#include "moe.h"
 
 namespace spm {
 namespace gemv {
@@ -346,9 +347,42 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream(const __grid_constant
     __shared__ float part[2][kConsumers][VR][NC];
     __shared__ float sqw[kConsumers][8];
     __shared__ float auxs[kAuxPrefetch];
+    __shared__ int32_t xrows[NC], yrows[NC], srows[NC];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t T = L.total_tiles, G = gridDim.x;
-    const uint32_t t0 = uint32_t(uint64_t(T) * blockIdx.x / G), t1 = uint32_t(uint64_t(T) * (blockIdx.x + 1) / G);
+    uint32_t t0, t1;
+    uint32_t rbase = 0, rlim = 0xffffffffu;  // expert mode: rows of the expert's matrix
+    int n_act = NC;  // clients of this CTA with data (expert mode: the expert's clients)
+    if (L.plan) {
+        // expert mode: the plan comes from the previous kernel
+        pdl_wait();
+        const int a = int(blockIdx.x) / L.expert_chunks, chunk = int(blockIdx.x) % L.expert_chunks;
+        if (a >= L.plan->count) {
+            pdl_trigger();
+            return;
+        }
+        const uint32_t e = uint32_t(L.plan->expert[a]), Te = L.expert_tiles, C = uint32_t(L.expert_chunks);
+        rbase = e * Te * kTileRows;
+        rlim = Te * kTileRows;
+        t0 = e * Te + uint32_t(uint64_t(Te) * chunk / C);
+        t1 = e * Te + uint32_t(uint64_t(Te) * (chunk + 1) / C);
+        n_act = L.plan->ntok[a];
+        if (threadIdx.x < NC) {
+            const int c = threadIdx.x;
+            const int client = L.plan->tok[a][c < n_act ? c : 0];
+            xrows[c] = L.xmode == 0 ? client : a * kMoeMaxClients + c;
+            yrows[c] = a * kMoeMaxClients + c;
+            srows[c] = client;
+        }
+    } else {
+        const uint32_t T = L.total_tiles, G = gridDim.x;
+        t0 = uint32_t(uint64_t(T) * blockIdx.x / G);
+        t1 = uint32_t(uint64_t(T) * (blockIdx.x + 1) / G);
+        if (threadIdx.x < NC) {
+            xrows[threadIdx.x] = threadIdx.x;
+            yrows[threadIdx.x] = threadIdx.x;
+            srows[threadIdx.x] = L.c0 + threadIdx.x;
+        }
+    }
     const uint32_t nt = t1 - t0, NS = uint32_t(L.slots);
     const uint32_t slot_bytes = L.tile_bytes * (DUAL ? 2u : 1u);
     if (threadIdx.x == 0) {
@@ -396,11 +430,11 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream(const __grid_constant
     float ssum = 0.f;
     const int sc_c = ctid >> 4, sc_j = ctid & 15;
     if (L.gain && sc_c < NC)
-        for (int p = sc_j; p < L.sumsq_parts; p += 16) ssum += L.sumsq[p * 8 + L.c0 + sc_c];
+        for (int p = sc_j; p < L.sumsq_parts; p += 16) ssum += L.sumsq[p * 8 + srows[sc_c]];
     for (uint32_t idx = ctid; idx < NC * k4; idx += CT) {
         const uint32_t c = idx / k4, col = 4 * (idx % k4);
         *reinterpret_cast<float4*>(ring + xbase + c * cstride + xoff(col >> 5, (col & 31) >> 2)) =
-            ldx4(L.x + size_t(c) * L.x_stride + col);
+            int(c) < n_act ? ldx4(L.x + size_t(xrows[c]) * L.x_stride + col) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     // the residual rows this CTA will add to (EPI_ADD), loaded with x
     const bool aux_pre = nt * kTileRows * NC <= uint32_t(kAuxPrefetch);
@@ -409,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream(const __grid_constant
             const uint32_t i = idx / (kTileRows * NC), e = (idx / NC) % kTileRows, c = idx % NC;
             const GemvJob& J = pick(L, t0 + i);
             const uint32_t row = (t0 + i - J.tile_begin) * kTileRows + e;
-            if (J.epi == EPI_ADD && row < J.rows) auxs[idx] = J.aux[size_t(c) * J.aux_stride + row];
+            if (J.epi == EPI_ADD && row < J.rows) auxs[idx] = J.aux[size_t(yrows[c]) * J.aux_stride + row];
         }
 #pragma unroll
     for (int o = 8; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
@@ -494,8 +528,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream(const __grid_constant
                     // DUAL: row pass*VR+e from groups 0 (gate) and 1 (up);
                     // single: row e = g + 2v of group g = e % 2, v = e / 2
                     const int gsel = DUAL ? 0 : (e & 1), v = DUAL ? e : (e >> 1);
-                    const uint32_t row = tile * kTileRows + (DUAL ? uint32_t(pass * VR + e) : uint32_t(e));
-                    if (row >= J.rows) continue;
+                    const uint32_t grow = tile * kTileRows + (DUAL ? uint32_t(pass * VR + e) : uint32_t(e));
+                    const uint32_t row = grow - rbase;
+                    if (grow >= J.rows || row >= rlim) continue;
 #pragma unroll
                     for (int c = 0; c < NC; c++) {
                         float a = 0.f, b = 0.f;
@@ -506,12 +541,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream(const __grid_constant
                         }
                         float r = a;
                         if constexpr (DUAL) r = silu_mul(a, b);
-                        if (lane == ((e * NC + c) & 31)) {
+                        if (lane == ((e * NC + c) & 31) && c < n_act) {
                             if (J.epi == EPI_ADD) {
                                 const uint32_t e2 = DUAL ? uint32_t(pass * VR + e) : uint32_t(e);
-                                r = (aux_pre ? auxs[(i * kTileRows + e2) * NC + c] : J.aux[size_t(c) * J.aux_stride + row]) + r;
+                                r = (aux_pre ? auxs[(i * kTileRows + e2) * NC + c] : J.aux[size_t(yrows[c]) * J.aux_stride + row]) + r;
                             }
-                            J.y[size_t(c) * J.y_stride + row] = r;
+                            J.y[size_t(yrows[c]) * J.y_stride + row] = r;
                             sqacc[c] = fmaf(r, r, sqacc[c]);
                         }
                     }

@@ -8,6 +8,8 @@
 
 namespace spm {
 
+struct MoePlan;
+
 enum Epilogue { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2 };
 
 // One matrix (or a gate/up pair) inside a GEMV launch.
@@ -39,6 +41,15 @@ struct GemvLaunch {
     int32_t slots;        // shared-memory ring slots (set by gemv_geometry)
     int32_t consumers;    // consuming warps (set by gemv_geometry)
     int32_t c0;           // index of client 0 of this launch in the sum-of-squares arrays
+    // Expert mode (plan != nullptr): one job over a [experts][rows][cols]
+    // tensor; CTA b works on active expert b / expert_chunks of the plan and
+    // streams only that expert's tiles; client slot p of the expert reads x
+    // row plan->tok[a][p] (xmode 0) or a*8+p (xmode 1) and writes y row a*8+p.
+    const MoePlan* plan;
+    int32_t expert_max;   // grid = expert_max * expert_chunks CTAs
+    int32_t expert_chunks;
+    uint32_t expert_tiles;
+    int32_t xmode;
 };
 
 // Grid, ring slots and dynamic shared memory of a streaming GEMV launch.

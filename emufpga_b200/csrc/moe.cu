@@ -1,0 +1,193 @@
+// Route and combine kernels of the routed feed-forward (moe.h).
+#include "device.cuh"
+#include "moe.h"
+
+namespace spm {
+namespace {
+using namespace dev;
+
+// f32::total_cmp order key (spm-granite-moe/src/math.rs:35-39 sorts by it).
+__device__ __forceinline__ int32_t total_key(float f) {
+    int32_t b = __float_as_int(f);
+    return b ^ int32_t(uint32_t(b >> 31) >> 1);
+}
+
+// One CTA.  Warp i routes client i; then the plan is built over experts.
+__global__ void __launch_bounds__(256) route_kernel(const float* logits, const float* bias, int n, int E, int K,
+                                                    MoePlan* plan) {
+    __shared__ float prob[kMoeMaxClients][kMoeMaxExperts];
+    __shared__ int32_t sel[kMoeMaxClients][kMoeMaxUsed];
+    __shared__ int32_t cnt[kMoeMaxExperts], base[kMoeMaxExperts + 1];
+    pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < n) {
+        const int i = warp;
+        // softmax: max by fold, exp(v - max), sum, divide (math.rs:23-29)
+        float mx = -INFINITY;
+        for (int e = lane; e < E; e += 32) {
+            const float v = bias ? logits[i * E + e] + bias[e] : logits[i * E + e];
+            prob[i][e] = v;
+            mx = fmaxf(mx, v);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float sum = 0.f;
+        for (int e = lane; e < E; e += 32) {
+            const float v = expf(prob[i][e] - mx);
+            prob[i][e] = v;
+            sum += v;
+        }
+        sum = warp_sum(sum);
+        __syncwarp();
+        for (int e = lane; e < E; e += 32) prob[i][e] = __fdiv_rn(prob[i][e], sum);
+        __syncwarp();
+        // top-K: largest probability first, the lower id among equals
+        uint64_t taken = 0, taken2 = 0, taken3 = 0, taken4 = 0;
+        for (int j = 0; j < K; j++) {
+            int32_t bk = INT32_MIN;
+            int bi = -1;
+            for (int e = lane; e < E; e += 32) {
+                const uint64_t bit = 1ull << (e & 63);
+                const uint64_t t = e < 64 ? taken : e < 128 ? taken2 : e < 192 ? taken3 : taken4;
+                if (t & bit) continue;
+                const int32_t k = total_key(prob[i][e]);
+                if (bi < 0 || k > bk) { bk = k; bi = e; }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const int32_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (oi >= 0 && (bi < 0 || ok > bk || (ok == bk && oi < bi))) { bk = ok; bi = oi; }
+            }
+            const uint64_t bit = 1ull << (bi & 63);
+            if (bi < 64) taken |= bit;
+            else if (bi < 128) taken2 |= bit;
+            else if (bi < 192) taken3 |= bit;
+            else taken4 |= bit;
+            if (lane == 0) sel[i][j] = bi;
+        }
+        __syncwarp();
+        if (lane == 0) {
+            float s = 0.f;  // in route order (layout.rs:289-293)
+            for (int j = 0; j < K; j++) s += prob[i][sel[i][j]];
+            plan->norm[i] = s;
+            for (int j = 0; j < K; j++) plan->route[i][j] = sel[i][j];
+        }
+    }
+    __syncthreads();
+    // ---- plan: active experts ascending, their clients ascending ----
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        int c = 0;
+        for (int i = 0; i < n; i++)
+            for (int j = 0; j < K; j++) c += sel[i][j] == e;
+        cnt[e] = c;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int a = 0;
+        for (int e = 0; e < E; e++) {
+            base[e] = a;
+            a += cnt[e] ? 1 : 0;
+        }
+        base[E] = a;
+        plan->count = a;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        if (!cnt[e]) continue;
+        const int a = base[e];
+        plan->expert[a] = e;
+        plan->ntok[a] = cnt[e];
+        int p = 0;
+        for (int i = 0; i < n; i++)
+            for (int j = 0; j < K; j++)
+                if (sel[i][j] == e) plan->tok[a][p++] = i;
+        for (; p < kMoeMaxClients; p++) plan->tok[a][p] = 0;
+    }
+    __syncthreads();
+    if (threadIdx.x < n) {
+        const int i = threadIdx.x;
+        // this client's experts in ascending id
+        int ids[kMoeMaxUsed];
+        for (int j = 0; j < K; j++) ids[j] = sel[i][j];
+        for (int x = 1; x < K; x++)
+            for (int y = x; y > 0 && ids[y - 1] > ids[y]; y--) {
+                const int t = ids[y];
+                ids[y] = ids[y - 1];
+                ids[y - 1] = t;
+            }
+        for (int j = 0; j < K; j++) {
+            const int e = ids[j], a = base[e];
+            int pos = 0;
+            for (int q = 0; q < i; q++)
+                for (int jj = 0; jj < K; jj++) pos += sel[q][jj] == e;
+            plan->slot_a[i][j] = a;
+            plan->slot_pos[i][j] = pos;
+            plan->slot_p[i][j] = prob[i][e];
+        }
+    }
+    pdl_trigger();
+}
+
+__global__ void __launch_bounds__(256) combine_kernel(const MoePlan* plan, const float* out, int out_stride,
+                                                      float* states, int width, int K, float* sumsq) {
+    __shared__ float red[33];
+    pdl_wait();
+    const int i = blockIdx.x;
+    const float norm = plan->norm[i];
+    float ss = 0.f;
+    for (int col = threadIdx.x; col < width; col += blockDim.x) {
+        float total = 0.f;
+        for (int j = 0; j < K; j++) {
+            const float* lane = out + size_t(plan->slot_a[i][j] * kMoeMaxClients + plan->slot_pos[i][j]) * out_stride;
+            total = total + __fdiv_rn(__fmul_rn(lane[col], plan->slot_p[i][j]), norm);
+        }
+        const float v = states[size_t(i) * width + col] + total;
+        states[size_t(i) * width + col] = v;
+        ss = fmaf(v, v, ss);
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    pdl_trigger();
+    if (threadIdx.x < 8) {
+        float t = 0.f;
+        if (threadIdx.x == 0)
+            for (int w = 0; w < int(blockDim.x >> 5); w++) t += red[w];
+        if (threadIdx.x == 0) red[32] = t;
+    }
+    __syncthreads();
+    if (threadIdx.x < 8) sumsq[i * 8 + threadIdx.x] = threadIdx.x == i ? red[32] : 0.f;
+}
+
+cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, cudaStream_t s, bool pdl, void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+}  // namespace
+
+cudaError_t launch_route(const float* logits, const float* bias, int n, int experts, int used, MoePlan* plan,
+                         cudaStream_t s, bool pdl) {
+    if (n < 1 || n > kMoeMaxClients || experts < 1 || experts > kMoeMaxExperts || used < 1 || used > kMoeMaxUsed ||
+        used > experts)
+        return cudaErrorInvalidValue;
+    void* args[] = {&logits, &bias, &n, &experts, &used, &plan};
+    return launch_pdl(reinterpret_cast<const void*>(route_kernel), dim3(1), dim3(256), s, pdl, args);
+}
+
+cudaError_t launch_combine(const MoePlan* plan, const float* out, int out_stride, float* states, int width, int n,
+                           int used, float* sumsq, cudaStream_t s, bool pdl) {
+    void* args[] = {&plan, &out, &out_stride, &states, &width, &used, &sumsq};
+    return launch_pdl(reinterpret_cast<const void*>(combine_kernel), dim3(n), dim3(256), s, pdl, args);
+}
+
+}  // namespace spm

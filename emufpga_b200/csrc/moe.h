@@ -1,0 +1,38 @@
+// Routed (mixture-of-experts) feed-forward: the device-side plan shared by
+// the route kernel, the expert-mode GEMVs and the combine kernel.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace spm {
+
+constexpr int kMoeMaxExperts = 256;
+constexpr int kMoeMaxClients = 8;
+constexpr int kMoeMaxUsed = 8;
+
+// Written by route_kernel once per routed layer and step.
+struct MoePlan {
+    int32_t count;                                       // active experts U
+    int32_t expert[kMoeMaxExperts];                      // ascending expert ids
+    int32_t ntok[kMoeMaxExperts];                        // clients routed to it
+    int32_t tok[kMoeMaxExperts][kMoeMaxClients];         // those clients, ascending
+    int32_t route[kMoeMaxClients][kMoeMaxUsed];          // selected ids, route order
+    // a client's routes in ascending expert order (the order outputs are added):
+    int32_t slot_a[kMoeMaxClients][kMoeMaxUsed];         // active index
+    int32_t slot_pos[kMoeMaxClients][kMoeMaxUsed];       // position among that expert's clients
+    float slot_p[kMoeMaxClients][kMoeMaxUsed];           // routing probability
+    float norm[kMoeMaxClients];                          // sum of the selected probabilities
+};
+
+// Softmax over (logits + bias), top-`used` (descending, ties to the lower id),
+// renormaliser, and the plan (spm-granite-moe/src/moe.rs:17-35, math.rs:23-39).
+cudaError_t launch_route(const float* logits, const float* bias, int n, int experts, int used, MoePlan* plan,
+                         cudaStream_t s, bool pdl);
+// states[i] += sum over client i's experts in ascending id of
+// (out[a][pos] * p) / norm  (spm-granite-moe/src/layout.rs:283-302); also the
+// sum of squares of each new state row (sumsq[i*8 + c] = c == i ? ss : 0).
+cudaError_t launch_combine(const MoePlan* plan, const float* out, int out_stride, float* states, int width, int n,
+                           int used, float* sumsq, cudaStream_t s, bool pdl);
+
+}  // namespace spm

@@ -279,6 +279,13 @@ class Session:
         call("spm_session_stream", self._h, C.byref(v))
         return v.value or 0
 
+    def routes(self, n: int) -> np.ndarray:
+        """Expert ids chosen in the last step: layers x clients x experts_used (route order)."""
+        sh = self.model.shape
+        out = np.zeros((sh.layers, n, sh.experts_used), dtype=np.int32)
+        call("spm_session_routes", self._h, n, out.ctypes.data_as(C.POINTER(C.c_int32)))
+        return out
+
     def launches_per_step(self, n: int) -> int:
         v = C.c_int32()
         call("spm_session_launches_per_step", self._h, n, C.byref(v))

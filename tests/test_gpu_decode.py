@@ -194,3 +194,58 @@ def test_long_context_attention_matches_the_oracle(cuda, models, name):
             assert logits_close(got, want), step
         assert best == [O.argmax_last(want[i]) for i in range(n)], step
     sess.close()
+
+
+MOE = ["olmoe-q6_k", "olmoe-q2_k", "qwen3moe-q5_k"]
+
+
+@pytest.mark.parametrize("name", MOE)
+def test_routed_layers_match_the_oracle(cuda, models, name):
+    # router softmax -> top-k -> renormalised expert mixture
+    # (spm-granite-moe/src/moe.rs:17-35, layout.rs:244-333)
+    r, img, m, om = models(name)
+    n, steps = 4, 5
+    sess = eb.Session(m, n, 16)
+    osess = om.session(n, 16)
+    for step in range(steps):
+        toks = [(step * 29 + i * 17) % r.shape.vocab for i in range(n)]
+        best, got = sess.decode_step(toks, want_logits=True)
+        want, oroutes = osess.step(toks, routes=True)
+        assert np.array_equal(sess.routes(n), oroutes), step
+        assert logits_close(got, want), (step, float(np.abs(got - want).max()), float(np.abs(want).max()))
+        assert best == [O.argmax_last(want[i]) for i in range(n)]
+    sess.close()
+
+
+@pytest.mark.parametrize("name", MOE)
+def test_routed_greedy_serving_matches_the_oracle(cuda, models, name):
+    r, img, m, om = models(name)
+    prompts = [configs.prompt_tokens(21, i, ln, r.shape.vocab) for i, ln in enumerate([3, 6, 4, 5, 2, 7, 3, 4])]
+    want, wl = om.serve(prompts, 8)
+    got, gl = eb.serve(m, prompts, 8, want_logits=True)
+    assert got == want
+    assert logits_close(gl, wl)
+
+
+def test_olmoe_shape_two_layers_matches_the_oracle(cuda):
+    """OLMoE-1B-7B dimensions (hidden 2048, 16 heads of 128, 64 experts of
+    1024, top-8, vocab 50304) with 2 of its 16 layers, Q2_K experts, 8 clients."""
+    import dataclasses
+
+    base = configs.RECIPES["olmoe-q2_k"]
+    r = base.replace(shape=dataclasses.replace(base.shape, layers=2))
+    img = eb.synth_gguf(r)
+    om = O.OracleModel(img, r.shape)
+    m = eb.Model(img, r.shape)
+    n = 8
+    sess = eb.Session(m, n, 8)
+    osess = om.session(n, 8)
+    for step in range(3):
+        toks = configs.prompt_tokens(30 + step, 0, n, r.shape.vocab)
+        best, got = sess.decode_step(toks, want_logits=True)
+        want, oroutes = osess.step(toks, routes=True)
+        assert np.array_equal(sess.routes(n), oroutes)
+        assert logits_close(got, want)
+        assert best == [O.argmax_last(want[i]) for i in range(n)]
+    sess.close()
+    m.close()
