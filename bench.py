@@ -38,6 +38,8 @@ def _args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="keep only the first N layers (small cases for profiler captures; not a bench number)")
     return ap.parse_args()
 
 
@@ -105,11 +107,16 @@ def _peaks():
     return 6650.0, "fallback"
 
 
-def _workload(name):
+def _workload(name, layers=0):
+    import dataclasses
+
     from emufpga_b200 import configs
 
     w = configs.WORKLOADS[name]
-    return w, configs.RECIPES[w["recipe"]], configs.workload_prompts(name)
+    r = configs.RECIPES[w["recipe"]]
+    if layers:
+        r = r.replace(shape=dataclasses.replace(r.shape, layers=min(layers, r.shape.layers)))
+    return w, r, configs.workload_prompts(name)
 
 
 def _tick_tokens(prompts, tick, best):
@@ -199,7 +206,7 @@ def main():
         pg = dist
     import emufpga_b200 as eb
 
-    w, recipe, prompts = _workload(a.workload)
+    w, recipe, prompts = _workload(a.workload, a.layers)
     img = eb.synth_gguf(recipe)
     model = eb.Model(img, recipe.shape, device=local)
     n = len(prompts)
@@ -256,11 +263,16 @@ def main():
         toks = _tick_tokens(prompts, t, best)
     if pg:
         pg.barrier()
-    t0 = time.perf_counter()
+    e2e_s = 0.0
+    touched = []  # MoE: experts the step streamed, summed over layers
     for i in range(steps):
+        t0 = time.perf_counter()
         best, _ = sess.decode_step(toks)
+        e2e_s += time.perf_counter() - t0
         toks = _tick_tokens(prompts, warm + i, best)
-    e2e_s = time.perf_counter() - t0
+        if recipe.shape.moe:
+            r = sess.routes(n)
+            touched.append(sum(len(set(r[l].ravel().tolist())) for l in range(r.shape[0])))
     if pg:
         tt = torch.tensor([e2e_s], device=dev)
         pg.all_reduce(tt, op=pg.ReduceOp.MAX)
@@ -272,6 +284,9 @@ def main():
     if rank == 0:
         roof = gemv_roofline(eb, model, n, dev)
     tokens_total = n * steps * world
+    step_bytes = model.weight_bytes
+    if recipe.shape.moe:
+        step_bytes += statistics.mean(touched) * expert_bytes(model)
     line = None
     if rank == 0:
         peak, how = _peaks()
@@ -283,9 +298,9 @@ def main():
             "data": "synthetic (seeded N(0,0.02) weights quantized by this repo's encoder, uniform prompt ids)",
             "config": {"workload": a.workload, "model": w["recipe"], "clients": n, "prompts": w["prompts"],
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                       "weight_bytes_per_step": model.weight_bytes,
-                       "l2": "flushed between timed steps (256 MiB write); weights 143 MB > 126 MB L2"},
-            "weight_stream_gbs": model.weight_bytes * steps / (job_ms / 1e3) / 1e9,
+                       "weight_bytes_per_step": round(step_bytes),
+                       "l2": "flushed between timed steps (256 MiB write)"},
+            "weight_stream_gbs": step_bytes * steps / (job_ms / 1e3) / 1e9,
             "e2e": {"value": tokens_total / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4 * n,
                     "d2h_bytes_per_step": 4 * n},
             "gpu_launches": launches * steps,
@@ -294,8 +309,15 @@ def main():
         if roof:
             ach = roof["bytes"] / roof["seconds"] / 1e9
             line["roofline"] = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
-                                "peak_source": how, "traffic": None, "kernel": "gemv_kernel (all streams, one sweep)",
+                                "peak_source": how, "traffic": None,
+                                "kernel": "gemv_stream (one sweep of every dense stream and the LM head)",
+                                "bytes_per_launch_avg": roof["bytes"] / roof["launches"],
                                 "launches_per_sweep": roof["launches"]}
+        if recipe.shape.moe:
+            line["config"]["experts_touched_per_step"] = statistics.mean(touched)
+        if a.layers:
+            line["config"]["layers_kept"] = recipe.shape.layers
+            line["invalid"] = "model truncated with --layers (profiling case, not a bench number)"
         if not a.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(recipe, img, prompts, w["steps"], a.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -303,6 +325,21 @@ def main():
         pg.barrier()
         pg.destroy_process_group()
     return 0
+
+
+def expert_streams(model):
+    sh = model.shape
+    if not sh.moe:
+        return []
+    return [model.stream_index(f"blk.{l}.ffn_{k}_exps.weight") for l in range(sh.layers)
+            for k in ("gate", "up", "down")]
+
+
+def expert_bytes(model):
+    """Quantized bytes of one expert's gate, up and down matrices (layer 0)."""
+    sh = model.shape
+    return sum(model.stream_info(model.stream_index(f"blk.0.ffn_{k}_exps.weight"))["bytes"]
+               for k in ("gate", "up", "down")) / sh.experts
 
 
 def gemv_roofline(eb, model, n, dev):
@@ -317,7 +354,8 @@ def gemv_roofline(eb, model, n, dev):
     embd = model.stream_index("token_embd.weight")
     # every matrix a step sweeps: all streams but the embedding, which is the
     # LM head itself when tied
-    keep = [i for i in idx if i != embd or model.shape.tied]
+    experts = set(expert_streams(model))
+    keep = [i for i in idx if (i != embd or model.shape.tied) and i not in experts]
     maxc = max(infos[i]["cols"] for i in keep)
     maxr = max(infos[i]["rows"] for i in keep)
     x = torch.randn(n * maxc, device=dev)
