@@ -80,6 +80,7 @@ PROTOTYPES = {
     "spm_model_stream_info": (C.c_int32, [_P, C.c_int32, _U64P, _U64P, _U32P, _U64P]),
     "spm_model_stream_index": (C.c_int32, [_P, C.c_char_p, _I32P]),
     "spm_dequant_rows": (C.c_int32, [_P, C.c_int32, C.c_uint64, C.c_uint64, _FP]),
+    "spm_dequant_rows_static": (C.c_int32, [_P, C.c_int32, C.c_uint64, C.c_uint64, _FP]),
     "spm_streamed": (C.c_int32, [_P, C.c_int32, _P, C.c_int32, _P, _P]),
     "spm_weights_upload": (C.c_int32, [C.c_uint32, C.c_uint64, C.c_uint64, _P, C.c_int, C.POINTER(_P)]),
     "spm_weights_free": (C.c_int32, [_P]),

@@ -14,6 +14,7 @@
 #include <fstream>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <set>
 #include <sstream>
 #include <thread>
@@ -947,6 +948,67 @@ spm_status spm_session_launches_per_step(spm_session* s, int32_t n, int32_t* lau
         auto it = s->launches.find(n);
         if (it == s->launches.end()) fail(SPM_E_ARG, "no step has been captured at this client count");
         *launches = it->second;
+    });
+}
+
+}  // extern "C"
+
+// ---- dequantization into a static device buffer (no allocation) ----
+//
+// spm_dequant_rows allocates a device buffer for the decoded rows on every
+// call.  Some callers cannot allocate device memory: a parity or monitoring
+// hook that runs beside a serving session which has committed the rest of
+// HBM to KV caches (an allocation there can fail), or one that must not add
+// the device-wide synchronisation that cudaMalloc and cudaFree may imply to a
+// device whose other streams are decoding.  spm_dequant_rows_static serves
+// them: it decodes into a fixed buffer that is part of this library's device
+// image, so it allocates nothing, at the price of a size limit and of one
+// buffer per device shared by every call.
+//
+// kStaticDequantFloats bounds rows x cols of one call (4 MiB of floats); every
+// GPU that loads the library holds the buffer until the process exits.  The
+// buffer keeps the previous call's contents, but nothing in it needs to start
+// at zero: the kernel writes every float that the call then copies out.
+// Calls that overlap on the GPU (from two host threads, say) use the same
+// buffer and race; serialise them.  The first call on each device resolves the
+// buffer's device address, so make that first call before any stream capture
+// begins on that device.
+constexpr uint64_t kStaticDequantFloats = uint64_t(1) << 20;
+static __device__ __align__(256) float g_static_dequant[kStaticDequantFloats];
+
+namespace {
+std::mutex g_static_dequant_mu;
+std::map<int, float*> g_static_dequant_ptr;  // device address of the buffer, per device
+
+// The calling thread's current device must be `device`.  In host code the
+// array's name is only a stand-in; its device address comes from the runtime.
+float* static_dequant_buffer(int device) {
+    std::lock_guard<std::mutex> lock(g_static_dequant_mu);
+    auto it = g_static_dequant_ptr.find(device);
+    if (it != g_static_dequant_ptr.end()) return it->second;
+    float* ptr = nullptr;
+    CUDA_OK(cudaGetSymbolAddress((void**)&ptr, g_static_dequant));
+    g_static_dequant_ptr[device] = ptr;
+    return ptr;
+}
+}  // namespace
+
+extern "C" {
+
+spm_status spm_dequant_rows_static(const spm_model* m, int32_t index, uint64_t row0, uint64_t rows,
+                                   float* out_host) {
+    return guarded([&] {
+        if (index < 0 || index >= int32_t(m->streams.size())) fail(SPM_E_ARG, "stream index out of range");
+        const Packed& p = m->streams[index].pk;
+        if (row0 > p.rows || rows > p.rows - row0) fail(SPM_E_ARG, "row range exceeds the matrix");
+        if (rows > kStaticDequantFloats / std::max<uint64_t>(p.cols, 1))
+            fail(SPM_E_ARG, "spm_dequant_rows_static: " + std::to_string(rows) + " rows x " + std::to_string(p.cols) +
+                                " cols exceeds the static buffer of " + std::to_string(kStaticDequantFloats) +
+                                " floats; request fewer rows per call");
+        CUDA_OK(cudaSetDevice(m->device));
+        float* buf = static_dequant_buffer(m->device);
+        CUDA_OK(launch_dequant(p.dtype, m->tiles(index), p, row0, rows, buf, nullptr));
+        CUDA_OK(cudaMemcpy(out_host, buf, rows * p.cols * sizeof(float), cudaMemcpyDeviceToHost));
     });
 }
 

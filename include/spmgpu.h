@@ -122,6 +122,17 @@ spm_status spm_model_stream_index(const spm_model* m, const char* tensor_name, i
  * memory (rows x cols floats).  Bit-exact with spm_decode_blocks. */
 spm_status spm_dequant_rows(const spm_model* m, int32_t index, uint64_t row0, uint64_t rows,
                             float* out_host);
+/* spm_dequant_rows without any device allocation; no counterpart in the
+ * reference.  For callers that cannot allocate device memory: a parity or
+ * monitoring hook beside a session that holds the rest of HBM, or one that must
+ * not add the device-wide synchronisation of cudaMalloc/cudaFree to a device
+ * that is decoding.  Decodes into one static 4 MiB buffer per device, part of
+ * the library's device image and held until exit: rows x cols must not exceed
+ * 1048576 floats (SPM_E_ARG otherwise).  Calls that overlap on the GPU share
+ * the buffer and race, so serialise them.  The first call on a device resolves
+ * the buffer's address; make it before any stream capture on that device. */
+spm_status spm_dequant_rows_static(const spm_model* m, int32_t index, uint64_t row0, uint64_t rows,
+                                   float* out_host);
 /* y[p][r] = sum_c W[r][c] * x[p][c] for one stream; x_dev is positions x cols,
  * y_dev positions x rows (device pointers); cuda_stream may be NULL. */
 spm_status spm_streamed(const spm_model* m, int32_t index, const float* x_dev, int32_t positions,
