@@ -107,6 +107,21 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 __device__ __forceinline__ void bar_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
+// Named barrier `id` over `threads` threads that also ORs a predicate across
+// them: every participant learns whether any of them passed true.
+__device__ __forceinline__ bool bar_or(int id, int threads, bool p) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"(uint32_t(p)), "r"(id), "r"(threads)
+        : "memory");
+    return r != 0;
+}
+// Orders this thread's (and, after a barrier, its peers') generic-proxy
+// accesses to shared memory before its later async-proxy operations (a bulk
+// copy that overwrites a ring slot the warps have just read).
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
 }  // namespace dev
 }  // namespace spm

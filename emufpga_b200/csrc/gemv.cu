@@ -1,76 +1,83 @@
 // Launch geometry and dispatch of the streaming GEMV (kernel in gemv_impl.cuh,
 // instantiated per block type in gemv_<type>.cu).
+#include <algorithm>
+
 #include "gemv_impl.cuh"
 
 namespace spm {
 namespace gemv {
-extern template cudaError_t launch_enc<SPM_Q8_0>(const GemvLaunch&, bool, int, size_t, cudaStream_t, bool);
-extern template cudaError_t launch_enc<SPM_Q6_K>(const GemvLaunch&, bool, int, size_t, cudaStream_t, bool);
-extern template cudaError_t launch_enc<SPM_Q5_K>(const GemvLaunch&, bool, int, size_t, cudaStream_t, bool);
-extern template cudaError_t launch_enc<SPM_Q2_K>(const GemvLaunch&, bool, int, size_t, cudaStream_t, bool);
-extern template cudaError_t launch_enc<SPM_F32>(const GemvLaunch&, bool, int, size_t, cudaStream_t, bool);
-extern template int occupancy_enc<SPM_Q8_0>(const GemvLaunch&, bool, size_t);
-extern template int occupancy_enc<SPM_Q6_K>(const GemvLaunch&, bool, size_t);
-extern template int occupancy_enc<SPM_Q5_K>(const GemvLaunch&, bool, size_t);
-extern template int occupancy_enc<SPM_Q2_K>(const GemvLaunch&, bool, size_t);
-extern template int occupancy_enc<SPM_F32>(const GemvLaunch&, bool, size_t);
+#define SPM_EXTERN(T)                                                                                    \
+    extern template cudaError_t launch_enc<T>(const GemvLaunch&, bool, int, int, size_t, cudaStream_t, bool); \
+    extern template int occupancy_enc<T>(const GemvLaunch&, bool, int, size_t);
+SPM_EXTERN(SPM_Q8_0)
+SPM_EXTERN(SPM_Q6_K)
+SPM_EXTERN(SPM_Q5_K)
+SPM_EXTERN(SPM_Q2_K)
+SPM_EXTERN(SPM_F32)
+#undef SPM_EXTERN
 }  // namespace gemv
 
 using namespace gemv;
 
-// Bytes of the clients' activations staged in shared memory, with their
-// 16-value sums.
-static size_t x_stage_bytes(const GemvLaunch& L) { return size_t(L.n) * (L.cols * 4 + (L.cols / 16) * 4); }
-
-static int occupancy(uint32_t dtype, const GemvLaunch& L, bool dual, size_t smem) {
+static int occupancy(uint32_t dtype, const GemvLaunch& L, bool dual, int threads, size_t smem) {
     switch (dtype) {
-        case SPM_Q8_0: return occupancy_enc<SPM_Q8_0>(L, dual, smem);
-        case SPM_Q6_K: return occupancy_enc<SPM_Q6_K>(L, dual, smem);
-        case SPM_Q5_K: return occupancy_enc<SPM_Q5_K>(L, dual, smem);
-        case SPM_Q2_K: return occupancy_enc<SPM_Q2_K>(L, dual, smem);
-        case SPM_F32: return occupancy_enc<SPM_F32>(L, dual, smem);
+        case SPM_Q8_0: return occupancy_enc<SPM_Q8_0>(L, dual, threads, smem);
+        case SPM_Q6_K: return occupancy_enc<SPM_Q6_K>(L, dual, threads, smem);
+        case SPM_Q5_K: return occupancy_enc<SPM_Q5_K>(L, dual, threads, smem);
+        case SPM_Q2_K: return occupancy_enc<SPM_Q2_K>(L, dual, threads, smem);
+        case SPM_F32: return occupancy_enc<SPM_F32>(L, dual, threads, smem);
         default: return 1;
     }
+}
+
+// CTA size, warp groups and ring slots.  Two CTAs of 8 warps share an SM
+// when their ring and activations fit in half of its shared memory (the next
+// kernel's CTAs can then start prefetching beside them); otherwise one CTA of
+// 16 warps has the SM to itself.  A group is the fewest warps that give each
+// lane at most four units of a row while every group still gets two ring
+// slots (one being read, one in flight), or as many as it has tiles.  The
+// slots are a multiple of the groups: slot s belongs to group s % G.
+GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms, int per_fixed) {
+    const size_t slot = size_t(L.tile_bytes) * (dual ? 2 : 1);
+    const uint32_t U = L.cols / 32;
+    for (int per_sm = 2; per_sm >= 1; per_sm--) {
+        const int W = per_sm == 2 ? kPairWarps : kMaxWarps;
+        const size_t cap = per_sm == 2 ? kHalfSm : kSmemMax;
+        const size_t fixed = smem_bytes(L, dual, 0, W);
+        if (fixed + slot > cap) continue;
+        const int ns_max = int(std::min<size_t>(kMaxSlots, (cap - fixed) / slot));
+        int grid = 0, per = per_fixed;
+        if (per_fixed <= 0) {
+            const uint32_t gcap = uint32_t(sms) * uint32_t(per_sm);
+            grid = int(std::min(L.total_tiles, gcap));
+            per = int((L.total_tiles + grid - 1) / grid);
+        }
+        for (int gw = 1; gw <= W; gw *= 2) {
+            const int G = W / gw;
+            if ((U + 32 * gw - 1) / (32 * gw) > 4 && gw < W) continue;
+            const int pg = (per + G - 1) / G;  // tiles per group
+            const int nsg_max = ns_max / G;
+            if (nsg_max < 1 || nsg_max < std::min(pg, 2)) continue;
+            const int nsg = std::max(1, std::min(nsg_max, pg));
+            return GemvGeometry{grid, G * nsg, W, gw, smem_bytes(L, dual, G * nsg, W)};
+        }
+    }
+    // one CTA per SM, all its warps on each tile, as many slots as fit
+    const int W = kMaxWarps;
+    const size_t fixed = smem_bytes(L, dual, 0, W);
+    const int ns = int(std::max<size_t>(1, std::min<size_t>(kMaxSlots, (kSmemMax - fixed) / slot)));
+    int grid = 0;
+    if (per_fixed <= 0) grid = int(std::min(L.total_tiles, uint32_t(sms)));
+    return GemvGeometry{grid, ns, W, W, smem_bytes(L, dual, ns, W)};
 }
 
 // Geometry with the grid capped at the CTAs that can be resident at once
 // (one wave), so that every CTA starts streaming immediately.
 static GemvGeometry geometry_resident(uint32_t dtype, const GemvLaunch& L, bool dual, int sms) {
     GemvGeometry g = gemv_geometry(L, dual, sms);
-    const int occ = occupancy(dtype, L, dual, g.smem);
+    const int occ = occupancy(dtype, L, dual, g.warps * 32, g.smem);
     const int cap = occ * sms;
     if (g.grid > cap) g.grid = cap;
-    return g;
-}
-
-// Ring slots and shared memory for CTAs that each own about `per` tiles.
-static GemvGeometry ring_geometry(const GemvLaunch& L, bool dual, int per) {
-    GemvGeometry g{};
-    const size_t slot = size_t(L.tile_bytes) * (dual ? 2 : 1);
-    const size_t xb = x_stage_bytes(L);
-    // Two CTAs per SM when ring + activations fit in half the SM's shared
-    // memory (the next kernel's CTAs can then start prefetching beside them).
-    size_t ring = kRingBytes;
-    if (xb + ring > kHalfSm) ring = xb + kRingMin <= kHalfSm ? kHalfSm - xb : kSmemMax - xb;
-    if (ring > kRingBytes) ring = kRingBytes;
-    int slots = int(ring / slot);
-    if (slots > kMaxSlots) slots = kMaxSlots;
-    if (slots > per) slots = per;
-    if (slots < 1) slots = 1;
-    g.slots = slots;
-    g.consumers = kConsumers;
-    g.smem = slot * size_t(slots) + xb;
-    return g;
-}
-
-GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms) {
-    const size_t xb = x_stage_bytes(L);
-    const int per_sm = xb + kRingMin <= kHalfSm ? 2 : 1;
-    const uint32_t gcap = uint32_t(sms) * per_sm;
-    const int grid = int(L.total_tiles < gcap ? L.total_tiles : gcap);
-    const int per = grid ? int((L.total_tiles + grid - 1) / grid) : 1;
-    GemvGeometry g = ring_geometry(L, dual, per);
-    g.grid = grid;
     return g;
 }
 
@@ -79,20 +86,21 @@ static cudaError_t launch_one(uint32_t dtype, GemvLaunch L, int sms, cudaStream_
     GemvGeometry g;
     if (L.plan) {
         // expert mode: a CTA owns 1/expert_chunks of one active expert's tiles
-        g = ring_geometry(L, dual, int((L.expert_tiles + L.expert_chunks - 1) / L.expert_chunks));
+        g = gemv_geometry(L, dual, sms, int((L.expert_tiles + L.expert_chunks - 1) / L.expert_chunks));
         g.grid = L.expert_max * L.expert_chunks;
     } else {
         g = geometry_resident(dtype, L, dual, sms);
     }
     if (grid > 0 && grid < g.grid) g.grid = grid;  // more tiles per CTA; the ring stays valid
     L.slots = g.slots;
-    L.consumers = g.consumers;
+    L.group_warps = g.group_warps;
+    const int threads = g.warps * 32;
     switch (dtype) {
-        case SPM_Q8_0: return launch_enc<SPM_Q8_0>(L, dual, g.grid, g.smem, s, pdl);
-        case SPM_Q6_K: return launch_enc<SPM_Q6_K>(L, dual, g.grid, g.smem, s, pdl);
-        case SPM_Q5_K: return launch_enc<SPM_Q5_K>(L, dual, g.grid, g.smem, s, pdl);
-        case SPM_Q2_K: return launch_enc<SPM_Q2_K>(L, dual, g.grid, g.smem, s, pdl);
-        case SPM_F32: return launch_enc<SPM_F32>(L, dual, g.grid, g.smem, s, pdl);
+        case SPM_Q8_0: return launch_enc<SPM_Q8_0>(L, dual, g.grid, threads, g.smem, s, pdl);
+        case SPM_Q6_K: return launch_enc<SPM_Q6_K>(L, dual, g.grid, threads, g.smem, s, pdl);
+        case SPM_Q5_K: return launch_enc<SPM_Q5_K>(L, dual, g.grid, threads, g.smem, s, pdl);
+        case SPM_Q2_K: return launch_enc<SPM_Q2_K>(L, dual, g.grid, threads, g.smem, s, pdl);
+        case SPM_F32: return launch_enc<SPM_F32>(L, dual, g.grid, threads, g.smem, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
@@ -102,10 +110,12 @@ cudaError_t launch_gemv(uint32_t dtype, GemvLaunch L, int sms, cudaStream_t s, b
     if (grid_out) *grid_out = 0;
     if (L.total_tiles == 0) return cudaSuccess;
     if (L.n < 1 || L.n > 8 || (L.cols & 31)) return cudaErrorInvalidValue;
-    const size_t slot = size_t(L.tile_bytes) * (dual ? 2 : 1);
-    if (slot + size_t(L.cols) * 4 + (L.cols / 16) * 4 > kSmemMax) return cudaErrorInvalidValue;
-    if (L.plan && slot + x_stage_bytes(L) > kSmemMax) return cudaErrorInvalidValue;
-    if (slot + x_stage_bytes(L) > kSmemMax) {
+    GemvLaunch one = L;
+    one.n = 1;
+    if (smem_bytes(one, dual, 1, kMaxWarps) > kSmemMax) return cudaErrorInvalidValue;
+    const bool fits = smem_bytes(L, dual, 1, kMaxWarps) <= kSmemMax;
+    if (L.plan && !fits) return cudaErrorInvalidValue;
+    if (!fits) {
         // The clients' activations do not fit beside one tile: one launch per
         // half of the clients (the weights are read twice), on a common grid
         // so that both halves write the same sum-of-squares parts.

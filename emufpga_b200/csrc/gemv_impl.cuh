@@ -1,13 +1,15 @@
 // The streamed dequant-GEMV: y[p][r] = sum_c W[r][c] * x[p][c] for up to 8
 // clients p off ONE pass over the packed weights (host_pack.cpp layout).
 //
-// Each CTA owns a contiguous run of 4-row tiles.  A producer warp streams the
-// run into a shared-memory ring with cp.async.bulk (one bulk copy per tile,
-// completion on an mbarrier), so the bytes in flight per SM do not depend on
-// registers or occupancy.  Eight consumer warps in two groups work on every
-// tile: a group takes two of its rows (or, for a gate/up pair, every row of
-// one of the two matrices), its four warps split the row's 32-weight units,
-// and partial sums are combined in shared memory in warp order.
+// Each CTA owns a contiguous run of 4-row tiles and streams them through a
+// shared-memory ring with cp.async.bulk (one copy per tile, or per gate/up
+// pair, completing on an mbarrier).  The CTA's warps form groups of
+// `group_warps` warps; group g works on the CTA's tiles g, g+G, g+2G, ...
+// with its lanes split over the 32-weight units of the tile's rows.  There is
+// no producer warp: the group that finishes a slot refills it with the tile
+// NS further on, so all warps compute and none idles waiting on the ring.
+// Short rows (SmolLM2: 18 units) take one warp per tile; long rows spread a
+// tile over several warps so that every lane has one to four units.
 //
 // Per unit a lane turns four codes at a time into floats with one byte
 // permute each and applies them to all clients' activations (staged once per
@@ -16,7 +18,7 @@
 // The K-quant codes q (< 128) become f = 1 + q/128 exactly (q in the
 // mantissa of 1.0), so that per 16- or 32-value sub-block
 //     sum_c q_c x_c = 128 * sum_c f_c x_c - 128 * sum_c x_c
-// with the activation sums precomputed once per CTA; Q8_0 codes become
+// with the activation sums precomputed when x is staged; Q8_0 codes become
 // 2^23 + (q ^ 128) and are re-centred exactly.  Block scales are applied once
 // per sub-block:
 //     sum_c w_c x_c = (d*sc) * sum_c q_c x_c  [- (dmin*m) * sum_c x_c]
@@ -24,9 +26,20 @@
 // reference's bit for bit (the dequant kernel checks that); the fp32 sums are
 // in a different order than the reference's FMA chain.
 //
+// A lane's partial sums for the pass's rows and clients are reduced across
+// the warp by a transposing butterfly (each exchange halves the values a lane
+// holds), so that afterwards lane l owns one (row, client) total; groups of
+// several warps add their warps' totals through shared memory, in warp order.
+// All sums are in a fixed order: results do not depend on timing.
+//
+// A fused RMSNorm multiplies the staged activations by the gain and applies
+// the client's scale 1/sqrt(mean + eps) to the dot product:
+// s * sum_c w_c (x_c g_c), the reference's sum_c w_c ((x_c s) g_c) with the
+// scale factored out.
+//
 // Launched with programmatic dependent launch: the ring is filled while the
-// previous kernel still runs (weights never depend on it), and the consumers
-// read the activations only after griddepcontrol.wait.
+// previous kernel still runs (weights never depend on it), and the
+// activations are read only after griddepcontrol.wait.
 #pragma once
 #include "device.cuh"
 #include "moe.h"
@@ -35,41 +48,33 @@ namespace spm {
 namespace gemv {
 using namespace dev;
 
-constexpr int kGroupWarps = 4;                 // warps per consumer group
-constexpr int kConsumers = 2 * kGroupWarps;    // consumer warps per CTA
-constexpr int kThreads = (kConsumers + 1) * 32;
+constexpr int kMaxWarps = 16;             // warps of a CTA that has an SM to itself
+constexpr int kPairWarps = 8;             // warps of each of two CTAs sharing an SM
 constexpr int kMaxSlots = 16;
-constexpr size_t kRingBytes = 96 * 1024;       // weight ring, at most
-constexpr size_t kSmemMax = 212 * 1024;        // dynamic shared memory, at most (static use ~7 KB)
-constexpr size_t kHalfSm = 104 * 1024;         // dynamic shared memory for two CTAs per SM
-constexpr size_t kRingMin = 24 * 1024;         // weight ring, at least
-constexpr int kAuxPrefetch = 1024;             // residual values prefetched per CTA, at most
-
-// Activations of the clients in shared memory (normalised when the launch
-// fuses an RMSNorm).  Unit u's 32 values are 8 chunks of 4; chunk t is stored
-// at slot t ^ (u & 7) so that the lanes of a quarter-warp, reading chunk t of
-// consecutive units, hit distinct banks.  xsum holds the sum of every 16
-// consecutive values (K-quant re-centring).
-__device__ __forceinline__ uint32_t xoff(uint32_t u, uint32_t chunk) {
-    return (u * 8 + (chunk ^ (u & 7))) * 16;
-}
+constexpr size_t kSmemMax = 200 * 1024;   // dynamic shared memory of a CTA alone on its SM
+constexpr size_t kHalfSm = 100 * 1024;    // dynamic shared memory of each of two CTAs per SM
+constexpr int kAuxPrefetch = 1024;        // residual values prefetched per CTA, at most
+// Staged activations: per client, one 144-byte record per 32-value unit --
+// 128 bytes of values, the two 16-value sums, 8 bytes of padding.  The
+// padding puts the records of consecutive units 4 banks apart, so the lanes
+// of a quarter-warp reading the same chunk of consecutive units never share
+// a bank.
+constexpr uint32_t kUnitBytes = 144;
 
 template <int NC>
 struct XIn {
-    uint32_t xs, cstride;  // shared base of x, bytes per client
-    uint32_t ss, sstride;  // shared base of the 16-value sums, bytes per client
+    uint32_t base[NC];  // shared address of client c's records
     __device__ __forceinline__ void load(uint32_t u, int off, float4 (&o)[NC]) const {
-        const uint32_t a = xs + xoff(u, uint32_t(off) >> 2);
 #pragma unroll
         for (int c = 0; c < NC; c++) {
-            const uint4 v = lds128(a + c * cstride);
+            const uint4 v = lds128(base[c] + u * kUnitBytes + off * 4);
             o[c] = make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
         }
     }
     // sum of the 16 values starting at 32*u + 16*half, per client
     __device__ __forceinline__ void sums(uint32_t u, int half, float (&o)[NC]) const {
 #pragma unroll
-        for (int c = 0; c < NC; c++) o[c] = __uint_as_float(lds32(ss + c * sstride + (2 * u + half) * 4));
+        for (int c = 0; c < NC; c++) o[c] = __uint_as_float(lds32(base[c] + u * kUnitBytes + 128 + half * 4));
     }
 };
 
@@ -96,71 +101,75 @@ __device__ __forceinline__ float onef(uint32_t q) {
 // int8 -> float exactly: 2^23 + (b ^ 128) - (2^23 + 128).
 __device__ __forceinline__ float i8f(uint32_t b) { return bytef<0>(b ^ 0x80u) - 8388736.0f; }
 
-template <int VR, int NC>
-__device__ __forceinline__ void zero(float (&s)[VR][NC]) {
+template <int R, int NC>
+__device__ __forceinline__ void zero(float (&s)[R][NC]) {
 #pragma unroll
-    for (int v = 0; v < VR; v++)
+    for (int v = 0; v < R; v++)
 #pragma unroll
         for (int c = 0; c < NC; c++) s[v][c] = 0.f;
 }
 
-// Every unit function adds unit u of the rows `rows` (row indices inside the
-// tile at shared address t) times the activations into acc[v][client].
+// One row of a pass: shared address of its tile, and its row index r inside
+// the tile as r * units and r * super-blocks.
+struct RowRef {
+    uint32_t t, ru, rb;
+};
+
+// Every unit function adds unit u of the rows R times the activations into
+// acc[row][client].
 
 // ------------------------------------------------------------------ Q8_0 --
-template <int NC, int VR>
-__device__ __forceinline__ void unit_q8_0(uint32_t t, const uint32_t (&rows)[VR], uint32_t u, const GemvLaunch& L,
-                                          const XIn<NC>& X, float (&acc)[VR][NC]) {
-    const uint32_t U = L.cols >> 5;
-    uint4 q0[VR], q1[VR];
-    float d[VR];
+template <int NC, int R>
+__device__ __forceinline__ void unit_q8_0(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XIn<NC>& X,
+                                          float (&acc)[R][NC]) {
+    uint4 q0[R], q1[R];
+    float d[R];
 #pragma unroll
-    for (int v = 0; v < VR; v++) {
-        const uint32_t unit = rows[v] * U + u;
-        q0[v] = lds128(t + unit * 32);
-        q1[v] = lds128(t + unit * 32 + 16);
-        d[v] = h2f(lds16(t + L.plane1 + unit * 2));
+    for (int v = 0; v < R; v++) {
+        const uint32_t unit = rr[v].ru + u;
+        q0[v] = lds128(rr[v].t + unit * 32);
+        q1[v] = lds128(rr[v].t + unit * 32 + 16);
+        d[v] = h2f(lds16(rr[v].t + L.plane1 + unit * 2));
     }
-    float s[VR][NC];
+    float s[R][NC];
     zero(s);
 #pragma unroll
     for (int k = 0; k < 8; k++) {
         float4 x[NC];
         X.load(u, 4 * k, x);
 #pragma unroll
-        for (int v = 0; v < VR; v++) {
+        for (int v = 0; v < R; v++) {
             const uint32_t w = (k < 4 ? word(q0[v], k) : word(q1[v], k - 4)) ^ 0x80808080u;
             const float c0 = 8388736.0f;  // 2^23 + 128: (u8 ^ 0x80) - 128 == int8
             dot4<NC>(s[v], bytef<0>(w) - c0, bytef<1>(w) - c0, bytef<2>(w) - c0, bytef<3>(w) - c0, x);
         }
     }
 #pragma unroll
-    for (int v = 0; v < VR; v++)
+    for (int v = 0; v < R; v++)
 #pragma unroll
         for (int c = 0; c < NC; c++) acc[v][c] = fmaf(d[v], s[v][c], acc[v][c]);
 }
 
 // ------------------------------------------------------------------ Q6_K --
-template <int NC, int VR>
-__device__ __forceinline__ void unit_q6_k(uint32_t t, const uint32_t (&rows)[VR], uint32_t u, const GemvLaunch& L,
-                                          const XIn<NC>& X, float (&acc)[VR][NC]) {
-    const uint32_t U = L.cols >> 5, B = L.cols >> 8;
-    uint4 ql[VR];
-    uint2 qh[VR];
-    float ds[VR][2];
+template <int NC, int R>
+__device__ __forceinline__ void unit_q6_k(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XIn<NC>& X,
+                                          float (&acc)[R][NC]) {
+    uint4 ql[R];
+    uint2 qh[R];
+    float ds[R][2];
 #pragma unroll
-    for (int v = 0; v < VR; v++) {
-        const uint32_t unit = rows[v] * U + u;
-        ql[v] = lds128(t + unit * 16);
-        qh[v] = lds64(t + L.plane1 + unit * 8);
-        const uint32_t sc = lds16(t + L.plane2 + unit * 2);
-        const float d = h2f(lds16(t + L.plane3 + (rows[v] * B + (u >> 3)) * 2));
+    for (int v = 0; v < R; v++) {
+        const uint32_t unit = rr[v].ru + u;
+        ql[v] = lds128(rr[v].t + unit * 16);
+        qh[v] = lds64(rr[v].t + L.plane1 + unit * 8);
+        const uint32_t sc = lds16(rr[v].t + L.plane2 + unit * 2);
+        const float d = h2f(lds16(rr[v].t + L.plane3 + (rr[v].rb + (u >> 3)) * 2));
         ds[v][0] = d * i8f(sc & 0xffu);
         ds[v][1] = d * i8f(sc >> 8);
     }
 #pragma unroll
     for (int run = 0; run < 2; run++) {
-        float s[VR][NC], xs[NC];
+        float s[R][NC], xs[NC];
         zero(s);
         X.sums(u, run, xs);
 #pragma unroll
@@ -168,7 +177,7 @@ __device__ __forceinline__ void unit_q6_k(uint32_t t, const uint32_t (&rows)[VR]
             float4 x[NC];
             X.load(u, 16 * run + 4 * k, x);
 #pragma unroll
-            for (int v = 0; v < VR; v++) {
+            for (int v = 0; v < R; v++) {
                 const uint32_t w = word(ql[v], k);
                 const uint32_t h = run ? qh[v].y : qh[v].x;
                 const uint32_t hs = ((k < 2 ? h << (4 - 2 * k) : h >> (2 * k - 4)) & 0x30303030u) | 0x80808080u;
@@ -178,7 +187,7 @@ __device__ __forceinline__ void unit_q6_k(uint32_t t, const uint32_t (&rows)[VR]
         }
         // sum (q - 32) x = 128 sum f x - 160 sum x
 #pragma unroll
-        for (int v = 0; v < VR; v++)
+        for (int v = 0; v < R; v++)
 #pragma unroll
             for (int c = 0; c < NC; c++) acc[v][c] = fmaf(ds[v][run], fmaf(s[v][c], 128.0f, -160.0f * xs[c]), acc[v][c]);
     }
@@ -190,20 +199,19 @@ __device__ __forceinline__ uint32_t sbyte(const uint4& m, int k) {  // scales by
     return (w >> (8 * (k & 3))) & 0xffu;
 }
 
-template <int NC, int VR>
-__device__ __forceinline__ void unit_q5_k(uint32_t t, const uint32_t (&rows)[VR], uint32_t u, const GemvLaunch& L,
-                                          const XIn<NC>& X, float (&acc)[VR][NC]) {
-    const uint32_t U = L.cols >> 5, B = L.cols >> 8;
+template <int NC, int R>
+__device__ __forceinline__ void unit_q5_k(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XIn<NC>& X,
+                                          float (&acc)[R][NC]) {
     const int j = int(u & 7);
-    uint4 qs[VR];
-    uint32_t qh[VR];
-    float ds[VR], dm[VR];
+    uint4 qs[R];
+    uint32_t qh[R];
+    float ds[R], dm[R];
 #pragma unroll
-    for (int v = 0; v < VR; v++) {
-        const uint32_t unit = rows[v] * U + u;
-        const uint4 m = lds128(t + (rows[v] * B + (u >> 3)) * 16);
-        qs[v] = lds128(t + L.plane1 + unit * 16);
-        qh[v] = lds32(t + L.plane2 + unit * 4);
+    for (int v = 0; v < R; v++) {
+        const uint32_t unit = rr[v].ru + u;
+        const uint4 m = lds128(rr[v].t + (rr[v].rb + (u >> 3)) * 16);
+        qs[v] = lds128(rr[v].t + L.plane1 + unit * 16);
+        qh[v] = lds32(rr[v].t + L.plane2 + unit * 4);
         uint32_t sc, mn;
         if (j < 4) {
             sc = sbyte(m, j) & 63;
@@ -215,7 +223,7 @@ __device__ __forceinline__ void unit_q5_k(uint32_t t, const uint32_t (&rows)[VR]
         ds[v] = h2f(m.x) * (bytef<0>(sc) - 8388608.0f);
         dm[v] = h2f(m.x >> 16) * (bytef<0>(mn) - 8388608.0f);
     }
-    float s[VR][NC], xa[NC], xb[NC];
+    float s[R][NC], xa[NC], xb[NC];
     zero(s);
     X.sums(u, 0, xa);
     X.sums(u, 1, xb);
@@ -226,7 +234,7 @@ __device__ __forceinline__ void unit_q5_k(uint32_t t, const uint32_t (&rows)[VR]
             float4 x[NC];
             X.load(u, 16 * run + 4 * k, x);
 #pragma unroll
-            for (int v = 0; v < VR; v++) {
+            for (int v = 0; v < R; v++) {
                 const uint32_t w = word(qs[v], k);
                 const uint32_t sp =
                     (((((qh[v] >> (16 * run + 4 * k)) & 0xfu) * 0x02040810u) & 0x10101010u)) | 0x80808080u;
@@ -237,7 +245,7 @@ __device__ __forceinline__ void unit_q5_k(uint32_t t, const uint32_t (&rows)[VR]
     }
     // sum w x = ds * (128 sum f x - 128 sum x) - dm * sum x
 #pragma unroll
-    for (int v = 0; v < VR; v++)
+    for (int v = 0; v < R; v++)
 #pragma unroll
         for (int c = 0; c < NC; c++) {
             const float xsum = xa[c] + xb[c];
@@ -246,25 +254,24 @@ __device__ __forceinline__ void unit_q5_k(uint32_t t, const uint32_t (&rows)[VR]
 }
 
 // ------------------------------------------------------------------ Q2_K --
-template <int NC, int VR>
-__device__ __forceinline__ void unit_q2_k(uint32_t t, const uint32_t (&rows)[VR], uint32_t u, const GemvLaunch& L,
-                                          const XIn<NC>& X, float (&acc)[VR][NC]) {
-    const uint32_t U = L.cols >> 5, B = L.cols >> 8;
-    uint2 qs[VR];
-    uint32_t sc[VR];
-    float d[VR], dmin[VR];
+template <int NC, int R>
+__device__ __forceinline__ void unit_q2_k(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XIn<NC>& X,
+                                          float (&acc)[R][NC]) {
+    uint2 qs[R];
+    uint32_t sc[R];
+    float d[R], dmin[R];
 #pragma unroll
-    for (int v = 0; v < VR; v++) {
-        const uint32_t unit = rows[v] * U + u;
-        qs[v] = lds64(t + unit * 8);
-        sc[v] = lds16(t + L.plane1 + unit * 2);
-        const uint32_t dd = lds32(t + L.plane2 + (rows[v] * B + (u >> 3)) * 4);
+    for (int v = 0; v < R; v++) {
+        const uint32_t unit = rr[v].ru + u;
+        qs[v] = lds64(rr[v].t + unit * 8);
+        sc[v] = lds16(rr[v].t + L.plane1 + unit * 2);
+        const uint32_t dd = lds32(rr[v].t + L.plane2 + (rr[v].rb + (u >> 3)) * 4);
         d[v] = h2f(dd);
         dmin[v] = h2f(dd >> 16);
     }
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-        float s[VR][NC], xs[NC];
+        float s[R][NC], xs[NC];
         zero(s);
         X.sums(u, h, xs);
 #pragma unroll
@@ -272,13 +279,13 @@ __device__ __forceinline__ void unit_q2_k(uint32_t t, const uint32_t (&rows)[VR]
             float4 x[NC];
             X.load(u, 16 * h + 4 * k, x);
 #pragma unroll
-            for (int v = 0; v < VR; v++) {
+            for (int v = 0; v < R; v++) {
                 const uint32_t q = (((h ? qs[v].y : qs[v].x) >> (2 * k)) & 0x03030303u) | 0x80808080u;
                 dot4<NC>(s[v], onef<0>(q), onef<1>(q), onef<2>(q), onef<3>(q), x);
             }
         }
 #pragma unroll
-        for (int v = 0; v < VR; v++) {
+        for (int v = 0; v < R; v++) {
             const uint32_t b = (sc[v] >> (8 * h)) & 0xffu;
             const float dl = d[v] * (bytef<0>(b & 15u) - 8388608.0f);
             const float ml = dmin[v] * (bytef<0>(b >> 4) - 8388608.0f);
@@ -290,30 +297,30 @@ __device__ __forceinline__ void unit_q2_k(uint32_t t, const uint32_t (&rows)[VR]
 }
 
 // ------------------------------------------------------------------- F32 --
-template <int NC, int VR>
-__device__ __forceinline__ void unit_f32(uint32_t t, const uint32_t (&rows)[VR], uint32_t u, const GemvLaunch& L,
-                                         const XIn<NC>& X, float (&acc)[VR][NC]) {
+template <int NC, int R>
+__device__ __forceinline__ void unit_f32(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XIn<NC>& X,
+                                         float (&acc)[R][NC]) {
 #pragma unroll
     for (int k = 0; k < 8; k++) {
         float4 x[NC];
         X.load(u, 4 * k, x);
 #pragma unroll
-        for (int v = 0; v < VR; v++) {
-            const uint4 w = lds128(t + (rows[v] * L.cols + 32 * u + 4 * k) * 4);
+        for (int v = 0; v < R; v++) {
+            const uint4 w = lds128(rr[v].t + (rr[v].ru + u) * 128 + 16 * k);
             dot4<NC>(acc[v], __uint_as_float(w.x), __uint_as_float(w.y), __uint_as_float(w.z), __uint_as_float(w.w),
                      x);
         }
     }
 }
 
-template <int ENC, int NC, int VR>
-__device__ __forceinline__ void unit_dot(uint32_t t, const uint32_t (&rows)[VR], uint32_t u, const GemvLaunch& L,
-                                         const XIn<NC>& X, float (&acc)[VR][NC]) {
-    if constexpr (ENC == SPM_Q8_0) unit_q8_0<NC, VR>(t, rows, u, L, X, acc);
-    else if constexpr (ENC == SPM_Q6_K) unit_q6_k<NC, VR>(t, rows, u, L, X, acc);
-    else if constexpr (ENC == SPM_Q5_K) unit_q5_k<NC, VR>(t, rows, u, L, X, acc);
-    else if constexpr (ENC == SPM_Q2_K) unit_q2_k<NC, VR>(t, rows, u, L, X, acc);
-    else unit_f32<NC, VR>(t, rows, u, L, X, acc);
+template <int ENC, int NC, int R>
+__device__ __forceinline__ void unit_dot(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XIn<NC>& X,
+                                         float (&acc)[R][NC]) {
+    if constexpr (ENC == SPM_Q8_0) unit_q8_0<NC, R>(rr, u, L, X, acc);
+    else if constexpr (ENC == SPM_Q6_K) unit_q6_k<NC, R>(rr, u, L, X, acc);
+    else if constexpr (ENC == SPM_Q5_K) unit_q5_k<NC, R>(rr, u, L, X, acc);
+    else if constexpr (ENC == SPM_Q2_K) unit_q2_k<NC, R>(rr, u, L, X, acc);
+    else unit_f32<NC, R>(rr, u, L, X, acc);
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return __fdiv_rn(g, 1.0f + expf(-g)) * u; }
@@ -325,30 +332,72 @@ __device__ __forceinline__ const GemvJob& pick(const GemvLaunch& L, uint32_t g) 
     return L.job[0];
 }
 
-// Rows of a pass per group: single matrix -> 2 of the tile's 4 rows per group
-// (group g: rows g, g+2) in one pass; gate/up pair -> group g takes matrix g,
-// VR rows per pass.
-template <int NC, bool DUAL>
-struct Shape {
-    static constexpr int VR = DUAL ? (NC <= 4 ? 4 : 2) : 2;
-    static constexpr int PASSES = DUAL ? kTileRows / VR : 1;
+// Transposing butterfly over the warp: lane values a[0..N) (N a power of two
+// <= 32).  Each exchange at distance O keeps half of the values (the upper
+// half on lanes with bit O set) and adds the partner's matching half; once a
+// lane holds one value the remaining exchanges are plain.  Afterwards a[0] of
+// lane l is the warp total of value (l >> (5 - log2 N)).
+template <int N, int O>
+struct XRed {
+    template <int V>
+    static __device__ __forceinline__ void run(float (&a)[V], int lane) {
+        if constexpr (O > 0) {
+            if constexpr (N > 1) {
+                constexpr int H = N / 2;
+                const bool up = (lane & O) != 0;
+#pragma unroll
+                for (int j = 0; j < H; j++) {
+                    const float send = up ? a[j] : a[j + H];
+                    const float keep = up ? a[j + H] : a[j];
+                    a[j] = keep + __shfl_xor_sync(0xffffffffu, send, O);
+                }
+                XRed<H, O / 2>::run(a, lane);
+            } else {
+                a[0] += __shfl_xor_sync(0xffffffffu, a[0], O);
+                XRed<1, O / 2>::run(a, lane);
+            }
+        }
+    }
 };
 
-// A CTA owns tiles [t0, t1).  Warp 8 (producer) streams them through the
-// ring; warps 0-7 (consumers) all pass every ring slot, so each full/empty
-// barrier phase is awaited in order by every waiter.
+constexpr int log2i(int v) { return v <= 1 ? 0 : 1 + log2i(v / 2); }
+
+// Rows of each matrix per pass: all four rows of a tile in one pass when the
+// lane's partial sums and codes fit in registers (one matrix and up to five
+// clients, or a gate/up pair for one client), else passes of two rows (or of
+// one row of a gate/up pair for more than five clients).
+template <int NC, bool DUAL>
+struct Shape {
+    static constexpr int VR = DUAL ? (NC == 1 ? 4 : NC <= 5 ? 2 : 1) : (NC <= 5 ? 4 : 2);
+    static constexpr int PASSES = kTileRows / VR;
+    static constexpr int M = DUAL ? 2 : 1;
+    static constexpr int NCP = NC <= 1 ? 1 : NC <= 2 ? 2 : NC <= 4 ? 4 : 8;  // clients, padded to 2^k
+    static constexpr int V = VR * NCP;                                        // sums per matrix per pass
+    static constexpr int SH = 5 - log2i(V);                                   // lane >> SH = sum index
+};
+
+// Bytes of dynamic shared memory the kernel uses for `slots` ring slots.
+inline size_t smem_bytes(const GemvLaunch& L, bool dual, int slots, int warps) {
+    const size_t slot = size_t(L.tile_bytes) * (dual ? 2 : 1);
+    const size_t xb = size_t(L.n) * (L.cols / 32) * kUnitBytes;
+    const size_t pb = size_t(2) * warps * 32 * (dual ? 2 : 1) * 4;
+    return slot * size_t(slots) + xb + pb;
+}
+
 template <int ENC, int NC, bool DUAL>
-__global__ void __launch_bounds__(kThreads, 2) gemv_stream(const __grid_constant__ GemvLaunch L) {
-    constexpr int VR = Shape<NC, DUAL>::VR, PASSES = Shape<NC, DUAL>::PASSES;
+__global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_constant__ GemvLaunch L) {
+    using S = Shape<NC, DUAL>;
+    constexpr int VR = S::VR, PASSES = S::PASSES, M = S::M, NCP = S::NCP, V = S::V, SH = S::SH;
     constexpr bool kquant = ENC == SPM_Q6_K || ENC == SPM_Q5_K || ENC == SPM_Q2_K;
-    extern __shared__ __align__(128) uint8_t ring[];
-    __shared__ uint64_t full[kMaxSlots], empty[kMaxSlots];
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t full[kMaxSlots];
     __shared__ float nscale[8];
-    __shared__ float part[2][kConsumers][VR][NC];
-    __shared__ float sqw[kConsumers][8];
     __shared__ float auxs[kAuxPrefetch];
-    __shared__ int32_t xrows[NC], yrows[NC], srows[NC];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ float sqw[kMaxWarps][8];
+    __shared__ int32_t xrows[8], yrows[8], srows[8];
+    const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
+    const int W = int(blockDim.x >> 5), gw = L.group_warps, G = W / gw;
+    const int grp = warp / gw, wig = warp % gw;
     uint32_t t0, t1;
     uint32_t rbase = 0, rlim = 0xffffffffu;  // expert mode: rows of the expert's matrix
     int n_act = NC;  // clients of this CTA with data (expert mode: the expert's clients)
@@ -366,214 +415,222 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_stream(const __grid_constant
         t0 = e * Te + uint32_t(uint64_t(Te) * chunk / C);
         t1 = e * Te + uint32_t(uint64_t(Te) * (chunk + 1) / C);
         n_act = L.plan->ntok[a];
-        if (threadIdx.x < NC) {
-            const int c = threadIdx.x;
+        if (threadIdx.x < 8) {
+            const int c = int(threadIdx.x);
             const int client = L.plan->tok[a][c < n_act ? c : 0];
             xrows[c] = L.xmode == 0 ? client : a * kMoeMaxClients + c;
             yrows[c] = a * kMoeMaxClients + c;
             srows[c] = client;
         }
     } else {
-        const uint32_t T = L.total_tiles, G = gridDim.x;
-        t0 = uint32_t(uint64_t(T) * blockIdx.x / G);
-        t1 = uint32_t(uint64_t(T) * (blockIdx.x + 1) / G);
-        if (threadIdx.x < NC) {
-            xrows[threadIdx.x] = threadIdx.x;
-            yrows[threadIdx.x] = threadIdx.x;
-            srows[threadIdx.x] = L.c0 + threadIdx.x;
+        const uint32_t T = L.total_tiles, Gd = gridDim.x;
+        t0 = uint32_t(uint64_t(T) * blockIdx.x / Gd);
+        t1 = uint32_t(uint64_t(T) * (blockIdx.x + 1) / Gd);
+        if (threadIdx.x < 8) {
+            xrows[threadIdx.x] = int(threadIdx.x);
+            yrows[threadIdx.x] = int(threadIdx.x);
+            srows[threadIdx.x] = L.c0 + int(threadIdx.x);
         }
     }
     const uint32_t nt = t1 - t0, NS = uint32_t(L.slots);
-    const uint32_t slot_bytes = L.tile_bytes * (DUAL ? 2u : 1u);
+    // Slot s belongs to group s % G alone (NS is a multiple of G), so each
+    // group waits for its slots' phases in order and refills them itself.
+    if (NS % uint32_t(G) != 0 || NS > uint32_t(kMaxSlots) || W * 32 != int(blockDim.x) || G * gw != W) {
+        if (threadIdx.x == 0) flag(L.status, 3);
+        return;
+    }
+    const uint32_t tile_bytes = L.tile_bytes, slot_bytes = tile_bytes * M;
+    const uint32_t U = L.cols >> 5, cstride = U * kUnitBytes;
+    const uint32_t xoff = NS * slot_bytes, poff = xoff + NC * cstride;
+    auto issue = [&](uint32_t i) {
+        const uint32_t s = i % NS, g = t0 + i;
+        const GemvJob& J = pick(L, g);
+        const size_t off = size_t(g - J.tile_begin) * tile_bytes;
+        mbar_expect_tx(&full[s], slot_bytes);
+        bulk_g2s(smem + size_t(s) * slot_bytes, J.a + off, tile_bytes, &full[s]);
+        if (DUAL) bulk_g2s(smem + size_t(s) * slot_bytes + tile_bytes, J.b + off, tile_bytes, &full[s]);
+    };
     if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < NS; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumers);
-        }
+        for (uint32_t s = 0; s < NS; s++) mbar_init(&full[s], 1);
         mbar_fence_init();
     }
     __syncthreads();
+    if (threadIdx.x == 0) {
+        for (uint32_t i = 0; i < NS && i < nt; i++) issue(i);
+        pdl_trigger();
+    }
+    pdl_wait();  // activations and norm partials come from the previous kernel
 
-    if (warp == kConsumers) {
-        // ---- producer: the weights of this CTA's tiles, in order ----
-        if (lane == 0) {
-            for (uint32_t i = 0; i < nt; i++) {
-                const uint32_t s = i % NS;
-                if (i >= NS && !mbar_wait(&empty[s], ((i / NS) - 1) & 1)) {
-                    flag(L.status, 1);
-                    break;
-                }
-                const uint32_t g = t0 + i;
-                const GemvJob& J = pick(L, g);
-                const size_t off = size_t(g - J.tile_begin) * L.tile_bytes;
-                mbar_expect_tx(&full[s], slot_bytes);
-                bulk_g2s(ring + size_t(s) * slot_bytes, J.a + off, L.tile_bytes, &full[s]);
-                if (DUAL) bulk_g2s(ring + size_t(s) * slot_bytes + L.tile_bytes, J.b + off, L.tile_bytes, &full[s]);
-                if (i + 1 == NS || i + 1 == nt) pdl_trigger();
-            }
-            if (nt == 0) pdl_trigger();
+    // ---- prologue: norm scales, staged activations, residual prefetch ----
+    if (L.gain && warp < NC) {
+        // warp c adds client c's per-CTA sums of squares, 32 lanes in parallel
+        const float* sp = L.sumsq + srows[warp];
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int p = lane;
+        for (; p + 96 < L.sumsq_parts; p += 128) {
+            a0 += sp[p * 8];
+            a1 += sp[(p + 32) * 8];
+            a2 += sp[(p + 64) * 8];
+            a3 += sp[(p + 96) * 8];
         }
-        return;
+        for (; p < L.sumsq_parts; p += 32) a0 += sp[p * 8];
+        const float ssum = warp_sum((a0 + a1) + (a2 + a3));
+        if (lane == 0) nscale[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssum, float(L.cols)), L.eps)));
     }
-
-    // ---- consumers ----
-    constexpr int CT = kConsumers * 32;
-    const int ctid = threadIdx.x;
-    pdl_wait();  // activations (and norm partials) come from the previous kernel
-    const uint32_t U = L.cols >> 5;
-    const uint32_t xbase = NS * slot_bytes;
-    const uint32_t cstride = U * 128;
-    const uint32_t sbase = xbase + NC * cstride, sstride = (L.cols >> 4) * 4;
-    // raw activations into shared memory while the norm partials are summed
-    // (16 lanes per client, fixed-order tree), then normalise in place
-    const uint32_t k4 = L.cols >> 2;
-    float ssum = 0.f;
-    const int sc_c = ctid >> 4, sc_j = ctid & 15;
-    if (L.gain && sc_c < NC)
-        for (int p = sc_j; p < L.sumsq_parts; p += 16) ssum += L.sumsq[p * 8 + srows[sc_c]];
-    for (uint32_t idx = ctid; idx < NC * k4; idx += CT) {
-        const uint32_t c = idx / k4, col = 4 * (idx % k4);
-        *reinterpret_cast<float4*>(ring + xbase + c * cstride + xoff(col >> 5, (col & 31) >> 2)) =
-            int(c) < n_act ? ldx4(L.x + size_t(xrows[c]) * L.x_stride + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const uint32_t h16 = L.cols >> 4;
+    for (uint32_t idx = threadIdx.x; idx < NC * h16; idx += blockDim.x) {
+        const uint32_t c = idx / h16, h = idx % h16, col = h * 16;
+        float4 v[4];
+        if (int(c) < n_act) {
+            const float* xp = L.x + size_t(xrows[c]) * L.x_stride + col;
+#pragma unroll
+            for (int k = 0; k < 4; k++) v[k] = ldx4(xp + 4 * k);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; k++) v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (L.gain) {
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const float4 g = ldx4(L.gain + col + 4 * k);
+                v[k] = make_float4(__fmul_rn(v[k].x, g.x), __fmul_rn(v[k].y, g.y), __fmul_rn(v[k].z, g.z),
+                                   __fmul_rn(v[k].w, g.w));
+            }
+        }
+        uint8_t* rec = smem + xoff + c * cstride + (h >> 1) * kUnitBytes;
+#pragma unroll
+        for (int k = 0; k < 4; k++) reinterpret_cast<float4*>(rec + (h & 1) * 64)[k] = v[k];
+        if constexpr (kquant) {
+            float sum = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; k++) sum += (v[k].x + v[k].y) + (v[k].z + v[k].w);
+            reinterpret_cast<float*>(rec + 128)[h & 1] = sum;
+        }
     }
-    // the residual rows this CTA will add to (EPI_ADD), loaded with x
+    // the residual rows this CTA will add to (EPI_ADD)
     const bool aux_pre = nt * kTileRows * NC <= uint32_t(kAuxPrefetch);
     if (aux_pre)
-        for (uint32_t idx = ctid; idx < nt * kTileRows * NC; idx += CT) {
+        for (uint32_t idx = threadIdx.x; idx < nt * kTileRows * NC; idx += blockDim.x) {
             const uint32_t i = idx / (kTileRows * NC), e = (idx / NC) % kTileRows, c = idx % NC;
             const GemvJob& J = pick(L, t0 + i);
             const uint32_t row = (t0 + i - J.tile_begin) * kTileRows + e;
             if (J.epi == EPI_ADD && row < J.rows) auxs[idx] = J.aux[size_t(yrows[c]) * J.aux_stride + row];
         }
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
-    if (L.gain && sc_c < NC && sc_j == 0)
-        nscale[sc_c] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssum, float(L.cols)), L.eps)));
-    bar_sync(1, CT);
-    if (L.gain) {
-        for (uint32_t idx = ctid; idx < NC * k4; idx += CT) {
-            const uint32_t c = idx / k4, col = 4 * (idx % k4);
-            float4* p = reinterpret_cast<float4*>(ring + xbase + c * cstride + xoff(col >> 5, (col & 31) >> 2));
-            const float4 v = *p, g = ldx4(L.gain + col);
-            const float sc = nscale[c];
-            *p = make_float4(__fmul_rn(__fmul_rn(v.x, sc), g.x), __fmul_rn(__fmul_rn(v.y, sc), g.y),
-                             __fmul_rn(__fmul_rn(v.z, sc), g.z), __fmul_rn(__fmul_rn(v.w, sc), g.w));
-        }
-        bar_sync(1, CT);
-    }
-    if constexpr (kquant) {
-        // sums of every 16 consecutive activations, per client
-        for (uint32_t idx = ctid; idx < NC * (L.cols >> 4); idx += CT) {
-            const uint32_t c = idx / (L.cols >> 4), h = idx % (L.cols >> 4), u = h >> 1;
-            const uint8_t* xc = ring + xbase + c * cstride;
-            float sum = 0.f;
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const float4 v = *reinterpret_cast<const float4*>(xc + xoff(u, (h & 1) * 4 + k));
-                sum += (v.x + v.y) + (v.z + v.w);
-            }
-            *reinterpret_cast<float*>(ring + sbase + c * sstride + h * 4) = sum;
-        }
-        bar_sync(1, CT);
-    }
+    __syncthreads();
+
+    // ---- main loop ----
+    const uint32_t smem_s = saddr(smem);
     XIn<NC> X;
-    X.xs = saddr(ring) + xbase;
-    X.cstride = cstride;
-    X.ss = saddr(ring) + sbase;
-    X.sstride = sstride;
-    float sqacc[NC];
 #pragma unroll
-    for (int c = 0; c < NC; c++) sqacc[c] = 0.f;
-    const uint32_t ring_s = saddr(ring);
-    const int grp = warp / kGroupWarps, gw = warp % kGroupWarps;
+    for (int c = 0; c < NC; c++) X.base[c] = smem_s + xoff + c * cstride;
+    // the (row in pass, client) total this thread finishes
+    const int kidx = gw == 1 ? (lane >> SH) : (wig * 32 + lane);
+    const bool finisher = gw == 1 ? (lane & ((1 << SH) - 1)) == 0 : kidx < V;
+    const int fv = kidx / NCP, fc = kidx % NCP;
+    const float fscale = (L.gain && fc < NC) ? nscale[fc] : 1.0f;
+    float* part = reinterpret_cast<float*>(smem + poff);  // [2][W][M][32]
+    float sq = 0.f;
     uint32_t buf = 0;
-    for (uint32_t i = 0; i < nt; i++) {
+    const uint32_t B = L.cols >> 8;
+    for (uint32_t i = uint32_t(grp); i < nt; i += uint32_t(G)) {
         const uint32_t s = i % NS;
-        if (!mbar_wait(&full[s], (i / NS) & 1)) {
-            flag(L.status, 2);
-            break;
-        }
+        const bool ok = mbar_wait(&full[s], (i / NS) & 1);
+        if (!ok) flag(L.status, 2);
+        if (gw == 1 && !ok) break;  // (groups decide together at their barrier)
         const uint32_t g = t0 + i;
         const GemvJob& J = pick(L, g);
         const uint32_t tile = g - J.tile_begin;
-        const uint32_t tbase = ring_s + s * slot_bytes + (DUAL && grp ? L.tile_bytes : 0);
+        const uint32_t tb = smem_s + s * slot_bytes;
+        bool abort = false;
 #pragma unroll 1
         for (int pass = 0; pass < PASSES; pass++) {
-            uint32_t rows[VR];
+            RowRef rr[M * VR];
 #pragma unroll
-            for (int v = 0; v < VR; v++) rows[v] = DUAL ? uint32_t(pass * VR + v) : uint32_t(grp + 2 * v);
-            float acc[VR][NC];
+            for (int m = 0; m < M; m++)
+#pragma unroll
+                for (int v = 0; v < VR; v++) {
+                    const uint32_t r = uint32_t(pass * VR + v);
+                    rr[m * VR + v] = RowRef{tb + uint32_t(m) * tile_bytes, r * U, r * B};
+                }
+            float acc[M * VR][NC];
             zero(acc);
 #pragma unroll 1
-            for (uint32_t u = uint32_t(gw) * 32 + lane; u < U; u += kGroupWarps * 32)
-                unit_dot<ENC, NC, VR>(tbase, rows, u, L, X, acc);
+            for (uint32_t u = uint32_t(wig * 32 + lane); u < U; u += uint32_t(gw * 32))
+                unit_dot<ENC, NC, M * VR>(rr, u, L, X, acc);
+            const bool last = pass + 1 == PASSES;
+            if (gw == 1 && last) {
+                // this warp alone read the slot: refill it
+                __syncwarp();
+                if (lane == 0 && i + NS < nt) {
+                    fence_proxy_async();
+                    issue(i + NS);
+                }
+            }
+            float red[M][V];
 #pragma unroll
-            for (int v = 0; v < VR; v++)
-#pragma unroll
-                for (int c = 0; c < NC; c++) acc[v][c] = warp_sum(acc[v][c]);
-            if (lane == 0)
+            for (int m = 0; m < M; m++)
 #pragma unroll
                 for (int v = 0; v < VR; v++)
 #pragma unroll
-                    for (int c = 0; c < NC; c++) part[buf][warp][v][c] = acc[v][c];
-            if (pass + 1 == PASSES) {  // this warp is done reading the slot
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
-            }
-            bar_sync(1, CT);
-            // one warp finishes the rows; the others go on (partials are double-buffered)
-            if (uint32_t(warp) == (i * PASSES + pass) % kConsumers) {
+                    for (int c = 0; c < NCP; c++) red[m][v * NCP + c] = c < NC ? acc[m * VR + v][c] : 0.f;
 #pragma unroll
-                for (int e = 0; e < (DUAL ? VR : 2 * VR); e++) {
-                    // DUAL: row pass*VR+e from groups 0 (gate) and 1 (up);
-                    // single: row e = g + 2v of group g = e % 2, v = e / 2
-                    const int gsel = DUAL ? 0 : (e & 1), v = DUAL ? e : (e >> 1);
-                    const uint32_t grow = tile * kTileRows + (DUAL ? uint32_t(pass * VR + e) : uint32_t(e));
-                    const uint32_t row = grow - rbase;
-                    if (grow >= J.rows || row >= rlim) continue;
+            for (int m = 0; m < M; m++) XRed<V, 16>::run(red[m], lane);
+            float a = red[0][0], b = M > 1 ? red[M - 1][0] : 0.f;
+            if (gw > 1) {
+                if ((lane & ((1 << SH) - 1)) == 0)
 #pragma unroll
-                    for (int c = 0; c < NC; c++) {
-                        float a = 0.f, b = 0.f;
-#pragma unroll
-                        for (int w = 0; w < kGroupWarps; w++) {
-                            a += part[buf][gsel * kGroupWarps + w][v][c];
-                            if (DUAL) b += part[buf][kGroupWarps + w][v][c];
-                        }
-                        float r = a;
-                        if constexpr (DUAL) r = silu_mul(a, b);
-                        if (lane == ((e * NC + c) & 31) && c < n_act) {
-                            if (J.epi == EPI_ADD) {
-                                const uint32_t e2 = DUAL ? uint32_t(pass * VR + e) : uint32_t(e);
-                                r = (aux_pre ? auxs[(i * kTileRows + e2) * NC + c] : J.aux[size_t(yrows[c]) * J.aux_stride + row]) + r;
-                            }
-                            J.y[size_t(yrows[c]) * J.y_stride + row] = r;
-                            sqacc[c] = fmaf(r, r, sqacc[c]);
-                        }
+                    for (int m = 0; m < M; m++) part[((buf * W + warp) * M + m) * 32 + (lane >> SH)] = red[m][0];
+                abort = bar_or(1 + grp, gw * 32, !ok);
+                if (abort) break;
+                if (last && wig == 0 && lane == 0 && i + NS < nt) {
+                    // every warp of the group is past its reads of the slot
+                    fence_proxy_async();
+                    issue(i + NS);
+                }
+                if (finisher) {
+                    a = 0.f;
+                    b = 0.f;
+                    for (int w = 0; w < gw; w++) {
+                        a += part[((buf * W + grp * gw + w) * M + 0) * 32 + kidx];
+                        if (M > 1) b += part[((buf * W + grp * gw + w) * M + M - 1) * 32 + kidx];
                     }
                 }
+                buf ^= 1;
             }
-            buf ^= 1;
+            if (finisher) {
+                const uint32_t e = uint32_t(pass * VR + fv);
+                const uint32_t grow = tile * kTileRows + e;
+                const uint32_t row = grow - rbase;
+                if (fc < n_act && grow < J.rows && row < rlim) {
+                    float r = a * fscale;
+                    if constexpr (DUAL) r = silu_mul(r, b * fscale);
+                    if (J.epi == EPI_ADD)
+                        r = (aux_pre ? auxs[(i * kTileRows + e) * NC + fc] : J.aux[size_t(yrows[fc]) * J.aux_stride + row]) + r;
+                    J.y[size_t(yrows[fc]) * J.y_stride + row] = r;
+                    sq = fmaf(r, r, sq);
+                }
+            }
         }
+        if (abort) break;
     }
     if (L.sumsq_out) {
         // per-CTA sum of squares of the rows written, reduced in a fixed order
 #pragma unroll
-        for (int c = 0; c < NC; c++) sqacc[c] = warp_sum(sqacc[c]);
-        if (lane == 0)
-#pragma unroll
-            for (int c = 0; c < NC; c++) sqw[warp][c] = sqacc[c];
-        bar_sync(1, CT);
-        if (ctid < NC) {
+        for (int c = 0; c < NC; c++) {
+            const float t = warp_sum(fc == c ? sq : 0.f);
+            if (lane == 0) sqw[warp][c] = t;
+        }
+        __syncthreads();
+        if (threadIdx.x < NC) {
             float t = 0.f;
-#pragma unroll
-            for (int w = 0; w < kConsumers; w++) t += sqw[w][ctid];
-            L.sumsq_out[blockIdx.x * 8 + L.c0 + ctid] = t;
+            for (int w = 0; w < W; w++) t += sqw[w][threadIdx.x];
+            L.sumsq_out[blockIdx.x * 8 + L.c0 + threadIdx.x] = t;
         }
     }
 }
 
 template <int ENC, int NC, bool DUAL>
-cudaError_t configure(int* occ, size_t smem) {
+cudaError_t configure(int* occ, int threads, size_t smem) {
     auto kern = gemv_stream<ENC, NC, DUAL>;
     static unsigned configured = 0;  // bit per device
     int dev = 0;
@@ -586,17 +643,17 @@ cudaError_t configure(int* occ, size_t smem) {
         if (e != cudaSuccess) return e;
         configured |= 1u << dev;
     }
-    if (occ) return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, kern, kThreads, smem);
+    if (occ) return cudaOccupancyMaxActiveBlocksPerMultiprocessor(occ, kern, threads, smem);
     return cudaSuccess;
 }
 
 template <int ENC, int NC, bool DUAL>
-cudaError_t launch_t(const GemvLaunch& L, int grid, size_t smem, cudaStream_t s, bool pdl) {
-    cudaError_t e = configure<ENC, NC, DUAL>(nullptr, smem);
+cudaError_t launch_t(const GemvLaunch& L, int grid, int threads, size_t smem, cudaStream_t s, bool pdl) {
+    cudaError_t e = configure<ENC, NC, DUAL>(nullptr, threads, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(threads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
@@ -609,9 +666,11 @@ cudaError_t launch_t(const GemvLaunch& L, int grid, size_t smem, cudaStream_t s,
 
 // All instantiations for one block type (compiled in gemv_<type>.cu).
 template <int ENC>
-cudaError_t launch_enc(const GemvLaunch& L, bool dual, int grid, size_t smem, cudaStream_t s, bool pdl) {
-#define SPM_NC(n) \
-    case n: return dual ? launch_t<ENC, n, true>(L, grid, smem, s, pdl) : launch_t<ENC, n, false>(L, grid, smem, s, pdl);
+cudaError_t launch_enc(const GemvLaunch& L, bool dual, int grid, int threads, size_t smem, cudaStream_t s, bool pdl) {
+#define SPM_NC(n)                                                                 \
+    case n:                                                                       \
+        return dual ? launch_t<ENC, n, true>(L, grid, threads, smem, s, pdl)      \
+                    : launch_t<ENC, n, false>(L, grid, threads, smem, s, pdl);
     switch (L.n) {
         SPM_NC(1) SPM_NC(2) SPM_NC(3) SPM_NC(4) SPM_NC(5) SPM_NC(6) SPM_NC(7) SPM_NC(8)
         default: return cudaErrorInvalidValue;
@@ -621,11 +680,13 @@ cudaError_t launch_enc(const GemvLaunch& L, bool dual, int grid, size_t smem, cu
 
 // Resident CTAs per SM of the kernel a launch would use.
 template <int ENC>
-int occupancy_enc(const GemvLaunch& L, bool dual, size_t smem) {
+int occupancy_enc(const GemvLaunch& L, bool dual, int threads, size_t smem) {
     int occ = 0;
     cudaError_t e = cudaErrorInvalidValue;
-#define SPM_NC(n) \
-    case n: e = dual ? configure<ENC, n, true>(&occ, smem) : configure<ENC, n, false>(&occ, smem); break;
+#define SPM_NC(n)                                                                                          \
+    case n:                                                                                                \
+        e = dual ? configure<ENC, n, true>(&occ, threads, smem) : configure<ENC, n, false>(&occ, threads, smem); \
+        break;
     switch (L.n) {
         SPM_NC(1) SPM_NC(2) SPM_NC(3) SPM_NC(4) SPM_NC(5) SPM_NC(6) SPM_NC(7) SPM_NC(8)
         default: break;

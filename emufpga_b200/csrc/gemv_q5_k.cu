@@ -3,7 +3,7 @@
 
 namespace spm {
 namespace gemv {
-template cudaError_t launch_enc<SPM_Q5_K>(const GemvLaunch&, bool, int, size_t, cudaStream_t, bool);
-template int occupancy_enc<SPM_Q5_K>(const GemvLaunch&, bool, size_t);
+template cudaError_t launch_enc<SPM_Q5_K>(const GemvLaunch&, bool, int, int, size_t, cudaStream_t, bool);
+template int occupancy_enc<SPM_Q5_K>(const GemvLaunch&, bool, int, size_t);
 }  // namespace gemv
 }  // namespace spm

@@ -38,8 +38,8 @@ struct GemvLaunch {
     float eps;
     float* sumsq_out;     // EPI_ADD: per-CTA sum of squares of the rows written, [grid][8]
     int32_t* status;      // device error word: a bounded wait that gave up sets it
-    int32_t slots;        // shared-memory ring slots (set by gemv_geometry)
-    int32_t consumers;    // consuming warps (set by gemv_geometry)
+    int32_t slots;        // shared-memory ring slots, a multiple of the groups (set by gemv_geometry)
+    int32_t group_warps;  // warps that share a tile (set by gemv_geometry)
     int32_t c0;           // index of client 0 of this launch in the sum-of-squares arrays
     // Expert mode (plan != nullptr): one job over a [experts][rows][cols]
     // tensor; CTA b works on active expert b / expert_chunks of the plan and
@@ -54,10 +54,11 @@ struct GemvLaunch {
 
 // Grid, ring slots and dynamic shared memory of a streaming GEMV launch.
 struct GemvGeometry {
-    int grid, slots, consumers;
+    int grid, slots, warps, group_warps;
     size_t smem;
 };
-GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms);
+// `per`: tiles per CTA when the caller fixes the grid (expert mode), else 0.
+GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms, int per = 0);
 // `pdl`: launch with programmatic stream serialization (prefetch of the
 // weights overlaps the previous kernel; activations are read after it ends).
 // `grid_out` receives the grid size (= sum-of-squares parts written by EPI_ADD).
