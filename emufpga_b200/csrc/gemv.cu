@@ -30,45 +30,54 @@ static int occupancy(uint32_t dtype, const GemvLaunch& L, bool dual, int threads
     }
 }
 
-// CTA size, warp groups and ring slots.  Two CTAs of 8 warps share an SM
-// when their ring and activations fit in half of its shared memory (the next
-// kernel's CTAs can then start prefetching beside them); otherwise one CTA of
-// 16 warps has the SM to itself.  A group is the fewest warps that give each
-// lane at most four units of a row while every group still gets two ring
-// slots (one being read, one in flight), or as many as it has tiles.  The
-// slots are a multiple of the groups: slot s belongs to group s % G.
+// CTA size, warp groups and ring slots.  Two CTAs of up to 8 warps share an
+// SM when their ring and activations fit in half of its shared memory (the
+// next kernel's CTAs can then start prefetching beside them); otherwise one
+// CTA of up to 16 warps has the SM to itself.  A group of gw warps works on
+// one tile at a time with its lanes over the tile's units; each group owns
+// its ring slots (slot s belongs to group s % G), at least two unless it has
+// a single tile, so that one slot is read while the next is in flight.
+// Among the shapes that fit, the one with the most busy warps per SM wins
+// (a warp counts in proportion to the lanes that have a unit, and only in a
+// group that has a tile), then two CTAs per SM, then smaller groups.
 GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms, int per_fixed) {
-    const size_t slot = size_t(L.tile_bytes) * (dual ? 2 : 1);
     const uint32_t U = L.cols / 32;
+    GemvGeometry best{};
+    double best_score = -1.0;
     for (int per_sm = 2; per_sm >= 1; per_sm--) {
-        const int W = per_sm == 2 ? kPairWarps : kMaxWarps;
+        const int Wmax = per_sm == 2 ? kPairWarps : kMaxWarps;
         const size_t cap = per_sm == 2 ? kHalfSm : kSmemMax;
-        const size_t fixed = smem_bytes(L, dual, 0, W);
-        if (fixed + slot > cap) continue;
-        const int ns_max = int(std::min<size_t>(kMaxSlots, (cap - fixed) / slot));
         int grid = 0, per = per_fixed;
         if (per_fixed <= 0) {
             const uint32_t gcap = uint32_t(sms) * uint32_t(per_sm);
             grid = int(std::min(L.total_tiles, gcap));
             per = int((L.total_tiles + grid - 1) / grid);
         }
-        for (int gw = 1; gw <= W; gw *= 2) {
-            const int G = W / gw;
-            if ((U + 32 * gw - 1) / (32 * gw) > 4 && gw < W) continue;
-            const int pg = (per + G - 1) / G;  // tiles per group
-            const int nsg_max = ns_max / G;
-            if (nsg_max < 1 || nsg_max < std::min(pg, 2)) continue;
-            const int nsg = std::max(1, std::min(nsg_max, pg));
-            return GemvGeometry{grid, G * nsg, W, gw, smem_bytes(L, dual, G * nsg, W)};
+        for (int gw = 1; gw <= Wmax; gw *= 2) {
+            if ((U + 32 * gw - 1) / (32 * gw) > 4 && gw < Wmax) continue;  // at most four units per lane
+            const double busy = std::min(1.0, double(U) / (32.0 * gw));
+            for (int G = Wmax / gw; G >= 1; G--) {
+                const int W = G * gw;
+                if (W < 4) break;
+                const int pg = (per + G - 1) / G;  // tiles per group
+                int nsg = std::min(pg, kMaxSlots / G);
+                while (nsg >= 1 && smem_bytes(L, dual, G * nsg, gw) > cap) nsg--;
+                if (nsg < 1 || nsg < std::min(pg, 2)) continue;
+                const double score = per_sm * std::min(G, per) * gw * busy;  // groups without tiles idle
+                if (score > best_score + 1e-9) {
+                    best_score = score;
+                    best = GemvGeometry{grid, G * nsg, W, gw, smem_bytes(L, dual, G * nsg, gw)};
+                }
+                break;  // fewer groups of this size only score lower
+            }
         }
     }
+    if (best_score >= 0) return best;
     // one CTA per SM, all its warps on each tile, as many slots as fit
-    const int W = kMaxWarps;
-    const size_t fixed = smem_bytes(L, dual, 0, W);
-    const int ns = int(std::max<size_t>(1, std::min<size_t>(kMaxSlots, (kSmemMax - fixed) / slot)));
-    int grid = 0;
-    if (per_fixed <= 0) grid = int(std::min(L.total_tiles, uint32_t(sms)));
-    return GemvGeometry{grid, ns, W, W, smem_bytes(L, dual, ns, W)};
+    int ns = kMaxSlots;
+    while (ns > 1 && smem_bytes(L, dual, ns, kMaxWarps) > kSmemMax) ns--;
+    const int grid = per_fixed > 0 ? 0 : int(std::min(L.total_tiles, uint32_t(sms)));
+    return GemvGeometry{grid, ns, kMaxWarps, kMaxWarps, smem_bytes(L, dual, ns, kMaxWarps)};
 }
 
 // Geometry with the grid capped at the CTAs that can be resident at once

@@ -376,11 +376,13 @@ struct Shape {
     static constexpr int SH = 5 - log2i(V);                                   // lane >> SH = sum index
 };
 
-// Bytes of dynamic shared memory the kernel uses for `slots` ring slots.
-inline size_t smem_bytes(const GemvLaunch& L, bool dual, int slots, int warps) {
+// Bytes of dynamic shared memory the kernel uses: `slots` ring slots, the
+// staged activations and, for groups of several warps, one 32-float record
+// of partial sums per slot, warp of the group and matrix.
+inline size_t smem_bytes(const GemvLaunch& L, bool dual, int slots, int group_warps) {
     const size_t slot = size_t(L.tile_bytes) * (dual ? 2 : 1);
     const size_t xb = size_t(L.n) * (L.cols / 32) * kUnitBytes;
-    const size_t pb = size_t(2) * warps * 32 * (dual ? 2 : 1) * 4;
+    const size_t pb = group_warps > 1 ? size_t(slots) * group_warps * (dual ? 2 : 1) * 128 : 0;
     return slot * size_t(slots) + xb + pb;
 }
 
@@ -390,7 +392,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     constexpr int VR = S::VR, PASSES = S::PASSES, M = S::M, NCP = S::NCP, V = S::V, SH = S::SH;
     constexpr bool kquant = ENC == SPM_Q6_K || ENC == SPM_Q5_K || ENC == SPM_Q2_K;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ uint64_t full[kMaxSlots];
+    __shared__ uint64_t full[kMaxSlots], ready[kMaxSlots];
     __shared__ float nscale[8];
     __shared__ float auxs[kAuxPrefetch];
     __shared__ float sqw[kMaxWarps][8];
@@ -441,7 +443,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     }
     const uint32_t tile_bytes = L.tile_bytes, slot_bytes = tile_bytes * M;
     const uint32_t U = L.cols >> 5, cstride = U * kUnitBytes;
-    const uint32_t xoff = NS * slot_bytes, poff = xoff + NC * cstride;
+    const uint32_t xoff = NS * slot_bytes, poff = xoff + NC * cstride;  // activations, group partials
     auto issue = [&](uint32_t i) {
         const uint32_t s = i % NS, g = t0 + i;
         const GemvJob& J = pick(L, g);
@@ -451,7 +453,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
         if (DUAL) bulk_g2s(smem + size_t(s) * slot_bytes + tile_bytes, J.b + off, tile_bytes, &full[s]);
     };
     if (threadIdx.x == 0) {
-        for (uint32_t s = 0; s < NS; s++) mbar_init(&full[s], 1);
+        for (uint32_t s = 0; s < NS; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&ready[s], uint32_t(gw));
+        }
         mbar_fence_init();
     }
     __syncthreads();
@@ -462,9 +467,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     pdl_wait();  // activations and norm partials come from the previous kernel
 
     // ---- prologue: norm scales, staged activations, residual prefetch ----
-    if (L.gain && warp < NC) {
-        // warp c adds client c's per-CTA sums of squares, 32 lanes in parallel
-        const float* sp = L.sumsq + srows[warp];
+    for (int cw = warp; L.gain && cw < NC; cw += W) {
+        // warp cw adds client cw's per-CTA sums of squares, 32 lanes in parallel
+        const float* sp = L.sumsq + srows[cw];
         float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
         int p = lane;
         for (; p + 96 < L.sumsq_parts; p += 128) {
@@ -475,7 +480,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
         }
         for (; p < L.sumsq_parts; p += 32) a0 += sp[p * 8];
         const float ssum = warp_sum((a0 + a1) + (a2 + a3));
-        if (lane == 0) nscale[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssum, float(L.cols)), L.eps)));
+        if (lane == 0) nscale[cw] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssum, float(L.cols)), L.eps)));
     }
     const uint32_t h16 = L.cols >> 4;
     for (uint32_t idx = threadIdx.x; idx < NC * h16; idx += blockDim.x) {
@@ -523,25 +528,39 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     XIn<NC> X;
 #pragma unroll
     for (int c = 0; c < NC; c++) X.base[c] = smem_s + xoff + c * cstride;
-    // the (row in pass, client) total this thread finishes
-    const int kidx = gw == 1 ? (lane >> SH) : (wig * 32 + lane);
-    const bool finisher = gw == 1 ? (lane & ((1 << SH) - 1)) == 0 : kidx < V;
-    const int fv = kidx / NCP, fc = kidx % NCP;
+    // Totals this thread finishes: with one warp per group, lane l holds
+    // (row-in-pass, client) index l >> SH of each pass; with several, lane l
+    // of the group's first warp holds index l = row * NCP + client of the
+    // tile, all passes together (4 * NCP <= 32).
+    const bool finisher = gw == 1 ? (lane & ((1 << SH) - 1)) == 0 : (wig == 0 && lane < kTileRows * NCP);
+    const int fc = (gw == 1 ? (lane >> SH) : lane) % NCP;
     const float fscale = (L.gain && fc < NC) ? nscale[fc] : 1.0f;
-    float* part = reinterpret_cast<float*>(smem + poff);  // [2][W][M][32]
+    float* part = reinterpret_cast<float*>(smem + poff);  // [NS][gw][M][32]
     float sq = 0.f;
-    uint32_t buf = 0;
     const uint32_t B = L.cols >> 8;
     for (uint32_t i = uint32_t(grp); i < nt; i += uint32_t(G)) {
-        const uint32_t s = i % NS;
-        const bool ok = mbar_wait(&full[s], (i / NS) & 1);
-        if (!ok) flag(L.status, 2);
-        if (gw == 1 && !ok) break;  // (groups decide together at their barrier)
+        const uint32_t s = i % NS, par = (i / NS) & 1;
+        if (!mbar_wait(&full[s], par)) {
+            flag(L.status, 2);
+            break;
+        }
         const uint32_t g = t0 + i;
         const GemvJob& J = pick(L, g);
         const uint32_t tile = g - J.tile_begin;
         const uint32_t tb = smem_s + s * slot_bytes;
-        bool abort = false;
+        // row e of the tile, client fc: scale, activation, residual, store
+        auto finish = [&](uint32_t e, float a, float b) {
+            const uint32_t grow = tile * kTileRows + e;
+            const uint32_t row = grow - rbase;
+            if (fc < n_act && grow < J.rows && row < rlim) {
+                float r = a * fscale;
+                if constexpr (DUAL) r = silu_mul(r, b * fscale);
+                if (J.epi == EPI_ADD)
+                    r = (aux_pre ? auxs[(i * kTileRows + e) * NC + fc] : J.aux[size_t(yrows[fc]) * J.aux_stride + row]) + r;
+                J.y[size_t(yrows[fc]) * J.y_stride + row] = r;
+                sq = fmaf(r, r, sq);
+            }
+        };
 #pragma unroll 1
         for (int pass = 0; pass < PASSES; pass++) {
             RowRef rr[M * VR];
@@ -557,8 +576,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
 #pragma unroll 1
             for (uint32_t u = uint32_t(wig * 32 + lane); u < U; u += uint32_t(gw * 32))
                 unit_dot<ENC, NC, M * VR>(rr, u, L, X, acc);
-            const bool last = pass + 1 == PASSES;
-            if (gw == 1 && last) {
+            if (gw == 1 && pass + 1 == PASSES) {
                 // this warp alone read the slot: refill it
                 __syncwarp();
                 if (lane == 0 && i + NS < nt) {
@@ -575,43 +593,38 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
                     for (int c = 0; c < NCP; c++) red[m][v * NCP + c] = c < NC ? acc[m * VR + v][c] : 0.f;
 #pragma unroll
             for (int m = 0; m < M; m++) XRed<V, 16>::run(red[m], lane);
-            float a = red[0][0], b = M > 1 ? red[M - 1][0] : 0.f;
-            if (gw > 1) {
-                if ((lane & ((1 << SH) - 1)) == 0)
+            if (gw == 1) {
+                if (finisher) finish(uint32_t(pass * VR + (lane >> SH) / NCP), red[0][0], red[M - 1][0]);
+            } else if ((lane & ((1 << SH) - 1)) == 0) {
 #pragma unroll
-                    for (int m = 0; m < M; m++) part[((buf * W + warp) * M + m) * 32 + (lane >> SH)] = red[m][0];
-                abort = bar_or(1 + grp, gw * 32, !ok);
-                if (abort) break;
-                if (last && wig == 0 && lane == 0 && i + NS < nt) {
-                    // every warp of the group is past its reads of the slot
+                for (int m = 0; m < M; m++) part[((s * gw + wig) * M + m) * 32 + pass * V + (lane >> SH)] = red[m][0];
+            }
+        }
+        if (gw > 1) {
+            // partials are in; the group's first warp adds them in warp order
+            // once every warp has arrived, then refills the slot
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&ready[s]);
+            if (wig == 0) {
+                if (!mbar_wait(&ready[s], par)) {
+                    flag(L.status, 4);
+                    break;
+                }
+                if (finisher) {
+                    float a = 0.f, b = 0.f;
+                    for (int w = 0; w < gw; w++) {
+                        a += part[((s * gw + w) * M + 0) * 32 + lane];
+                        if (M > 1) b += part[((s * gw + w) * M + M - 1) * 32 + lane];
+                    }
+                    finish(uint32_t(lane / NCP), a, b);
+                }
+                __syncwarp();
+                if (lane == 0 && i + NS < nt) {
                     fence_proxy_async();
                     issue(i + NS);
                 }
-                if (finisher) {
-                    a = 0.f;
-                    b = 0.f;
-                    for (int w = 0; w < gw; w++) {
-                        a += part[((buf * W + grp * gw + w) * M + 0) * 32 + kidx];
-                        if (M > 1) b += part[((buf * W + grp * gw + w) * M + M - 1) * 32 + kidx];
-                    }
-                }
-                buf ^= 1;
-            }
-            if (finisher) {
-                const uint32_t e = uint32_t(pass * VR + fv);
-                const uint32_t grow = tile * kTileRows + e;
-                const uint32_t row = grow - rbase;
-                if (fc < n_act && grow < J.rows && row < rlim) {
-                    float r = a * fscale;
-                    if constexpr (DUAL) r = silu_mul(r, b * fscale);
-                    if (J.epi == EPI_ADD)
-                        r = (aux_pre ? auxs[(i * kTileRows + e) * NC + fc] : J.aux[size_t(yrows[fc]) * J.aux_stride + row]) + r;
-                    J.y[size_t(yrows[fc]) * J.y_stride + row] = r;
-                    sq = fmaf(r, r, sq);
-                }
             }
         }
-        if (abort) break;
     }
     if (L.sumsq_out) {
         // per-CTA sum of squares of the rows written, reduced in a fixed order
