@@ -45,6 +45,19 @@ __device__ __forceinline__ float bytef(uint32_t w) {
     return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | B));
 }
 
+// Four-way byte dot products accumulated in int32: a's bytes signed (ss) or
+// unsigned (us) times b's signed bytes, plus c.
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -119,6 +119,7 @@ cudaError_t launch_gemv(uint32_t dtype, GemvLaunch L, int sms, cudaStream_t s, b
     if (grid_out) *grid_out = 0;
     if (L.total_tiles == 0) return cudaSuccess;
     if (L.n < 1 || L.n > 8 || (L.cols & 31)) return cudaErrorInvalidValue;
+    L.xrec = unit_bytes(int(dtype));
     GemvLaunch one = L;
     one.n = 1;
     if (smem_bytes(one, dual, 1, kMaxWarps) > kSmemMax) return cudaErrorInvalidValue;

@@ -11,20 +11,20 @@
 // Short rows (SmolLM2: 18 units) take one warp per tile; long rows spread a
 // tile over several warps so that every lane has one to four units.
 //
-// Per unit a lane turns four codes at a time into floats with one byte
-// permute each and applies them to all clients' activations (staged once per
-// CTA in shared memory) while they sit in registers -- the reference's "one
-// weight, every position" schedule (spm-linear/src/resident.rs:120-137).
-// The K-quant codes q (< 128) become f = 1 + q/128 exactly (q in the
-// mantissa of 1.0), so that per 16- or 32-value sub-block
-//     sum_c q_c x_c = 128 * sum_c f_c x_c - 128 * sum_c x_c
-// with the activation sums precomputed when x is staged; Q8_0 codes become
-// 2^23 + (q ^ 128) and are re-centred exactly.  Block scales are applied once
-// per sub-block:
-//     sum_c w_c x_c = (d*sc) * sum_c q_c x_c  [- (dmin*m) * sum_c x_c]
-// which is the reference dot product regrouped.  The weights are the
-// reference's bit for bit (the dequant kernel checks that); the fp32 sums are
-// in a different order than the reference's FMA chain.
+// Per unit a lane unpacks the rows' codes into bytes (four per word) and
+// applies them to every client's staged activations.  The activations are
+// staged once per CTA in shared memory as 22-bit fixed point per 32-value
+// unit (a power-of-two scale and three planes of 8-bit digits), so that four
+// codes times four activations are three dp4a, exact in int32 -- the
+// reference's "one weight, every position" schedule
+// (spm-linear/src/resident.rs:120-137) with the multiply-adds in integer
+// units.  Block scales are applied once per sub-block in fp32:
+//     sum_c w_c x_c = (d*sc) * s * sum_c q_c m_c  [- (dmin*m or 32 d*sc) * sum_c x_c]
+// which is the reference dot product regrouped, with x_c = s * m_c rounded
+// to 22 bits below the unit's largest |x| (2^-23 of it at most).  The
+// weights are the reference's bit for bit (the dequant kernel checks that);
+// the sums are in a different order than the reference's fp32 FMA chain.
+// F32 matrices (the MoE router) keep fp32 activations and FMAs.
 //
 // A lane's partial sums for the pass's rows and clients are reduced across
 // the warp by a transposing butterfly (each exchange halves the values a lane
@@ -41,6 +41,8 @@
 // previous kernel still runs (weights never depend on it), and the
 // activations are read only after griddepcontrol.wait.
 #pragma once
+#include <type_traits>
+
 #include "device.cuh"
 #include "moe.h"
 
@@ -54,27 +56,54 @@ constexpr int kMaxSlots = 16;
 constexpr size_t kSmemMax = 200 * 1024;   // dynamic shared memory of a CTA alone on its SM
 constexpr size_t kHalfSm = 100 * 1024;    // dynamic shared memory of each of two CTAs per SM
 constexpr int kAuxPrefetch = 1024;        // residual values prefetched per CTA, at most
-// Staged activations: per client, one 144-byte record per 32-value unit --
-// 128 bytes of values, the two 16-value sums, 8 bytes of padding.  The
-// padding puts the records of consecutive units 4 banks apart, so the lanes
-// of a quarter-warp reading the same chunk of consecutive units never share
-// a bank.
-constexpr uint32_t kUnitBytes = 144;
+// Staged activations of the integer block types: per client one 112-byte
+// record per 32-value unit -- three planes of 32 signed 8-bit digits (8 words
+// each), then the unit's scale s and the two 16-value sums of the staged
+// values.  The unit's values x are held as m * s, m = rint(x / s) with
+// s = 2^(e-22) and max|x| < 2^e, so |m| <= 2^22 and m = d0 + 256 d1 + 65536 d2
+// with every digit in [-128, 127]: 22 significant bits against the unit's
+// largest value.  A code word (four codes as bytes) times a digit word is one
+// dp4a, exact in int32, so sum_c q_c m_c needs three dp4a per four codes and
+// one conversion to float per (sub-)block.  F32 weights keep 144-byte records
+// of the values themselves (128 bytes, two sums, padding).  Both strides put
+// the records of consecutive units 4 banks apart, so the lanes of a
+// quarter-warp reading the same part of consecutive units share no bank.
+constexpr uint32_t kDigitUnit = 112;
+constexpr uint32_t kFloatUnit = 144;
+inline __host__ __device__ constexpr uint32_t unit_bytes(int enc) { return enc == SPM_F32 ? kFloatUnit : kDigitUnit; }
+
+struct XUnit {
+    uint32_t d[3][8];  // digit planes, word k = values 4k..4k+3
+    float s, sum0, sum1;
+};
+
+template <int NC>
+struct XDig {
+    uint32_t base[NC];  // shared address of client c's records
+    __device__ __forceinline__ void unit(uint32_t u, int c, XUnit& o) const {
+        const uint32_t a = base[c] + u * kDigitUnit;
+#pragma unroll
+        for (int j = 0; j < 3; j++) {
+            const uint4 v0 = lds128(a + j * 32), v1 = lds128(a + j * 32 + 16);
+            o.d[j][0] = v0.x, o.d[j][1] = v0.y, o.d[j][2] = v0.z, o.d[j][3] = v0.w;
+            o.d[j][4] = v1.x, o.d[j][5] = v1.y, o.d[j][6] = v1.z, o.d[j][7] = v1.w;
+        }
+        const uint4 t = lds128(a + 96);
+        o.s = __uint_as_float(t.x);
+        o.sum0 = __uint_as_float(t.y);
+        o.sum1 = __uint_as_float(t.z);
+    }
+};
 
 template <int NC>
 struct XIn {
-    uint32_t base[NC];  // shared address of client c's records
+    uint32_t base[NC];  // shared address of client c's float records
     __device__ __forceinline__ void load(uint32_t u, int off, float4 (&o)[NC]) const {
 #pragma unroll
         for (int c = 0; c < NC; c++) {
-            const uint4 v = lds128(base[c] + u * kUnitBytes + off * 4);
+            const uint4 v = lds128(base[c] + u * kFloatUnit + off * 4);
             o[c] = make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
         }
-    }
-    // sum of the 16 values starting at 32*u + 16*half, per client
-    __device__ __forceinline__ void sums(uint32_t u, int half, float (&o)[NC]) const {
-#pragma unroll
-        for (int c = 0; c < NC; c++) o[c] = __uint_as_float(lds32(base[c] + u * kUnitBytes + 128 + half * 4));
     }
 };
 
@@ -93,11 +122,6 @@ __device__ __forceinline__ uint32_t word(const uint4& v, int t) {
     return t == 0 ? v.x : t == 1 ? v.y : t == 2 ? v.z : v.w;
 }
 
-// 1 + (byte B of q & 127)/128 exactly, for q bytes with bit 7 set.
-template <int B>
-__device__ __forceinline__ float onef(uint32_t q) {
-    return __uint_as_float(__byte_perm(q, 0x3F000000u, 0x7044u | (B << 8)));
-}
 // int8 -> float exactly: 2^23 + (b ^ 128) - (2^23 + 128).
 __device__ __forceinline__ float i8f(uint32_t b) { return bytef<0>(b ^ 0x80u) - 8388736.0f; }
 
@@ -109,6 +133,19 @@ __device__ __forceinline__ void zero(float (&s)[R][NC]) {
         for (int c = 0; c < NC; c++) s[v][c] = 0.f;
 }
 
+// Digit sums of four codes (the bytes of q; signed for Q8_0, unsigned for
+// the K-quants) times staged word k.
+template <bool SIGNED>
+__device__ __forceinline__ void dot_digits(uint32_t q, const XUnit& x, int k, int (&S)[3]) {
+#pragma unroll
+    for (int j = 0; j < 3; j++) S[j] = SIGNED ? dp4a_ss(q, x.d[j][k], S[j]) : dp4a_us(q, x.d[j][k], S[j]);
+}
+// sum_c q_c m_c from the digit sums (float; the low two planes combined
+// exactly in int32 first).
+__device__ __forceinline__ float digits_total(const int (&S)[3]) {
+    return fmaf(__int2float_rn(S[2]), 65536.0f, __int2float_rn(S[1] * 256 + S[0]));
+}
+
 // One row of a pass: shared address of its tile, and its row index r inside
 // the tile as r * units and r * super-blocks.
 struct RowRef {
@@ -116,11 +153,12 @@ struct RowRef {
 };
 
 // Every unit function adds unit u of the rows R times the activations into
-// acc[row][client].
+// acc[row][client]: the rows' codes are unpacked once, then each client's
+// record is read and applied to every row.
 
 // ------------------------------------------------------------------ Q8_0 --
 template <int NC, int R>
-__device__ __forceinline__ void unit_q8_0(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XIn<NC>& X,
+__device__ __forceinline__ void unit_q8_0(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XDig<NC>& X,
                                           float (&acc)[R][NC]) {
     uint4 q0[R], q1[R];
     float d[R];
@@ -131,65 +169,61 @@ __device__ __forceinline__ void unit_q8_0(const RowRef (&rr)[R], uint32_t u, con
         q1[v] = lds128(rr[v].t + unit * 32 + 16);
         d[v] = h2f(lds16(rr[v].t + L.plane1 + unit * 2));
     }
-    float s[R][NC];
-    zero(s);
 #pragma unroll
-    for (int k = 0; k < 8; k++) {
-        float4 x[NC];
-        X.load(u, 4 * k, x);
+    for (int c = 0; c < NC; c++) {
+        XUnit xu;
+        X.unit(u, c, xu);
 #pragma unroll
         for (int v = 0; v < R; v++) {
-            const uint32_t w = (k < 4 ? word(q0[v], k) : word(q1[v], k - 4)) ^ 0x80808080u;
-            const float c0 = 8388736.0f;  // 2^23 + 128: (u8 ^ 0x80) - 128 == int8
-            dot4<NC>(s[v], bytef<0>(w) - c0, bytef<1>(w) - c0, bytef<2>(w) - c0, bytef<3>(w) - c0, x);
+            int S[3] = {0, 0, 0};
+#pragma unroll
+            for (int k = 0; k < 8; k++) dot_digits<true>(k < 4 ? word(q0[v], k) : word(q1[v], k - 4), xu, k, S);
+            // sum w x = d * s * sum q m
+            acc[v][c] = fmaf(d[v] * xu.s, digits_total(S), acc[v][c]);
         }
     }
-#pragma unroll
-    for (int v = 0; v < R; v++)
-#pragma unroll
-        for (int c = 0; c < NC; c++) acc[v][c] = fmaf(d[v], s[v][c], acc[v][c]);
 }
 
 // ------------------------------------------------------------------ Q6_K --
 template <int NC, int R>
-__device__ __forceinline__ void unit_q6_k(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XIn<NC>& X,
+__device__ __forceinline__ void unit_q6_k(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XDig<NC>& X,
                                           float (&acc)[R][NC]) {
-    uint4 ql[R];
-    uint2 qh[R];
+    uint32_t q[R][8];  // 6-bit codes as bytes; word 4*run + k = values 16*run + 4k ..
     float ds[R][2];
 #pragma unroll
     for (int v = 0; v < R; v++) {
         const uint32_t unit = rr[v].ru + u;
-        ql[v] = lds128(rr[v].t + unit * 16);
-        qh[v] = lds64(rr[v].t + L.plane1 + unit * 8);
+        const uint4 ql = lds128(rr[v].t + unit * 16);
+        const uint2 qh = lds64(rr[v].t + L.plane1 + unit * 8);
         const uint32_t sc = lds16(rr[v].t + L.plane2 + unit * 2);
         const float d = h2f(lds16(rr[v].t + L.plane3 + (rr[v].rb + (u >> 3)) * 2));
         ds[v][0] = d * i8f(sc & 0xffu);
         ds[v][1] = d * i8f(sc >> 8);
+#pragma unroll
+        for (int run = 0; run < 2; run++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const uint32_t w = word(ql, k);
+                const uint32_t h = run ? qh.y : qh.x;
+                const uint32_t hs = (k < 2 ? h << (4 - 2 * k) : h >> (2 * k - 4)) & 0x30303030u;
+                q[v][4 * run + k] = ((run ? (w >> 4) : w) & 0x0F0F0F0Fu) | hs;
+            }
     }
 #pragma unroll
-    for (int run = 0; run < 2; run++) {
-        float s[R][NC], xs[NC];
-        zero(s);
-        X.sums(u, run, xs);
-#pragma unroll
-        for (int k = 0; k < 4; k++) {
-            float4 x[NC];
-            X.load(u, 16 * run + 4 * k, x);
-#pragma unroll
-            for (int v = 0; v < R; v++) {
-                const uint32_t w = word(ql[v], k);
-                const uint32_t h = run ? qh[v].y : qh[v].x;
-                const uint32_t hs = ((k < 2 ? h << (4 - 2 * k) : h >> (2 * k - 4)) & 0x30303030u) | 0x80808080u;
-                const uint32_t q = ((run ? (w >> 4) : w) & 0x0F0F0F0Fu) | hs;
-                dot4<NC>(s[v], onef<0>(q), onef<1>(q), onef<2>(q), onef<3>(q), x);
-            }
-        }
-        // sum (q - 32) x = 128 sum f x - 160 sum x
+    for (int c = 0; c < NC; c++) {
+        XUnit xu;
+        X.unit(u, c, xu);
+        const float o0 = -32.0f * xu.sum0, o1 = -32.0f * xu.sum1;
 #pragma unroll
         for (int v = 0; v < R; v++)
 #pragma unroll
-            for (int c = 0; c < NC; c++) acc[v][c] = fmaf(ds[v][run], fmaf(s[v][c], 128.0f, -160.0f * xs[c]), acc[v][c]);
+            for (int run = 0; run < 2; run++) {
+                int S[3] = {0, 0, 0};
+#pragma unroll
+                for (int k = 0; k < 4; k++) dot_digits<false>(q[v][4 * run + k], xu, 4 * run + k, S);
+                // sum (q - 32) x = s * sum q m - 32 * sum x
+                acc[v][c] = fmaf(ds[v][run], fmaf(digits_total(S), xu.s, run ? o1 : o0), acc[v][c]);
+            }
     }
 }
 
@@ -200,18 +234,17 @@ __device__ __forceinline__ uint32_t sbyte(const uint4& m, int k) {  // scales by
 }
 
 template <int NC, int R>
-__device__ __forceinline__ void unit_q5_k(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XIn<NC>& X,
+__device__ __forceinline__ void unit_q5_k(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XDig<NC>& X,
                                           float (&acc)[R][NC]) {
     const int j = int(u & 7);
-    uint4 qs[R];
-    uint32_t qh[R];
+    uint32_t q[R][8];  // 5-bit codes as bytes
     float ds[R], dm[R];
 #pragma unroll
     for (int v = 0; v < R; v++) {
         const uint32_t unit = rr[v].ru + u;
         const uint4 m = lds128(rr[v].t + (rr[v].rb + (u >> 3)) * 16);
-        qs[v] = lds128(rr[v].t + L.plane1 + unit * 16);
-        qh[v] = lds32(rr[v].t + L.plane2 + unit * 4);
+        const uint4 qs = lds128(rr[v].t + L.plane1 + unit * 16);
+        const uint32_t qh = lds32(rr[v].t + L.plane2 + unit * 4);
         uint32_t sc, mn;
         if (j < 4) {
             sc = sbyte(m, j) & 63;
@@ -222,77 +255,66 @@ __device__ __forceinline__ void unit_q5_k(const RowRef (&rr)[R], uint32_t u, con
         }
         ds[v] = h2f(m.x) * (bytef<0>(sc) - 8388608.0f);
         dm[v] = h2f(m.x >> 16) * (bytef<0>(mn) - 8388608.0f);
-    }
-    float s[R][NC], xa[NC], xb[NC];
-    zero(s);
-    X.sums(u, 0, xa);
-    X.sums(u, 1, xb);
 #pragma unroll
-    for (int run = 0; run < 2; run++) {
+        for (int run = 0; run < 2; run++)
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            float4 x[NC];
-            X.load(u, 16 * run + 4 * k, x);
-#pragma unroll
-            for (int v = 0; v < R; v++) {
-                const uint32_t w = word(qs[v], k);
-                const uint32_t sp =
-                    (((((qh[v] >> (16 * run + 4 * k)) & 0xfu) * 0x02040810u) & 0x10101010u)) | 0x80808080u;
-                const uint32_t q = ((run ? (w >> 4) : w) & 0x0F0F0F0Fu) | sp;
-                dot4<NC>(s[v], onef<0>(q), onef<1>(q), onef<2>(q), onef<3>(q), x);
+            for (int k = 0; k < 4; k++) {
+                const uint32_t w = word(qs, k);
+                const uint32_t sp = (((qh >> (16 * run + 4 * k)) & 0xfu) * 0x02040810u) & 0x10101010u;
+                q[v][4 * run + k] = ((run ? (w >> 4) : w) & 0x0F0F0F0Fu) | sp;
             }
+    }
+#pragma unroll
+    for (int c = 0; c < NC; c++) {
+        XUnit xu;
+        X.unit(u, c, xu);
+        const float xsum = xu.sum0 + xu.sum1;
+#pragma unroll
+        for (int v = 0; v < R; v++) {
+            int S[3] = {0, 0, 0};
+#pragma unroll
+            for (int k = 0; k < 8; k++) dot_digits<false>(q[v][k], xu, k, S);
+            // sum w x = ds * s * sum q m - dm * sum x
+            acc[v][c] = fmaf(-dm[v], xsum, fmaf(ds[v], digits_total(S) * xu.s, acc[v][c]));
         }
     }
-    // sum w x = ds * (128 sum f x - 128 sum x) - dm * sum x
-#pragma unroll
-    for (int v = 0; v < R; v++)
-#pragma unroll
-        for (int c = 0; c < NC; c++) {
-            const float xsum = xa[c] + xb[c];
-            acc[v][c] = fmaf(-dm[v], xsum, fmaf(ds[v], fmaf(s[v][c], 128.0f, -128.0f * xsum), acc[v][c]));
-        }
 }
 
 // ------------------------------------------------------------------ Q2_K --
 template <int NC, int R>
-__device__ __forceinline__ void unit_q2_k(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XIn<NC>& X,
+__device__ __forceinline__ void unit_q2_k(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XDig<NC>& X,
                                           float (&acc)[R][NC]) {
     uint2 qs[R];
-    uint32_t sc[R];
-    float d[R], dmin[R];
+    float dl[R][2], ml[R][2];
 #pragma unroll
     for (int v = 0; v < R; v++) {
         const uint32_t unit = rr[v].ru + u;
         qs[v] = lds64(rr[v].t + unit * 8);
-        sc[v] = lds16(rr[v].t + L.plane1 + unit * 2);
+        const uint32_t sc = lds16(rr[v].t + L.plane1 + unit * 2);
         const uint32_t dd = lds32(rr[v].t + L.plane2 + (rr[v].rb + (u >> 3)) * 4);
-        d[v] = h2f(dd);
-        dmin[v] = h2f(dd >> 16);
+        const float d = h2f(dd), dmin = h2f(dd >> 16);
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t b = (sc >> (8 * h)) & 0xffu;
+            dl[v][h] = d * (bytef<0>(b & 15u) - 8388608.0f);
+            ml[v][h] = dmin * (bytef<0>(b >> 4) - 8388608.0f);
+        }
     }
 #pragma unroll
-    for (int h = 0; h < 2; h++) {
-        float s[R][NC], xs[NC];
-        zero(s);
-        X.sums(u, h, xs);
+    for (int c = 0; c < NC; c++) {
+        XUnit xu;
+        X.unit(u, c, xu);
 #pragma unroll
-        for (int k = 0; k < 4; k++) {
-            float4 x[NC];
-            X.load(u, 16 * h + 4 * k, x);
+        for (int v = 0; v < R; v++)
 #pragma unroll
-            for (int v = 0; v < R; v++) {
-                const uint32_t q = (((h ? qs[v].y : qs[v].x) >> (2 * k)) & 0x03030303u) | 0x80808080u;
-                dot4<NC>(s[v], onef<0>(q), onef<1>(q), onef<2>(q), onef<3>(q), x);
+            for (int h = 0; h < 2; h++) {
+                int S[3] = {0, 0, 0};
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    dot_digits<false>(((h ? qs[v].y : qs[v].x) >> (2 * k)) & 0x03030303u, xu, 4 * h + k, S);
+                // sum w x = dl * s * sum q m - ml * sum x
+                acc[v][c] = fmaf(-ml[v][h], h ? xu.sum1 : xu.sum0, fmaf(dl[v][h], digits_total(S) * xu.s, acc[v][c]));
             }
-        }
-#pragma unroll
-        for (int v = 0; v < R; v++) {
-            const uint32_t b = (sc[v] >> (8 * h)) & 0xffu;
-            const float dl = d[v] * (bytef<0>(b & 15u) - 8388608.0f);
-            const float ml = dmin[v] * (bytef<0>(b >> 4) - 8388608.0f);
-#pragma unroll
-            for (int c = 0; c < NC; c++)
-                acc[v][c] = fmaf(-ml, xs[c], fmaf(dl, fmaf(s[v][c], 128.0f, -128.0f * xs[c]), acc[v][c]));
-        }
     }
 }
 
@@ -313,8 +335,8 @@ __device__ __forceinline__ void unit_f32(const RowRef (&rr)[R], uint32_t u, cons
     }
 }
 
-template <int ENC, int NC, int R>
-__device__ __forceinline__ void unit_dot(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XIn<NC>& X,
+template <int ENC, int NC, int R, class XT>
+__device__ __forceinline__ void unit_dot(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XT& X,
                                          float (&acc)[R][NC]) {
     if constexpr (ENC == SPM_Q8_0) unit_q8_0<NC, R>(rr, u, L, X, acc);
     else if constexpr (ENC == SPM_Q6_K) unit_q6_k<NC, R>(rr, u, L, X, acc);
@@ -381,7 +403,7 @@ struct Shape {
 // of partial sums per slot, warp of the group and matrix.
 inline size_t smem_bytes(const GemvLaunch& L, bool dual, int slots, int group_warps) {
     const size_t slot = size_t(L.tile_bytes) * (dual ? 2 : 1);
-    const size_t xb = size_t(L.n) * (L.cols / 32) * kUnitBytes;
+    const size_t xb = size_t(L.n) * (L.cols / 32) * L.xrec;
     const size_t pb = group_warps > 1 ? size_t(slots) * group_warps * (dual ? 2 : 1) * 128 : 0;
     return slot * size_t(slots) + xb + pb;
 }
@@ -390,7 +412,6 @@ template <int ENC, int NC, bool DUAL>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_constant__ GemvLaunch L) {
     using S = Shape<NC, DUAL>;
     constexpr int VR = S::VR, PASSES = S::PASSES, M = S::M, NCP = S::NCP, V = S::V, SH = S::SH;
-    constexpr bool kquant = ENC == SPM_Q6_K || ENC == SPM_Q5_K || ENC == SPM_Q2_K;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[kMaxSlots], ready[kMaxSlots];
     __shared__ float nscale[8];
@@ -442,7 +463,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
         return;
     }
     const uint32_t tile_bytes = L.tile_bytes, slot_bytes = tile_bytes * M;
-    const uint32_t U = L.cols >> 5, cstride = U * kUnitBytes;
+    constexpr uint32_t XREC = unit_bytes(ENC);
+    const uint32_t U = L.cols >> 5, cstride = U * XREC;
     const uint32_t xoff = NS * slot_bytes, poff = xoff + NC * cstride;  // activations, group partials
     auto issue = [&](uint32_t i) {
         const uint32_t s = i % NS, g = t0 + i;
@@ -482,34 +504,90 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
         const float ssum = warp_sum((a0 + a1) + (a2 + a3));
         if (lane == 0) nscale[cw] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssum, float(L.cols)), L.eps)));
     }
-    const uint32_t h16 = L.cols >> 4;
-    for (uint32_t idx = threadIdx.x; idx < NC * h16; idx += blockDim.x) {
-        const uint32_t c = idx / h16, h = idx % h16, col = h * 16;
-        float4 v[4];
-        if (int(c) < n_act) {
-            const float* xp = L.x + size_t(xrows[c]) * L.x_stride + col;
+    if constexpr (ENC == SPM_F32) {
+        // float records: 16 values per thread
+        const uint32_t h16 = L.cols >> 4;
+        for (uint32_t idx = threadIdx.x; idx < NC * h16; idx += blockDim.x) {
+            const uint32_t c = idx / h16, h = idx % h16, col = h * 16;
+            float4 v[4];
+            if (int(c) < n_act) {
+                const float* xp = L.x + size_t(xrows[c]) * L.x_stride + col;
 #pragma unroll
-            for (int k = 0; k < 4; k++) v[k] = ldx4(xp + 4 * k);
-        } else {
+                for (int k = 0; k < 4; k++) v[k] = ldx4(xp + 4 * k);
+            } else {
 #pragma unroll
-            for (int k = 0; k < 4; k++) v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-        if (L.gain) {
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const float4 g = ldx4(L.gain + col + 4 * k);
-                v[k] = make_float4(__fmul_rn(v[k].x, g.x), __fmul_rn(v[k].y, g.y), __fmul_rn(v[k].z, g.z),
-                                   __fmul_rn(v[k].w, g.w));
+                for (int k = 0; k < 4; k++) v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
+            if (L.gain) {
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const float4 g = ldx4(L.gain + col + 4 * k);
+                    v[k] = make_float4(__fmul_rn(v[k].x, g.x), __fmul_rn(v[k].y, g.y), __fmul_rn(v[k].z, g.z),
+                                       __fmul_rn(v[k].w, g.w));
+                }
+            }
+            uint8_t* rec = smem + xoff + c * cstride + (h >> 1) * XREC;
+#pragma unroll
+            for (int k = 0; k < 4; k++) reinterpret_cast<float4*>(rec + (h & 1) * 64)[k] = v[k];
         }
-        uint8_t* rec = smem + xoff + c * cstride + (h >> 1) * kUnitBytes;
+    } else {
+        // digit records: each pair of lanes holds one unit, 16 values each,
+        // and agrees on the unit's exponent through a shuffle (whole warps
+        // step through the loop together so that every lane shuffles)
+        const uint32_t total = NC * U * 2;
+        for (uint32_t w0 = uint32_t(warp) * 32; w0 < total; w0 += blockDim.x) {
+            const uint32_t idx = w0 + uint32_t(lane);
+            const bool live = idx < total;
+            const uint32_t c = live ? idx / (2 * U) : 0, u = (idx % (2 * U)) >> 1, half = idx & 1;
+            const uint32_t col = u * 32 + half * 16;
+            float v[16];
 #pragma unroll
-        for (int k = 0; k < 4; k++) reinterpret_cast<float4*>(rec + (h & 1) * 64)[k] = v[k];
-        if constexpr (kquant) {
-            float sum = 0.f;
+            for (int k = 0; k < 16; k++) v[k] = 0.f;
+            if (live && int(c) < n_act) {
+                const float* xp = L.x + size_t(xrows[c]) * L.x_stride + col;
 #pragma unroll
-            for (int k = 0; k < 4; k++) sum += (v[k].x + v[k].y) + (v[k].z + v[k].w);
-            reinterpret_cast<float*>(rec + 128)[h & 1] = sum;
+                for (int k = 0; k < 4; k++) {
+                    const float4 t = ldx4(xp + 4 * k);
+                    v[4 * k] = t.x, v[4 * k + 1] = t.y, v[4 * k + 2] = t.z, v[4 * k + 3] = t.w;
+                }
+                if (L.gain)
+#pragma unroll
+                    for (int k = 0; k < 4; k++) {
+                        const float4 g = ldx4(L.gain + col + 4 * k);
+                        v[4 * k] = __fmul_rn(v[4 * k], g.x), v[4 * k + 1] = __fmul_rn(v[4 * k + 1], g.y);
+                        v[4 * k + 2] = __fmul_rn(v[4 * k + 2], g.z), v[4 * k + 3] = __fmul_rn(v[4 * k + 3], g.w);
+                    }
+            }
+            float mx = 0.f;
+#pragma unroll
+            for (int k = 0; k < 16; k++) mx = fmaxf(mx, fabsf(v[k]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            // e with mx < 2^e (at least -100, so that 2^(22-e) and 2^(e-22) are normal floats)
+            const int e = max(int((__float_as_uint(mx) >> 23) & 0xffu) - 126, -100);
+            const float up = __uint_as_float(uint32_t(149 - e) << 23), sc = __uint_as_float(uint32_t(105 + e) << 23);
+            uint32_t dw[3][4] = {};
+            int msum = 0;
+#pragma unroll
+            for (int k = 0; k < 16; k++) {
+                const int m = __float2int_rn(v[k] * up);
+                const int d0 = ((m + 128) & 255) - 128, r = (m - d0) >> 8;
+                const int d1 = ((r + 128) & 255) - 128, d2 = (r - d1) >> 8;
+                dw[0][k >> 2] |= uint32_t(d0 & 255) << (8 * (k & 3));
+                dw[1][k >> 2] |= uint32_t(d1 & 255) << (8 * (k & 3));
+                dw[2][k >> 2] |= uint32_t(d2 & 255) << (8 * (k & 3));
+                msum += m;
+            }
+            const float hsum = __int2float_rn(msum) * sc;
+            const float other = __shfl_xor_sync(0xffffffffu, hsum, 1);
+            if (live) {
+                uint8_t* rec = smem + xoff + c * cstride + u * XREC;
+#pragma unroll
+                for (int j = 0; j < 3; j++)
+                    *reinterpret_cast<uint4*>(rec + j * 32 + half * 16) = make_uint4(dw[j][0], dw[j][1], dw[j][2], dw[j][3]);
+                if (half == 0)
+                    *reinterpret_cast<uint4*>(rec + 96) =
+                        make_uint4(__float_as_uint(sc), __float_as_uint(hsum), __float_as_uint(other), 0u);
+            }
         }
     }
     // the residual rows this CTA will add to (EPI_ADD)
@@ -525,7 +603,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
 
     // ---- main loop ----
     const uint32_t smem_s = saddr(smem);
-    XIn<NC> X;
+    using XT = std::conditional_t<ENC == SPM_F32, XIn<NC>, XDig<NC>>;
+    XT X;
 #pragma unroll
     for (int c = 0; c < NC; c++) X.base[c] = smem_s + xoff + c * cstride;
     // Totals this thread finishes: with one warp per group, lane l holds
@@ -575,7 +654,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
             zero(acc);
 #pragma unroll 1
             for (uint32_t u = uint32_t(wig * 32 + lane); u < U; u += uint32_t(gw * 32))
-                unit_dot<ENC, NC, M * VR>(rr, u, L, X, acc);
+                unit_dot<ENC, NC, M * VR, XT>(rr, u, L, X, acc);
             if (gw == 1 && pass + 1 == PASSES) {
                 // this warp alone read the slot: refill it
                 __syncwarp();
