@@ -347,11 +347,12 @@ __device__ __forceinline__ void unit_dot(const RowRef (&rr)[R], uint32_t u, cons
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return __fdiv_rn(g, 1.0f + expf(-g)) * u; }
 
-__device__ __forceinline__ const GemvJob& pick(const GemvLaunch& L, uint32_t g) {
-    if (L.njobs > 3 && g >= L.job[3].tile_begin) return L.job[3];
-    if (L.njobs > 2 && g >= L.job[2].tile_begin) return L.job[2];
-    if (L.njobs > 1 && g >= L.job[1].tile_begin) return L.job[1];
-    return L.job[0];
+// The job of global tile g, from the CTA's shared copy of the job table.
+__device__ __forceinline__ const GemvJob& pick(const GemvJob* jobs, int njobs, uint32_t g) {
+    if (njobs > 3 && g >= jobs[3].tile_begin) return jobs[3];
+    if (njobs > 2 && g >= jobs[2].tile_begin) return jobs[2];
+    if (njobs > 1 && g >= jobs[1].tile_begin) return jobs[1];
+    return jobs[0];
 }
 
 // Transposing butterfly over the warp: lane values a[0..N) (N a power of two
@@ -418,6 +419,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     __shared__ float auxs[kAuxPrefetch];
     __shared__ float sqw[kMaxWarps][8];
     __shared__ int32_t xrows[8], yrows[8], srows[8];
+    __shared__ GemvJob jobs[4];
     const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
     const int W = int(blockDim.x >> 5), gw = L.group_warps, G = W / gw;
     const int grp = warp / gw, wig = warp % gw;
@@ -468,12 +470,13 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     const uint32_t xoff = NS * slot_bytes, poff = xoff + NC * cstride;  // activations, group partials
     auto issue = [&](uint32_t i) {
         const uint32_t s = i % NS, g = t0 + i;
-        const GemvJob& J = pick(L, g);
+        const GemvJob& J = pick(jobs, L.njobs, g);
         const size_t off = size_t(g - J.tile_begin) * tile_bytes;
         mbar_expect_tx(&full[s], slot_bytes);
         bulk_g2s(smem + size_t(s) * slot_bytes, J.a + off, tile_bytes, &full[s]);
         if (DUAL) bulk_g2s(smem + size_t(s) * slot_bytes + tile_bytes, J.b + off, tile_bytes, &full[s]);
     };
+    if (threadIdx.x < 4) jobs[threadIdx.x] = L.job[threadIdx.x];
     if (threadIdx.x == 0) {
         for (uint32_t s = 0; s < NS; s++) {
             mbar_init(&full[s], 1);
@@ -595,7 +598,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     if (aux_pre)
         for (uint32_t idx = threadIdx.x; idx < nt * kTileRows * NC; idx += blockDim.x) {
             const uint32_t i = idx / (kTileRows * NC), e = (idx / NC) % kTileRows, c = idx % NC;
-            const GemvJob& J = pick(L, t0 + i);
+            const GemvJob& J = pick(jobs, L.njobs, t0 + i);
             const uint32_t row = (t0 + i - J.tile_begin) * kTileRows + e;
             if (J.epi == EPI_ADD && row < J.rows) auxs[idx] = J.aux[size_t(yrows[c]) * J.aux_stride + row];
         }
@@ -624,7 +627,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
             break;
         }
         const uint32_t g = t0 + i;
-        const GemvJob& J = pick(L, g);
+        const GemvJob& J = pick(jobs, L.njobs, g);
         const uint32_t tile = g - J.tile_begin;
         const uint32_t tb = smem_s + s * slot_bytes;
         // row e of the tile, client fc: scale, activation, residual, store
