@@ -825,7 +825,7 @@ spm_status spm_session_create(spm_model* m, int32_t max_clients, int32_t max_con
         s->argmax = s->alloc<uint32_t>(n);
         s->sumsq = s->alloc<float>(2 * size_t(kMaxParts) * 8);
         s->status = s->alloc<int32_t>(1);
-        const size_t chunks = (size_t(max_context) + kAttnChunk - 1) / kAttnChunk;
+        const size_t chunks = (size_t(max_context) + kAttnMinChunk - 1) / kAttnMinChunk;
         const size_t group = c.heads / c.kv_heads;
         if (group * c.head_dim > 1024) fail(SPM_E_ARG, "attention supports at most 1024 query values per kv head");
         s->attn_scratch = s->alloc<float>(n * c.kv_heads * chunks * group * (c.head_dim + 2));

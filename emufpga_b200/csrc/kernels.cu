@@ -193,7 +193,7 @@ __global__ void advance_kernel(int32_t* pos, int n) {
 }
 
 // ------------------------------------------------------------- attention ----
-// Grid (kv head, client, position chunk of kChunk).  Every CTA applies the
+// Grid (kv head, client, position chunk of P.chunk).  Every CTA applies the
 // QK-norm and RoPE (host-computed cos/sin table) to its group's queries and
 // the new key; the CTA whose chunk holds the new position appends k, v to the
 // cache (spm-kv/src/cache.rs:49-58).  Each CTA scores its positions for all
@@ -236,8 +236,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     float* red = sc + group * kAttnChunk;   // 64
     pdl_wait();
     const int pos = P.pos[i];
-    const int p0 = chunk * kAttnChunk;
-    const int p1 = min(pos + 1, p0 + kAttnChunk);
+    const int p0 = chunk * P.chunk;
+    const int p1 = min(pos + 1, p0 + P.chunk);
     const float* qg = P.q + size_t(i) * qw + size_t(kvh) * group * hd;
     for (int t = threadIdx.x; t < group * hd; t += kAttnThreads) qs[t] = qg[t];
     for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
@@ -284,7 +284,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     const size_t base = (size_t(i) * P.layers + P.layer) * P.context * size_t(kvw) + size_t(kvh) * hd;
     float* kc = P.kcache + base;
     float* vc = P.vcache + base;
-    if (pos >= p0 && pos < p0 + kAttnChunk)
+    if (pos >= p0 && pos < p0 + P.chunk)
         for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
             kc[size_t(pos) * kvw + t] = kn[t];
             vc[size_t(pos) * kvw + t] = vn[t];
@@ -402,15 +402,17 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     for (int t = threadIdx.x; t < group * hd; t += kAttnThreads) {
         const int h = t / hd, dd = t % hd;
         float M = -INFINITY;
+#pragma unroll 4
         for (int s = 0; s < S; s++) M = fmaxf(M, __ldcg(parts + (size_t(s) * group + h) * (hd + 2) + hd));
+        // chunks in order; the loads of four chunks are in flight together
         float Lsum = 0.f, O = 0.f;
+#pragma unroll 4
         for (int s = 0; s < S; s++) {
             const float* ps = parts + (size_t(s) * group + h) * (hd + 2);
-            const float m = __ldcg(ps + hd);
-            if (m == -INFINITY) continue;
-            const float w = expf(m - M);
-            Lsum = fmaf(__ldcg(ps + hd + 1), w, Lsum);
-            O = fmaf(__ldcg(ps + dd), w, O);
+            const float m = __ldcg(ps + hd), l = __ldcg(ps + hd + 1), o = __ldcg(ps + dd);
+            const float w = m == -INFINITY ? 0.f : expf(m - M);
+            Lsum = fmaf(l, w, Lsum);
+            O = fmaf(o, w, O);
         }
         P.out[size_t(i) * qw + (size_t(kvh) * group + h) * hd + dd] = __fdiv_rn(O, Lsum);
     }
@@ -449,8 +451,14 @@ cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t s, bool pd
         if (e != cudaSuccess) return e;
         configured_for = dev;
     }
-    const int chunks = (P.context + kAttnChunk - 1) / kAttnChunk;
+    static int sms[64] = {};
+    if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    const int target = dev < 64 && sms[dev] ? sms[dev] : 148;
+    int chunk = kAttnChunk;
+    while (chunk > kAttnMinChunk && ((P.context + chunk - 1) / chunk) * P.kv_heads * n < target) chunk /= 2;
+    const int chunks = (P.context + chunk - 1) / chunk;
     AttnParams p = P;
+    p.chunk = chunk;
     void* args[] = {&p};
     return launch_pdl(reinterpret_cast<const void*>(attention_kernel), dim3(P.kv_heads, n, chunks),
                       dim3(kAttnThreads), smem, s, pdl, args);

@@ -65,9 +65,12 @@ GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms, int per = 0)
 // `grid_out` receives the grid size (= sum-of-squares parts written by EPI_ADD).
 cudaError_t launch_gemv(uint32_t dtype, GemvLaunch L, int sms, cudaStream_t stream, bool pdl, int* grid_out = nullptr);
 
-// Positions per attention CTA; a (kv head, client) is split over
-// ceil(context / kAttnChunk) CTAs whose softmax partials are combined.
+// Positions per attention CTA, at most and at least; a (kv head, client) is
+// split over ceil(context / chunk) CTAs whose softmax partials are combined,
+// with the chunk halved from the maximum while the grid has fewer CTAs than
+// the device has SMs.
 constexpr int kAttnChunk = 256;
+constexpr int kAttnMinChunk = 64;
 
 struct AttnParams {
     const float *q, *k, *v;        // [n][q_width], [n][kv_width]
@@ -80,6 +83,7 @@ struct AttnParams {
     int32_t* counters;             // [n][kv_heads], zero between launches
     int32_t layer, layers, context, heads, kv_heads, head_dim, family;
     float eps;
+    int32_t chunk;                 // positions per CTA (set by launch_attention)
 };
 size_t attention_smem(const AttnParams& P);
 cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t stream, bool pdl);
