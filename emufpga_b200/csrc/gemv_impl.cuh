@@ -80,6 +80,7 @@ struct XUnit {
 template <int NC>
 struct XDig {
     uint32_t base[NC];  // shared address of client c's records
+    int nact;           // clients with data (expert mode: the expert's clients); later ones are skipped
     __device__ __forceinline__ void unit(uint32_t u, int c, XUnit& o) const {
         const uint32_t a = base[c] + u * kDigitUnit;
 #pragma unroll
@@ -171,6 +172,7 @@ __device__ __forceinline__ void unit_q8_0(const RowRef (&rr)[R], uint32_t u, con
     }
 #pragma unroll
     for (int c = 0; c < NC; c++) {
+        if (c >= X.nact) break;
         XUnit xu;
         X.unit(u, c, xu);
 #pragma unroll
@@ -211,6 +213,7 @@ __device__ __forceinline__ void unit_q6_k(const RowRef (&rr)[R], uint32_t u, con
     }
 #pragma unroll
     for (int c = 0; c < NC; c++) {
+        if (c >= X.nact) break;
         XUnit xu;
         X.unit(u, c, xu);
         const float o0 = -32.0f * xu.sum0, o1 = -32.0f * xu.sum1;
@@ -266,6 +269,7 @@ __device__ __forceinline__ void unit_q5_k(const RowRef (&rr)[R], uint32_t u, con
     }
 #pragma unroll
     for (int c = 0; c < NC; c++) {
+        if (c >= X.nact) break;
         XUnit xu;
         X.unit(u, c, xu);
         const float xsum = xu.sum0 + xu.sum1;
@@ -302,6 +306,7 @@ __device__ __forceinline__ void unit_q2_k(const RowRef (&rr)[R], uint32_t u, con
     }
 #pragma unroll
     for (int c = 0; c < NC; c++) {
+        if (c >= X.nact) break;
         XUnit xu;
         X.unit(u, c, xu);
 #pragma unroll
@@ -537,7 +542,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
         // digit records: each pair of lanes holds one unit, 16 values each,
         // and agrees on the unit's exponent through a shuffle (whole warps
         // step through the loop together so that every lane shuffles)
-        const uint32_t total = NC * U * 2;
+        const uint32_t total = uint32_t(n_act) * U * 2;  // records of slots without data are never read
         for (uint32_t w0 = uint32_t(warp) * 32; w0 < total; w0 += blockDim.x) {
             const uint32_t idx = w0 + uint32_t(lane);
             const bool live = idx < total;
@@ -610,6 +615,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     XT X;
 #pragma unroll
     for (int c = 0; c < NC; c++) X.base[c] = smem_s + xoff + c * cstride;
+    if constexpr (ENC != SPM_F32) X.nact = n_act;
     // Totals this thread finishes: with one warp per group, lane l holds
     // (row-in-pass, client) index l >> SH of each pass; with several, lane l
     // of the group's first warp holds index l = row * NCP + client of the

@@ -17,7 +17,8 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
                                                     MoePlan* plan) {
     __shared__ float prob[kMoeMaxClients][kMoeMaxExperts];
     __shared__ int32_t sel[kMoeMaxClients][kMoeMaxUsed];
-    __shared__ int32_t cnt[kMoeMaxExperts], base[kMoeMaxExperts + 1];
+    __shared__ int32_t cnt[kMoeMaxExperts], base[kMoeMaxExperts];
+    __shared__ int32_t pos_of[kMoeMaxClients][kMoeMaxUsed];
     pdl_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < n) {
@@ -76,21 +77,28 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
     }
     __syncthreads();
     // ---- plan: active experts ascending, their clients ascending ----
+    // Thread e counts expert e's routes and records, for each of them, its
+    // position among the expert's clients (clients ascending).
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         int c = 0;
         for (int i = 0; i < n; i++)
-            for (int j = 0; j < K; j++) c += sel[i][j] == e;
+            for (int j = 0; j < K; j++)
+                if (sel[i][j] == e) pos_of[i][j] = c++;
         cnt[e] = c;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int a = 0;
-        for (int e = 0; e < E; e++) {
-            base[e] = a;
-            a += cnt[e] ? 1 : 0;
+    // active index of every expert: exclusive prefix count of cnt[e] > 0,
+    // 32 experts per step by ballot
+    if (warp == 0) {
+        int run = 0;
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            const bool act = e < E && cnt[e] > 0;
+            const uint32_t m = __ballot_sync(0xffffffffu, act);
+            if (e < E) base[e] = run + __popc(m & ((1u << lane) - 1u));
+            run += __popc(m);
         }
-        base[E] = a;
-        plan->count = a;
+        if (lane == 0) plan->count = run;
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -104,26 +112,21 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
                 if (sel[i][j] == e) plan->tok[a][p++] = i;
         for (; p < kMoeMaxClients; p++) plan->tok[a][p] = 0;
     }
-    __syncthreads();
     if (threadIdx.x < n) {
         const int i = threadIdx.x;
-        // this client's experts in ascending id
-        int ids[kMoeMaxUsed];
-        for (int j = 0; j < K; j++) ids[j] = sel[i][j];
+        // this client's routes in ascending expert id
+        int ids[kMoeMaxUsed], js[kMoeMaxUsed];
+        for (int j = 0; j < K; j++) ids[j] = sel[i][j], js[j] = j;
         for (int x = 1; x < K; x++)
             for (int y = x; y > 0 && ids[y - 1] > ids[y]; y--) {
-                const int t = ids[y];
-                ids[y] = ids[y - 1];
-                ids[y - 1] = t;
+                const int t = ids[y], tj = js[y];
+                ids[y] = ids[y - 1], js[y] = js[y - 1];
+                ids[y - 1] = t, js[y - 1] = tj;
             }
         for (int j = 0; j < K; j++) {
-            const int e = ids[j], a = base[e];
-            int pos = 0;
-            for (int q = 0; q < i; q++)
-                for (int jj = 0; jj < K; jj++) pos += sel[q][jj] == e;
-            plan->slot_a[i][j] = a;
-            plan->slot_pos[i][j] = pos;
-            plan->slot_p[i][j] = prob[i][e];
+            plan->slot_a[i][j] = base[ids[j]];
+            plan->slot_pos[i][j] = pos_of[i][js[j]];
+            plan->slot_p[i][j] = prob[i][ids[j]];
         }
     }
     pdl_trigger();
@@ -135,13 +138,20 @@ __global__ void __launch_bounds__(256) combine_kernel(const MoePlan* plan, const
     pdl_wait();
     const int i = blockIdx.x;
     const float norm = plan->norm[i];
+    // the client's expert outputs in ascending expert id, and their weights
+    const float* lanes[kMoeMaxUsed];
+    float p[kMoeMaxUsed];
+#pragma unroll
+    for (int j = 0; j < kMoeMaxUsed; j++) {
+        lanes[j] = j < K ? out + size_t(plan->slot_a[i][j] * kMoeMaxClients + plan->slot_pos[i][j]) * out_stride : out;
+        p[j] = j < K ? plan->slot_p[i][j] : 0.f;
+    }
     float ss = 0.f;
     for (int col = threadIdx.x; col < width; col += blockDim.x) {
         float total = 0.f;
-        for (int j = 0; j < K; j++) {
-            const float* lane = out + size_t(plan->slot_a[i][j] * kMoeMaxClients + plan->slot_pos[i][j]) * out_stride;
-            total = total + __fdiv_rn(__fmul_rn(lane[col], plan->slot_p[i][j]), norm);
-        }
+#pragma unroll
+        for (int j = 0; j < kMoeMaxUsed; j++)
+            if (j < K) total = total + __fdiv_rn(__fmul_rn(lanes[j][col], p[j]), norm);
         const float v = states[size_t(i) * width + col] + total;
         states[size_t(i) * width + col] = v;
         ss = fmaf(v, v, ss);
@@ -150,11 +160,10 @@ __global__ void __launch_bounds__(256) combine_kernel(const MoePlan* plan, const
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
     pdl_trigger();
-    if (threadIdx.x < 8) {
+    if (threadIdx.x == 0) {
         float t = 0.f;
-        if (threadIdx.x == 0)
-            for (int w = 0; w < int(blockDim.x >> 5); w++) t += red[w];
-        if (threadIdx.x == 0) red[32] = t;
+        for (int w = 0; w < int(blockDim.x >> 5); w++) t += red[w];
+        red[32] = t;
     }
     __syncthreads();
     if (threadIdx.x < 8) sumsq[i * 8 + threadIdx.x] = threadIdx.x == i ? red[32] : 0.f;

@@ -249,3 +249,27 @@ def test_olmoe_shape_two_layers_matches_the_oracle(cuda):
         assert best == [O.argmax_last(want[i]) for i in range(n)]
     sess.close()
     m.close()
+
+
+def test_qwen3_30b_shape_two_layers_matches_the_oracle(cuda):
+    """Qwen3-30B-A3B dimensions (hidden 2048, 32/4 heads of 128, 128 experts
+    of 768, top-8, vocab 151936, Q5_K) with 2 of its 48 layers, 8 clients."""
+    import dataclasses
+
+    base = configs.RECIPES["qwen3-30b-a3b-q5_k"]
+    r = base.replace(shape=dataclasses.replace(base.shape, layers=2))
+    img = eb.synth_gguf(r)
+    om = O.OracleModel(img, r.shape)
+    m = eb.Model(img, r.shape)
+    n = 8
+    sess = eb.Session(m, n, 8)
+    osess = om.session(n, 8)
+    for step in range(3):
+        toks = configs.prompt_tokens(40 + step, 0, n, r.shape.vocab)
+        best, got = sess.decode_step(toks, want_logits=True)
+        want, oroutes = osess.step(toks, routes=True)
+        assert np.array_equal(sess.routes(n), oroutes)
+        assert logits_close(got, want)
+        assert best == [O.argmax_last(want[i]) for i in range(n)]
+    sess.close()
+    m.close()
