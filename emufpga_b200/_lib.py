@@ -81,6 +81,12 @@ PROTOTYPES = {
     "spm_model_stream_index": (C.c_int32, [_P, C.c_char_p, _I32P]),
     "spm_dequant_rows": (C.c_int32, [_P, C.c_int32, C.c_uint64, C.c_uint64, _FP]),
     "spm_dequant_rows_static": (C.c_int32, [_P, C.c_int32, C.c_uint64, C.c_uint64, _FP]),
+    "spm_model_open_ep": (C.c_int32, [C.c_char_p, C.c_char_p, C.POINTER(ModelCfg), C.c_int, C.c_int32, C.c_int32,
+                                      C.POINTER(_P)]),
+    "spm_model_open_memory_ep": (C.c_int32, [_P, C.c_uint64, C.c_char_p, C.POINTER(ModelCfg), C.c_int, C.c_int32,
+                                             C.c_int32, C.POINTER(_P)]),
+    "spm_session_ep_handle": (C.c_int32, [_P, _P]),
+    "spm_session_ep_connect": (C.c_int32, [_P, _P]),
     "spm_streamed": (C.c_int32, [_P, C.c_int32, _P, C.c_int32, _P, _P]),
     "spm_weights_upload": (C.c_int32, [C.c_uint32, C.c_uint64, C.c_uint64, _P, C.c_int, C.POINTER(_P)]),
     "spm_weights_free": (C.c_int32, [_P]),

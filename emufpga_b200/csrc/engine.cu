@@ -7,8 +7,13 @@
 // every weight exactly once and serves all clients
 // (spm-batch/src/step.rs:19-53).
 #include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <algorithm>
+#include <cstring>
 #include <atomic>
 #include <cmath>
 #include <fstream>
@@ -76,6 +81,7 @@ struct LayerIdx {
 struct spm_model {
     spm_model_cfg cfg{};
     int device = 0, sms = 148;
+    int world = 1, rank = 0;  // expert parallel: this GPU holds experts e with e % world == rank
     uint8_t* image = nullptr;
     uint64_t image_bytes = 0;
     std::vector<StreamDesc> streams;
@@ -122,6 +128,18 @@ struct spm_session {
     int32_t* attn_counters = nullptr;
     int32_t* status = nullptr;         // device error word of bounded waits
     int32_t* h_status = nullptr;
+    uint32_t* step = nullptr;          // steps taken (advance kernel); names the exchange rounds
+    // Expert parallel exchange (model world > 1): one allocation, exported by
+    // CUDA IPC, holding flags[2][64] (512 bytes) then two parity buffers of
+    // expert output rows; every rank writes its experts' rows into every
+    // rank's buffer and raises its flag there.
+    uint8_t* ep_region = nullptr;
+    size_t ep_xbytes = 0;              // bytes of one parity buffer
+    uint32_t* ep_done = nullptr;       // CTA counter of the expert down launch
+    float** ep_peer_y = nullptr;       // device [2][world]
+    uint32_t** ep_peer_flag = nullptr; // device [2][world]
+    std::vector<void*> ep_mapped;      // peers' regions opened by IPC
+    bool ep_ready = false;
     std::vector<int> lens;
     bool graphs = true, pdl = true;
     std::map<int, cudaGraphExec_t> exec;
@@ -129,6 +147,7 @@ struct spm_session {
     std::vector<void*> allocs;
     ~spm_session() {
         for (auto& kv : exec) cudaGraphExecDestroy(kv.second);
+        for (void* p : ep_mapped) cudaIpcCloseMemHandle(p);
         for (void* p : allocs) cudaFree(p);
         if (h_tokens) cudaFreeHost(h_tokens);
         if (h_argmax) cudaFreeHost(h_argmax);
@@ -211,7 +230,7 @@ void check_order(const Order& o, const Gguf& g) {
 }
 
 spm_model* open_model(const uint8_t* buf, uint64_t len, const std::string* order_text, const spm_model_cfg* cfg,
-                      int device) {
+                      int device, int world = 1, int rank = 0) {
     Gguf g = gguf_parse(buf, len);
     std::unique_ptr<spm_model> m(new spm_model());
     m->cfg = cfg ? *cfg : cfg_from_gguf(g);
@@ -224,6 +243,10 @@ spm_model* open_model(const uint8_t* buf, uint64_t len, const std::string* order
     if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) fail(SPM_E_NO_DEVICE, "no CUDA device is visible");
     if (device < 0 || device >= ndev) fail(SPM_E_ARG, "device index out of range");
     m->device = device;
+    if (world < 1 || world > 8 || rank < 0 || rank >= world) fail(SPM_E_ARG, "expert parallel: 1 to 8 ranks");
+    if (world > 1 && !is_moe(c)) fail(SPM_E_ARG, "expert parallel needs a routed (MoE) model");
+    m->world = world;
+    m->rank = rank;
     CUDA_OK(cudaSetDevice(device));
     CUDA_OK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, device));
 
@@ -340,6 +363,21 @@ spm_model* open_model(const uint8_t* buf, uint64_t len, const std::string* order
                 if (i >= m->streams.size()) break;
                 const StreamDesc& s = m->streams[i];
                 const GgufTensor* t = g.find(s.name);
+                if (world > 1 && s.experts > 1) {
+                    // this rank's experts only; each is a whole run of tiles
+                    const uint64_t er = s.pk.rows / s.experts;
+                    Packed sub = packed_shape(s.pk.dtype, er, s.pk.cols);
+                    if (sub.tile_bytes != s.pk.tile_bytes || sub.tiles * s.experts != s.pk.tiles)
+                        fail(SPM_E_ARG, s.name + ": experts are not whole tiles");
+                    const uint64_t src = t->len / s.experts;
+                    host.resize(sub.tiles * sub.tile_bytes);
+                    for (uint64_t e = uint64_t(rank); e < s.experts; e += uint64_t(world)) {
+                        pack_matrix(sub, buf + t->offset + e * src, host.data());
+                        CUDA_OK(cudaMemcpy(m->image + s.pk.offset + e * host.size(), host.data(), host.size(),
+                                           cudaMemcpyHostToDevice));
+                    }
+                    continue;
+                }
                 host.resize(s.pk.tiles * s.pk.tile_bytes);
                 pack_matrix(s.pk, buf + t->offset, host.data());
                 CUDA_OK(cudaMemcpy(m->image + s.pk.offset, host.data(), host.size(), cudaMemcpyHostToDevice));
@@ -357,6 +395,30 @@ spm_model* open_model(const uint8_t* buf, uint64_t len, const std::string* order
     CUDA_OK(cudaMemcpy(m->gains, gains.data(), gains.size() * sizeof(float), cudaMemcpyHostToDevice));
     return m.release();
 }
+
+// A GGUF file mapped read-only: ranks that open the same file share its
+// pages instead of each holding a copy.
+struct Mapped {
+    const uint8_t* p = nullptr;
+    size_t n = 0;
+    explicit Mapped(const char* path) {
+        const int fd = open(path, O_RDONLY);
+        if (fd < 0) fail(SPM_E_STREAM, std::string(path) + ": cannot open");
+        struct stat st {};
+        if (fstat(fd, &st) != 0 || st.st_size <= 0) {
+            close(fd);
+            fail(SPM_E_STREAM, std::string(path) + ": cannot read");
+        }
+        n = size_t(st.st_size);
+        void* q = mmap(nullptr, n, PROT_READ, MAP_SHARED, fd, 0);
+        close(fd);
+        if (q == MAP_FAILED) fail(SPM_E_STREAM, std::string(path) + ": cannot map");
+        p = static_cast<const uint8_t*>(q);
+    }
+    ~Mapped() {
+        if (p) munmap(const_cast<uint8_t*>(p), n);
+    }
+};
 
 std::string read_file(const char* path) {
     std::ifstream f(path, std::ios::binary);
@@ -465,6 +527,8 @@ void enqueue_step(spm_session* s, int n) {
             const int chunks_gu = std::max(1, std::min(eff / kTileRows, (2 * m->sms + s->moe_max_active - 1) / s->moe_max_active));
             GemvLaunch ge = gemv_base(m, L.gate_exps, s->states, kMoeMaxClients);
             ge.status = s->status;
+            ge.world = m->world;
+            ge.rank = m->rank;
             norm_in(ge, L.ffn_norm, 1);
             add_job(ge, m, L.gate_exps, m->tiles(L.up_exps), s->moe_act, eff, nullptr, 0, EPI_SWIGLU);
             ge.plan = plan;
@@ -477,6 +541,23 @@ void enqueue_step(spm_session* s, int n) {
             const int chunks_d = std::max(1, std::min(d / kTileRows, (2 * m->sms + s->moe_max_active - 1) / s->moe_max_active));
             GemvLaunch gx = gemv_base(m, L.down_exps, s->moe_act, kMoeMaxClients);
             gx.status = s->status;
+            gx.world = m->world;
+            gx.rank = m->rank;
+            MoeExchange ex{};
+            const float* outs = s->moe_out;
+            if (m->world > 1) {
+                // rows go to every rank's buffer; the combine waits for all ranks
+                if (!s->ep_ready) fail(SPM_E_ARG, "expert parallel session: call spm_session_ep_connect first");
+                gx.ep_peer_y = s->ep_peer_y;
+                gx.ep_peer_flag = s->ep_peer_flag;
+                gx.ep_done = s->ep_done;
+                gx.ep_step = s->step;
+                gx.ep_layers = int32_t(c.layers);
+                gx.ep_layer = int32_t(l);
+                ex = MoeExchange{reinterpret_cast<const uint32_t*>(s->ep_region), s->step, m->world, int32_t(c.layers),
+                                 int32_t(l), s->ep_xbytes / sizeof(float), s->status};
+                outs = reinterpret_cast<const float*>(s->ep_region + 512);
+            }
             add_job(gx, m, L.down_exps, nullptr, s->moe_out, d, nullptr, 0, EPI_STORE);
             gx.plan = plan;
             gx.expert_max = s->moe_max_active;
@@ -485,7 +566,7 @@ void enqueue_step(spm_session* s, int n) {
             gx.total_tiles = gx.expert_tiles;
             gx.xmode = 1;
             run_gemv(m, gx, m->streams[L.down_exps].pk.dtype, st, pdl);
-            CUDA_OK(launch_combine(plan, s->moe_out, d, s->states, d, n, K, part[0], st, pdl));
+            CUDA_OK(launch_combine(plan, outs, d, s->states, d, n, K, part[0], m->world > 1 ? &ex : nullptr, st, pdl));
             parts = n;
             continue;
         }
@@ -506,7 +587,7 @@ void enqueue_step(spm_session* s, int n) {
     add_job(gh, m, m->head, nullptr, s->logits, int(c.vocab), nullptr, 0, EPI_STORE);
     run_gemv(m, gh, m->streams[m->head].pk.dtype, st, pdl);
     CUDA_OK(launch_argmax(s->logits, n, int(c.vocab), s->argmax, st, pdl));
-    CUDA_OK(launch_advance(s->pos, n, st, pdl));
+    CUDA_OK(launch_advance(s->pos, n, s->step, st, pdl));
 }
 
 // A bounded device wait that gave up leaves a code in the status word; the
@@ -653,11 +734,10 @@ spm_status spm_order_default(const spm_model_cfg* cfg, const uint8_t* gguf, uint
 spm_status spm_model_open(const char* gguf_path, const char* order_path, const spm_model_cfg* cfg, int device,
                           spm_model** out) {
     return guarded([&] {
-        std::string img = read_file(gguf_path);
+        Mapped img(gguf_path);
         std::string order;
         if (order_path) order = read_file(order_path);
-        *out = open_model(reinterpret_cast<const uint8_t*>(img.data()), img.size(), order_path ? &order : nullptr, cfg,
-                          device);
+        *out = open_model(img.p, img.n, order_path ? &order : nullptr, cfg, device);
     });
 }
 
@@ -666,6 +746,25 @@ spm_status spm_model_open_memory(const uint8_t* gguf, uint64_t len, const char* 
     return guarded([&] {
         std::string order = order_text ? order_text : "";
         *out = open_model(gguf, len, order_text ? &order : nullptr, cfg, device);
+    });
+}
+
+spm_status spm_model_open_ep(const char* gguf_path, const char* order_path, const spm_model_cfg* cfg, int device,
+                             int32_t world, int32_t rank, spm_model** out) {
+    return guarded([&] {
+        Mapped img(gguf_path);
+        std::string order;
+        if (order_path) order = read_file(order_path);
+        *out = open_model(img.p, img.n, order_path ? &order : nullptr, cfg, device, world, rank);
+    });
+}
+
+spm_status spm_model_open_memory_ep(const uint8_t* gguf, uint64_t len, const char* order_text,
+                                    const spm_model_cfg* cfg, int device, int32_t world, int32_t rank,
+                                    spm_model** out) {
+    return guarded([&] {
+        std::string order = order_text ? order_text : "";
+        *out = open_model(gguf, len, order_text ? &order : nullptr, cfg, device, world, rank);
     });
 }
 
@@ -839,7 +938,15 @@ spm_status spm_session_create(spm_model* m, int32_t max_clients, int32_t max_con
             s->plans = s->alloc<MoePlan>(c.layers);
             s->moe_act = s->alloc<float>(size_t(s->moe_max_active) * kMoeMaxClients * c.expert_ff);
             s->moe_out = s->alloc<float>(size_t(s->moe_max_active) * kMoeMaxClients * c.hidden);
+            if (m->world > 1) {
+                s->ep_xbytes = (size_t(s->moe_max_active) * kMoeMaxClients * c.hidden * sizeof(float) + 255) & ~size_t(255);
+                s->ep_region = s->alloc<uint8_t>(512 + 2 * s->ep_xbytes);
+                s->ep_done = s->alloc<uint32_t>(1);
+                s->ep_peer_y = s->alloc<float*>(2 * size_t(m->world));
+                s->ep_peer_flag = s->alloc<uint32_t*>(2 * size_t(m->world));
+            }
         }
+        s->step = s->alloc<uint32_t>(1);
         auto table = rope_table(c, max_context);
         s->rope = s->alloc<float2>(table.size());
         CUDA_OK(cudaMemcpy(s->rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice));
@@ -940,6 +1047,49 @@ spm_status spm_session_routes(const spm_session* s, int32_t n, int32_t* routes_h
             for (int i = 0; i < n; i++)
                 for (uint32_t j = 0; j < c.experts_used; j++)
                     routes_host[(size_t(l) * n + i) * c.experts_used + j] = plans[l].route[i][j];
+    });
+}
+
+spm_status spm_session_ep_handle(spm_session* s, void* handle) {
+    return guarded([&] {
+        if (s->m->world < 2) fail(SPM_E_ARG, "the model is not expert parallel");
+        CUDA_OK(cudaSetDevice(s->m->device));
+        cudaIpcMemHandle_t h;
+        CUDA_OK(cudaIpcGetMemHandle(&h, s->ep_region));
+        static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+        std::memcpy(handle, &h, sizeof(h));
+    });
+}
+
+spm_status spm_session_ep_connect(spm_session* s, const void* handles) {
+    return guarded([&] {
+        const int world = s->m->world, rank = s->m->rank;
+        if (world < 2) fail(SPM_E_ARG, "the model is not expert parallel");
+        if (s->ep_ready) fail(SPM_E_ARG, "the session is already connected");
+        CUDA_OK(cudaSetDevice(s->m->device));
+        std::vector<uint8_t*> base(world);
+        for (int p = 0; p < world; p++) {
+            if (p == rank) {
+                base[p] = s->ep_region;
+                continue;
+            }
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, static_cast<const uint8_t*>(handles) + size_t(p) * 64, sizeof(h));
+            void* q = nullptr;
+            CUDA_OK(cudaIpcOpenMemHandle(&q, h, cudaIpcMemLazyEnablePeerAccess));
+            s->ep_mapped.push_back(q);
+            base[p] = static_cast<uint8_t*>(q);
+        }
+        std::vector<float*> y(2 * size_t(world));
+        std::vector<uint32_t*> f(2 * size_t(world));
+        for (int k = 0; k < 2; k++)
+            for (int p = 0; p < world; p++) {
+                y[k * world + p] = reinterpret_cast<float*>(base[p] + 512 + k * s->ep_xbytes);
+                f[k * world + p] = reinterpret_cast<uint32_t*>(base[p]) + k * 64 + rank;
+            }
+        CUDA_OK(cudaMemcpy(s->ep_peer_y, y.data(), y.size() * sizeof(float*), cudaMemcpyHostToDevice));
+        CUDA_OK(cudaMemcpy(s->ep_peer_flag, f.data(), f.size() * sizeof(uint32_t*), cudaMemcpyHostToDevice));
+        s->ep_ready = true;
     });
 }
 

@@ -352,6 +352,20 @@ __device__ __forceinline__ void unit_dot(const RowRef (&rr)[R], uint32_t u, cons
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return __fdiv_rn(g, 1.0f + expf(-g)) * u; }
 
+// Expert parallel: the launch's CTA counter.  The last CTA to arrive raises
+// this rank's flag in every rank's flag array.  One thread per CTA calls it,
+// after the CTA's stores to the ranks' buffers are fenced at system scope.
+__device__ __forceinline__ void ep_arrive(const GemvLaunch& L) {
+    const uint32_t prev = atomicAdd(L.ep_done, 1u);
+    if (prev + 1 == gridDim.x) {
+        *L.ep_done = 0;
+        __threadfence_system();
+        const uint32_t E = *L.ep_step * uint32_t(L.ep_layers) + uint32_t(L.ep_layer) + 1;
+        const uint32_t par = E & 1u;
+        for (int p = 0; p < L.world; p++) st_release_sys(L.ep_peer_flag[par * L.world + p], E);
+    }
+}
+
 // The job of global tile g, from the CTA's shared copy of the job table.
 __device__ __forceinline__ const GemvJob& pick(const GemvJob* jobs, int njobs, uint32_t g) {
     if (njobs > 3 && g >= jobs[3].tile_begin) return jobs[3];
@@ -425,6 +439,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     __shared__ float sqw[kMaxWarps][8];
     __shared__ int32_t xrows[8], yrows[8], srows[8];
     __shared__ GemvJob jobs[4];
+    __shared__ float* ep_y[8];  // expert parallel: every rank's output buffer for this layer
     const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
     const int W = int(blockDim.x >> 5), gw = L.group_warps, G = W / gw;
     const int grp = warp / gw, wig = warp % gw;
@@ -435,9 +450,15 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
         // expert mode: the plan comes from the previous kernel
         pdl_wait();
         const int a = int(blockIdx.x) / L.expert_chunks, chunk = int(blockIdx.x) % L.expert_chunks;
-        if (a >= L.plan->count) {
+        if (a >= L.plan->count || (L.world > 1 && L.plan->expert[a] % L.world != L.rank)) {
+            // no active expert here, or another rank's
             pdl_trigger();
+            if (L.ep_done && threadIdx.x == 0) ep_arrive(L);
             return;
+        }
+        if (L.ep_peer_y && threadIdx.x < uint32_t(L.world)) {
+            const uint32_t E = *L.ep_step * uint32_t(L.ep_layers) + uint32_t(L.ep_layer) + 1;
+            ep_y[threadIdx.x] = L.ep_peer_y[(E & 1u) * L.world + threadIdx.x];
         }
         const uint32_t e = uint32_t(L.plan->expert[a]), Te = L.expert_tiles, C = uint32_t(L.expert_chunks);
         rbase = e * Te * kTileRows;
@@ -645,7 +666,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
                 if constexpr (DUAL) r = silu_mul(r, b * fscale);
                 if (J.epi == EPI_ADD)
                     r = (aux_pre ? auxs[(i * kTileRows + e) * NC + fc] : J.aux[size_t(yrows[fc]) * J.aux_stride + row]) + r;
-                J.y[size_t(yrows[fc]) * J.y_stride + row] = r;
+                if (L.ep_peer_y) {
+                    for (int p = 0; p < L.world; p++) ep_y[p][size_t(yrows[fc]) * J.y_stride + row] = r;
+                } else {
+                    J.y[size_t(yrows[fc]) * J.y_stride + row] = r;
+                }
                 sq = fmaf(r, r, sq);
             }
         };
@@ -727,6 +752,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
             for (int w = 0; w < W; w++) t += sqw[w][threadIdx.x];
             L.sumsq_out[blockIdx.x * 8 + L.c0 + threadIdx.x] = t;
         }
+    }
+    if (L.ep_done) {
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0) ep_arrive(L);
     }
 }
 

@@ -186,10 +186,11 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* logits, int v
     }
 }
 
-__global__ void advance_kernel(int32_t* pos, int n) {
+__global__ void advance_kernel(int32_t* pos, int n, uint32_t* step) {
     pdl_wait();
     pdl_trigger();
     if (threadIdx.x < n) pos[threadIdx.x] += 1;
+    if (step && threadIdx.x == 0) *step += 1;
 }
 
 // ------------------------------------------------------------- attention ----
@@ -486,8 +487,8 @@ cudaError_t launch_argmax(const float* logits, int n, int vocab, uint32_t* out, 
     return launch_pdl(reinterpret_cast<const void*>(argmax_kernel), dim3(n), dim3(1024), 0, s, pdl, args);
 }
 
-cudaError_t launch_advance(int32_t* pos, int n, cudaStream_t s, bool pdl) {
-    void* args[] = {&pos, &n};
+cudaError_t launch_advance(int32_t* pos, int n, uint32_t* step, cudaStream_t s, bool pdl) {
+    void* args[] = {&pos, &n, &step};
     return launch_pdl(reinterpret_cast<const void*>(advance_kernel), dim3(1), dim3(32), 0, s, pdl, args);
 }
 

@@ -51,6 +51,19 @@ struct GemvLaunch {
     int32_t expert_chunks;
     uint32_t expert_tiles;
     int32_t xmode;
+    // Expert parallel (world > 1, expert mode): experts e with e % world ==
+    // rank are this GPU's; CTAs of other experts do no work.  When ep_peer_y
+    // is set, each output row goes to the same place in every rank's buffer
+    // (ep_peer_y[parity * world + p]) and the launch's last CTA, once every
+    // CTA's stores are fenced, writes the flag value E = *ep_step * ep_layers +
+    // ep_layer + 1 to ep_peer_flag[parity * world + p] for every rank p
+    // (parity = E & 1; ep_done counts finished CTAs and returns to zero).
+    int32_t world, rank;
+    float* const* ep_peer_y;
+    uint32_t* const* ep_peer_flag;
+    uint32_t* ep_done;
+    const uint32_t* ep_step;
+    int32_t ep_layers, ep_layer;
 };
 
 // Grid, ring slots and dynamic shared memory of a streaming GEMV launch.
@@ -97,6 +110,7 @@ cudaError_t launch_dequant(uint32_t dtype, const uint8_t* tiles, const Packed& p
                            float* out, cudaStream_t stream);
 // Greedy pick per client over logits [n][vocab]: largest value, last index on ties.
 cudaError_t launch_argmax(const float* logits, int n, int vocab, uint32_t* out, cudaStream_t stream, bool pdl);
-cudaError_t launch_advance(int32_t* pos, int n, cudaStream_t stream, bool pdl);
+// positions += 1 for clients 0..n-1; the step counter (if any) += 1.
+cudaError_t launch_advance(int32_t* pos, int n, uint32_t* step, cudaStream_t stream, bool pdl);
 
 }  // namespace spm

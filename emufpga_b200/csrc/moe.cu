@@ -133,9 +133,26 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
 }
 
 __global__ void __launch_bounds__(256) combine_kernel(const MoePlan* plan, const float* out, int out_stride,
-                                                      float* states, int width, int K, float* sumsq) {
+                                                      float* states, int width, int K, float* sumsq, MoeExchange ex) {
     __shared__ float red[33];
     pdl_wait();
+    if (ex.world > 1) {
+        // every rank's expert rows for this layer are in place once all flags are up
+        const uint32_t E = *ex.step * uint32_t(ex.layers) + uint32_t(ex.layer) + 1;
+        if (threadIdx.x < uint32_t(ex.world)) {
+            const uint32_t* f = ex.flags + (E & 1u) * 64 + threadIdx.x;
+            if (ld_acquire_sys(f) != E) {
+                const uint64_t t0 = now_ns();
+                while (ld_acquire_sys(f) != E)
+                    if (now_ns() - t0 > kWaitLimitNs) {
+                        flag(ex.status, 5);
+                        break;
+                    }
+            }
+        }
+        __syncthreads();
+        out += (E & 1u) * ex.xstride;
+    }
     const int i = blockIdx.x;
     const float norm = plan->norm[i];
     // the client's expert outputs in ascending expert id, and their weights
@@ -151,7 +168,7 @@ __global__ void __launch_bounds__(256) combine_kernel(const MoePlan* plan, const
         float total = 0.f;
 #pragma unroll
         for (int j = 0; j < kMoeMaxUsed; j++)
-            if (j < K) total = total + __fdiv_rn(__fmul_rn(lanes[j][col], p[j]), norm);
+            if (j < K) total = total + __fdiv_rn(__fmul_rn(__ldcg(lanes[j] + col), p[j]), norm);
         const float v = states[size_t(i) * width + col] + total;
         states[size_t(i) * width + col] = v;
         ss = fmaf(v, v, ss);
@@ -194,8 +211,10 @@ cudaError_t launch_route(const float* logits, const float* bias, int n, int expe
 }
 
 cudaError_t launch_combine(const MoePlan* plan, const float* out, int out_stride, float* states, int width, int n,
-                           int used, float* sumsq, cudaStream_t s, bool pdl) {
-    void* args[] = {&plan, &out, &out_stride, &states, &width, &used, &sumsq};
+                           int used, float* sumsq, const MoeExchange* ex, cudaStream_t s, bool pdl) {
+    MoeExchange e = ex ? *ex : MoeExchange{};
+    if (!ex) e.world = 1;
+    void* args[] = {&plan, &out, &out_stride, &states, &width, &used, &sumsq, &e};
     return launch_pdl(reinterpret_cast<const void*>(combine_kernel), dim3(n), dim3(256), s, pdl, args);
 }
 

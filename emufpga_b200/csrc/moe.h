@@ -29,10 +29,23 @@ struct MoePlan {
 // renormaliser, and the plan (spm-granite-moe/src/moe.rs:17-35, math.rs:23-39).
 cudaError_t launch_route(const float* logits, const float* bias, int n, int experts, int used, MoePlan* plan,
                          cudaStream_t s, bool pdl);
+// Expert parallel combine: before reading the expert outputs, wait until
+// every rank has raised its flag for this layer (flag value E = *step *
+// layers + layer + 1, in flags[(E & 1) * 64 + rank]); the outputs are in the
+// buffer of parity E & 1, xstride floats after the parity-0 one.  A wait that
+// gives up after 1 s sets *status and goes on.
+struct MoeExchange {
+    const uint32_t* flags;
+    const uint32_t* step;
+    int32_t world, layers, layer;
+    size_t xstride;
+    int32_t* status;
+};
+
 // states[i] += sum over client i's experts in ascending id of
 // (out[a][pos] * p) / norm  (spm-granite-moe/src/layout.rs:283-302); also the
 // sum of squares of each new state row (sumsq[i*8 + c] = c == i ? ss : 0).
 cudaError_t launch_combine(const MoePlan* plan, const float* out, int out_stride, float* states, int width, int n,
-                           int used, float* sumsq, cudaStream_t s, bool pdl);
+                           int used, float* sumsq, const MoeExchange* ex, cudaStream_t s, bool pdl);
 
 }  // namespace spm

@@ -122,25 +122,40 @@ def _dev_ptr(t) -> C.c_void_p:
 class Model:
     """The weight stream of one model, packed in HBM in consumption order."""
 
-    def __init__(self, image: np.ndarray, shape: Shape | None = None, order: str | None = None, device: int = 0):
+    def __init__(self, image: np.ndarray, shape: Shape | None = None, order: str | None = None, device: int = 0,
+                 ep: tuple[int, int] | None = None):
+        """`ep=(world, rank)`: expert parallel -- only experts e with
+        e % world == rank are uploaded and computed on this GPU."""
         self.shape = shape
         cfg = shape.cfg() if shape is not None else None
         h = C.c_void_p()
-        call("spm_model_open_memory", _ptr(image), len(image), order.encode() if order else None,
-             C.byref(cfg) if cfg is not None else None, device, C.byref(h))
+        o = order.encode() if order else None
+        cp = C.byref(cfg) if cfg is not None else None
+        if ep:
+            call("spm_model_open_memory_ep", _ptr(image), len(image), o, cp, device, ep[0], ep[1], C.byref(h))
+        else:
+            call("spm_model_open_memory", _ptr(image), len(image), o, cp, device, C.byref(h))
         self._h = h
         self.device = device
+        self.ep = ep
 
     @classmethod
-    def from_file(cls, path: str, shape: Shape | None = None, order_path: str | None = None, device: int = 0):
+    def from_file(cls, path: str, shape: Shape | None = None, order_path: str | None = None, device: int = 0,
+                  ep: tuple[int, int] | None = None):
+        """Open a GGUF file (memory-mapped: ranks opening the same file share its pages)."""
         self = cls.__new__(cls)
         self.shape = shape
         cfg = shape.cfg() if shape is not None else None
         h = C.c_void_p()
-        call("spm_model_open", path.encode(), order_path.encode() if order_path else None,
-             C.byref(cfg) if cfg is not None else None, device, C.byref(h))
+        o = order_path.encode() if order_path else None
+        cp = C.byref(cfg) if cfg is not None else None
+        if ep:
+            call("spm_model_open_ep", path.encode(), o, cp, device, ep[0], ep[1], C.byref(h))
+        else:
+            call("spm_model_open", path.encode(), o, cp, device, C.byref(h))
         self._h = h
         self.device = device
+        self.ep = ep
         return self
 
     def close(self) -> None:
@@ -285,6 +300,20 @@ class Session:
         out = np.zeros((sh.layers, n, sh.experts_used), dtype=np.int32)
         call("spm_session_routes", self._h, n, out.ctypes.data_as(C.POINTER(C.c_int32)))
         return out
+
+    def ep_handle(self) -> bytes:
+        """This rank's exchange buffer as a 64-byte CUDA IPC handle."""
+        buf = (C.c_uint8 * 64)()
+        call("spm_session_ep_handle", self._h, buf)
+        return bytes(buf)
+
+    def ep_connect(self, handles: list[bytes]) -> None:
+        """Map every rank's exchange buffer (handles in rank order)."""
+        blob = b"".join(handles)
+        if len(blob) != 64 * len(handles):
+            raise SpmError(-1, "CUDA IPC handles are 64 bytes")
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        call("spm_session_ep_connect", self._h, buf)
 
     def launches_per_step(self, n: int) -> int:
         v = C.c_int32()

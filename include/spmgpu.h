@@ -169,6 +169,26 @@ spm_status spm_session_stream(const spm_session* s, void** cuda_stream);
 spm_status spm_session_set_graphs(spm_session* s, int32_t enable);
 /* Routes of the last step (MoE): layers x n x experts_used expert ids. */
 spm_status spm_session_routes(const spm_session* s, int32_t n, int32_t* routes_host);
+/* ---- expert parallel (routed models over 1..8 GPUs of one node) ----
+ * Replaces the reference's single-process expert loop
+ * (spm-granite-moe/src/layout.rs:244-304) across GPUs: each rank runs the
+ * whole step for every client (attention, router, norms and LM head are
+ * replicated), but computes only the experts e with e % world == rank and
+ * writes their output rows over NVLink into every rank's exchange buffer;
+ * the combine waits (1 s bound) for all ranks' rows and sums them in
+ * ascending expert id, so every rank's results equal the single-GPU ones.
+ * Open the model with spm_model_open_ep (only this rank's experts are
+ * uploaded; the file is memory-mapped, so ranks share its pages), create
+ * the session, exchange the 64-byte handles of spm_session_ep_handle between
+ * the ranks (rank order), and pass them all to spm_session_ep_connect before
+ * the first step. */
+spm_status spm_model_open_ep(const char* gguf_path, const char* order_path, const spm_model_cfg* cfg, int device,
+                             int32_t world, int32_t rank, spm_model** out);
+spm_status spm_model_open_memory_ep(const uint8_t* gguf, uint64_t len, const char* order_text,
+                                    const spm_model_cfg* cfg, int device, int32_t world, int32_t rank,
+                                    spm_model** out);
+spm_status spm_session_ep_handle(spm_session* s, void* handle64);
+spm_status spm_session_ep_connect(spm_session* s, const void* handles);
 /* Kernel launches issued by one step at client count n (graph nodes). */
 spm_status spm_session_launches_per_step(spm_session* s, int32_t n, int32_t* launches);
 
