@@ -9,7 +9,10 @@ CUDA events on the session stream and L2 flushed (a 256 MiB write) between
 steps; `e2e` runs the same ticks through spm_decode_step with host token
 buffers (H2D of the tokens and D2H of the greedy picks inside the timed
 region).  Dense models do not shard: N>1 runs N independent replicas
-("replicas only"), and the slowest rank's time sets the job time.
+("replicas only"), and the slowest rank's time sets the job time.  Routed
+(MoE) models over N>1 GPUs run expert parallel: one job serving the same
+clients on every rank, experts dealt round robin over the ranks, expert
+outputs exchanged over NVLink ("scaling": "strong").
 """
 from __future__ import annotations
 
@@ -38,6 +41,8 @@ def _args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--gguf-dir", default="/dev/shm",
+                    help="where rank 0 writes the synthetic GGUF that expert-parallel ranks memory-map")
     ap.add_argument("--layers", type=int, default=0,
                     help="keep only the first N layers (small cases for profiler captures; not a bench number)")
     return ap.parse_args()
@@ -207,8 +212,27 @@ def main():
     import emufpga_b200 as eb
 
     w, recipe, prompts = _workload(a.workload, a.layers)
-    img = eb.synth_gguf(recipe)
-    model = eb.Model(img, recipe.shape, device=local)
+    # Routed models over several GPUs run expert parallel: every rank serves
+    # all clients, and the experts are dealt round robin over the ranks (one
+    # job; tokens/s is not multiplied by the ranks).  Dense models run one
+    # replica per GPU.  Rank 0 writes the synthetic GGUF once; every rank
+    # memory-maps it.
+    ep_mode = world > 1 and recipe.shape.moe
+    img = None
+    if ep_mode:
+        from emufpga_b200 import ep as eplib
+
+        path = f"{a.gguf_dir}/emufpga_{a.workload}_{recipe.shape.layers}l.gguf"
+        if rank == 0:
+            img = eb.synth_gguf(recipe)
+            if not os.path.exists(path) or os.path.getsize(path) != len(img):
+                img.tofile(path + ".part")
+                os.replace(path + ".part", path)
+        pg.barrier()
+        model = eb.Model.from_file(path, recipe.shape, device=local, ep=(world, rank))
+    else:
+        img = eb.synth_gguf(recipe)
+        model = eb.Model(img, recipe.shape, device=local)
     n = len(prompts)
     longest = max(len(p) for p in prompts)
     total_ticks = longest + w["steps"] - 1
@@ -217,6 +241,9 @@ def main():
         steps = max(1, total_ticks - warm)
     context = longest + w["steps"] + 1
     sess = eb.Session(model, n, context)
+    if ep_mode:
+        eplib.connect(sess)
+        pg.barrier()
     stream = torch.cuda.ExternalStream(sess.cuda_stream, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     argmax = torch.zeros(n, dtype=torch.int32, device=dev)
@@ -257,6 +284,9 @@ def main():
 
     # ---- end to end through the C ABI with host buffers (e2e) ----
     sess = eb.Session(model, n, context)
+    if ep_mode:
+        eplib.connect(sess)
+        pg.barrier()
     toks = [p[0] for p in prompts]
     for t in range(warm):
         best, _ = sess.decode_step(toks)
@@ -283,7 +313,13 @@ def main():
     roof = None
     if rank == 0:
         roof = gemv_roofline(eb, model, n, dev)
-    tokens_total = n * steps * world
+    tokens_total = n * steps * (1 if ep_mode else world)
+    ranks_agree = None
+    if ep_mode:
+        # every rank serves the same clients: their greedy tokens must agree
+        got = [None] * world
+        pg.all_gather_object(got, list(toks))
+        ranks_agree = all(g == got[0] for g in got)
     step_bytes = model.weight_bytes
     if recipe.shape.moe:
         step_bytes += statistics.mean(touched) * expert_bytes(model)
@@ -294,10 +330,11 @@ def main():
         line = {
             "metric": "decode tokens/s", "value": tokens_total / (job_ms / 1e3), "unit": "tokens/s",
             "n_gpus": world, "steps": steps, "warmup": warm, "ms_per_step": job_ms / steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong" if ep_mode else "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,0.02) weights quantized by this repo's encoder, uniform prompt ids)",
             "config": {"workload": a.workload, "model": w["recipe"], "clients": n, "prompts": w["prompts"],
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "parallelism": (f"expert parallel x{world}" if ep_mode else f"replicas x{world}")
+                       if world > 1 else "single GPU",
                        "weight_bytes_per_step": round(step_bytes),
                        "l2": "flushed between timed steps (256 MiB write)"},
             "weight_stream_gbs": step_bytes * steps / (job_ms / 1e3) / 1e9,
@@ -315,10 +352,12 @@ def main():
                                 "launches_per_sweep": roof["launches"]}
         if recipe.shape.moe:
             line["config"]["experts_touched_per_step"] = statistics.mean(touched)
+        if ep_mode:
+            line["config"]["ranks_tokens_agree"] = ranks_agree
         if a.layers:
             line["config"]["layers_kept"] = recipe.shape.layers
             line["invalid"] = "model truncated with --layers (profiling case, not a bench number)"
-        if not a.no_cpu_baseline:
+        if not a.no_cpu_baseline and img is not None:
             line["cpu_baseline"] = cpu_baseline(recipe, img, prompts, w["steps"], a.cpu_seconds)
         print(json.dumps(line), flush=True)
     if pg:
