@@ -567,7 +567,7 @@ void enqueue_step(spm_session* s, int n) {
             gx.xmode = 1;
             run_gemv(m, gx, m->streams[L.down_exps].pk.dtype, st, pdl);
             CUDA_OK(launch_combine(plan, outs, d, s->states, d, n, K, part[0], m->world > 1 ? &ex : nullptr, st, pdl));
-            parts = n;
+            parts = combine_parts(d, n);
             continue;
         }
         GemvLaunch gu = gemv_base(m, L.gate, s->states, n);

@@ -42,6 +42,11 @@ static int occupancy(uint32_t dtype, const GemvLaunch& L, bool dual, int threads
 // group that has a tile), then two CTAs per SM, then smaller groups.
 GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms, int per_fixed) {
     const uint32_t U = L.cols / 32;
+    // work items: tiles, or pairs of tiles for the tensor-core loop (whose
+    // warps take whole units of a slot instead of lanes taking units)
+    const bool pair = L.tc && !dual;
+    const uint32_t work = pair ? (L.total_tiles + 1) / 2 : L.total_tiles;
+    if (per_fixed > 0 && pair) per_fixed = (per_fixed + 1) / 2;
     GemvGeometry best{};
     double best_score = -1.0;
     for (int per_sm = 2; per_sm >= 1; per_sm--) {
@@ -50,12 +55,14 @@ GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms, int per_fixe
         int grid = 0, per = per_fixed;
         if (per_fixed <= 0) {
             const uint32_t gcap = uint32_t(sms) * uint32_t(per_sm);
-            grid = int(std::min(L.total_tiles, gcap));
-            per = int((L.total_tiles + grid - 1) / grid);
+            grid = int(std::min(work, gcap));
+            per = int((work + grid - 1) / grid);
         }
         for (int gw = 1; gw <= Wmax; gw *= 2) {
-            if ((U + 32 * gw - 1) / (32 * gw) > 4 && gw < Wmax) continue;  // at most four units per lane
-            const double busy = std::min(1.0, double(U) / (32.0 * gw));
+            // at most four units per lane (tensor cores: 32 units per warp)
+            const uint32_t lanes = L.tc ? uint32_t(gw) : 32u * gw, most = L.tc ? 32u : 4u;
+            if ((U + lanes - 1) / lanes > most && gw < Wmax) continue;
+            const double busy = std::min(1.0, double(U) / double(lanes));
             for (int G = Wmax / gw; G >= 1; G--) {
                 const int W = G * gw;
                 if (W < 4) break;
@@ -76,13 +83,20 @@ GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms, int per_fixe
     // one CTA per SM, all its warps on each tile, as many slots as fit
     int ns = kMaxSlots;
     while (ns > 1 && smem_bytes(L, dual, ns, kMaxWarps) > kSmemMax) ns--;
-    const int grid = per_fixed > 0 ? 0 : int(std::min(L.total_tiles, uint32_t(sms)));
+    const int grid = per_fixed > 0 ? 0 : int(std::min(work, uint32_t(sms)));
     return GemvGeometry{grid, ns, kMaxWarps, kMaxWarps, smem_bytes(L, dual, ns, kMaxWarps)};
+}
+
+// The launch fields that follow from the block type and client count.
+static void prepare(GemvLaunch& L, uint32_t dtype) {
+    L.xrec = unit_bytes(int(dtype));
+    L.tc = use_tc(int(dtype), L.n) && !L.plan ? 1 : 0;
 }
 
 // Geometry with the grid capped at the CTAs that can be resident at once
 // (one wave), so that every CTA starts streaming immediately.
-static GemvGeometry geometry_resident(uint32_t dtype, const GemvLaunch& L, bool dual, int sms) {
+static GemvGeometry geometry_resident(uint32_t dtype, GemvLaunch L, bool dual, int sms) {
+    prepare(L, dtype);
     GemvGeometry g = gemv_geometry(L, dual, sms);
     const int occ = occupancy(dtype, L, dual, g.warps * 32, g.smem);
     const int cap = occ * sms;
@@ -92,6 +106,7 @@ static GemvGeometry geometry_resident(uint32_t dtype, const GemvLaunch& L, bool 
 
 static cudaError_t launch_one(uint32_t dtype, GemvLaunch L, int sms, cudaStream_t s, bool pdl, int grid) {
     const bool dual = L.job[0].b != nullptr;
+    prepare(L, dtype);
     GemvGeometry g;
     if (L.plan) {
         // expert mode: a CTA owns 1/expert_chunks of one active expert's tiles
@@ -119,9 +134,10 @@ cudaError_t launch_gemv(uint32_t dtype, GemvLaunch L, int sms, cudaStream_t s, b
     if (grid_out) *grid_out = 0;
     if (L.total_tiles == 0) return cudaSuccess;
     if (L.n < 1 || L.n > 8 || (L.cols & 31)) return cudaErrorInvalidValue;
-    L.xrec = unit_bytes(int(dtype));
+    prepare(L, dtype);
     GemvLaunch one = L;
     one.n = 1;
+    prepare(one, dtype);
     if (smem_bytes(one, dual, 1, kMaxWarps) > kSmemMax) return cudaErrorInvalidValue;
     const bool fits = smem_bytes(L, dual, 1, kMaxWarps) <= kSmemMax;
     if (L.plan && !fits) return cudaErrorInvalidValue;

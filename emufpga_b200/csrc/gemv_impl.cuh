@@ -71,6 +71,20 @@ constexpr int kAuxPrefetch = 1024;        // residual values prefetched per CTA,
 constexpr uint32_t kDigitUnit = 112;
 constexpr uint32_t kFloatUnit = 144;
 inline __host__ __device__ constexpr uint32_t unit_bytes(int enc) { return enc == SPM_F32 ? kFloatUnit : kDigitUnit; }
+// Q8_0 with four or more clients takes the tensor-core inner loop
+// (gemv_tc.cuh); its records hold each plane's words in the order
+// 0,4,1,5,2,6,3,7, so that lane t reads words t and 4+t with one 8-byte load.
+// (Measured on B200: for the K-quants, whose scales change every 16 or 32
+// values, the per-sub-block fp32 work that the tensor-core loop keeps on the
+// CUDA cores makes it no faster than the dp4a loop even with eight clients.)
+inline __host__ __device__ constexpr bool use_tc(int enc, int n) { return enc == SPM_Q8_0 && n >= 4; }
+// Bytes between two clients' records.  The tensor-core loop reads 8 bytes of
+// eight clients at once; a stride of 32 mod 128 bytes keeps them on
+// different banks.
+inline __host__ __device__ uint32_t client_stride(uint32_t unit, bool tc, uint32_t units) {
+    const uint32_t c = units * unit;
+    return tc ? c + (160u - c % 128u) % 128u : c;
+}
 
 struct XUnit {
     uint32_t d[3][8];  // digit planes, word k = values 4k..4k+3
@@ -340,6 +354,8 @@ __device__ __forceinline__ void unit_f32(const RowRef (&rr)[R], uint32_t u, cons
     }
 }
 
+#include "gemv_tc.cuh"
+
 template <int ENC, int NC, int R, class XT>
 __device__ __forceinline__ void unit_dot(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XT& X,
                                          float (&acc)[R][NC]) {
@@ -422,16 +438,23 @@ struct Shape {
 // staged activations and, for groups of several warps, one 32-float record
 // of partial sums per slot, warp of the group and matrix.
 inline size_t smem_bytes(const GemvLaunch& L, bool dual, int slots, int group_warps) {
-    const size_t slot = size_t(L.tile_bytes) * (dual ? 2 : 1);
-    const size_t xb = size_t(L.n) * (L.cols / 32) * L.xrec;
-    const size_t pb = group_warps > 1 ? size_t(slots) * group_warps * (dual ? 2 : 1) * 128 : 0;
+    // a tensor-core slot holds eight rows: two tiles, or one gate/up pair
+    const size_t slot = size_t(L.tile_bytes) * (dual || L.tc ? 2 : 1);
+    const size_t xb = size_t(L.n) * client_stride(L.xrec, L.tc != 0, L.cols / 32);
+    const size_t rec = L.tc ? 256 : (dual ? 256 : 128);  // partials per slot and warp
+    const size_t pb = group_warps > 1 ? size_t(slots) * group_warps * rec : 0;
     return slot * size_t(slots) + xb + pb;
 }
 
-template <int ENC, int NC, bool DUAL>
+// TCX: the tensor-core loop is allowed (dense Q8_0 launches of four or more
+// clients; expert launches skip client slots without data, which only the
+// CUDA-core loop can).
+template <int ENC, int NC, bool DUAL, bool TCX>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_constant__ GemvLaunch L) {
     using S = Shape<NC, DUAL>;
     constexpr int VR = S::VR, PASSES = S::PASSES, M = S::M, NCP = S::NCP, V = S::V, SH = S::SH;
+    constexpr bool TC = TCX && use_tc(ENC, NC);
+    constexpr bool PAIR = TC && !DUAL;  // slot = two consecutive tiles
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[kMaxSlots], ready[kMaxSlots];
     __shared__ float nscale[8];
@@ -475,27 +498,44 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
         }
     } else {
         const uint32_t T = L.total_tiles, Gd = gridDim.x;
-        t0 = uint32_t(uint64_t(T) * blockIdx.x / Gd);
-        t1 = uint32_t(uint64_t(T) * (blockIdx.x + 1) / Gd);
+        if (PAIR) {  // whole pairs per CTA
+            const uint32_t P = (T + 1) / 2;
+            t0 = 2 * uint32_t(uint64_t(P) * blockIdx.x / Gd);
+            t1 = min(T, 2 * uint32_t(uint64_t(P) * (blockIdx.x + 1) / Gd));
+        } else {
+            t0 = uint32_t(uint64_t(T) * blockIdx.x / Gd);
+            t1 = uint32_t(uint64_t(T) * (blockIdx.x + 1) / Gd);
+        }
         if (threadIdx.x < 8) {
             xrows[threadIdx.x] = int(threadIdx.x);
             yrows[threadIdx.x] = int(threadIdx.x);
             srows[threadIdx.x] = L.c0 + int(threadIdx.x);
         }
     }
-    const uint32_t nt = t1 - t0, NS = uint32_t(L.slots);
+    const uint32_t nt = PAIR ? (t1 - t0 + 1) / 2 : t1 - t0, NS = uint32_t(L.slots);  // work items (slots to fill)
     // Slot s belongs to group s % G alone (NS is a multiple of G), so each
     // group waits for its slots' phases in order and refills them itself.
     if (NS % uint32_t(G) != 0 || NS > uint32_t(kMaxSlots) || W * 32 != int(blockDim.x) || G * gw != W) {
         if (threadIdx.x == 0) flag(L.status, 3);
         return;
     }
-    const uint32_t tile_bytes = L.tile_bytes, slot_bytes = tile_bytes * M;
+    const uint32_t tile_bytes = L.tile_bytes, slot_bytes = tile_bytes * (DUAL || PAIR ? 2u : 1u);
     constexpr uint32_t XREC = unit_bytes(ENC);
-    const uint32_t U = L.cols >> 5, cstride = U * XREC;
+    const uint32_t U = L.cols >> 5, cstride = client_stride(XREC, TC, U);
     const uint32_t xoff = NS * slot_bytes, poff = xoff + NC * cstride;  // activations, group partials
     auto issue = [&](uint32_t i) {
-        const uint32_t s = i % NS, g = t0 + i;
+        const uint32_t s = i % NS;
+        if (PAIR) {
+            const uint32_t g = t0 + 2 * i, h = g + 1 < t1 ? 2u : 1u;
+            mbar_expect_tx(&full[s], tile_bytes * h);
+            for (uint32_t k = 0; k < h; k++) {
+                const GemvJob& J = pick(jobs, L.njobs, g + k);
+                bulk_g2s(smem + size_t(s) * slot_bytes + k * tile_bytes, J.a + size_t(g + k - J.tile_begin) * tile_bytes,
+                         tile_bytes, &full[s]);
+            }
+            return;
+        }
+        const uint32_t g = t0 + i;
         const GemvJob& J = pick(jobs, L.njobs, g);
         const size_t off = size_t(g - J.tile_begin) * tile_bytes;
         mbar_expect_tx(&full[s], slot_bytes);
@@ -611,8 +651,14 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
             if (live) {
                 uint8_t* rec = smem + xoff + c * cstride + u * XREC;
 #pragma unroll
-                for (int j = 0; j < 3; j++)
-                    *reinterpret_cast<uint4*>(rec + j * 32 + half * 16) = make_uint4(dw[j][0], dw[j][1], dw[j][2], dw[j][3]);
+                for (int j = 0; j < 3; j++) {
+                    if (TC) {  // word w = 4*half + k at (w % 4) * 8 + (w / 4) * 4
+#pragma unroll
+                        for (int k = 0; k < 4; k++) *reinterpret_cast<uint32_t*>(rec + j * 32 + k * 8 + half * 4) = dw[j][k];
+                    } else {
+                        *reinterpret_cast<uint4*>(rec + j * 32 + half * 16) = make_uint4(dw[j][0], dw[j][1], dw[j][2], dw[j][3]);
+                    }
+                }
                 if (half == 0)
                     *reinterpret_cast<uint4*>(rec + 96) =
                         make_uint4(__float_as_uint(sc), __float_as_uint(hsum), __float_as_uint(other), 0u);
@@ -620,9 +666,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
         }
     }
     // the residual rows this CTA will add to (EPI_ADD)
-    const bool aux_pre = nt * kTileRows * NC <= uint32_t(kAuxPrefetch);
+    const uint32_t ntiles = t1 - t0;
+    const bool aux_pre = ntiles * kTileRows * NC <= uint32_t(kAuxPrefetch);
     if (aux_pre)
-        for (uint32_t idx = threadIdx.x; idx < nt * kTileRows * NC; idx += blockDim.x) {
+        for (uint32_t idx = threadIdx.x; idx < ntiles * kTileRows * NC; idx += blockDim.x) {
             const uint32_t i = idx / (kTileRows * NC), e = (idx / NC) % kTileRows, c = idx % NC;
             const GemvJob& J = pick(jobs, L.njobs, t0 + i);
             const uint32_t row = (t0 + i - J.tile_begin) * kTileRows + e;
@@ -642,99 +689,188 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     // of the group's first warp holds index l = row * NCP + client of the
     // tile, all passes together (4 * NCP <= 32).
     const bool finisher = gw == 1 ? (lane & ((1 << SH) - 1)) == 0 : (wig == 0 && lane < kTileRows * NCP);
-    const int fc = (gw == 1 ? (lane >> SH) : lane) % NCP;
+    const int fc = TC ? (lane >> 2) : (gw == 1 ? (lane >> SH) : lane) % NCP;
     const float fscale = (L.gain && fc < NC) ? nscale[fc] : 1.0f;
     float* part = reinterpret_cast<float*>(smem + poff);  // [NS][gw][M][32]
     float sq = 0.f;
     const uint32_t B = L.cols >> 8;
-    for (uint32_t i = uint32_t(grp); i < nt; i += uint32_t(G)) {
-        const uint32_t s = i % NS, par = (i / NS) & 1;
-        if (!mbar_wait(&full[s], par)) {
-            flag(L.status, 2);
-            break;
-        }
-        const uint32_t g = t0 + i;
-        const GemvJob& J = pick(jobs, L.njobs, g);
-        const uint32_t tile = g - J.tile_begin;
-        const uint32_t tb = smem_s + s * slot_bytes;
-        // row e of the tile, client fc: scale, activation, residual, store
-        auto finish = [&](uint32_t e, float a, float b) {
-            const uint32_t grow = tile * kTileRows + e;
-            const uint32_t row = grow - rbase;
-            if (fc < n_act && grow < J.rows && row < rlim) {
-                float r = a * fscale;
-                if constexpr (DUAL) r = silu_mul(r, b * fscale);
-                if (J.epi == EPI_ADD)
-                    r = (aux_pre ? auxs[(i * kTileRows + e) * NC + fc] : J.aux[size_t(yrows[fc]) * J.aux_stride + row]) + r;
-                if (L.ep_peer_y) {
-                    for (int p = 0; p < L.world; p++) ep_y[p][size_t(yrows[fc]) * J.y_stride + row] = r;
-                } else {
-                    J.y[size_t(yrows[fc]) * J.y_stride + row] = r;
-                }
-                sq = fmaf(r, r, sq);
+    if constexpr (TC) {
+        // lane (g, t): client g; codes of slot row g; totals of slot rows 2t, 2t+1
+        const int g = lane >> 2, t = lane & 3;
+        TcLane z;
+        z.t = t;
+        z.cl = g < n_act;
+        z.xa = smem_s + xoff + uint32_t(g < NC ? g : 0) * cstride;
+        for (uint32_t i = uint32_t(grp); i < nt; i += uint32_t(G)) {
+            const uint32_t s = i % NS, par = (i / NS) & 1;
+            if (!mbar_wait(&full[s], par)) {
+                flag(L.status, 2);
+                break;
             }
-        };
-#pragma unroll 1
-        for (int pass = 0; pass < PASSES; pass++) {
-            RowRef rr[M * VR];
-#pragma unroll
-            for (int m = 0; m < M; m++)
-#pragma unroll
-                for (int v = 0; v < VR; v++) {
-                    const uint32_t r = uint32_t(pass * VR + v);
-                    rr[m * VR + v] = RowRef{tb + uint32_t(m) * tile_bytes, r * U, r * B};
-                }
-            float acc[M * VR][NC];
-            zero(acc);
-#pragma unroll 1
-            for (uint32_t u = uint32_t(wig * 32 + lane); u < U; u += uint32_t(gw * 32))
-                unit_dot<ENC, NC, M * VR, XT>(rr, u, L, X, acc);
-            if (gw == 1 && pass + 1 == PASSES) {
+            const uint32_t tb = smem_s + s * slot_bytes;
+            const uint32_t tA = PAIR ? t0 + 2 * i : t0 + i;
+            z.cb = tb + uint32_t(g >> 2) * tile_bytes;
+            z.cr = uint32_t(g & 3);
+            z.ob = tb + uint32_t(t >> 1) * tile_bytes;
+            z.or0 = uint32_t(2 * t) & 3u;
+            float acc[2] = {0.f, 0.f};
+            tc_slot<ENC>(z, uint32_t(wig), uint32_t(gw), L, acc);
+            bool fin = true;
+            if (gw == 1) {
                 // this warp alone read the slot: refill it
                 __syncwarp();
                 if (lane == 0 && i + NS < nt) {
                     fence_proxy_async();
                     issue(i + NS);
                 }
+            } else {
+                // the group's first warp adds the warps' totals in warp order
+                float* pr = part + (s * gw + wig) * 64 + g * 8 + 2 * t;
+                pr[0] = acc[0];
+                pr[1] = acc[1];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ready[s]);
+                fin = wig == 0;
+                if (fin) {
+                    if (!mbar_wait(&ready[s], par)) {
+                        flag(L.status, 4);
+                        break;
+                    }
+                    acc[0] = acc[1] = 0.f;
+                    for (int w = 0; w < gw; w++) {
+                        const float* q = part + (s * gw + w) * 64 + g * 8 + 2 * t;
+                        acc[0] += q[0];
+                        acc[1] += q[1];
+                    }
+                    __syncwarp();
+                    if (lane == 0 && i + NS < nt) {
+                        fence_proxy_async();
+                        issue(i + NS);
+                    }
+                }
             }
-            float red[M][V];
+            if (fin) {
+                // a gate/up pair: lanes t < 2 hold gate rows 2t, 2t+1, lanes t + 2 the up rows
+                float b0 = 0.f, b1 = 0.f;
+                if (DUAL) {
+                    b0 = __shfl_down_sync(0xffffffffu, acc[0], 2);
+                    b1 = __shfl_down_sync(0xffffffffu, acc[1], 2);
+                }
+                const uint32_t tile = PAIR ? tA + uint32_t(t >> 1) : tA;
+                if ((!DUAL || t < 2) && tile < t1) {
+                    const GemvJob& J = pick(jobs, L.njobs, tile);
 #pragma unroll
-            for (int m = 0; m < M; m++)
-#pragma unroll
-                for (int v = 0; v < VR; v++)
-#pragma unroll
-                    for (int c = 0; c < NCP; c++) red[m][v * NCP + c] = c < NC ? acc[m * VR + v][c] : 0.f;
-#pragma unroll
-            for (int m = 0; m < M; m++) XRed<V, 16>::run(red[m], lane);
-            if (gw == 1) {
-                if (finisher) finish(uint32_t(pass * VR + (lane >> SH) / NCP), red[0][0], red[M - 1][0]);
-            } else if ((lane & ((1 << SH) - 1)) == 0) {
-#pragma unroll
-                for (int m = 0; m < M; m++) part[((s * gw + wig) * M + m) * 32 + pass * V + (lane >> SH)] = red[m][0];
+                    for (int j = 0; j < 2; j++) {
+                        const uint32_t e = uint32_t(2 * t + j) & 3u;
+                        const uint32_t grow = (tile - J.tile_begin) * kTileRows + e;
+                        const uint32_t row = grow - rbase;
+                        if (g < n_act && grow < J.rows && row < rlim) {
+                            float r = acc[j] * fscale;
+                            if constexpr (DUAL) r = silu_mul(r, (j ? b1 : b0) * fscale);
+                            if (J.epi == EPI_ADD)
+                                r = (aux_pre ? auxs[((tile - t0) * kTileRows + e) * NC + g]
+                                             : J.aux[size_t(yrows[g]) * J.aux_stride + row]) + r;
+                            if (L.ep_peer_y) {
+                                for (int p = 0; p < L.world; p++) ep_y[p][size_t(yrows[g]) * J.y_stride + row] = r;
+                            } else {
+                                J.y[size_t(yrows[g]) * J.y_stride + row] = r;
+                            }
+                            sq = fmaf(r, r, sq);
+                        }
+                    }
+                }
             }
         }
-        if (gw > 1) {
-            // partials are in; the group's first warp adds them in warp order
-            // once every warp has arrived, then refills the slot
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&ready[s]);
-            if (wig == 0) {
-                if (!mbar_wait(&ready[s], par)) {
-                    flag(L.status, 4);
-                    break;
-                }
-                if (finisher) {
-                    float a = 0.f, b = 0.f;
-                    for (int w = 0; w < gw; w++) {
-                        a += part[((s * gw + w) * M + 0) * 32 + lane];
-                        if (M > 1) b += part[((s * gw + w) * M + M - 1) * 32 + lane];
+    } else {
+    for (uint32_t i = uint32_t(grp); i < nt; i += uint32_t(G)) {
+            const uint32_t s = i % NS, par = (i / NS) & 1;
+            if (!mbar_wait(&full[s], par)) {
+                flag(L.status, 2);
+                break;
+            }
+            const uint32_t g = t0 + i;
+            const GemvJob& J = pick(jobs, L.njobs, g);
+            const uint32_t tile = g - J.tile_begin;
+            const uint32_t tb = smem_s + s * slot_bytes;
+            // row e of the tile, client fc: scale, activation, residual, store
+            auto finish = [&](uint32_t e, float a, float b) {
+                const uint32_t grow = tile * kTileRows + e;
+                const uint32_t row = grow - rbase;
+                if (fc < n_act && grow < J.rows && row < rlim) {
+                    float r = a * fscale;
+                    if constexpr (DUAL) r = silu_mul(r, b * fscale);
+                    if (J.epi == EPI_ADD)
+                        r = (aux_pre ? auxs[(i * kTileRows + e) * NC + fc] : J.aux[size_t(yrows[fc]) * J.aux_stride + row]) + r;
+                    if (L.ep_peer_y) {
+                        for (int p = 0; p < L.world; p++) ep_y[p][size_t(yrows[fc]) * J.y_stride + row] = r;
+                    } else {
+                        J.y[size_t(yrows[fc]) * J.y_stride + row] = r;
                     }
-                    finish(uint32_t(lane / NCP), a, b);
+                    sq = fmaf(r, r, sq);
                 }
+            };
+    #pragma unroll 1
+            for (int pass = 0; pass < PASSES; pass++) {
+                RowRef rr[M * VR];
+    #pragma unroll
+                for (int m = 0; m < M; m++)
+    #pragma unroll
+                    for (int v = 0; v < VR; v++) {
+                        const uint32_t r = uint32_t(pass * VR + v);
+                        rr[m * VR + v] = RowRef{tb + uint32_t(m) * tile_bytes, r * U, r * B};
+                    }
+                float acc[M * VR][NC];
+                zero(acc);
+    #pragma unroll 1
+                for (uint32_t u = uint32_t(wig * 32 + lane); u < U; u += uint32_t(gw * 32))
+                    unit_dot<ENC, NC, M * VR, XT>(rr, u, L, X, acc);
+                if (gw == 1 && pass + 1 == PASSES) {
+                    // this warp alone read the slot: refill it
+                    __syncwarp();
+                    if (lane == 0 && i + NS < nt) {
+                        fence_proxy_async();
+                        issue(i + NS);
+                    }
+                }
+                float red[M][V];
+    #pragma unroll
+                for (int m = 0; m < M; m++)
+    #pragma unroll
+                    for (int v = 0; v < VR; v++)
+    #pragma unroll
+                        for (int c = 0; c < NCP; c++) red[m][v * NCP + c] = c < NC ? acc[m * VR + v][c] : 0.f;
+    #pragma unroll
+                for (int m = 0; m < M; m++) XRed<V, 16>::run(red[m], lane);
+                if (gw == 1) {
+                    if (finisher) finish(uint32_t(pass * VR + (lane >> SH) / NCP), red[0][0], red[M - 1][0]);
+                } else if ((lane & ((1 << SH) - 1)) == 0) {
+    #pragma unroll
+                    for (int m = 0; m < M; m++) part[((s * gw + wig) * M + m) * 32 + pass * V + (lane >> SH)] = red[m][0];
+                }
+            }
+            if (gw > 1) {
+                // partials are in; the group's first warp adds them in warp order
+                // once every warp has arrived, then refills the slot
                 __syncwarp();
-                if (lane == 0 && i + NS < nt) {
-                    fence_proxy_async();
-                    issue(i + NS);
+                if (lane == 0) mbar_arrive(&ready[s]);
+                if (wig == 0) {
+                    if (!mbar_wait(&ready[s], par)) {
+                        flag(L.status, 4);
+                        break;
+                    }
+                    if (finisher) {
+                        float a = 0.f, b = 0.f;
+                        for (int w = 0; w < gw; w++) {
+                            a += part[((s * gw + w) * M + 0) * 32 + lane];
+                            if (M > 1) b += part[((s * gw + w) * M + M - 1) * 32 + lane];
+                        }
+                        finish(uint32_t(lane / NCP), a, b);
+                    }
+                    __syncwarp();
+                    if (lane == 0 && i + NS < nt) {
+                        fence_proxy_async();
+                        issue(i + NS);
+                    }
                 }
             }
         }
@@ -760,9 +896,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     }
 }
 
-template <int ENC, int NC, bool DUAL>
+template <int ENC, int NC, bool DUAL, bool TCX>
 cudaError_t configure(int* occ, int threads, size_t smem) {
-    auto kern = gemv_stream<ENC, NC, DUAL>;
+    auto kern = gemv_stream<ENC, NC, DUAL, TCX>;
     static unsigned configured = 0;  // bit per device
     int dev = 0;
     cudaGetDevice(&dev);
@@ -778,9 +914,9 @@ cudaError_t configure(int* occ, int threads, size_t smem) {
     return cudaSuccess;
 }
 
-template <int ENC, int NC, bool DUAL>
+template <int ENC, int NC, bool DUAL, bool TCX>
 cudaError_t launch_t(const GemvLaunch& L, int grid, int threads, size_t smem, cudaStream_t s, bool pdl) {
-    cudaError_t e = configure<ENC, NC, DUAL>(nullptr, threads, smem);
+    cudaError_t e = configure<ENC, NC, DUAL, TCX>(nullptr, threads, smem);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -792,16 +928,32 @@ cudaError_t launch_t(const GemvLaunch& L, int grid, int threads, size_t smem, cu
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_stream<ENC, NC, DUAL>, L);
+    return cudaLaunchKernelEx(&cfg, gemv_stream<ENC, NC, DUAL, TCX>, L);
 }
 
-// All instantiations for one block type (compiled in gemv_<type>.cu).
+// All instantiations for one block type (compiled in gemv_<type>.cu).  Dense
+// launches with L.tc set by the host take the tensor-core loop; expert
+// launches never do.
+template <int ENC, int NC, bool DUAL>
+cudaError_t launch_n(const GemvLaunch& L, int grid, int threads, size_t smem, cudaStream_t s, bool pdl) {
+    if constexpr (use_tc(ENC, NC))
+        if (L.tc) return launch_t<ENC, NC, DUAL, true>(L, grid, threads, smem, s, pdl);
+    return launch_t<ENC, NC, DUAL, false>(L, grid, threads, smem, s, pdl);
+}
+
+template <int ENC, int NC, bool DUAL>
+cudaError_t configure_n(const GemvLaunch& L, int* occ, int threads, size_t smem) {
+    if constexpr (use_tc(ENC, NC))
+        if (L.tc) return configure<ENC, NC, DUAL, true>(occ, threads, smem);
+    return configure<ENC, NC, DUAL, false>(occ, threads, smem);
+}
+
 template <int ENC>
 cudaError_t launch_enc(const GemvLaunch& L, bool dual, int grid, int threads, size_t smem, cudaStream_t s, bool pdl) {
-#define SPM_NC(n)                                                                 \
-    case n:                                                                       \
-        return dual ? launch_t<ENC, n, true>(L, grid, threads, smem, s, pdl)      \
-                    : launch_t<ENC, n, false>(L, grid, threads, smem, s, pdl);
+#define SPM_NC(n)                                                                   \
+    case n:                                                                         \
+        return dual ? launch_n<ENC, n, true>(L, grid, threads, smem, s, pdl)        \
+                    : launch_n<ENC, n, false>(L, grid, threads, smem, s, pdl);
     switch (L.n) {
         SPM_NC(1) SPM_NC(2) SPM_NC(3) SPM_NC(4) SPM_NC(5) SPM_NC(6) SPM_NC(7) SPM_NC(8)
         default: return cudaErrorInvalidValue;
@@ -814,9 +966,10 @@ template <int ENC>
 int occupancy_enc(const GemvLaunch& L, bool dual, int threads, size_t smem) {
     int occ = 0;
     cudaError_t e = cudaErrorInvalidValue;
-#define SPM_NC(n)                                                                                          \
-    case n:                                                                                                \
-        e = dual ? configure<ENC, n, true>(&occ, threads, smem) : configure<ENC, n, false>(&occ, threads, smem); \
+#define SPM_NC(n)                                                                                        \
+    case n:                                                                                              \
+        e = dual ? configure_n<ENC, n, true>(L, &occ, threads, smem)                                     \
+                 : configure_n<ENC, n, false>(L, &occ, threads, smem);                                  \
         break;
     switch (L.n) {
         SPM_NC(1) SPM_NC(2) SPM_NC(3) SPM_NC(4) SPM_NC(5) SPM_NC(6) SPM_NC(7) SPM_NC(8)

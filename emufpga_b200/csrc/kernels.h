@@ -41,6 +41,7 @@ struct GemvLaunch {
     int32_t slots;        // shared-memory ring slots, a multiple of the groups (set by gemv_geometry)
     int32_t group_warps;  // warps that share a tile (set by gemv_geometry)
     uint32_t xrec;        // bytes of one client's staged 32-value unit (set by launch_gemv)
+    int32_t tc;           // tensor-core inner loop (integer codes, four or more clients; set by launch_gemv)
     int32_t c0;           // index of client 0 of this launch in the sum-of-squares arrays
     // Expert mode (plan != nullptr): one job over a [experts][rows][cols]
     // tensor; CTA b works on active expert b / expert_chunks of the plan and

@@ -132,9 +132,14 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
     pdl_trigger();
 }
 
-__global__ void __launch_bounds__(256) combine_kernel(const MoePlan* plan, const float* out, int out_stride,
-                                                      float* states, int width, int K, float* sumsq, MoeExchange ex) {
-    __shared__ float red[33];
+// Grid (column chunk, client): a CTA of kCombineCols threads adds one column
+// per thread, and writes its chunk's sum of squares as its own part.
+constexpr int kCombineCols = 128;
+
+__global__ void __launch_bounds__(kCombineCols) combine_kernel(const MoePlan* plan, const float* out, int out_stride,
+                                                               float* states, int width, int K, float* sumsq,
+                                                               MoeExchange ex) {
+    __shared__ float red[kCombineCols / 32];
     pdl_wait();
     if (ex.world > 1) {
         // every rank's expert rows for this layer are in place once all flags are up
@@ -153,37 +158,28 @@ __global__ void __launch_bounds__(256) combine_kernel(const MoePlan* plan, const
         __syncthreads();
         out += (E & 1u) * ex.xstride;
     }
-    const int i = blockIdx.x;
-    const float norm = plan->norm[i];
-    // the client's expert outputs in ascending expert id, and their weights
-    const float* lanes[kMoeMaxUsed];
-    float p[kMoeMaxUsed];
-#pragma unroll
-    for (int j = 0; j < kMoeMaxUsed; j++) {
-        lanes[j] = j < K ? out + size_t(plan->slot_a[i][j] * kMoeMaxClients + plan->slot_pos[i][j]) * out_stride : out;
-        p[j] = j < K ? plan->slot_p[i][j] : 0.f;
-    }
+    const int i = blockIdx.y, col = blockIdx.x * kCombineCols + threadIdx.x;
     float ss = 0.f;
-    for (int col = threadIdx.x; col < width; col += blockDim.x) {
+    if (col < width) {
+        const float norm = plan->norm[i];
         float total = 0.f;
-#pragma unroll
-        for (int j = 0; j < kMoeMaxUsed; j++)
-            if (j < K) total = total + __fdiv_rn(__fmul_rn(__ldcg(lanes[j] + col), p[j]), norm);
+        for (int j = 0; j < K; j++) {
+            const float* lane = out + size_t(plan->slot_a[i][j] * kMoeMaxClients + plan->slot_pos[i][j]) * out_stride;
+            total = total + __fdiv_rn(__fmul_rn(__ldcg(lane + col), plan->slot_p[i][j]), norm);
+        }
         const float v = states[size_t(i) * width + col] + total;
         states[size_t(i) * width + col] = v;
-        ss = fmaf(v, v, ss);
+        ss = v * v;
     }
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
     pdl_trigger();
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < 8) {
         float t = 0.f;
-        for (int w = 0; w < int(blockDim.x >> 5); w++) t += red[w];
-        red[32] = t;
+        for (int w = 0; w < kCombineCols / 32; w++) t += red[w];
+        sumsq[(size_t(i) * gridDim.x + blockIdx.x) * 8 + threadIdx.x] = int(threadIdx.x) == i ? t : 0.f;
     }
-    __syncthreads();
-    if (threadIdx.x < 8) sumsq[i * 8 + threadIdx.x] = threadIdx.x == i ? red[32] : 0.f;
 }
 
 cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, cudaStream_t s, bool pdl, void** args) {
@@ -210,12 +206,15 @@ cudaError_t launch_route(const float* logits, const float* bias, int n, int expe
     return launch_pdl(reinterpret_cast<const void*>(route_kernel), dim3(1), dim3(256), s, pdl, args);
 }
 
+int combine_parts(int width, int n) { return ((width + kCombineCols - 1) / kCombineCols) * n; }
+
 cudaError_t launch_combine(const MoePlan* plan, const float* out, int out_stride, float* states, int width, int n,
                            int used, float* sumsq, const MoeExchange* ex, cudaStream_t s, bool pdl) {
     MoeExchange e = ex ? *ex : MoeExchange{};
     if (!ex) e.world = 1;
     void* args[] = {&plan, &out, &out_stride, &states, &width, &used, &sumsq, &e};
-    return launch_pdl(reinterpret_cast<const void*>(combine_kernel), dim3(n), dim3(256), s, pdl, args);
+    return launch_pdl(reinterpret_cast<const void*>(combine_kernel), dim3((width + kCombineCols - 1) / kCombineCols, n),
+                      dim3(kCombineCols), s, pdl, args);
 }
 
 }  // namespace spm

@@ -44,7 +44,9 @@ struct MoeExchange {
 
 // states[i] += sum over client i's experts in ascending id of
 // (out[a][pos] * p) / norm  (spm-granite-moe/src/layout.rs:283-302); also the
-// sum of squares of each new state row (sumsq[i*8 + c] = c == i ? ss : 0).
+// sums of squares of the new state rows, in combine_parts(width, n) parts:
+// part (i * chunks + chunk) holds [c == i ? ss : 0 for c < 8].
+int combine_parts(int width, int n);
 cudaError_t launch_combine(const MoePlan* plan, const float* out, int out_stride, float* states, int width, int n,
                            int used, float* sumsq, const MoeExchange* ex, cudaStream_t s, bool pdl);
 
