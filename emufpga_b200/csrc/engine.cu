@@ -523,8 +523,12 @@ void enqueue_step(spm_session* s, int n) {
             add_job(gr, m, L.router, nullptr, s->moe_logits, E, nullptr, 0, EPI_STORE);
             run_gemv(m, gr, m->streams[L.router].pk.dtype, st, pdl);
             MoePlan* plan = s->plans + l;
-            CUDA_OK(launch_route(s->moe_logits, L.bias >= 0 ? m->gains + L.bias : nullptr, n, E, K, plan, st, pdl));
-            const int chunks_gu = std::max(1, std::min(eff / kTileRows, (2 * m->sms + s->moe_max_active - 1) / s->moe_max_active));
+            CUDA_OK(launch_route(s->moe_logits, L.bias >= 0 ? m->gains + L.bias : nullptr, n, E, K, m->world, m->rank,
+                                 plan, st, pdl));
+            // active experts of this rank, at most: the expert launches split
+            // each over enough chunks to give every SM two CTAs
+            const int local_max = std::min(s->moe_max_active, (E + m->world - 1) / m->world);
+            const int chunks_gu = std::max(1, std::min(eff / kTileRows, (2 * m->sms + local_max - 1) / local_max));
             GemvLaunch ge = gemv_base(m, L.gate_exps, s->states, kMoeMaxClients);
             ge.status = s->status;
             ge.world = m->world;
@@ -532,13 +536,13 @@ void enqueue_step(spm_session* s, int n) {
             norm_in(ge, L.ffn_norm, 1);
             add_job(ge, m, L.gate_exps, m->tiles(L.up_exps), s->moe_act, eff, nullptr, 0, EPI_SWIGLU);
             ge.plan = plan;
-            ge.expert_max = s->moe_max_active;
+            ge.expert_max = local_max;
             ge.expert_chunks = chunks_gu;
             ge.expert_tiles = uint32_t(eff / kTileRows);
             ge.total_tiles = ge.expert_tiles;
             ge.xmode = 0;
             run_gemv(m, ge, m->streams[L.gate_exps].pk.dtype, st, pdl);
-            const int chunks_d = std::max(1, std::min(d / kTileRows, (2 * m->sms + s->moe_max_active - 1) / s->moe_max_active));
+            const int chunks_d = std::max(1, std::min(d / kTileRows, (2 * m->sms + local_max - 1) / local_max));
             GemvLaunch gx = gemv_base(m, L.down_exps, s->moe_act, kMoeMaxClients);
             gx.status = s->status;
             gx.world = m->world;
@@ -560,7 +564,7 @@ void enqueue_step(spm_session* s, int n) {
             }
             add_job(gx, m, L.down_exps, nullptr, s->moe_out, d, nullptr, 0, EPI_STORE);
             gx.plan = plan;
-            gx.expert_max = s->moe_max_active;
+            gx.expert_max = local_max;
             gx.expert_chunks = chunks_d;
             gx.expert_tiles = uint32_t(d / kTileRows);
             gx.total_tiles = gx.expert_tiles;

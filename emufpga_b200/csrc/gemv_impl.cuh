@@ -472,13 +472,14 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     if (L.plan) {
         // expert mode: the plan comes from the previous kernel
         pdl_wait();
-        const int a = int(blockIdx.x) / L.expert_chunks, chunk = int(blockIdx.x) % L.expert_chunks;
-        if (a >= L.plan->count || (L.world > 1 && L.plan->expert[a] % L.world != L.rank)) {
-            // no active expert here, or another rank's
+        // CTA b works on chunk b % chunks of this rank's active expert b / chunks
+        const int la = int(blockIdx.x) / L.expert_chunks, chunk = int(blockIdx.x) % L.expert_chunks;
+        if (la >= L.plan->nlocal) {
             pdl_trigger();
             if (L.ep_done && threadIdx.x == 0) ep_arrive(L);
             return;
         }
+        const int a = L.plan->local[la];
         if (L.ep_peer_y && threadIdx.x < uint32_t(L.world)) {
             const uint32_t E = *L.ep_step * uint32_t(L.ep_layers) + uint32_t(L.ep_layer) + 1;
             ep_y[threadIdx.x] = L.ep_peer_y[(E & 1u) * L.world + threadIdx.x];

@@ -14,7 +14,7 @@ __device__ __forceinline__ int32_t total_key(float f) {
 
 // One CTA.  Warp i routes client i; then the plan is built over experts.
 __global__ void __launch_bounds__(256) route_kernel(const float* logits, const float* bias, int n, int E, int K,
-                                                    MoePlan* plan) {
+                                                    int world, int rank, MoePlan* plan) {
     __shared__ float prob[kMoeMaxClients][kMoeMaxExperts];
     __shared__ int32_t sel[kMoeMaxClients][kMoeMaxUsed];
     __shared__ int32_t cnt[kMoeMaxExperts], base[kMoeMaxExperts];
@@ -99,6 +99,19 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
             run += __popc(m);
         }
         if (lane == 0) plan->count = run;
+    } else if (warp == 1) {
+        // this rank's active experts, by the same ballot scan
+        int run = 0, local = 0;
+        for (int e0 = 0; e0 < E; e0 += 32) {
+            const int e = e0 + lane;
+            const bool act = e < E && cnt[e] > 0;
+            const bool own = act && e % world == rank;
+            const uint32_t ma = __ballot_sync(0xffffffffu, act), mo = __ballot_sync(0xffffffffu, own);
+            if (own) plan->local[local + __popc(mo & ((1u << lane) - 1u))] = run + __popc(ma & ((1u << lane) - 1u));
+            run += __popc(ma);
+            local += __popc(mo);
+        }
+        if (lane == 0) plan->nlocal = local;
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -197,12 +210,13 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, cudaStream_t s, bo
 
 }  // namespace
 
-cudaError_t launch_route(const float* logits, const float* bias, int n, int experts, int used, MoePlan* plan,
-                         cudaStream_t s, bool pdl) {
+cudaError_t launch_route(const float* logits, const float* bias, int n, int experts, int used, int world, int rank,
+                         MoePlan* plan, cudaStream_t s, bool pdl) {
     if (n < 1 || n > kMoeMaxClients || experts < 1 || experts > kMoeMaxExperts || used < 1 || used > kMoeMaxUsed ||
         used > experts)
         return cudaErrorInvalidValue;
-    void* args[] = {&logits, &bias, &n, &experts, &used, &plan};
+    if (world < 1 || rank < 0 || rank >= world) return cudaErrorInvalidValue;
+    void* args[] = {&logits, &bias, &n, &experts, &used, &world, &rank, &plan};
     return launch_pdl(reinterpret_cast<const void*>(route_kernel), dim3(1), dim3(256), s, pdl, args);
 }
 

@@ -23,12 +23,16 @@ struct MoePlan {
     int32_t slot_pos[kMoeMaxClients][kMoeMaxUsed];       // position among that expert's clients
     float slot_p[kMoeMaxClients][kMoeMaxUsed];           // routing probability
     float norm[kMoeMaxClients];                          // sum of the selected probabilities
+    // the active experts this rank computes (expert parallel: e % world ==
+    // rank; one GPU: all), as active indices ascending
+    int32_t nlocal;
+    int32_t local[kMoeMaxExperts];
 };
 
 // Softmax over (logits + bias), top-`used` (descending, ties to the lower id),
 // renormaliser, and the plan (spm-granite-moe/src/moe.rs:17-35, math.rs:23-39).
-cudaError_t launch_route(const float* logits, const float* bias, int n, int experts, int used, MoePlan* plan,
-                         cudaStream_t s, bool pdl);
+cudaError_t launch_route(const float* logits, const float* bias, int n, int experts, int used, int world, int rank,
+                         MoePlan* plan, cudaStream_t s, bool pdl);
 // Expert parallel combine: before reading the expert outputs, wait until
 // every rank has raised its flag for this layer (flag value E = *step *
 // layers + layer + 1, in flags[(E & 1) * 64 + rank]); the outputs are in the
