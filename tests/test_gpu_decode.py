@@ -273,3 +273,20 @@ def test_qwen3_30b_shape_two_layers_matches_the_oracle(cuda):
         assert best == [O.argmax_last(want[i]) for i in range(n)]
     sess.close()
     m.close()
+
+
+def test_continuous_batching_matches_the_oracle_served_alone(cuda, models):
+    """Requests join free slots mid-flight and leave when done: each one's
+    tokens equal the oracle's for that request served alone."""
+    from emufpga_b200.scheduler import Request, serve_continuous
+
+    r, img, m, om = models("qwen3-q6_k")
+    v = r.shape.vocab
+    reqs = [Request(configs.prompt_tokens(50 + i, 0, ln, v), new, arr)
+            for i, (ln, new, arr) in enumerate([(3, 6, 0), (5, 4, 0), (2, 7, 1), (4, 5, 3), (6, 3, 4), (1, 8, 9)])]
+    sess = eb.Session(m, 3, 24)
+    got = serve_continuous(sess, reqs)
+    sess.close()
+    for q, g in zip(reqs, got):
+        want, _ = om.serve([list(q.prompt)], q.max_new)
+        assert g == want[0]
