@@ -232,13 +232,28 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     float* qs = sm;                         // group * hd
     float* kn = qs + group * hd;            // hd (new key)
     float* vn = kn + hd;                    // hd (new value)
-    float* kv = vn + hd;                    // kSub * ld (staged keys, then values)
-    float* sc = kv + kSub * ld;             // group * kChunk scores
+    float* kv = vn + hd;                    // kSub * ld (staged keys; values of later passes)
+    float* vb = kv + kSub * ld;             // kSub * ld (values of the first pass)
+    float* sc = vb + kSub * ld;             // group * kChunk scores
     float* red = sc + group * kAttnChunk;   // 64
-    pdl_wait();
+    // The position and the cached rows before it come from earlier steps, so
+    // the first pass's keys and values are fetched before waiting for the
+    // kernel that produces this step's q, k, v.
     const int pos = P.pos[i];
     const int p0 = chunk * P.chunk;
     const int p1 = min(pos + 1, p0 + P.chunk);
+    const size_t base = (size_t(i) * P.layers + P.layer) * P.context * size_t(kvw) + size_t(kvh) * hd;
+    float* kc = P.kcache + base;
+    float* vc = P.vcache + base;
+    {
+        const int pre = max(0, min(min(pos, p1), p0 + kSub) - p0);  // cached rows of the first pass
+        for (int t = threadIdx.x; t < pre * (hd / 4); t += kAttnThreads) {
+            const int p = t / (hd / 4), c4 = t % (hd / 4);
+            *reinterpret_cast<float4*>(kv + p * ld + 4 * c4) = *reinterpret_cast<const float4*>(kc + size_t(p0 + p) * kvw + 4 * c4);
+            *reinterpret_cast<float4*>(vb + p * ld + 4 * c4) = *reinterpret_cast<const float4*>(vc + size_t(p0 + p) * kvw + 4 * c4);
+        }
+    }
+    pdl_wait();
     const float* qg = P.q + size_t(i) * qw + size_t(kvh) * group * hd;
     for (int t = threadIdx.x; t < group * hd; t += kAttnThreads) qs[t] = qg[t];
     for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
@@ -282,13 +297,14 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         rope_pair(x[j], x[j + half], cs.x, cs.y, llama);
     }
     __syncthreads();
-    const size_t base = (size_t(i) * P.layers + P.layer) * P.context * size_t(kvw) + size_t(kvh) * hd;
-    float* kc = P.kcache + base;
-    float* vc = P.vcache + base;
     if (pos >= p0 && pos < p0 + P.chunk)
         for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
             kc[size_t(pos) * kvw + t] = kn[t];
             vc[size_t(pos) * kvw + t] = vn[t];
+            if (pos < p0 + kSub) {  // the new row of the first pass
+                kv[(pos - p0) * ld + t] = kn[t];
+                vb[(pos - p0) * ld + t] = vn[t];
+            }
         }
     __syncthreads();
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(float(hd)));
@@ -297,12 +313,15 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     // ---- scores for this chunk, all heads of the group ----
     for (int b0 = 0; b0 < npos; b0 += kSub) {
         const int nb = min(kSub, npos - b0);
-        for (int t = threadIdx.x; t < nb * (hd / 4); t += kAttnThreads) {
-            const int p = t / (hd / 4), c4 = t % (hd / 4);
-            const float4 v = *reinterpret_cast<const float4*>(kc + size_t(p0 + b0 + p) * kvw + 4 * c4);
-            *reinterpret_cast<float4*>(kv + p * ld + 4 * c4) = v;
+        if (b0 > 0) {  // the first pass was staged before the wait
+            __syncthreads();
+            for (int t = threadIdx.x; t < nb * (hd / 4); t += kAttnThreads) {
+                const int p = t / (hd / 4), c4 = t % (hd / 4);
+                const float4 v = *reinterpret_cast<const float4*>(kc + size_t(p0 + b0 + p) * kvw + 4 * c4);
+                *reinterpret_cast<float4*>(kv + p * ld + 4 * c4) = v;
+            }
+            __syncthreads();
         }
-        __syncthreads();
         for (int t = threadIdx.x; t < nb * group; t += kAttnThreads) {
             const int p = t % nb, h = t / nb;
             const float* q = qs + h * hd;
@@ -346,19 +365,22 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     float acc[4] = {0.f, 0.f, 0.f, 0.f};  // (head, dim) pairs t, t+256, ... (group*hd <= 1024)
     for (int b0 = 0; b0 < npos; b0 += kSub) {
         const int nb = min(kSub, npos - b0);
-        for (int t = threadIdx.x; t < nb * (hd / 4); t += kAttnThreads) {
-            const int p = t / (hd / 4), c4 = t % (hd / 4);
-            *reinterpret_cast<float4*>(kv + p * ld + 4 * c4) =
-                *reinterpret_cast<const float4*>(vc + size_t(p0 + b0 + p) * kvw + 4 * c4);
+        const float* vv = b0 == 0 ? vb : kv;
+        if (b0 > 0) {
+            for (int t = threadIdx.x; t < nb * (hd / 4); t += kAttnThreads) {
+                const int p = t / (hd / 4), c4 = t % (hd / 4);
+                *reinterpret_cast<float4*>(kv + p * ld + 4 * c4) =
+                    *reinterpret_cast<const float4*>(vc + size_t(p0 + b0 + p) * kvw + 4 * c4);
+            }
+            __syncthreads();
         }
-        __syncthreads();
 #pragma unroll
         for (int r = 0; r < 4; r++) {
             const int t = threadIdx.x + r * kAttnThreads;
             if (t < group * hd) {
                 const int h = t / hd, dd = t % hd;
                 float a = acc[r];
-                for (int p = 0; p < nb; p++) a = fmaf(sc[h * kAttnChunk + b0 + p], kv[p * ld + dd], a);
+                for (int p = 0; p < nb; p++) a = fmaf(sc[h * kAttnChunk + b0 + p], vv[p * ld + dd], a);
                 acc[r] = a;
             }
         }
@@ -423,8 +445,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
 
 size_t attention_smem(const AttnParams& P) {
     const int group = P.heads / P.kv_heads;
-    return (size_t(group) * P.head_dim + 2 * P.head_dim + size_t(kSub) * (P.head_dim + 4) + size_t(group) * kAttnChunk +
-            64) * sizeof(float);
+    return (size_t(group) * P.head_dim + 2 * P.head_dim + 2 * size_t(kSub) * (P.head_dim + 4) +
+            size_t(group) * kAttnChunk + 64) * sizeof(float);
 }
 
 static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
