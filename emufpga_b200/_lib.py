@@ -85,6 +85,9 @@ PROTOTYPES = {
                                       C.POINTER(_P)]),
     "spm_model_open_memory_ep": (C.c_int32, [_P, C.c_uint64, C.c_char_p, C.POINTER(ModelCfg), C.c_int, C.c_int32,
                                              C.c_int32, C.POINTER(_P)]),
+    "spm_pack_image": (C.c_int32, [_P, C.c_uint64, C.c_char_p, C.POINTER(ModelCfg), C.c_char_p]),
+    "spm_image_probe": (C.c_int32, [C.c_char_p, _U64P, C.POINTER(C.c_int32)]),
+    "spm_model_open_image": (C.c_int32, [C.c_char_p, C.c_int, C.POINTER(_P)]),
     "spm_session_ep_handle": (C.c_int32, [_P, _P]),
     "spm_session_ep_connect": (C.c_int32, [_P, _P]),
     "spm_streamed": (C.c_int32, [_P, C.c_int32, _P, C.c_int32, _P, _P]),

@@ -229,85 +229,49 @@ void check_order(const Order& o, const Gguf& g) {
         if (!wanted.count(t.name)) fail(SPM_E_STREAM, t.name + ": in the checkpoint but not named in the order file");
 }
 
-spm_model* open_model(const uint8_t* buf, uint64_t len, const std::string* order_text, const spm_model_cfg* cfg,
-                      int device, int world = 1, int rank = 0) {
-    Gguf g = gguf_parse(buf, len);
-    std::unique_ptr<spm_model> m(new spm_model());
-    m->cfg = cfg ? *cfg : cfg_from_gguf(g);
-    check_cfg(m->cfg);
-    const spm_model_cfg& c = m->cfg;
-    Order order = parse_order(order_text ? *order_text : default_order(c, g.find("blk.0.exp_probs_b.bias") != nullptr));
-    check_order(order, g);
-
-    int ndev = 0;
-    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) fail(SPM_E_NO_DEVICE, "no CUDA device is visible");
-    if (device < 0 || device >= ndev) fail(SPM_E_ARG, "device index out of range");
-    m->device = device;
-    if (world < 1 || world > 8 || rank < 0 || rank >= world) fail(SPM_E_ARG, "expert parallel: 1 to 8 ranks");
-    if (world > 1 && !is_moe(c)) fail(SPM_E_ARG, "expert parallel needs a routed (MoE) model");
-    m->world = world;
-    m->rank = rank;
-    CUDA_OK(cudaSetDevice(device));
-    CUDA_OK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, device));
-
-    // Streams in consumption order; 1-D tensors are resident gains.
+// Host-side description of a model: streams in consumption order with their
+// packed shapes and offsets in the device image, the norm gains, and the
+// per-layer stream and gain indices.  Built from a GGUF (describe) or read
+// from a packed image file (read_image); no GPU involved.
+struct ModelDesc {
+    spm_model_cfg cfg{};
+    std::vector<StreamDesc> streams;
     std::vector<float> gains;
-    std::map<std::string, int64_t> gain_off;
     std::map<std::string, int> stream_of;
-    uint64_t off = 0;
-    auto add_names = [&](const std::vector<std::string>& names, bool rotating) {
-        for (auto& n : names) {
-            const GgufTensor* t = g.find(n);
-            if (t->dims.size() == 1) {
-                if (t->dtype != SPM_F32 && t->dtype != SPM_F16)
-                    fail(SPM_E_ENCODING, n + ": 1-D tensors must be F32 or F16");
-                gain_off[n] = int64_t(gains.size());
-                std::vector<float> v(t->dims[0]);
-                decode_blocks(t->dtype, buf + t->offset, t->len, v.data());
-                gains.insert(gains.end(), v.begin(), v.end());
-                while (gains.size() % 4) gains.push_back(0.f);
-                continue;
-            }
-            StreamDesc s;
-            s.name = n;
-            s.rotating = rotating;
-            uint64_t rows = 1;
-            for (size_t d = 1; d < t->dims.size(); d++) rows *= t->dims[d];
-            s.experts = t->dims.size() > 2 ? t->dims[2] : 1;
-            s.pk = packed_shape(t->dtype, rows, t->dims[0]);
-            s.pk.offset = off;
-            off += (s.pk.tiles * s.pk.tile_bytes + 255) & ~uint64_t(255);
-            stream_of[n] = int(m->streams.size());
-            m->streams.push_back(s);
-        }
-    };
-    add_names(order.rotating, true);
-    add_names(order.resident, false);
-    m->image_bytes = off;
+    std::map<std::string, std::pair<int64_t, uint64_t>> gain_of;  // offset in gains, length
+    std::vector<LayerIdx> layers;
+    int embed = -1, head = -1;
+    int64_t output_norm = -1;
+    uint64_t image_bytes = 0, weight_bytes = 0;
+};
 
+// Layer indices, shape and encoding checks, and the weight bytes of a sweep,
+// from the stream and gain tables.
+void index_layers(ModelDesc& d) {
+    const spm_model_cfg& c = d.cfg;
     auto need_stream = [&](const std::string& n) {
-        auto it = stream_of.find(n);
-        if (it == stream_of.end()) fail(SPM_E_STREAM, "missing tensor " + n);
+        auto it = d.stream_of.find(n);
+        if (it == d.stream_of.end()) fail(SPM_E_STREAM, "missing tensor " + n);
         return it->second;
     };
     auto need_gain = [&](const std::string& n, uint64_t count) {
-        auto it = gain_off.find(n);
-        if (it == gain_off.end()) fail(SPM_E_STREAM, "missing tensor " + n);
-        if (g.find(n)->dims[0] != count) fail(SPM_E_ARG, n + " has the wrong length");
-        return it->second;
+        auto it = d.gain_of.find(n);
+        if (it == d.gain_of.end()) fail(SPM_E_STREAM, "missing tensor " + n);
+        if (it->second.second != count) fail(SPM_E_ARG, n + " has the wrong length");
+        return it->second.first;
     };
     auto check_shape = [&](int idx, uint64_t rows, uint64_t cols) {
-        const StreamDesc& s = m->streams[idx];
+        const StreamDesc& s = d.streams[idx];
         if (s.pk.rows != rows || s.pk.cols != cols)
             fail(SPM_E_ARG, s.name + ": shape " + std::to_string(s.pk.rows) + "x" + std::to_string(s.pk.cols) +
                                 " does not match the model (" + std::to_string(rows) + "x" + std::to_string(cols) + ")");
         return idx;
     };
     const uint64_t qw = uint64_t(c.heads) * c.head_dim, kvw = uint64_t(c.kv_heads) * c.head_dim;
-    m->layers.resize(c.layers);
+    d.layers.assign(c.layers, LayerIdx{});
     for (uint32_t l = 0; l < c.layers; l++) {
         const std::string p = "blk." + std::to_string(l) + ".";
-        LayerIdx& L = m->layers[l];
+        LayerIdx& L = d.layers[l];
         L.q = check_shape(need_stream(p + "attn_q.weight"), qw, c.hidden);
         L.k = check_shape(need_stream(p + "attn_k.weight"), kvw, c.hidden);
         L.v = check_shape(need_stream(p + "attn_v.weight"), kvw, c.hidden);
@@ -326,74 +290,170 @@ spm_model* open_model(const uint8_t* buf, uint64_t len, const std::string* order
             L.gate_exps = check_shape(need_stream(p + "ffn_gate_exps.weight"), uint64_t(c.experts) * c.expert_ff, c.hidden);
             L.up_exps = check_shape(need_stream(p + "ffn_up_exps.weight"), uint64_t(c.experts) * c.expert_ff, c.hidden);
             L.down_exps = check_shape(need_stream(p + "ffn_down_exps.weight"), uint64_t(c.experts) * c.hidden, c.expert_ff);
-            if (gain_off.count(p + "exp_probs_b.bias")) L.bias = need_gain(p + "exp_probs_b.bias", c.experts);
+            if (d.gain_of.count(p + "exp_probs_b.bias")) L.bias = need_gain(p + "exp_probs_b.bias", c.experts);
         } else {
             L.gate = check_shape(need_stream(p + "ffn_gate.weight"), c.intermediate, c.hidden);
             L.up = check_shape(need_stream(p + "ffn_up.weight"), c.intermediate, c.hidden);
             L.down = check_shape(need_stream(p + "ffn_down.weight"), c.hidden, c.intermediate);
-            if (m->streams[L.gate].pk.dtype != m->streams[L.up].pk.dtype)
+            if (d.streams[L.gate].pk.dtype != d.streams[L.up].pk.dtype)
                 fail(SPM_E_ENCODING, p + "ffn_gate and ffn_up must share an encoding");
         }
-        if (m->streams[L.q].pk.dtype != m->streams[L.k].pk.dtype || m->streams[L.q].pk.dtype != m->streams[L.v].pk.dtype)
+        if (d.streams[L.q].pk.dtype != d.streams[L.k].pk.dtype || d.streams[L.q].pk.dtype != d.streams[L.v].pk.dtype)
             fail(SPM_E_ENCODING, p + "attn_q/k/v must share an encoding");
     }
-    m->embed = check_shape(need_stream("token_embd.weight"), c.vocab, c.hidden);
-    m->head = c.tied ? m->embed : check_shape(need_stream("output.weight"), c.vocab, c.hidden);
-    m->output_norm = need_gain("output_norm.weight", c.hidden);
-    if (m->streams[m->embed].pk.dtype == SPM_F32 && c.hidden % 32) fail(SPM_E_ARG, "bad embedding width");
-
+    d.embed = check_shape(need_stream("token_embd.weight"), c.vocab, c.hidden);
+    d.head = c.tied ? d.embed : check_shape(need_stream("output.weight"), c.vocab, c.hidden);
+    d.output_norm = need_gain("output_norm.weight", c.hidden);
+    if (d.streams[d.embed].pk.dtype == SPM_F32 && c.hidden % 32) fail(SPM_E_ARG, "bad embedding width");
     // StepReport::for_sweep (spm-batch/src/session.rs:263-278): descriptor
     // bytes of every matrix one step reads -- here the rotating streams plus
     // the LM head.  MoE steps read only the routed experts; their per-step
     // bytes are counted by the session.
-    for (auto& s : m->streams)
-        if (s.rotating && s.experts == 1) m->weight_bytes += s.pk.quant_bytes;
-    if (!m->streams[m->head].rotating) m->weight_bytes += m->streams[m->head].pk.quant_bytes;
+    d.weight_bytes = 0;
+    for (auto& s : d.streams)
+        if (s.rotating && s.experts == 1) d.weight_bytes += s.pk.quant_bytes;
+    if (!d.streams[d.head].rotating) d.weight_bytes += d.streams[d.head].pk.quant_bytes;
+}
 
-    // Upload: pack each matrix on the host (threads over matrices) and copy.
-    CUDA_OK(cudaMalloc(&m->image, std::max<uint64_t>(m->image_bytes, 256)));
+ModelDesc describe(const Gguf& g, const uint8_t* buf, const std::string* order_text, const spm_model_cfg* cfg) {
+    ModelDesc d;
+    d.cfg = cfg ? *cfg : cfg_from_gguf(g);
+    check_cfg(d.cfg);
+    Order order =
+        parse_order(order_text ? *order_text : default_order(d.cfg, g.find("blk.0.exp_probs_b.bias") != nullptr));
+    check_order(order, g);
+    // Streams in consumption order; 1-D tensors are resident gains.
+    uint64_t off = 0;
+    auto add_names = [&](const std::vector<std::string>& names, bool rotating) {
+        for (auto& n : names) {
+            const GgufTensor* t = g.find(n);
+            if (t->dims.size() == 1) {
+                if (t->dtype != SPM_F32 && t->dtype != SPM_F16)
+                    fail(SPM_E_ENCODING, n + ": 1-D tensors must be F32 or F16");
+                d.gain_of[n] = {int64_t(d.gains.size()), t->dims[0]};
+                std::vector<float> v(t->dims[0]);
+                decode_blocks(t->dtype, buf + t->offset, t->len, v.data());
+                d.gains.insert(d.gains.end(), v.begin(), v.end());
+                while (d.gains.size() % 4) d.gains.push_back(0.f);
+                continue;
+            }
+            StreamDesc s;
+            s.name = n;
+            s.rotating = rotating;
+            uint64_t rows = 1;
+            for (size_t k = 1; k < t->dims.size(); k++) rows *= t->dims[k];
+            s.experts = t->dims.size() > 2 ? t->dims[2] : 1;
+            s.pk = packed_shape(t->dtype, rows, t->dims[0]);
+            s.pk.offset = off;
+            off += (s.pk.tiles * s.pk.tile_bytes + 255) & ~uint64_t(255);
+            d.stream_of[n] = int(d.streams.size());
+            d.streams.push_back(s);
+        }
+    };
+    add_names(order.rotating, true);
+    add_names(order.resident, false);
+    d.image_bytes = off;
+    index_layers(d);
+    return d;
+}
+
+// Pack stream i of a GGUF-described model into host memory (all experts, or
+// with world > 1 only rank's, each at its own place).  Calls sink(offset in
+// the image, bytes, size) for every packed run.
+template <class Sink>
+void pack_stream(const ModelDesc& d, const Gguf& g, const uint8_t* buf, size_t i, int world, int rank,
+                 std::vector<uint8_t>& host, Sink&& sink) {
+    const StreamDesc& s = d.streams[i];
+    const GgufTensor* t = g.find(s.name);
+    if (world > 1 && s.experts > 1) {
+        // this rank's experts only; each is a whole run of tiles
+        const uint64_t er = s.pk.rows / s.experts;
+        Packed sub = packed_shape(s.pk.dtype, er, s.pk.cols);
+        if (sub.tile_bytes != s.pk.tile_bytes || sub.tiles * s.experts != s.pk.tiles)
+            fail(SPM_E_ARG, s.name + ": experts are not whole tiles");
+        const uint64_t src = t->len / s.experts;
+        host.resize(sub.tiles * sub.tile_bytes);
+        for (uint64_t e = uint64_t(rank); e < s.experts; e += uint64_t(world)) {
+            pack_matrix(sub, buf + t->offset + e * src, host.data());
+            sink(s.pk.offset + e * host.size(), host.data(), host.size());
+        }
+        return;
+    }
+    host.resize(s.pk.tiles * s.pk.tile_bytes);
+    pack_matrix(s.pk, buf + t->offset, host.data());
+    sink(s.pk.offset, host.data(), host.size());
+}
+
+// Runs f(i, worker) for i < count on up to 16 host threads; the first error wins.
+template <class F>
+void parallel_streams(size_t count, F&& f) {
     std::atomic<size_t> next{0};
     std::vector<std::string> errs(std::max(1u, std::min(16u, std::thread::hardware_concurrency())));
+    std::vector<int> codes(errs.size(), 0);
     auto worker = [&](size_t w) {
         try {
-            if (cudaSetDevice(device) != cudaSuccess) fail(SPM_E_CUDA, "cudaSetDevice failed");
-            std::vector<uint8_t> host;
             for (;;) {
-                size_t i = next.fetch_add(1);
-                if (i >= m->streams.size()) break;
-                const StreamDesc& s = m->streams[i];
-                const GgufTensor* t = g.find(s.name);
-                if (world > 1 && s.experts > 1) {
-                    // this rank's experts only; each is a whole run of tiles
-                    const uint64_t er = s.pk.rows / s.experts;
-                    Packed sub = packed_shape(s.pk.dtype, er, s.pk.cols);
-                    if (sub.tile_bytes != s.pk.tile_bytes || sub.tiles * s.experts != s.pk.tiles)
-                        fail(SPM_E_ARG, s.name + ": experts are not whole tiles");
-                    const uint64_t src = t->len / s.experts;
-                    host.resize(sub.tiles * sub.tile_bytes);
-                    for (uint64_t e = uint64_t(rank); e < s.experts; e += uint64_t(world)) {
-                        pack_matrix(sub, buf + t->offset + e * src, host.data());
-                        CUDA_OK(cudaMemcpy(m->image + s.pk.offset + e * host.size(), host.data(), host.size(),
-                                           cudaMemcpyHostToDevice));
-                    }
-                    continue;
-                }
-                host.resize(s.pk.tiles * s.pk.tile_bytes);
-                pack_matrix(s.pk, buf + t->offset, host.data());
-                CUDA_OK(cudaMemcpy(m->image + s.pk.offset, host.data(), host.size(), cudaMemcpyHostToDevice));
+                const size_t i = next.fetch_add(1);
+                if (i >= count) break;
+                f(i, w);
             }
         } catch (const Error& e) {
             errs[w] = e.msg;
+            codes[w] = e.code;
         }
     };
     std::vector<std::thread> pool;
     for (size_t w = 0; w < errs.size(); w++) pool.emplace_back(worker, w);
     for (auto& th : pool) th.join();
-    for (auto& e : errs)
-        if (!e.empty()) fail(SPM_E_CUDA, e);
-    CUDA_OK(cudaMalloc(&m->gains, std::max<size_t>(gains.size(), 4) * sizeof(float)));
-    CUDA_OK(cudaMemcpy(m->gains, gains.data(), gains.size() * sizeof(float), cudaMemcpyHostToDevice));
+    for (size_t w = 0; w < errs.size(); w++)
+        if (!errs[w].empty()) fail(codes[w], errs[w]);
+}
+
+// A model on `device` from its description: allocation, gains, and fill(m)
+// to put the packed tiles in place.
+template <class Fill>
+spm_model* make_model(ModelDesc&& d, int device, int world, int rank, Fill&& fill) {
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) fail(SPM_E_NO_DEVICE, "no CUDA device is visible");
+    if (device < 0 || device >= ndev) fail(SPM_E_ARG, "device index out of range");
+    if (world < 1 || world > 8 || rank < 0 || rank >= world) fail(SPM_E_ARG, "expert parallel: 1 to 8 ranks");
+    if (world > 1 && !is_moe(d.cfg)) fail(SPM_E_ARG, "expert parallel needs a routed (MoE) model");
+    std::unique_ptr<spm_model> m(new spm_model());
+    m->cfg = d.cfg;
+    m->device = device;
+    m->world = world;
+    m->rank = rank;
+    CUDA_OK(cudaSetDevice(device));
+    CUDA_OK(cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, device));
+    m->streams = std::move(d.streams);
+    m->layers = std::move(d.layers);
+    m->embed = d.embed;
+    m->head = d.head;
+    m->output_norm = d.output_norm;
+    m->image_bytes = d.image_bytes;
+    m->weight_bytes = d.weight_bytes;
+    CUDA_OK(cudaMalloc(&m->image, std::max<uint64_t>(m->image_bytes, 256)));
+    fill(m.get());
+    CUDA_OK(cudaMalloc(&m->gains, std::max<size_t>(d.gains.size(), 4) * sizeof(float)));
+    CUDA_OK(cudaMemcpy(m->gains, d.gains.data(), d.gains.size() * sizeof(float), cudaMemcpyHostToDevice));
     return m.release();
+}
+
+spm_model* open_model(const uint8_t* buf, uint64_t len, const std::string* order_text, const spm_model_cfg* cfg,
+                      int device, int world = 1, int rank = 0) {
+    Gguf g = gguf_parse(buf, len);
+    ModelDesc d = describe(g, buf, order_text, cfg);
+    ModelDesc keep = d;  // stream table for packing after make_model takes d
+    return make_model(std::move(d), device, world, rank, [&](spm_model* m) {
+        // pack each matrix on the host (threads over matrices) and copy
+        parallel_streams(keep.streams.size(), [&](size_t i, size_t) {
+            if (cudaSetDevice(device) != cudaSuccess) fail(SPM_E_CUDA, "cudaSetDevice failed");
+            std::vector<uint8_t> host;
+            pack_stream(keep, g, buf, i, world, rank, host, [&](uint64_t off, const uint8_t* p, size_t n) {
+                CUDA_OK(cudaMemcpy(m->image + off, p, n, cudaMemcpyHostToDevice));
+            });
+        });
+    });
 }
 
 // A GGUF file mapped read-only: ranks that open the same file share its
@@ -419,6 +479,168 @@ struct Mapped {
         if (p) munmap(const_cast<uint8_t*>(p), n);
     }
 };
+
+// ---- packed device image files ----
+// A model already packed for the device: the stream table, the norm gains,
+// then the tiles exactly as they sit in HBM, so that opening it is one
+// sequential read and upload.  Layout (little endian):
+//   "SPMIMG01", u64 data offset (4096-aligned), u64 image bytes, the
+//   spm_model_cfg, u32 streams { u16 name length, name, u32 dtype, u64 rows,
+//   cols, experts, u8 rotating, u64 tiles, tile bytes, u32 planes[4], u64
+//   offset, quant bytes }, u32 gains { u16 name length, name, u64 offset,
+//   length }, u64 floats, the floats; zeros up to the data offset; the image.
+constexpr char kImageMagic[8] = {'S', 'P', 'M', 'I', 'M', 'G', '0', '1'};
+constexpr uint64_t kImageAlign = 4096;
+
+struct ImgWriter {
+    std::vector<uint8_t> b;
+    template <class T>
+    void put(const T& v) {
+        const uint8_t* p = reinterpret_cast<const uint8_t*>(&v);
+        b.insert(b.end(), p, p + sizeof(T));
+    }
+    void str(const std::string& s) {
+        put(uint16_t(s.size()));
+        b.insert(b.end(), s.begin(), s.end());
+    }
+};
+
+struct ImgReader {
+    const uint8_t* p;
+    uint64_t n, at = 0;
+    template <class T>
+    T get() {
+        if (n - at < sizeof(T)) fail(SPM_E_TRUNCATED, "image header is truncated");
+        T v;
+        std::memcpy(&v, p + at, sizeof(T));
+        at += sizeof(T);
+        return v;
+    }
+    std::string str() {
+        const uint16_t k = get<uint16_t>();
+        if (n - at < k) fail(SPM_E_TRUNCATED, "image header is truncated");
+        std::string s(reinterpret_cast<const char*>(p + at), k);
+        at += k;
+        return s;
+    }
+};
+
+std::vector<uint8_t> image_header(const ModelDesc& d) {
+    ImgWriter w;
+    w.b.insert(w.b.end(), kImageMagic, kImageMagic + 8);
+    w.put(uint64_t(0));  // data offset, patched below
+    w.put(d.image_bytes);
+    w.put(d.cfg);
+    w.put(uint32_t(d.streams.size()));
+    for (const StreamDesc& s : d.streams) {
+        w.str(s.name);
+        w.put(s.pk.dtype);
+        w.put(s.pk.rows);
+        w.put(s.pk.cols);
+        w.put(s.experts);
+        w.put(uint8_t(s.rotating ? 1 : 0));
+        w.put(s.pk.tiles);
+        w.put(s.pk.tile_bytes);
+        for (int k = 0; k < 4; k++) w.put(s.pk.plane[k]);
+        w.put(s.pk.offset);
+        w.put(s.pk.quant_bytes);
+    }
+    w.put(uint32_t(d.gain_of.size()));
+    for (const auto& kv : d.gain_of) {
+        w.str(kv.first);
+        w.put(uint64_t(kv.second.first));
+        w.put(kv.second.second);
+    }
+    w.put(uint64_t(d.gains.size()));
+    for (float f : d.gains) w.put(f);
+    const uint64_t data = (w.b.size() + kImageAlign - 1) / kImageAlign * kImageAlign;
+    std::memcpy(w.b.data() + 8, &data, 8);
+    w.b.resize(data, 0);
+    return w.b;
+}
+
+// The description and data offset of an image file held in memory.
+ModelDesc read_image(const uint8_t* p, uint64_t n, uint64_t* data) {
+    if (n < 8 || std::memcmp(p, kImageMagic, 8) != 0) fail(SPM_E_STREAM, "not a packed image (bad magic)");
+    ImgReader r{p, n, 8};
+    ModelDesc d;
+    *data = r.get<uint64_t>();
+    d.image_bytes = r.get<uint64_t>();
+    d.cfg = r.get<spm_model_cfg>();
+    check_cfg(d.cfg);
+    const uint32_t ns = r.get<uint32_t>();
+    if (ns > 1u << 20) fail(SPM_E_STREAM, "image stream count is not plausible");
+    for (uint32_t i = 0; i < ns; i++) {
+        StreamDesc s;
+        s.name = r.str();
+        const uint32_t dtype = r.get<uint32_t>();
+        const uint64_t rows = r.get<uint64_t>(), cols = r.get<uint64_t>();
+        s.experts = r.get<uint64_t>();
+        s.rotating = r.get<uint8_t>() != 0;
+        Packed want = packed_shape(dtype, rows, cols);  // the layout this library packs
+        Packed got = want;
+        got.tiles = r.get<uint64_t>();
+        got.tile_bytes = r.get<uint64_t>();
+        for (int k = 0; k < 4; k++) got.plane[k] = r.get<uint32_t>();
+        got.offset = r.get<uint64_t>();
+        got.quant_bytes = r.get<uint64_t>();
+        if (got.tiles != want.tiles || got.tile_bytes != want.tile_bytes || got.quant_bytes != want.quant_bytes ||
+            std::memcmp(got.plane, want.plane, sizeof(want.plane)) != 0 || s.experts == 0 || rows % s.experts)
+            fail(SPM_E_STREAM, s.name + ": packed layout does not match this library");
+        if (got.offset > d.image_bytes || got.tiles * got.tile_bytes > d.image_bytes - got.offset)
+            fail(SPM_E_STREAM, s.name + ": outside the image");
+        s.pk = got;
+        if (!d.stream_of.emplace(s.name, int(d.streams.size())).second) fail(SPM_E_STREAM, "duplicate stream " + s.name);
+        d.streams.push_back(s);
+    }
+    const uint32_t ng = r.get<uint32_t>();
+    std::vector<std::pair<std::string, std::pair<int64_t, uint64_t>>> gains;
+    for (uint32_t i = 0; i < ng && i < (1u << 20); i++) {
+        std::string name = r.str();
+        const uint64_t off = r.get<uint64_t>(), len = r.get<uint64_t>();
+        gains.push_back({name, {int64_t(off), len}});
+    }
+    const uint64_t nf = r.get<uint64_t>();
+    if (nf > (n - r.at) / 4) fail(SPM_E_TRUNCATED, "image gains are truncated");
+    d.gains.resize(nf);
+    std::memcpy(d.gains.data(), p + r.at, nf * 4);
+    r.at += nf * 4;
+    for (auto& gk : gains) {
+        if (gk.second.first < 0 || uint64_t(gk.second.first) > nf || gk.second.second > nf - uint64_t(gk.second.first))
+            fail(SPM_E_STREAM, gk.first + ": gain outside the table");
+        d.gain_of[gk.first] = gk.second;
+    }
+    if (*data < r.at || *data % kImageAlign || *data > n || d.image_bytes > n - *data)
+        fail(SPM_E_TRUNCATED, "image data is truncated");
+    index_layers(d);
+    return d;
+}
+
+void write_image(const uint8_t* buf, uint64_t len, const std::string* order_text, const spm_model_cfg* cfg,
+                 const char* path) {
+    Gguf g = gguf_parse(buf, len);
+    ModelDesc d = describe(g, buf, order_text, cfg);
+    const std::vector<uint8_t> head = image_header(d);
+    const int fd = open(path, O_WRONLY | O_CREAT | O_TRUNC, 0644);
+    if (fd < 0) fail(SPM_E_STREAM, std::string(path) + ": cannot create");
+    struct Closer {
+        int fd;
+        ~Closer() { close(fd); }
+    } closer{fd};
+    auto put = [&](uint64_t off, const uint8_t* p, size_t n) {
+        while (n) {
+            const ssize_t k = pwrite(fd, p, n, off_t(off));
+            if (k <= 0) fail(SPM_E_STREAM, std::string(path) + ": write failed");
+            p += k, n -= size_t(k), off += uint64_t(k);
+        }
+    };
+    if (ftruncate(fd, off_t(head.size() + d.image_bytes)) != 0) fail(SPM_E_STREAM, std::string(path) + ": cannot size");
+    put(0, head.data(), head.size());
+    parallel_streams(d.streams.size(), [&](size_t i, size_t) {
+        std::vector<uint8_t> host;
+        pack_stream(d, g, buf, i, 1, 0, host, [&](uint64_t off, const uint8_t* p, size_t n) { put(head.size() + off, p, n); });
+    });
+}
 
 std::string read_file(const char* path) {
     std::ifstream f(path, std::ios::binary);
@@ -769,6 +991,36 @@ spm_status spm_model_open_memory_ep(const uint8_t* gguf, uint64_t len, const cha
     return guarded([&] {
         std::string order = order_text ? order_text : "";
         *out = open_model(gguf, len, order_text ? &order : nullptr, cfg, device, world, rank);
+    });
+}
+
+spm_status spm_pack_image(const uint8_t* gguf, uint64_t len, const char* order_text, const spm_model_cfg* cfg,
+                          const char* path) {
+    return guarded([&] {
+        std::string order = order_text ? order_text : "";
+        write_image(gguf, len, order_text ? &order : nullptr, cfg, path);
+    });
+}
+
+spm_status spm_image_probe(const char* path, uint64_t* image_bytes, int32_t* streams) {
+    return guarded([&] {
+        Mapped f(path);
+        uint64_t data = 0;
+        ModelDesc d = read_image(f.p, f.n, &data);
+        if (image_bytes) *image_bytes = d.image_bytes;
+        if (streams) *streams = int32_t(d.streams.size());
+    });
+}
+
+spm_status spm_model_open_image(const char* path, int device, spm_model** out) {
+    return guarded([&] {
+        Mapped f(path);
+        uint64_t data = 0;
+        ModelDesc d = read_image(f.p, f.n, &data);
+        const uint64_t bytes = d.image_bytes;
+        *out = make_model(std::move(d), device, 1, 0, [&](spm_model* m) {
+            CUDA_OK(cudaMemcpy(m->image, f.p + data, bytes, cudaMemcpyHostToDevice));  // one sequential upload
+        });
     });
 }
 

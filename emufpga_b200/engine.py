@@ -119,6 +119,20 @@ def _dev_ptr(t) -> C.c_void_p:
     return C.c_void_p(t.data_ptr())
 
 
+def pack_image(image: np.ndarray, path: str, shape: Shape | None = None, order: str | None = None) -> None:
+    """Pack a GGUF model into a device-image file (host only, no GPU)."""
+    cfg = shape.cfg() if shape is not None else None
+    call("spm_pack_image", _ptr(image), len(image), order.encode() if order else None,
+         C.byref(cfg) if cfg is not None else None, path.encode())
+
+
+def image_probe(path: str) -> tuple[int, int]:
+    """(image bytes, stream count) of a device-image file; raises if it is malformed."""
+    b, n = C.c_uint64(), C.c_int32()
+    call("spm_image_probe", path.encode(), C.byref(b), C.byref(n))
+    return b.value, n.value
+
+
 class Model:
     """The weight stream of one model, packed in HBM in consumption order."""
 
@@ -156,6 +170,18 @@ class Model:
         self._h = h
         self.device = device
         self.ep = ep
+        return self
+
+    @classmethod
+    def from_image(cls, path: str, shape: Shape | None = None, device: int = 0):
+        """Open a packed image file (pack_image): one sequential upload."""
+        self = cls.__new__(cls)
+        self.shape = shape
+        h = C.c_void_p()
+        call("spm_model_open_image", path.encode(), device, C.byref(h))
+        self._h = h
+        self.device = device
+        self.ep = None
         return self
 
     def close(self) -> None:

@@ -110,6 +110,17 @@ spm_status spm_model_open(const char* gguf_path, const char* order_path,
                           const spm_model_cfg* cfg, int device, spm_model** out);
 spm_status spm_model_open_memory(const uint8_t* gguf, uint64_t len, const char* order_text,
                                  const spm_model_cfg* cfg, int device, spm_model** out);
+/* Packed device image files (the .spm device image of the blueprint's next
+ * steps; the reference reads its streams from .spm/.order files,
+ * spm-file/src and spm-order/src/order.rs:28-52): spm_pack_image packs a GGUF
+ * model on the host (no GPU) into a file holding the stream table, the norm
+ * gains and every matrix's tiles in consumption order; spm_model_open_image
+ * uploads it with one sequential read, without re-packing; spm_image_probe
+ * validates a file and reports its image bytes and stream count. */
+spm_status spm_pack_image(const uint8_t* gguf, uint64_t len, const char* order_text,
+                          const spm_model_cfg* cfg, const char* path);
+spm_status spm_image_probe(const char* path, uint64_t* image_bytes, int32_t* streams);
+spm_status spm_model_open_image(const char* path, int device, spm_model** out);
 spm_status spm_model_close(spm_model* m);
 /* Weight bytes one decode sweep reads (descriptor sizes, LM head included). */
 spm_status spm_model_weight_bytes(const spm_model* m, uint64_t* bytes);

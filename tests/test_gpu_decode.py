@@ -290,3 +290,24 @@ def test_continuous_batching_matches_the_oracle_served_alone(cuda, models):
     for q, g in zip(reqs, got):
         want, _ = om.serve([list(q.prompt)], q.max_new)
         assert g == want[0]
+
+
+@pytest.mark.parametrize("name", ["qwen3-q5_k", "olmoe-q2_k"])
+def test_packed_image_file_opens_the_same_model(cuda, models, tmp_path, name):
+    """A model opened from its packed image file (one upload, no re-packing)
+    decodes bit-for-bit like the one packed from the GGUF."""
+    r, img, m, om = models(name)
+    path = tmp_path / "m.spmimg"
+    eb.pack_image(img, str(path), r.shape)
+    mi = eb.Model.from_image(str(path), r.shape)
+    assert mi.weight_bytes == m.weight_bytes
+    n = 3
+    a, b = eb.Session(m, n, 8), eb.Session(mi, n, 8)
+    for t in range(4):
+        toks = [(t * 5 + i * 3) % r.shape.vocab for i in range(n)]
+        _, la = a.decode_step(toks, want_logits=True)
+        _, lb = b.decode_step(toks, want_logits=True)
+        assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+    a.close()
+    b.close()
+    mi.close()
