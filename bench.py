@@ -13,6 +13,12 @@ region).  Dense models do not shard: N>1 runs N independent replicas
 (MoE) models over N>1 GPUs run expert parallel: one job serving the same
 clients on every rank, experts dealt round robin over the ranks, expert
 outputs exchanged over NVLink ("scaling": "strong").
+
+`--workload ternary-4096-b8` times the ternary GEMV of spm-gemv-ref instead
+(one launch over a 4096 x 4096 ternary stream with one scale per column and
+8 activation lanes per step; metric: weight applications/s, the reference's
+useful-weights rate), with the same clocks, L2 flush, e2e and CPU-baseline
+fields; N>1 runs replicas.
 """
 from __future__ import annotations
 
@@ -30,6 +36,8 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 DEFAULT_WORKLOAD = "smollm2-b5"
+# ternary GEMV workloads: rows, cols, group size, lanes
+TERNARY = {"ternary-4096-b8": (4096, 4096, 4096, 8)}
 
 
 def _args():
@@ -196,6 +204,8 @@ def run_reference(a, rank, world):
 def main():
     a = _args()
     rank, world, local = _dist()
+    if a.workload in TERNARY:
+        return run_ternary_reference(a, rank, world) if a.impl == "reference" else run_ternary(a, rank, world, local)
     if a.impl == "reference":
         return run_reference(a, rank, world)
     import torch
@@ -426,6 +436,188 @@ def gemv_roofline(eb, model, n, dev):
     del g
     return {"bytes": nbytes, "seconds": total / reps, "launches": len(keep)}
 
+
+
+
+# ---------------------------------------------------------------------------
+# ternary GEMV (spm-gemv-ref run_gemv)
+# ---------------------------------------------------------------------------
+
+def ternary_input(name: str, seed: int = 0):
+    """A one-stream ternary .spm file and the activations of the workload,
+    drawn with the value distributions of the reference's golden generator
+    (spm-vectors/src/draw.rs): weights uniform over {0, +1, -1}, scales
+    k/16 + 1/16 (k < 32), activations k/16 - 2 (k < 64)."""
+    import numpy as np
+
+    from emufpga_b200 import spmfile as sf
+
+    rows, cols, group, lanes = TERNARY[name]
+    rng = np.random.default_rng(seed)
+    codes = np.array([0, 1, 3], np.uint8)[rng.integers(0, 3, rows * cols)]
+    groups = -(-rows * cols // group)
+    scales = (rng.integers(0, 32, groups) / 16 + 0.0625).astype(np.float32)
+    x = (rng.integers(0, 64, (lanes, cols)) / 16 - 2.0).astype(np.float32)
+    return sf.ternary_file(rows, cols, group, codes, scales), x
+
+
+def _ternary_config(name):
+    rows, cols, group, lanes = TERNARY[name]
+    return {"workload": name, "rows": rows, "cols": cols, "group_size": group, "lanes": lanes}
+
+
+def ternary_cpu_baseline(data, x, seconds: float):
+    """The oracle's run_gemv (single-threaded, like the reference) on the
+    whole workload, repeated until `seconds` of work."""
+    from oracle import oracle as O
+
+    lanes, cols = x.shape
+    rows = O.spm_describe(data)["rows"]
+    t0 = time.perf_counter()
+    runs = 0
+    while True:
+        O.spm_run_gemv(data, x)
+        runs += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": runs * rows * cols * lanes / dt, "unit": "weights/s", "cores": 1, "kind": "port",
+            "sample": f"{runs} whole scans of the workload (oracle run_gemv, one thread)"}
+
+
+def run_ternary(a, rank, world, local):
+    import torch
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        pg = dist
+    from emufpga_b200 import ternary as T
+
+    rows, cols, group, lanes = TERNARY[a.workload]
+    data, x = ternary_input(a.workload)
+    m = T.TernaryMatrix(data, 0, local)
+    xd = torch.from_numpy(x).to(dev)
+    y = torch.empty((lanes, rows), dtype=torch.float32, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    warm, steps = max(a.warmup, 3), a.steps
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for _ in range(warm):
+        m.gemv(xd, out=y)
+    torch.cuda.synchronize(dev)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize(dev)
+    with Clocks(local) as clocks:
+        for i in range(steps):
+            flush.zero_()
+            starts[i].record(stream)
+            m.gemv(xd, out=y)
+            ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+    local_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    job_ms = local_ms
+    if pg:
+        tt = torch.tensor([local_ms], device=dev)
+        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
+        job_ms = float(tt.item())
+
+    # e2e: host activations in (pinned), results out, every step
+    x_host = torch.from_numpy(x).pin_memory()
+    y_host = torch.empty((lanes, rows), dtype=torch.float32).pin_memory()
+    for _ in range(warm):
+        xd.copy_(x_host, non_blocking=True)
+        m.gemv(xd, out=y)
+        y_host.copy_(y, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    if pg:
+        pg.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        xd.copy_(x_host, non_blocking=True)
+        m.gemv(xd, out=y)
+        y_host.copy_(y, non_blocking=True)
+        torch.cuda.synchronize(dev)
+    e2e_s = time.perf_counter() - t0
+    if pg:
+        tt = torch.tensor([e2e_s], device=dev)
+        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
+        e2e_s = float(tt.item())
+
+    if rank == 0:
+        from oracle import oracle as O
+
+        ok = bool((y_host.numpy().view("u4") == O.spm_run_gemv(data, x).view("u4")).all())
+        apps = rows * cols * lanes
+        peak, how = _peaks()
+        launch_s = local_ms / 1e3 / steps
+        ach = m.payload_bytes / launch_s / 1e9
+        line = {
+            "metric": "ternary weight applications/s", "value": apps * steps * world / (job_ms / 1e3),
+            "unit": "weights/s", "n_gpus": world, "steps": steps, "warmup": warm, "ms_per_step": job_ms / steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (weights uniform over {0,+1,-1}, scales and activations in sixteenths, as the "
+                    "reference's golden generator draws them)",
+            "config": dict(_ternary_config(a.workload), parallelism=f"replicas x{world}" if world > 1 else
+                           "single GPU", l2="flushed between timed steps (256 MiB write)",
+                           bit_identical_to_oracle=ok),
+            "e2e": {"value": apps * steps * world / e2e_s, "unit": "weights/s", "h2d_bytes_per_step": x.nbytes,
+                    "d2h_bytes_per_step": lanes * rows * 4},
+            "gpu_launches": steps,
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                         "peak_source": how, "traffic": None, "kernel": "ternary_gemv_kernel",
+                         "bytes_per_launch": m.payload_bytes,
+                         "note": "bound by the sequential f32 chain per (row, lane) that bit-exactness "
+                                 "requires, not by HBM"},
+            "clocks": clocks.summary(),
+        }
+        if not a.no_cpu_baseline:
+            line["cpu_baseline"] = ternary_cpu_baseline(data, x, a.cpu_seconds)
+        print(json.dumps(line), flush=True)
+    m.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def run_ternary_reference(a, rank, world):
+    """The reference arm for a ternary workload: the oracle's run_gemv
+    (single-threaded, as the reference's scan is) timed per step."""
+    if rank != 0:
+        return 0
+    from oracle import oracle as O
+
+    rows, cols, group, lanes = TERNARY[a.workload]
+    data, x = ternary_input(a.workload)
+    for _ in range(a.warmup):
+        O.spm_run_gemv(data, x)
+    times = []
+    for _ in range(a.steps):
+        t0 = time.perf_counter()
+        O.spm_run_gemv(data, x)
+        times.append(time.perf_counter() - t0)
+        if sum(times) > 150.0:
+            break
+    value = rows * cols * lanes * len(times) / sum(times)
+    line = {"metric": "ternary weight applications/s", "value": value, "unit": "weights/s", "impl": "reference",
+            "n_gpus": world, "steps": len(times), "warmup": a.warmup,
+            "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (as the ours arm)",
+            "config": _ternary_config(a.workload),
+            "cpu_baseline": {"value": value, "unit": "weights/s", "kind": "port", "cores": 1,
+                             "sample": f"{len(times)} whole scans after {a.warmup} warm-up scans"},
+            "e2e": {"value": value, "unit": "weights/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 if __name__ == "__main__":

@@ -61,6 +61,20 @@ _U64P = C.POINTER(C.c_uint64)
 _I32P = C.POINTER(C.c_int32)
 
 # name -> (restype, argtypes); this table is also the list of exported symbols.
+class FileStreamInfo(C.Structure):
+    """spm_file_stream_info (spmgpu.h)."""
+    _fields_ = [("rows", C.c_uint32), ("cols", C.c_uint32), ("group_size", C.c_uint32), ("encoding", C.c_uint32),
+                ("lane_count", C.c_uint32), ("pad_", C.c_uint32), ("groups", C.c_uint64), ("offset", C.c_uint64),
+                ("bytes", C.c_uint64)]
+
+
+class TernaryInfo(C.Structure):
+    """spm_ternary_info (spmgpu.h)."""
+    _fields_ = [("rows", C.c_uint32), ("cols", C.c_uint32), ("group_size", C.c_uint32), ("pad_", C.c_uint32),
+                ("groups", C.c_uint64), ("payload_bytes", C.c_uint64), ("reserved_codes", C.c_uint64),
+                ("device_bytes", C.c_uint64)]
+
+
 PROTOTYPES = {
     "spm_last_error": (C.c_char_p, []),
     "spm_version": (C.c_char_p, []),
@@ -106,6 +120,12 @@ PROTOTYPES = {
     "spm_session_set_graphs": (C.c_int32, [_P, C.c_int32]),
     "spm_session_routes": (C.c_int32, [_P, C.c_int32, _I32P]),
     "spm_session_launches_per_step": (C.c_int32, [_P, C.c_int32, _I32P]),
+    "spm_file_probe": (C.c_int32, [_P, C.c_uint64, _U32P, _U32P, _I32P]),
+    "spm_file_stream": (C.c_int32, [_P, C.c_uint64, C.c_int32, C.POINTER(FileStreamInfo)]),
+    "spm_ternary_upload": (C.c_int32, [_P, C.c_uint64, C.c_int32, C.c_int, C.POINTER(_P)]),
+    "spm_ternary_free": (C.c_int32, [_P]),
+    "spm_ternary_describe": (C.c_int32, [_P, C.POINTER(TernaryInfo)]),
+    "spm_ternary_gemv": (C.c_int32, [_P, _P, C.c_int32, C.c_uint64, _P, _P]),
 }
 
 _lib: C.CDLL | None = None

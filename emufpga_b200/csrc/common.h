@@ -85,4 +85,42 @@ Packed packed_shape(uint32_t dtype, uint64_t rows, uint64_t cols);
 // Repack GGML row-major blocks into `dst` (packed.tiles * tile_bytes bytes).
 void pack_matrix(const Packed& p, const uint8_t* gguf_blocks, uint8_t* dst);
 
+// ---- .spm files (spm-header, spm-layout, spm-file) ----
+enum : uint8_t { SPM_ENC_TERNARY = 1, SPM_ENC_F32 = 2, SPM_ENC_BF16 = 3, SPM_ENC_Q6K = 4, SPM_ENC_Q5K = 5,
+                 SPM_ENC_Q8_0 = 6 };
+struct SpmDesc {
+    uint32_t rows = 0, cols = 0, group_size = 0;
+    uint8_t encoding = 0;
+    uint16_t lane_count = 0;
+};
+struct SpmFile {
+    uint16_t major = 0, minor = 0;
+    std::vector<SpmDesc> desc;
+    uint64_t payload = 0;  // offset of the first group
+};
+// Header and directory; throws like the reference's parse functions.
+SpmFile spm_file_parse(const uint8_t* buf, uint64_t len);
+// Placement of one stream's groups in the file.
+struct SpmSpan {
+    uint64_t offset = 0;   // first group
+    uint64_t bytes = 0;    // scales plus payloads of all its groups
+    uint64_t groups = 0;
+};
+// Walks the groups of streams 0..index in file order; throws SPM_E_TRUNCATED
+// with the reference's PayloadTruncated message when the file ends inside one.
+SpmSpan spm_file_locate(const SpmFile& f, uint64_t len, uint32_t index);
+
+// A ternary stream repacked for the device.  codes[w * rows_pad + r] holds the
+// 2-bit codes of row r for columns 16w..16w+15 (column 16w+j at bits 2j, 2j+1;
+// padding rows and columns hold code 0); scales[g] is group g's scale.
+struct TernaryHost {
+    uint32_t rows = 0, cols = 0, group_size = 0;
+    uint64_t groups = 0, col_words = 0, rows_pad = 0;
+    uint64_t payload_bytes = 0;   // packed weight bytes of the stream (scales excluded)
+    uint64_t reserved_codes = 0;  // 0b10 codes: no-ops for the datapath, as in the reference
+    std::vector<uint32_t> codes;
+    std::vector<float> scales;
+};
+TernaryHost pack_ternary(const uint8_t* buf, uint64_t len, uint32_t index);
+
 }  // namespace spm

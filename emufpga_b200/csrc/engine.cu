@@ -24,6 +24,7 @@
 #include <sstream>
 #include <thread>
 
+#include "abi.h"
 #include "kernels.h"
 #include "moe.h"
 
@@ -31,38 +32,6 @@ namespace spm {
 const std::string& last_error();
 }
 using namespace spm;
-
-#define CUDA_OK(expr)                                                                        \
-    do {                                                                                     \
-        cudaError_t e_ = (expr);                                                             \
-        if (e_ != cudaSuccess) fail(SPM_E_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
-    } while (0)
-
-namespace {
-
-template <class F>
-spm_status guarded(F&& f) {
-    try {
-        f();
-        return SPM_OK;
-    } catch (const Error& e) {
-        set_error(e.msg);
-        return e.code;
-    } catch (const std::bad_alloc&) {
-        set_error("host allocation failed");
-        return SPM_E_ARG;
-    } catch (const std::exception& e) {
-        set_error(e.what());
-        return SPM_E_ARG;
-    }
-}
-
-struct DeviceBuf {
-    void* p = nullptr;
-    ~DeviceBuf() { if (p) cudaFree(p); }
-};
-
-}  // namespace
 
 // A packed matrix in the device image.
 struct StreamDesc {

@@ -1,0 +1,162 @@
+// Ternary GEMV over a .spm stream (Encoding::Ternary2F32I32): the device form
+// of spm_gemv_ref::run_gemv (spm-gemv-ref/src/gemv.rs:39-126,
+// datapath.rs:19-55, spm-accum/src/bank.rs:56-66).
+//
+// The reference's result is defined by its order of operations: for every
+// output row and lane, an f32 accumulator starts at +0 and, for the row's
+// weights in stream order (columns ascending), adds or subtracts
+// scale(group) * x[col] -- the product rounded once, then the sum rounded
+// once -- and is left untouched by zero codes.  f32 addition is not
+// associative, so a split over columns or a reduction tree would change the
+// low bits; this kernel keeps one sequential chain per (row, lane) and
+// spreads the work over rows and lanes instead.  Rounding is pinned with
+// __fmul_rn / __fadd_rn / __fsub_rn, which the compiler never contracts.
+//
+// Layout in HBM (packed on the host by pack_ternary): for every 16 columns one
+// 32-bit word per row, rows padded to a multiple of 32, so a warp of 32 rows
+// reads 128 contiguous bytes per 16 columns; the scales follow.  Threads of a
+// warp share their lanes, so activation loads are warp-uniform broadcasts.
+//
+// Roofline: HBM is not the bound.  Each (row, lane) chain is `cols` dependent
+// adds, and the issue cost is about seven instructions per weight and lane,
+// so a launch takes about max(cols x add latency, rows x lanes x cols x 7 /
+// (4 x SMs) issue cycles).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <memory>
+
+#include "abi.h"
+#include "ternary_kernel.cuh"
+
+namespace spm {
+namespace {
+
+// Lanes per thread: more lanes share one code word and group walk, fewer
+// lanes spread the chains over more warps.  Take the most lanes that still
+// leave about two warps per scheduler.
+int lanes_per_thread(uint64_t rows_pad, int lanes, int sms) {
+    const uint64_t target = 8ull * uint64_t(sms);
+    for (int L : {8, 4, 2})
+        if (lanes >= L && rows_pad / 32 * uint64_t((lanes + L - 1) / L) >= target) return L;
+    return 1;
+}
+
+template <int LPT>
+cudaError_t launch(const TernaryArgs& a, cudaStream_t stream) {
+    const uint64_t threads = a.rows_pad * uint64_t((a.lanes + LPT - 1) / LPT);
+    const uint64_t blocks = (threads + kTernaryThreads - 1) / kTernaryThreads;
+    if (blocks > 0x7FFFFFFFull) return cudaErrorInvalidConfiguration;
+    ternary_gemv_kernel<LPT><<<unsigned(blocks), kTernaryThreads, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+}  // namespace spm
+
+using namespace spm;
+
+struct spm_ternary {
+    uint32_t rows = 0, cols = 0, group_size = 0;
+    uint64_t groups = 0, col_words = 0, rows_pad = 0;
+    uint64_t payload_bytes = 0, reserved_codes = 0, device_bytes = 0;
+    int device = 0, sms = 148;
+    uint8_t* mem = nullptr;
+    const uint32_t* codes = nullptr;
+    const float* scales = nullptr;
+    ~spm_ternary() { if (mem) cudaFree(mem); }
+};
+
+spm_status spm_ternary_upload(const uint8_t* spm, uint64_t len, int32_t index, int device, spm_ternary** out) {
+    return guarded([&] {
+        if (!out) fail(SPM_E_ARG, "null output");
+        if (index < 0) fail(SPM_E_ARG, "stream index out of range");
+        const TernaryHost h = pack_ternary(spm, len, uint32_t(index));
+        int ndev = 0;
+        if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) fail(SPM_E_NO_DEVICE, "no CUDA device is visible");
+        std::unique_ptr<spm_ternary> t(new spm_ternary());
+        t->rows = h.rows;
+        t->cols = h.cols;
+        t->group_size = h.group_size;
+        t->groups = h.groups;
+        t->col_words = h.col_words;
+        t->rows_pad = h.rows_pad;
+        t->payload_bytes = h.payload_bytes;
+        t->reserved_codes = h.reserved_codes;
+        t->device = device;
+        CUDA_OK(cudaSetDevice(device));
+        CUDA_OK(cudaDeviceGetAttribute(&t->sms, cudaDevAttrMultiProcessorCount, device));
+        const uint64_t code_bytes = h.codes.size() * sizeof(uint32_t);
+        const uint64_t scale_at = (code_bytes + 255) / 256 * 256;
+        t->device_bytes = std::max<uint64_t>(scale_at + h.scales.size() * sizeof(float), 256);
+        CUDA_OK(cudaMalloc(&t->mem, t->device_bytes));
+        if (code_bytes) CUDA_OK(cudaMemcpy(t->mem, h.codes.data(), code_bytes, cudaMemcpyHostToDevice));
+        if (!h.scales.empty())
+            CUDA_OK(cudaMemcpy(t->mem + scale_at, h.scales.data(), h.scales.size() * sizeof(float),
+                               cudaMemcpyHostToDevice));
+        t->codes = reinterpret_cast<const uint32_t*>(t->mem);
+        t->scales = reinterpret_cast<const float*>(t->mem + scale_at);
+        *out = t.release();
+    });
+}
+
+spm_status spm_ternary_free(spm_ternary* t) {
+    return guarded([&] { delete t; });
+}
+
+spm_status spm_ternary_describe(const spm_ternary* t, spm_ternary_info* out) {
+    return guarded([&] {
+        if (!t || !out) fail(SPM_E_ARG, "null argument");
+        *out = spm_ternary_info{};
+        out->rows = t->rows;
+        out->cols = t->cols;
+        out->group_size = t->group_size;
+        out->groups = t->groups;
+        out->payload_bytes = t->payload_bytes;
+        out->reserved_codes = t->reserved_codes;
+        out->device_bytes = t->device_bytes;
+    });
+}
+
+spm_status spm_ternary_gemv(const spm_ternary* t, const float* x_dev, int32_t lanes, uint64_t x_cols, float* y_dev,
+                            void* cuda_stream) {
+    return guarded([&] {
+        if (!t) fail(SPM_E_ARG, "null matrix");
+        if (lanes < 0) fail(SPM_E_ARG, "negative lane count");
+        if (x_cols < t->cols) {
+            char msg[96];
+            std::snprintf(msg, sizeof msg, "need %u activations per lane, got %llu", t->cols,
+                          (unsigned long long)x_cols);
+            fail(SPM_E_ACTIVATION_LEN, msg);
+        }
+        if (lanes == 0 || t->rows == 0) return;
+        if (!y_dev || (t->cols && !x_dev)) fail(SPM_E_ARG, "null activation or output pointer");
+        CUDA_OK(cudaSetDevice(t->device));
+        TernaryArgs a{};
+        a.codes = t->codes;
+        a.scales = t->scales;
+        a.x = x_dev;
+        a.y = y_dev;
+        a.rows_pad = t->rows_pad;
+        a.col_words = t->col_words;
+        a.x_cols = x_cols;
+        a.rows = t->rows;
+        a.cols = t->cols;
+        a.group = t->group_size;
+        a.q = t->rows / t->group_size;
+        a.r = t->rows % t->group_size;
+        a.last_group = t->groups ? uint32_t(t->groups - 1) : 0u;
+        a.lanes = lanes;
+        const cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
+        cudaError_t e;
+        switch (lanes_per_thread(t->rows_pad, lanes, t->sms)) {
+            case 8: e = launch<8>(a, s); break;
+            case 4: e = launch<4>(a, s); break;
+            case 2: e = launch<2>(a, s); break;
+            default: e = launch<1>(a, s); break;
+        }
+        if (e == cudaErrorInvalidConfiguration) fail(SPM_E_ARG, "too many rows x lanes for one launch");
+        CUDA_OK(e);
+    });
+}

@@ -203,6 +203,59 @@ spm_status spm_session_ep_connect(spm_session* s, const void* handles);
 /* Kernel launches issued by one step at client count n (graph nodes). */
 spm_status spm_session_launches_per_step(spm_session* s, int32_t n, int32_t* launches);
 
+/* ---- .spm files and the ternary profile (Encoding::Ternary2F32I32) ----
+ * A .spm file is a 32-byte header (spm-header/src/parse.rs:10-62), one
+ * 32-byte descriptor per stream (spm-layout/src/wire.rs:12-30), then every
+ * stream's scale groups in order, each an f32 scale followed by its payload
+ * (spm-file/src/read.rs:69-101).  Errors follow the reference's:
+ * HeaderError/LayoutError::TooShort and FileError::PayloadTruncated ->
+ * SPM_E_TRUNCATED; BadMagic, UnsupportedVersion, UnknownEndianness,
+ * ZeroGroupSize -> SPM_E_STREAM; UnknownEncoding -> SPM_E_ENCODING.  These
+ * two calls run on the host only. */
+typedef struct spm_file_stream_info {
+    uint32_t rows, cols, group_size, encoding, lane_count, pad_;
+    uint64_t groups;   /* scale groups in the stream                      */
+    uint64_t offset;   /* file offset of its first group                  */
+    uint64_t bytes;    /* its scales and payloads                         */
+} spm_file_stream_info;
+/* Header and directory (SpmReader::parse, spm-file/src/read.rs:46-67). */
+spm_status spm_file_probe(const uint8_t* spm, uint64_t len, uint32_t* version_major, uint32_t* version_minor,
+                          int32_t* streams);
+/* Descriptor and placement of stream `index`; every group of streams
+ * 0..index must be whole (SpmReader::next_group, read.rs:69-89). */
+spm_status spm_file_stream(const uint8_t* spm, uint64_t len, int32_t index, spm_file_stream_info* out);
+
+/* The ternary GEMV of spm_gemv_ref::run_gemv (spm-gemv-ref/src/gemv.rs:39-57,
+ * datapath.rs:19-55) on the device.  Stream position k holds W[k % rows]
+ * [k / rows]; a weight's group scale multiplies the activation, and each
+ * nonzero code (bit 0) adds or, with bit 1, subtracts that product into the
+ * row's f32 accumulator, in stream order.  Results are bit-identical to the
+ * reference's for every input: each output keeps the reference's sequential
+ * order of additions.  The reserved code 0b10 is a no-op, as in the
+ * reference's datapath (spm_ternary_upload counts them).
+ * spm_ternary_upload packs stream `index` into HBM; like run_gemv's scan, it
+ * refuses a file whose next group after the stream is cut short, and it
+ * refuses non-ternary streams (SPM_E_ENCODING) and files with no streams
+ * (GemvError::NoStreams -> SPM_E_ARG). */
+typedef struct spm_ternary spm_ternary;
+spm_status spm_ternary_upload(const uint8_t* spm, uint64_t len, int32_t index, int device, spm_ternary** out);
+spm_status spm_ternary_free(spm_ternary* t);
+typedef struct spm_ternary_info {
+    uint32_t rows, cols, group_size, pad_;
+    uint64_t groups;
+    uint64_t payload_bytes;   /* packed weight bytes of the stream (scales excluded) */
+    uint64_t reserved_codes;  /* 0b10 codes in the stream                          */
+    uint64_t device_bytes;    /* HBM held by the packed codes and scales           */
+} spm_ternary_info;
+spm_status spm_ternary_describe(const spm_ternary* t, spm_ternary_info* out);
+/* y = W x for `lanes` activation vectors: x_dev is lanes x x_cols floats
+ * (lane-major, Activations::per_lane), y_dev lanes x rows (bank.lane(l) for
+ * each lane).  x_cols < cols is GemvError::MissingActivations
+ * (SPM_E_ACTIVATION_LEN); extra activations are ignored.  Device pointers;
+ * enqueued on cuda_stream (NULL = default stream). */
+spm_status spm_ternary_gemv(const spm_ternary* t, const float* x_dev, int32_t lanes, uint64_t x_cols,
+                            float* y_dev, void* cuda_stream);
+
 #ifdef __cplusplus
 }
 #endif

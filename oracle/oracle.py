@@ -73,6 +73,11 @@ def lib() -> C.CDLL:
         L.or_serve.restype = C.c_int
         L.or_serve.argtypes = [C.c_void_p, C.POINTER(C.c_uint32), C.POINTER(C.c_int), C.c_int, C.c_int,
                                C.POINTER(C.c_uint32), C.POINTER(C.c_int), fp, C.c_int, C.c_int]
+        u32p = C.POINTER(C.c_uint32)
+        L.or_spm_describe.restype = C.c_int
+        L.or_spm_describe.argtypes = [u8, C.c_uint64, C.c_int32, u32p, u32p, u32p, u32p, u32p, C.c_char_p, C.c_int]
+        L.or_spm_run_gemv.restype = C.c_int
+        L.or_spm_run_gemv.argtypes = [u8, C.c_uint64, fp, C.c_int, C.c_uint64, fp, C.c_uint64, C.c_char_p, C.c_int]
         _lib = L
     return _lib
 
@@ -187,6 +192,50 @@ def gguf_parse_error(image: np.ndarray) -> str | None:
         lib().or_gguf_free(h)
         return None
     return err.value.decode()
+
+
+class SpmError(ValueError):
+    """A .spm file or ternary GEMV the oracle refused; `code` is its OR_SPM_* status."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg)
+        self.code = code
+
+
+def _spm_bytes(spm) -> np.ndarray:
+    return np.ascontiguousarray(np.frombuffer(bytes(spm), dtype=np.uint8))
+
+
+def spm_describe(spm, index: int = 0) -> dict:
+    """Stream count and stream `index`'s descriptor fields (header and directory only)."""
+    raw = _spm_bytes(spm)
+    v = [C.c_uint32() for _ in range(5)]
+    err = C.create_string_buffer(256)
+    rc = lib().or_spm_describe(raw.ctypes.data, raw.size, index, *[C.byref(x) for x in v], err, 256)
+    if rc:
+        raise SpmError(rc, err.value.decode())
+    return dict(zip(("streams", "rows", "cols", "group_size", "encoding"), (x.value for x in v)))
+
+
+def spm_run_gemv(spm, x: np.ndarray) -> np.ndarray:
+    """spm_gemv_ref::run_gemv on the first stream: x is lanes x x_cols, the
+    result lanes x rows (bank.lane(l) for every lane)."""
+    raw = _spm_bytes(spm)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if x.ndim != 2:
+        raise ValueError("x must be lanes x cols")
+    lanes, x_cols = x.shape
+    err = C.create_string_buffer(256)
+    head = C.c_uint32()
+    rows = C.c_uint32()
+    rc = lib().or_spm_describe(raw.ctypes.data, raw.size, 0, C.byref(head), C.byref(rows), None, None, None, err, 256)
+    if rc:
+        raise SpmError(rc, err.value.decode())
+    bank = np.empty(max(1, rows.value * lanes), dtype=np.float32)
+    rc = lib().or_spm_run_gemv(raw.ctypes.data, raw.size, _f(x), lanes, x_cols, _f(bank), bank.size, err, 256)
+    if rc:
+        raise SpmError(rc, err.value.decode())
+    return bank[: rows.value * lanes].reshape(rows.value, lanes).T.copy()
 
 
 def cfg_of(shape) -> Cfg:

@@ -1009,3 +1009,214 @@ int or_serve(or_model* m, const uint32_t* prompts_flat, const int* prompt_lens, 
     or_session_free(s);
     return rc;
 }
+
+/* ------------------------------------------------------------------ */
+/* .spm files and the ternary GEMV of spm-gemv-ref.                    */
+/* ------------------------------------------------------------------ */
+
+typedef struct {
+    uint32_t rows, cols, group_size;
+    uint8_t encoding;
+} or_spm_desc;
+
+static int spm_err(char* err, int errlen, int code, const char* msg) {
+    if (err && errlen > 0) snprintf(err, (size_t)errlen, "%s", msg);
+    return code;
+}
+
+static uint32_t rd_le32(const uint8_t* p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+/* Encoding::bytes_for (spm-layout/src/model.rs): bytes a group of `count`
+ * weights occupies on the wire. */
+static uint64_t spm_bytes_for(uint8_t enc, uint64_t count) {
+    switch (enc) {
+        case 1: return (count + 3) / 4;              /* Ternary2F32I32 */
+        case 2: return count * 4;                    /* F32            */
+        case 3: return count * 2;                    /* Bf16           */
+        case 4: return (count + 255) / 256 * 210;    /* Q6K            */
+        case 5: return (count + 255) / 256 * 176;    /* Q5K            */
+        default: return (count + 31) / 32 * 34;      /* Q8_0           */
+    }
+}
+
+/* spm-header/src/parse.rs:10-62 then the directory loop of
+ * spm-file/src/read.rs:51-60 with spm-layout/src/wire.rs:12-30. */
+static int spm_parse(const uint8_t* src, uint64_t len, uint32_t* count, or_spm_desc** out, uint64_t* payload,
+                     char* err, int errlen) {
+    static const uint8_t magic[8] = {0x89, 'S', 'P', 'M', 0x0D, 0x0A, 0x1A, 0x0A};
+    char msg[128];
+    *out = NULL;
+    if (len < 32) {
+        snprintf(msg, sizeof msg, "header truncated: %llu bytes available, need 32", (unsigned long long)len);
+        return spm_err(err, errlen, OR_SPM_TRUNCATED, msg);
+    }
+    if (memcmp(src, magic, 8) != 0)
+        return spm_err(err, errlen, OR_SPM_MALFORMED, "bad magic: not a .spm file, or corrupted in transit");
+    const uint16_t major = le16(src + 8);
+    if (major > 1) {
+        snprintf(msg, sizeof msg, "unsupported .spm major version %u: this build reads up to 1", major);
+        return spm_err(err, errlen, OR_SPM_MALFORMED, msg);
+    }
+    if (src[12] != 0) {
+        snprintf(msg, sizeof msg, "unknown endianness discriminant %u", src[12]);
+        return spm_err(err, errlen, OR_SPM_MALFORMED, msg);
+    }
+    const uint32_t n = rd_le32(src + 16);
+    /* only as many entries as the file can hold: a hostile count fails as a
+     * truncated directory, not as a huge allocation */
+    const uint64_t fit = (len - 32) / 32;
+    const uint64_t room = n < fit ? n : fit;
+    or_spm_desc* d = (or_spm_desc*)calloc(room ? room : 1, sizeof(or_spm_desc));
+    if (!d) return spm_err(err, errlen, OR_SPM_TRUNCATED, "out of memory");
+    uint64_t at = 32;
+    for (uint32_t i = 0; i < n; ++i) {
+        const uint64_t avail = at <= len ? len - at : 0;
+        if (avail < 32) {
+            free(d);
+            snprintf(msg, sizeof msg, "descriptor truncated: %llu bytes, need 32", (unsigned long long)avail);
+            return spm_err(err, errlen, OR_SPM_TRUNCATED, msg);
+        }
+        const uint8_t* p = src + at;
+        d[i].group_size = rd_le32(p + 8);
+        if (d[i].group_size == 0) {
+            free(d);
+            return spm_err(err, errlen, OR_SPM_MALFORMED, "group_size must be at least 1");
+        }
+        if (p[12] < 1 || p[12] > 6) {
+            free(d);
+            snprintf(msg, sizeof msg, "unknown .spm encoding profile %u", p[12]);
+            return spm_err(err, errlen, OR_SPM_ENCODING, msg);
+        }
+        d[i].rows = rd_le32(p);
+        d[i].cols = rd_le32(p + 4);
+        d[i].encoding = p[12];
+        at += 32;
+    }
+    *count = n;
+    *out = d;
+    *payload = at;
+    return 0;
+}
+
+int or_spm_describe(const uint8_t* spm, uint64_t len, int32_t index, uint32_t* streams, uint32_t* rows,
+                    uint32_t* cols, uint32_t* group_size, uint32_t* encoding, char* err, int errlen) {
+    uint32_t n = 0;
+    or_spm_desc* d = NULL;
+    uint64_t payload = 0;
+    int rc = spm_parse(spm, len, &n, &d, &payload, err, errlen);
+    if (rc) return rc;
+    if (streams) *streams = n;
+    if (index >= 0 && (uint32_t)index < n) {
+        if (rows) *rows = d[index].rows;
+        if (cols) *cols = d[index].cols;
+        if (group_size) *group_size = d[index].group_size;
+        if (encoding) *encoding = d[index].encoding;
+    }
+    free(d);
+    return 0;
+}
+
+/* Cursor (spm-walk/src/cursor.rs:20-68): a (stream, group) position that
+ * skips streams with no groups left. */
+typedef struct {
+    uint32_t stream;
+    uint64_t group;
+} or_cursor;
+
+static uint64_t spm_total(const or_spm_desc* d) { return (uint64_t)d->rows * d->cols; }
+
+static void cursor_settle(or_cursor* c, const or_spm_desc* d, uint32_t n) {
+    while (c->stream < n) {
+        const uint64_t total = spm_total(&d[c->stream]);
+        const uint64_t groups = (total + d[c->stream].group_size - 1) / d[c->stream].group_size;
+        if (c->group < groups) return;
+        c->stream++;
+        c->group = 0;
+    }
+}
+
+/* spm-layout/src/tiling.rs:37-55 group_len. */
+static uint64_t cursor_group_len(const or_cursor* c, const or_spm_desc* d) {
+    const uint64_t total = spm_total(&d[c->stream]);
+    const uint64_t start = (uint64_t)d[c->stream].group_size * c->group;
+    const uint64_t left = total - start;
+    return left < d[c->stream].group_size ? left : d[c->stream].group_size;
+}
+
+int or_spm_run_gemv(const uint8_t* spm, uint64_t len, const float* x, int lanes, uint64_t x_cols,
+                    float* bank, uint64_t bank_cap, char* err, int errlen) {
+    uint32_t n = 0;
+    or_spm_desc* d = NULL;
+    uint64_t at = 0;
+    char msg[128];
+    int rc = spm_parse(spm, len, &n, &d, &at, err, errlen);
+    if (rc) return rc;
+    /* prepare (gemv.rs:66-85) */
+    if (n == 0) {
+        free(d);
+        return spm_err(err, errlen, OR_SPM_NO_STREAMS, "parameter stream declares no operations");
+    }
+    const uint64_t rows = d[0].rows, cols = d[0].cols;
+    if (x_cols < cols) {
+        free(d);
+        snprintf(msg, sizeof msg, "need %llu activations per lane, got %llu", (unsigned long long)cols,
+                 (unsigned long long)x_cols);
+        return spm_err(err, errlen, OR_SPM_ACTIVATIONS, msg);
+    }
+    if (lanes < 0 || rows * (uint64_t)lanes > bank_cap) {
+        free(d);
+        return spm_err(err, errlen, OR_SPM_ACTIVATIONS, "bank capacity too small");
+    }
+    memset(bank, 0, sizeof(float) * rows * (uint64_t)lanes);
+    float* scaled = (float*)calloc(lanes > 0 ? (size_t)lanes : 1, sizeof(float));
+    or_cursor cur = {0, 0};
+    cursor_settle(&cur, d, n);
+    uint64_t position = 0;
+    /* drive (gemv.rs:88-104): pull groups until the first one of another stream */
+    while (cur.stream < n) {
+        const uint32_t stream = cur.stream;
+        const uint64_t count = cursor_group_len(&cur, d);
+        const uint64_t bytes = spm_bytes_for(d[stream].encoding, count);
+        const uint64_t needed = 4 + bytes, available = len - at;
+        if (available < needed) { /* spm-file/src/read.rs:91-101 */
+            free(scaled);
+            free(d);
+            snprintf(msg, sizeof msg, "payload truncated: group needs %llu bytes, %llu remain",
+                     (unsigned long long)needed, (unsigned long long)available);
+            return spm_err(err, errlen, OR_SPM_TRUNCATED, msg);
+        }
+        float scale;
+        memcpy(&scale, spm + at, 4); /* f32::from_le_bytes on a little-endian host */
+        const uint8_t* packed = spm + at + 4;
+        at += needed;
+        cur.group++;
+        cursor_settle(&cur, d, n);
+        if (stream != 0) break;
+        /* apply_group (datapath.rs:19-40): the scaled activations are
+         * refreshed whenever the column changes, starting afresh in every
+         * group; each weight then adds or subtracts them, never multiplies. */
+        uint64_t current_col = UINT64_MAX;
+        for (uint64_t local = 0; local < count; ++local) {
+            const uint8_t code = (uint8_t)((packed[local / 4] >> ((local % 4) * 2)) & 3);
+            const uint64_t index = position + local;
+            const uint64_t col = index / rows;
+            if (col != current_col) {
+                for (int l = 0; l < lanes; ++l) scaled[l] = scale * x[(uint64_t)l * x_cols + col];
+                current_col = col;
+            }
+            if (code & 1) { /* NONZERO_BIT: accumulator enable (datapath.rs:50-55) */
+                float* slot = bank + (index % rows) * (uint64_t)lanes;
+                if (code & 2) /* NEGATIVE_BIT: subtract (bank.rs:56-66) */
+                    for (int l = 0; l < lanes; ++l) slot[l] -= scaled[l];
+                else
+                    for (int l = 0; l < lanes; ++l) slot[l] += scaled[l];
+            }
+        }
+        position += count;
+    }
+    free(scaled);
+    free(d);
+    return 0;
+}

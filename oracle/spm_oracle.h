@@ -102,6 +102,31 @@ int or_serve(or_model* m, const uint32_t* prompts_flat, const int* prompt_lens, 
              int steps, uint32_t* produced, int* produced_lens, float* last_logits, int threads,
              int max_ticks);
 
+/* ---- .spm files and the ternary profile ----
+ * spm-header/src/parse.rs (32-byte header), spm-layout/src/wire.rs:12-30 and
+ * model.rs (32-byte descriptors, Encoding::bytes_for), spm-walk/src/cursor.rs
+ * (group order), spm-file/src/read.rs:69-101 (scale, then payload) and
+ * spm-gemv-ref/src/{gemv.rs:39-126, datapath.rs:19-55} with
+ * spm-accum/src/bank.rs:56-66 (run_gemv).  Status codes: */
+enum {
+    OR_SPM_NO_STREAMS = -1,   /* GemvError::NoStreams                        */
+    OR_SPM_ACTIVATIONS = -2,  /* GemvError::MissingActivations               */
+    OR_SPM_TRUNCATED = -3,    /* HeaderError/LayoutError::TooShort, PayloadTruncated */
+    OR_SPM_MALFORMED = -4,    /* BadMagic, UnsupportedVersion, UnknownEndianness, ZeroGroupSize */
+    OR_SPM_ENCODING = -5      /* LayoutError::UnknownEncoding                */
+};
+/* Header and directory: stream count, and rows/cols/group/encoding of stream
+ * `index` (any of them may be NULL). */
+int or_spm_describe(const uint8_t* spm, uint64_t len, int32_t index, uint32_t* streams, uint32_t* rows,
+                    uint32_t* cols, uint32_t* group_size, uint32_t* encoding, char* err, int errlen);
+/* spm_gemv_ref::run_gemv over the first stream with `lanes` activation vectors
+ * (lane-major, x_cols floats each).  bank receives rows x lanes floats in the
+ * reference's row-major AccumulatorBank order; bank_cap is its capacity in
+ * floats.  Like the reference, the scan reads the first group after the stream
+ * before it stops, so a truncated one is an error too. */
+int or_spm_run_gemv(const uint8_t* spm, uint64_t len, const float* x, int lanes, uint64_t x_cols,
+                    float* bank, uint64_t bank_cap, char* err, int errlen);
+
 #ifdef __cplusplus
 }
 #endif
