@@ -71,7 +71,8 @@ def test_scan_productivity_equals_the_batch_size(cuda):
 
 
 SHAPES = [(3, 2, 4), (1, 1, 1), (33, 17, 33), (33, 17, 1), (33, 17, 5), (64, 16, 64), (31, 47, 31 * 47),
-          (100, 40, 7), (5, 100, 500), (40, 33, 16), (96, 35, 192), (257, 19, 100), (32, 1, 2), (1000, 300, 1000)]
+          (100, 40, 7), (5, 100, 500), (40, 33, 16), (96, 35, 192), (257, 19, 100), (32, 1, 2), (1000, 300, 1000),
+          (70, 1000, 70), (9, 2049, 5)]
 
 
 @pytest.mark.parametrize("shape", SHAPES)
