@@ -10,7 +10,9 @@
 // associative, so a split over columns or a reduction tree would change the
 // low bits; this kernel keeps one sequential chain per (row, lane) and
 // spreads the work over rows and lanes instead.  Rounding is pinned with
-// __fmul_rn / __fadd_rn / __fsub_rn, which the compiler never contracts.
+// __fmul_rn / __fadd_rn, which the compiler never contracts; a subtraction
+// is the addition of the negated product, which IEEE arithmetic defines to
+// be the same operation.
 //
 // Layout in HBM (packed on the host by pack_ternary): for every 16 columns one
 // 32-bit word per row, rows padded to a multiple of 32, so a warp of 32 rows
@@ -18,9 +20,9 @@
 // warp share their lanes, so activation loads are warp-uniform broadcasts.
 //
 // Roofline: HBM is not the bound.  Each (row, lane) chain is `cols` dependent
-// adds, and the issue cost is about seven instructions per weight and lane,
-// so a launch takes about max(cols x add latency, rows x lanes x cols x 7 /
-// (4 x SMs) issue cycles).
+// adds, so a launch takes at least cols x the add latency, and the issue cost
+// (a handful of instructions per weight and lane) spreads over rows x lanes
+// chains.
 #include <cuda_runtime.h>
 
 #include <algorithm>
