@@ -17,8 +17,9 @@ outputs exchanged over NVLink ("scaling": "strong").
 `--workload ternary-4096-b8` times the ternary GEMV of spm-gemv-ref instead
 (one launch over a 4096 x 4096 ternary stream with one scale per column and
 8 activation lanes per step; metric: weight applications/s, the reference's
-useful-weights rate), with the same clocks, L2 flush, e2e and CPU-baseline
-fields; N>1 runs replicas.
+useful-weights rate), and `--workload dense-f32-4096-b8` the dense .spm
+streamed GEMV of spm-linear (a 4096 x 4096 F32 stream, 8 positions), with the
+same clocks, L2 flush, e2e and CPU-baseline fields; N>1 runs replicas.
 """
 from __future__ import annotations
 
@@ -36,8 +37,9 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 DEFAULT_WORKLOAD = "smollm2-b5"
-# ternary GEMV workloads: rows, cols, group size, lanes
+# .spm operator workloads: rows, cols, group size, lanes (positions)
 TERNARY = {"ternary-4096-b8": (4096, 4096, 4096, 8)}
+DENSE = {"dense-f32-4096-b8": (4096, 4096, 4096, 8)}
 
 
 def _args():
@@ -204,7 +206,7 @@ def run_reference(a, rank, world):
 def main():
     a = _args()
     rank, world, local = _dist()
-    if a.workload in TERNARY:
+    if a.workload in TERNARY or a.workload in DENSE:
         return run_ternary_reference(a, rank, world) if a.impl == "reference" else run_ternary(a, rank, world, local)
     if a.impl == "reference":
         return run_reference(a, rank, world)
@@ -440,20 +442,27 @@ def gemv_roofline(eb, model, n, dev):
 
 
 # ---------------------------------------------------------------------------
-# ternary GEMV (spm-gemv-ref run_gemv)
+# .spm operators: ternary GEMV (spm-gemv-ref run_gemv), dense streamed (spm-linear)
 # ---------------------------------------------------------------------------
 
 def ternary_input(name: str, seed: int = 0):
-    """A one-stream ternary .spm file and the activations of the workload,
-    drawn with the value distributions of the reference's golden generator
+    """A one-stream .spm file and the activations of the workload.  Ternary:
+    the value distributions of the reference's golden generator
     (spm-vectors/src/draw.rs): weights uniform over {0, +1, -1}, scales
-    k/16 + 1/16 (k < 32), activations k/16 - 2 (k < 64)."""
+    k/16 + 1/16 (k < 32), activations k/16 - 2 (k < 64).  Dense F32: weights
+    and activations k/16 - 2 (k < 64), as spm-linear/tests/agreement.rs draws
+    them."""
     import numpy as np
 
     from emufpga_b200 import spmfile as sf
 
-    rows, cols, group, lanes = TERNARY[name]
     rng = np.random.default_rng(seed)
+    if name in DENSE:
+        rows, cols, group, lanes = DENSE[name]
+        w = (rng.integers(0, 64, rows * cols) / 16 - 2.0).astype(np.float32)
+        x = (rng.integers(0, 64, (lanes, cols)) / 16 - 2.0).astype(np.float32)
+        return sf.dense_file([(rows, cols)], group, [w]), x
+    rows, cols, group, lanes = TERNARY[name]
     codes = np.array([0, 1, 3], np.uint8)[rng.integers(0, 3, rows * cols)]
     groups = -(-rows * cols // group)
     scales = (rng.integers(0, 32, groups) / 16 + 0.0625).astype(np.float32)
@@ -462,13 +471,22 @@ def ternary_input(name: str, seed: int = 0):
 
 
 def _ternary_config(name):
-    rows, cols, group, lanes = TERNARY[name]
+    rows, cols, group, lanes = TERNARY.get(name) or DENSE[name]
     return {"workload": name, "rows": rows, "cols": cols, "group_size": group, "lanes": lanes}
 
 
-def ternary_cpu_baseline(data, x, seconds: float):
-    """The oracle's run_gemv (single-threaded, like the reference) on the
-    whole workload, repeated until `seconds` of work."""
+def _oracle_run(name, data, x):
+    """The oracle's form of the workload's operator: lanes x rows."""
+    from oracle import oracle as O
+
+    if name in DENSE:
+        return O.spm_streamed(data, x.ravel(), x.shape[0])
+    return O.spm_run_gemv(data, x)
+
+
+def ternary_cpu_baseline(name, data, x, seconds: float):
+    """The oracle's operator (single-threaded, like the reference's scan) on
+    the whole workload, repeated until `seconds` of work."""
     from oracle import oracle as O
 
     lanes, cols = x.shape
@@ -476,13 +494,13 @@ def ternary_cpu_baseline(data, x, seconds: float):
     t0 = time.perf_counter()
     runs = 0
     while True:
-        O.spm_run_gemv(data, x)
+        _oracle_run(name, data, x)
         runs += 1
         if time.perf_counter() - t0 > seconds:
             break
     dt = time.perf_counter() - t0
     return {"value": runs * rows * cols * lanes / dt, "unit": "weights/s", "cores": 1, "kind": "port",
-            "sample": f"{runs} whole scans of the workload (oracle run_gemv, one thread)"}
+            "sample": f"{runs} whole scans of the workload (oracle, one thread)"}
 
 
 def run_ternary(a, rank, world, local):
@@ -498,20 +516,28 @@ def run_ternary(a, rank, world, local):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         pg = dist
+    from emufpga_b200 import linear as L
     from emufpga_b200 import ternary as T
 
-    rows, cols, group, lanes = TERNARY[a.workload]
+    dense = a.workload in DENSE
+    rows, cols, group, lanes = (DENSE if dense else TERNARY)[a.workload]
     data, x = ternary_input(a.workload)
-    m = T.TernaryMatrix(data, 0, local)
+    m = L.DenseMatrix(data, 0, local) if dense else T.TernaryMatrix(data, 0, local)
     xd = torch.from_numpy(x).to(dev)
     y = torch.empty((lanes, rows), dtype=torch.float32, device=dev)
+
+    def gemv():
+        if dense:
+            m.streamed(xd, lanes, out=y)
+        else:
+            m.gemv(xd, out=y)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     warm, steps = max(a.warmup, 3), a.steps
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     for _ in range(warm):
-        m.gemv(xd, out=y)
+        gemv()
     torch.cuda.synchronize(dev)
     if pg:
         pg.barrier()
@@ -520,7 +546,7 @@ def run_ternary(a, rank, world, local):
         for i in range(steps):
             flush.zero_()
             starts[i].record(stream)
-            m.gemv(xd, out=y)
+            gemv()
             ends[i].record(stream)
         torch.cuda.synchronize(dev)
     local_ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
@@ -535,7 +561,7 @@ def run_ternary(a, rank, world, local):
     y_host = torch.empty((lanes, rows), dtype=torch.float32).pin_memory()
     for _ in range(warm):
         xd.copy_(x_host, non_blocking=True)
-        m.gemv(xd, out=y)
+        gemv()
         y_host.copy_(y, non_blocking=True)
     torch.cuda.synchronize(dev)
     if pg:
@@ -543,7 +569,7 @@ def run_ternary(a, rank, world, local):
     t0 = time.perf_counter()
     for _ in range(steps):
         xd.copy_(x_host, non_blocking=True)
-        m.gemv(xd, out=y)
+        gemv()
         y_host.copy_(y, non_blocking=True)
         torch.cuda.synchronize(dev)
     e2e_s = time.perf_counter() - t0
@@ -555,17 +581,20 @@ def run_ternary(a, rank, world, local):
     if rank == 0:
         from oracle import oracle as O
 
-        ok = bool((y_host.numpy().view("u4") == O.spm_run_gemv(data, x).view("u4")).all())
+        ok = bool((y_host.numpy().view("u4") == _oracle_run(a.workload, data, x).view("u4")).all())
         apps = rows * cols * lanes
         peak, how = _peaks()
         launch_s = local_ms / 1e3 / steps
         ach = m.payload_bytes / launch_s / 1e9
         line = {
-            "metric": "ternary weight applications/s", "value": apps * steps * world / (job_ms / 1e3),
+            "metric": ("dense" if dense else "ternary") + " weight applications/s",
+            "value": apps * steps * world / (job_ms / 1e3),
             "unit": "weights/s", "n_gpus": world, "steps": steps, "warmup": warm, "ms_per_step": job_ms / steps,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (weights uniform over {0,+1,-1}, scales and activations in sixteenths, as the "
-                    "reference's golden generator draws them)",
+            "data": ("synthetic (f32 weights and activations in sixteenths, as the reference's agreement test "
+                     "draws them)") if dense else ("synthetic (weights uniform over {0,+1,-1}, scales and "
+                                                  "activations in sixteenths, as the reference's golden generator "
+                                                  "draws them)"),
             "config": dict(_ternary_config(a.workload), parallelism=f"replicas x{world}" if world > 1 else
                            "single GPU", l2="flushed between timed steps (256 MiB write)",
                            bit_identical_to_oracle=ok),
@@ -573,14 +602,15 @@ def run_ternary(a, rank, world, local):
                     "d2h_bytes_per_step": lanes * rows * 4},
             "gpu_launches": steps,
             "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
-                         "peak_source": how, "traffic": None, "kernel": "ternary_gemv_kernel",
+                         "peak_source": how, "traffic": None,
+                         "kernel": "dense_streamed_kernel" if dense else "ternary_gemv_kernel",
                          "bytes_per_launch": m.payload_bytes,
                          "note": "bound by the sequential f32 chain per (row, lane) that bit-exactness "
                                  "requires, not by HBM"},
             "clocks": clocks.summary(),
         }
         if not a.no_cpu_baseline:
-            line["cpu_baseline"] = ternary_cpu_baseline(data, x, a.cpu_seconds)
+            line["cpu_baseline"] = ternary_cpu_baseline(a.workload, data, x, a.cpu_seconds)
         print(json.dumps(line), flush=True)
     m.close()
     if pg:
@@ -596,19 +626,20 @@ def run_ternary_reference(a, rank, world):
         return 0
     from oracle import oracle as O
 
-    rows, cols, group, lanes = TERNARY[a.workload]
+    rows, cols, group, lanes = TERNARY.get(a.workload) or DENSE[a.workload]
     data, x = ternary_input(a.workload)
     for _ in range(a.warmup):
-        O.spm_run_gemv(data, x)
+        _oracle_run(a.workload, data, x)
     times = []
     for _ in range(a.steps):
         t0 = time.perf_counter()
-        O.spm_run_gemv(data, x)
+        _oracle_run(a.workload, data, x)
         times.append(time.perf_counter() - t0)
         if sum(times) > 150.0:
             break
     value = rows * cols * lanes * len(times) / sum(times)
-    line = {"metric": "ternary weight applications/s", "value": value, "unit": "weights/s", "impl": "reference",
+    line = {"metric": ("dense" if a.workload in DENSE else "ternary") + " weight applications/s", "value": value,
+            "unit": "weights/s", "impl": "reference",
             "n_gpus": world, "steps": len(times), "warmup": a.warmup,
             "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (as the ours arm)",

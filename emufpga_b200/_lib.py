@@ -75,6 +75,12 @@ class TernaryInfo(C.Structure):
                 ("device_bytes", C.c_uint64)]
 
 
+class DenseInfo(C.Structure):
+    """spm_dense_info (spmgpu.h)."""
+    _fields_ = [("rows", C.c_uint32), ("cols", C.c_uint32), ("group_size", C.c_uint32), ("encoding", C.c_uint32),
+                ("groups", C.c_uint64), ("payload_bytes", C.c_uint64), ("device_bytes", C.c_uint64)]
+
+
 PROTOTYPES = {
     "spm_last_error": (C.c_char_p, []),
     "spm_version": (C.c_char_p, []),
@@ -126,6 +132,10 @@ PROTOTYPES = {
     "spm_ternary_free": (C.c_int32, [_P]),
     "spm_ternary_describe": (C.c_int32, [_P, C.POINTER(TernaryInfo)]),
     "spm_ternary_gemv": (C.c_int32, [_P, _P, C.c_int32, C.c_uint64, _P, _P]),
+    "spm_dense_upload": (C.c_int32, [_P, C.c_uint64, C.c_int32, C.c_int, C.POINTER(_P)]),
+    "spm_dense_free": (C.c_int32, [_P]),
+    "spm_dense_describe": (C.c_int32, [_P, C.POINTER(DenseInfo)]),
+    "spm_dense_streamed": (C.c_int32, [_P, _P, C.c_uint64, C.c_int32, _P, _P]),
 }
 
 _lib: C.CDLL | None = None

@@ -123,4 +123,15 @@ struct TernaryHost {
 };
 TernaryHost pack_ternary(const uint8_t* buf, uint64_t len, uint32_t index);
 
+// A dense (F32 or Bf16) stream repacked for the device: the group framing
+// removed, column-major with rows padded to a multiple of 32 (zeros), element
+// (r, c) at c * rows_pad + r, as f32 or as the raw bf16 bits.
+struct DenseHost {
+    uint32_t rows = 0, cols = 0, group_size = 0;
+    uint8_t encoding = 0;
+    uint64_t rows_pad = 0, groups = 0, payload_bytes = 0;
+    std::vector<uint8_t> data;
+};
+DenseHost pack_dense(const uint8_t* buf, uint64_t len, uint32_t index);
+
 }  // namespace spm

@@ -169,6 +169,55 @@ TernaryHost pack_ternary(const uint8_t* buf, uint64_t len, uint32_t index) {
     return t;
 }
 
+static const char* encoding_name(uint8_t enc) {  // Debug names of spm_layout::Encoding
+    switch (enc) {
+        case SPM_ENC_TERNARY: return "Ternary2F32I32";
+        case SPM_ENC_F32: return "F32";
+        case SPM_ENC_BF16: return "Bf16";
+        case SPM_ENC_Q6K: return "Q6K";
+        case SPM_ENC_Q5K: return "Q5K";
+        default: return "Q8_0";
+    }
+}
+
+DenseHost pack_dense(const uint8_t* buf, uint64_t len, uint32_t index) {
+    const SpmFile f = spm_file_parse(buf, len);
+    if (index >= f.desc.size()) fail(SPM_E_ARG, "stream index out of range");
+    const SpmDesc& d = f.desc[index];
+    // spm-codec-any/src/decode.rs:36-45: only the dense profiles decode to
+    // weights; the others need a scale-aware engine (LinearError::Stream)
+    if (d.encoding != SPM_ENC_F32 && d.encoding != SPM_ENC_BF16)
+        fail(SPM_E_STREAM, std::string("parameter stream: ") + encoding_name(d.encoding) +
+                               " needs a scale-aware engine");
+    const SpmSpan span = spm_file_locate(f, len, index);
+    DenseHost h;
+    h.rows = d.rows;
+    h.cols = d.cols;
+    h.group_size = d.group_size;
+    h.encoding = d.encoding;
+    h.groups = span.groups;
+    h.rows_pad = (uint64_t(d.rows) + 31) / 32 * 32;
+    const uint32_t es = d.encoding == SPM_ENC_F32 ? 4 : 2;
+    h.data.assign(h.rows_pad * d.cols * es, 0);
+    const uint64_t total = uint64_t(d.rows) * d.cols;
+    const uint8_t* p = buf + span.offset;
+    uint64_t r = 0, c = 0;  // element of the next weight: stream position c * rows + r
+    for (uint64_t g = 0; g < h.groups; ++g) {
+        const uint64_t count = std::min<uint64_t>(d.group_size, total - g * d.group_size);
+        const uint8_t* w = p + 4;  // the group scale is inert for the dense profiles
+        for (uint64_t i = 0; i < count; ++i) {
+            std::memcpy(&h.data[(c * h.rows_pad + r) * es], w + i * es, es);
+            if (++r == d.rows) {
+                r = 0;
+                ++c;
+            }
+        }
+        h.payload_bytes += count * es;
+        p += 4 + count * es;
+    }
+    return h;
+}
+
 }  // namespace spm
 
 using namespace spm;

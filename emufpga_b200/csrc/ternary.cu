@@ -30,20 +30,11 @@
 #include <memory>
 
 #include "abi.h"
+#include "chain.h"
 #include "ternary_kernel.cuh"
 
 namespace spm {
 namespace {
-
-// Lanes per thread: more lanes share one code word and group walk, fewer
-// lanes spread the chains over more warps.  Take the most lanes that still
-// leave about two warps per scheduler.
-int lanes_per_thread(uint64_t rows_pad, int lanes, int sms) {
-    const uint64_t target = 8ull * uint64_t(sms);
-    for (int L : {8, 4, 2})
-        if (lanes >= L && rows_pad / 32 * uint64_t((lanes + L - 1) / L) >= target) return L;
-    return 1;
-}
 
 template <int LPT>
 cudaError_t launch(const TernaryArgs& a, cudaStream_t stream) {
@@ -152,7 +143,7 @@ spm_status spm_ternary_gemv(const spm_ternary* t, const float* x_dev, int32_t la
         a.lanes = lanes;
         const cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
         cudaError_t e;
-        switch (lanes_per_thread(t->rows_pad, lanes, t->sms)) {
+        switch (chains_per_thread(t->rows_pad, lanes, t->sms)) {
             case 8: e = launch<8>(a, s); break;
             case 4: e = launch<4>(a, s); break;
             case 2: e = launch<2>(a, s); break;

@@ -149,6 +149,49 @@ def ternary_stream_bytes(codes: np.ndarray, scales: np.ndarray, group_size: int)
     return b"".join(parts)
 
 
+def bf16_round(values) -> np.ndarray:
+    """f32 -> bf16 bits, round to nearest even; NaN stays a quiet NaN
+    (spm-codec-bf16/src/convert.rs round)."""
+    bits = np.ascontiguousarray(values, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    lsb = (bits >> 16) & 1
+    out = (((bits + 0x7FFF + lsb) & 0xFFFFFFFF) >> 16).astype(np.uint16)
+    nan = np.isnan(np.asarray(values, dtype=np.float32))
+    out[nan] = ((bits[nan] >> 16) | 0x0040).astype(np.uint16)
+    return out
+
+
+def dense_stream_bytes(weights: np.ndarray, group_size: int, encoding: int = F32) -> bytes:
+    """The groups of one dense stream: f32 weights in stream order (column-
+    major), framed with the inert scale 1.0, stored as f32 or rounded to bf16."""
+    w = np.ascontiguousarray(weights, dtype=np.float32).ravel()
+    if encoding == F32:
+        payload = w.astype("<f4").view(np.uint8)
+        es = 4
+    elif encoding == BF16:
+        payload = bf16_round(w).astype("<u2").view(np.uint8)
+        es = 2
+    else:
+        raise ValueError("dense streams are F32 or BF16")
+    one = struct.pack("<f", 1.0)
+    parts = []
+    for start in range(0, w.size, group_size):
+        n = min(group_size, w.size - start)
+        parts.append(one + payload[start * es:(start + n) * es].tobytes())
+    return b"".join(parts)
+
+
+def dense_file(shapes: Sequence[tuple[int, int]], group_size: int, matrices: Sequence[np.ndarray],
+               encoding: int = F32) -> bytes:
+    """A .spm file of dense streams, one per (rows, cols) shape, each matrix
+    given in stream order."""
+    out = render_header(len(shapes))
+    for rows, cols in shapes:
+        out += render_descriptor(rows, cols, group_size, encoding)
+    for m in matrices:
+        out += dense_stream_bytes(m, group_size, encoding)
+    return out
+
+
 def ternary_file(rows: int, cols: int, group_size: int, codes: np.ndarray, scales: np.ndarray,
                  lane_count: int = 1) -> bytes:
     """A one-stream ternary .spm file (codes in stream order)."""

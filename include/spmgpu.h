@@ -256,6 +256,30 @@ spm_status spm_ternary_describe(const spm_ternary* t, spm_ternary_info* out);
 spm_status spm_ternary_gemv(const spm_ternary* t, const float* x_dev, int32_t lanes, uint64_t x_cols,
                             float* y_dev, void* cuda_stream);
 
+/* spm_linear::streamed (spm-linear/src/stream.rs:31-125) for one dense .spm
+ * stream (Encoding::F32 or Bf16; the group scale is inert): y[p][r] =
+ * sum over c ascending of fma(W[r][c], x[p][c], .) from +0, one fused
+ * multiply-add per weight and position as in resident.rs:124-137, so results
+ * are bit-identical to the reference's.  spm_dense_upload packs stream
+ * `index` into HBM; a profile without a dense decoder is refused as the
+ * reference's DecodeError::Unsupported (SPM_E_STREAM, "parameter stream: Q6K
+ * needs a scale-aware engine").  spm_dense_streamed: x_dev holds x_len floats
+ * (positions x cols, LinearError::ActivationLen -> SPM_E_ACTIVATION_LEN when
+ * x_len < positions x cols), y_dev positions x rows; device pointers,
+ * enqueued on cuda_stream (NULL = default stream). */
+typedef struct spm_dense spm_dense;
+typedef struct spm_dense_info {
+    uint32_t rows, cols, group_size, encoding;
+    uint64_t groups;
+    uint64_t payload_bytes;   /* weight bytes of the stream (scales excluded) */
+    uint64_t device_bytes;    /* HBM held by the packed stream                */
+} spm_dense_info;
+spm_status spm_dense_upload(const uint8_t* spm, uint64_t len, int32_t index, int device, spm_dense** out);
+spm_status spm_dense_free(spm_dense* t);
+spm_status spm_dense_describe(const spm_dense* t, spm_dense_info* out);
+spm_status spm_dense_streamed(const spm_dense* t, const float* x_dev, uint64_t x_len, int32_t positions,
+                              float* y_dev, void* cuda_stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -78,6 +78,10 @@ def lib() -> C.CDLL:
         L.or_spm_describe.argtypes = [u8, C.c_uint64, C.c_int32, u32p, u32p, u32p, u32p, u32p, C.c_char_p, C.c_int]
         L.or_spm_run_gemv.restype = C.c_int
         L.or_spm_run_gemv.argtypes = [u8, C.c_uint64, fp, C.c_int, C.c_uint64, fp, C.c_uint64, C.c_char_p, C.c_int]
+        L.or_spm_streamed.restype = C.c_int
+        L.or_spm_streamed.argtypes = [u8, C.c_uint64, C.c_int32, C.c_uint32, C.c_uint32, fp, C.c_uint64, C.c_int,
+                                      fp, C.c_char_p, C.c_int]
+        L.or_resident.argtypes = [fp, C.c_uint32, C.c_uint32, fp, C.c_int, fp]
         _lib = L
     return _lib
 
@@ -236,6 +240,31 @@ def spm_run_gemv(spm, x: np.ndarray) -> np.ndarray:
     if rc:
         raise SpmError(rc, err.value.decode())
     return bank[: rows.value * lanes].reshape(rows.value, lanes).T.copy()
+
+
+def spm_streamed(spm, x: np.ndarray, positions: int, index: int = 0, shape: tuple | None = None) -> np.ndarray:
+    """spm_linear::streamed on stream `index`: x is the flat activation
+    buffer (positions x cols); returns positions x rows.  `shape` (rows,
+    cols) defaults to the stream's descriptor."""
+    raw = _spm_bytes(spm)
+    rows, cols = shape if shape is not None else (lambda d: (d["rows"], d["cols"]))(spm_describe(spm, index))
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    out = np.empty(max(1, positions * rows), dtype=np.float32)
+    err = C.create_string_buffer(256)
+    rc = lib().or_spm_streamed(raw.ctypes.data, raw.size, index, rows, cols, _f(x), x.size, positions, _f(out),
+                               err, 256)
+    if rc:
+        raise SpmError(rc, err.value.decode())
+    return out[: positions * rows].reshape(positions, rows)
+
+
+def resident(w: np.ndarray, rows: int, cols: int, x: np.ndarray, positions: int) -> np.ndarray:
+    """spm_linear::resident: w in stream order (w[k] = W[k % rows][k / rows])."""
+    w = np.ascontiguousarray(w, dtype=np.float32).ravel()
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    out = np.empty(max(1, positions * rows), dtype=np.float32)
+    lib().or_resident(_f(w), rows, cols, _f(x), positions, _f(out))
+    return out[: positions * rows].reshape(positions, rows)
 
 
 def cfg_of(shape) -> Cfg:

@@ -1220,3 +1220,124 @@ int or_spm_run_gemv(const uint8_t* spm, uint64_t len, const float* x, int lanes,
     free(d);
     return 0;
 }
+
+/* spm_linear::resident / apply_weight (resident.rs:79-137): for every weight
+ * in stream order, every position: out = fma(w, x, out). */
+void or_resident(const float* w, uint32_t rows, uint32_t cols, const float* x, int positions, float* out) {
+    memset(out, 0, sizeof(float) * (size_t)positions * rows);
+    const uint64_t total = (uint64_t)rows * cols;
+    for (uint64_t k = 0; k < total; ++k) {
+        const uint64_t row = k % rows, col = k / rows;
+        for (int p = 0; p < positions; ++p) {
+            float* slot = out + (uint64_t)p * rows + row;
+            *slot = fmaf(w[k], x[(uint64_t)p * cols + col], *slot);
+        }
+    }
+}
+
+static const char* spm_encoding_name(uint8_t enc) {
+    switch (enc) { /* Debug names of spm_layout::Encoding */
+        case 1: return "Ternary2F32I32";
+        case 2: return "F32";
+        case 3: return "Bf16";
+        case 4: return "Q6K";
+        case 5: return "Q5K";
+        default: return "Q8_0";
+    }
+}
+
+int or_spm_streamed(const uint8_t* spm, uint64_t len, int32_t index, uint32_t rows, uint32_t cols,
+                    const float* x, uint64_t x_len, int positions, float* out, char* err, int errlen) {
+    uint32_t n = 0;
+    or_spm_desc* d = NULL;
+    uint64_t at = 0;
+    char msg[160];
+    int rc = spm_parse(spm, len, &n, &d, &at, err, errlen);
+    if (rc) return rc;
+    /* check (stream.rs:63-76): before any group is pulled */
+    const uint64_t need = (uint64_t)positions * cols;
+    if (x_len < need) {
+        free(d);
+        snprintf(msg, sizeof msg, "need %llu activations, got %llu", (unsigned long long)need,
+                 (unsigned long long)x_len);
+        return spm_err(err, errlen, OR_SPM_ACTIVATIONS, msg);
+    }
+    const uint64_t total = (uint64_t)rows * cols;
+    memset(out, 0, sizeof(float) * (size_t)positions * rows);
+    or_cursor cur = {0, 0};
+    cursor_settle(&cur, d, n);
+    /* the streams before `index` are read past group by group */
+    while (cur.stream < n && cur.stream < (uint32_t)index) {
+        const uint64_t count = cursor_group_len(&cur, d);
+        const uint64_t needed = 4 + spm_bytes_for(d[cur.stream].encoding, count), available = len - at;
+        if (available < needed) {
+            free(d);
+            snprintf(msg, sizeof msg, "payload truncated: group needs %llu bytes, %llu remain",
+                     (unsigned long long)needed, (unsigned long long)available);
+            return spm_err(err, errlen, OR_SPM_TRUNCATED, msg);
+        }
+        at += needed;
+        cur.group++;
+        cursor_settle(&cur, d, n);
+    }
+    float* buf = NULL;
+    uint64_t done = 0;
+    while (done < total) { /* streamed (stream.rs:31-55) */
+        if (cur.stream >= n) {
+            free(buf);
+            free(d);
+            snprintf(msg, sizeof msg, "stream ended after %llu of %llu weights", (unsigned long long)done,
+                     (unsigned long long)total);
+            return spm_err(err, errlen, OR_SPM_STREAMED_TRUNCATED, msg);
+        }
+        const uint8_t enc = d[cur.stream].encoding;
+        const uint64_t count = cursor_group_len(&cur, d);
+        const uint64_t needed = 4 + spm_bytes_for(enc, count), available = len - at;
+        if (available < needed) {
+            free(buf);
+            free(d);
+            snprintf(msg, sizeof msg, "payload truncated: group needs %llu bytes, %llu remain",
+                     (unsigned long long)needed, (unsigned long long)available);
+            return spm_err(err, errlen, OR_SPM_TRUNCATED, msg);
+        }
+        const uint8_t* p = spm + at + 4;
+        at += needed;
+        cur.group++;
+        cursor_settle(&cur, d, n);
+        if (enc != 2 && enc != 3) { /* spm-codec-any/src/decode.rs:36-45 */
+            free(buf);
+            free(d);
+            snprintf(msg, sizeof msg, "parameter stream: %s needs a scale-aware engine", spm_encoding_name(enc));
+            return spm_err(err, errlen, OR_SPM_UNSUPPORTED, msg);
+        }
+        float* nb = (float*)realloc(buf, sizeof(float) * (count ? count : 1));
+        if (!nb) {
+            free(buf);
+            free(d);
+            return spm_err(err, errlen, OR_SPM_TRUNCATED, "out of memory");
+        }
+        buf = nb;
+        for (uint64_t i = 0; i < count; ++i) {
+            if (enc == 2) {
+                memcpy(&buf[i], p + 4 * i, 4);
+            } else { /* widen: the bf16 bits become the high half of an f32 */
+                const uint32_t bits = ((uint32_t)p[2 * i] | ((uint32_t)p[2 * i + 1] << 8)) << 16;
+                memcpy(&buf[i], &bits, 4);
+            }
+        }
+        /* apply (stream.rs:107-125): every weight, every position */
+        for (uint64_t i = 0; i < count; ++i) {
+            const uint64_t k = done + i;
+            if (k >= total) break; /* a group that runs past the matrix: its tail is not applied */
+            const uint64_t row = k % rows, col = k / rows;
+            for (int q = 0; q < positions; ++q) {
+                float* slot = out + (uint64_t)q * rows + row;
+                *slot = fmaf(buf[i], x[(uint64_t)q * cols + col], *slot);
+            }
+        }
+        done += count;
+    }
+    free(buf);
+    free(d);
+    return 0;
+}

@@ -127,6 +127,22 @@ int or_spm_describe(const uint8_t* spm, uint64_t len, int32_t index, uint32_t* s
 int or_spm_run_gemv(const uint8_t* spm, uint64_t len, const float* x, int lanes, uint64_t x_cols,
                     float* bank, uint64_t bank_cap, char* err, int errlen);
 
+/* spm_linear::streamed (spm-linear/src/stream.rs:31-125) for the stream
+ * `index` of a .spm file: skip the groups of the streams before it, then pull
+ * groups until rows x cols weights, decoding F32 (spm-codec-dense) or Bf16
+ * (spm-codec-bf16/src/convert.rs widen) and applying each weight to every
+ * position as out = fma(w, x, out) (resident.rs:124-137).  x holds x_len
+ * floats (positions x cols); out positions x rows.  Extra status codes: */
+enum {
+    OR_SPM_STREAMED_TRUNCATED = -6,  /* LinearError::Truncated: stream ended early     */
+    OR_SPM_UNSUPPORTED = -7          /* DecodeError::Unsupported -> LinearError::Stream */
+};
+int or_spm_streamed(const uint8_t* spm, uint64_t len, int32_t index, uint32_t rows, uint32_t cols,
+                    const float* x, uint64_t x_len, int positions, float* out, char* err, int errlen);
+/* spm_linear::resident (resident.rs:79-96): the same product with the weights
+ * given in stream order (w[k] = W[k % rows][k / rows]). */
+void or_resident(const float* w, uint32_t rows, uint32_t cols, const float* x, int positions, float* out);
+
 #ifdef __cplusplus
 }
 #endif

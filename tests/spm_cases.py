@@ -1,4 +1,6 @@
-"""Seeded ternary test cases, as the reference's golden generator draws them.
+"""Seeded .spm test cases, as the reference's tests draw them.
+
+Ternary cases:
 
 Restates spm-vectors/src/draw.rs and generate.rs: an xorshift64 state
 (seed | 1; s ^= s << 13, s ^= s >> 7, s ^= s << 17), weights drawn first
@@ -7,6 +9,9 @@ Restates spm-vectors/src/draw.rs and generate.rs: an xorshift64 state
 (k / 16 - 2.0, k = state % 64).  Sixteenths are exact in f32, so these cases
 add no rounding of their own.  Also the f64 reference of spm-numeric
 (src/matmul.rs:38-48) that the reference's correctness test compares against.
+
+Dense cases: the weights of spm-linear/tests/agreement.rs:17-31, the same
+xorshift64 with values state % 64 / 16 - 2.
 """
 from __future__ import annotations
 
@@ -81,3 +86,13 @@ def random_file(rng: np.random.Generator, rows: int, cols: int, group: int, rese
     groups = -(-total // group)
     scales = (rng.standard_normal(groups) * rng.choice([1e-3, 1.0, 1e3], groups)).astype(np.float32)
     return sf.ternary_file(rows, cols, group, codes, scales), codes, scales
+
+
+def sixteenths(seed: int, count: int) -> np.ndarray:
+    """spm-linear/tests/agreement.rs weights(seed, count)."""
+    state = seed | 1
+    out = np.empty(count, np.float32)
+    for i in range(count):
+        state = _next(state)
+        out[i] = np.float32(state % 64) / np.float32(16.0) - np.float32(2.0)
+    return out

@@ -15,7 +15,7 @@ import emufpga_b200 as eb
 from emufpga_b200 import spmfile as sf
 from emufpga_b200 import ternary as T
 from oracle import oracle as O
-from tests.ternary_cases import generate, random_file, reference_gemv
+from tests.spm_cases import generate, random_file, reference_gemv
 
 pytestmark = pytest.mark.gpu
 

@@ -17,7 +17,7 @@ import emufpga_b200 as eb
 from emufpga_b200 import spmfile as sf
 from emufpga_b200 import ternary as T
 from oracle import oracle as O
-from tests.ternary_cases import generate, random_file, reference_gemv
+from tests.spm_cases import generate, random_file, reference_gemv
 
 GOLDEN = (Path(__file__).resolve().parent / "golden" / "tiny_ternary.spm").read_bytes()
 SPM_E_ARG, SPM_E_ACTIVATION_LEN, SPM_E_TRUNCATED, SPM_E_STREAM, SPM_E_ENCODING = -1, -2, -3, -4, -5
