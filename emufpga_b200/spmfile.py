@@ -10,10 +10,12 @@ covers `group_size` consecutive positions and the last one is short.
 
 Ternary payloads (spm-codec/src/lib.rs:1-31) pack four weights to a byte,
 least significant pair first: code 00 = 0, 01 = +1, 11 = -1 (10 is reserved);
-a short group's final byte is zero-padded.
+a short group's final byte is zero-padded.  Dense payloads are little-endian
+f32, or bf16 rounded to nearest even (spm-codec-bf16/src/convert.rs), behind
+the inert scale 1.0.
 
-Reading is done by the library (spm_file_probe / spm_file_stream and
-spm_ternary_upload); this module only builds files.
+Reading is done by the library (spm_file_probe / spm_file_stream,
+spm_ternary_upload, spm_dense_upload); this module only builds files.
 """
 from __future__ import annotations
 
