@@ -81,6 +81,12 @@ class DenseInfo(C.Structure):
                 ("groups", C.c_uint64), ("payload_bytes", C.c_uint64), ("device_bytes", C.c_uint64)]
 
 
+class SweepInfo(C.Structure):
+    """spm_sweep_info (spmgpu.h)."""
+    _fields_ = [("streams", C.c_int32), ("position", C.c_int32), ("host_bytes", C.c_uint64),
+                ("device_bytes", C.c_uint64), ("copies", C.c_uint64), ("bytes_copied", C.c_uint64)]
+
+
 PROTOTYPES = {
     "spm_last_error": (C.c_char_p, []),
     "spm_version": (C.c_char_p, []),
@@ -136,6 +142,15 @@ PROTOTYPES = {
     "spm_dense_free": (C.c_int32, [_P]),
     "spm_dense_describe": (C.c_int32, [_P, C.POINTER(DenseInfo)]),
     "spm_dense_streamed": (C.c_int32, [_P, _P, C.c_uint64, C.c_int32, _P, _P]),
+    "spm_sweep_open": (C.c_int32, [_P, C.c_uint64, C.c_int, C.c_uint64, C.POINTER(_P)]),
+    "spm_sweep_open_file": (C.c_int32, [C.c_char_p, C.c_int, C.c_uint64, C.POINTER(_P)]),
+    "spm_sweep_close": (C.c_int32, [_P]),
+    "spm_sweep_describe": (C.c_int32, [_P, C.POINTER(SweepInfo)]),
+    "spm_sweep_stream": (C.c_int32, [_P, C.c_int32, _U32P, _U32P, _U32P]),
+    "spm_sweep_next": (C.c_int32, [_P, _P, C.c_uint64, C.c_int32, _P, _P, _I32P]),
+    "spm_sweep_rewind": (C.c_int32, [_P]),
+    "spm_sweep_plan": (C.c_int32, [_U64P, C.c_int32, C.c_uint64, _I32P, C.c_int32, C.POINTER(C.c_int64),
+                                   C.c_int64, C.POINTER(C.c_int64)]),
 }
 
 _lib: C.CDLL | None = None

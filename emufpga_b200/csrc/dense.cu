@@ -18,7 +18,7 @@
 
 #include "abi.h"
 #include "chain.h"
-#include "dense_kernel.cuh"
+#include "chain_launch.h"
 
 namespace spm {
 namespace {
@@ -42,6 +42,14 @@ cudaError_t launch_dense_ppt(int ppt, const DenseArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace
+
+cudaError_t launch_dense_streamed(const DenseArgs& a, bool bf16, int sms, cudaStream_t stream) {
+    // four positions per thread at most: eight would need more than 255
+    // registers for the hoisted activations
+    const int ppt = chains_per_thread(a.rows_pad, a.positions, sms, 4);
+    return bf16 ? launch_dense_ppt<true>(ppt, a, stream) : launch_dense_ppt<false>(ppt, a, stream);
+}
+
 }  // namespace spm
 
 using namespace spm;
@@ -120,12 +128,8 @@ spm_status spm_dense_streamed(const spm_dense* t, const float* x_dev, uint64_t x
         a.rows = t->rows;
         a.cols = t->cols;
         a.positions = positions;
-        const cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
-        // four positions per thread at most: eight would need more than 255
-        // registers for the hoisted activations
-        const int ppt = chains_per_thread(t->rows_pad, positions, t->sms, 4);
-        const cudaError_t e = t->encoding == SPM_ENC_BF16 ? launch_dense_ppt<true>(ppt, a, s)
-                                                          : launch_dense_ppt<false>(ppt, a, s);
+        const cudaError_t e = launch_dense_streamed(a, t->encoding == SPM_ENC_BF16, t->sms,
+                                                    static_cast<cudaStream_t>(cuda_stream));
         if (e == cudaErrorInvalidConfiguration) fail(SPM_E_ARG, "too many rows x positions for one launch");
         CUDA_OK(e);
     });

@@ -7,9 +7,6 @@
 #endif
 
 namespace spm {
-namespace {
-
-constexpr int kDenseThreads = 128;
 
 struct DenseArgs {
     const void* w;     // column-major, element (r, c) at c * rows_pad + r (f32 or bf16 bits)
@@ -19,6 +16,10 @@ struct DenseArgs {
     uint32_t rows, cols;
     int32_t positions;
 };
+
+namespace {
+
+constexpr int kDenseThreads = 128;
 
 template <bool BF16>
 __device__ __forceinline__ float dense_weight(const void* w, uint64_t at) {

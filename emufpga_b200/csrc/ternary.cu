@@ -31,7 +31,7 @@
 
 #include "abi.h"
 #include "chain.h"
-#include "ternary_kernel.cuh"
+#include "chain_launch.h"
 
 namespace spm {
 namespace {
@@ -46,6 +46,16 @@ cudaError_t launch(const TernaryArgs& a, cudaStream_t stream) {
 }
 
 }  // namespace
+
+cudaError_t launch_ternary_gemv(const TernaryArgs& a, int sms, cudaStream_t stream) {
+    switch (chains_per_thread(a.rows_pad, a.lanes, sms)) {
+        case 8: return launch<8>(a, stream);
+        case 4: return launch<4>(a, stream);
+        case 2: return launch<2>(a, stream);
+        default: return launch<1>(a, stream);
+    }
+}
+
 }  // namespace spm
 
 using namespace spm;
@@ -141,14 +151,7 @@ spm_status spm_ternary_gemv(const spm_ternary* t, const float* x_dev, int32_t la
         a.r = t->rows % t->group_size;
         a.last_group = t->groups ? uint32_t(t->groups - 1) : 0u;
         a.lanes = lanes;
-        const cudaStream_t s = static_cast<cudaStream_t>(cuda_stream);
-        cudaError_t e;
-        switch (chains_per_thread(t->rows_pad, lanes, t->sms)) {
-            case 8: e = launch<8>(a, s); break;
-            case 4: e = launch<4>(a, s); break;
-            case 2: e = launch<2>(a, s); break;
-            default: e = launch<1>(a, s); break;
-        }
+        const cudaError_t e = launch_ternary_gemv(a, t->sms, static_cast<cudaStream_t>(cuda_stream));
         if (e == cudaErrorInvalidConfiguration) fail(SPM_E_ARG, "too many rows x lanes for one launch");
         CUDA_OK(e);
     });

@@ -12,11 +12,6 @@
 #endif
 
 namespace spm {
-namespace {
-
-constexpr int kTernaryThreads = 128;
-constexpr int kCodeAhead = 4;   // code words in flight per thread (64 columns)
-constexpr uint32_t kAhead = 64; // columns between an activation/scale prefetch and its use
 
 struct TernaryArgs {
     const uint32_t* codes;
@@ -29,6 +24,12 @@ struct TernaryArgs {
     uint32_t last_group;  // groups - 1
     int32_t lanes;
 };
+
+namespace {
+
+constexpr int kTernaryThreads = 128;
+constexpr int kCodeAhead = 4;   // code words in flight per thread (64 columns)
+constexpr uint32_t kAhead = 64; // columns between an activation/scale prefetch and its use
 
 template <int LPT>
 __global__ void __launch_bounds__(kTernaryThreads) ternary_gemv_kernel(const TernaryArgs a) {

@@ -280,6 +280,54 @@ spm_status spm_dense_describe(const spm_dense* t, spm_dense_info* out);
 spm_status spm_dense_streamed(const spm_dense* t, const float* x_dev, uint64_t x_len, int32_t positions,
                               float* y_dev, void* cuda_stream);
 
+/* ---- host-to-HBM streaming of a .spm file ----
+ * The reference's file-backed weight stream (spm-stream-file/src/prefetch.rs:
+ * PrefetchFileWeightStream reads ahead into a bounded buffer) consumed stream
+ * by stream in file order by streamed()/run_gemv and rewound between sweeps
+ * (spm-stream-groups/src/groups.rs:88-117).  spm_sweep_open packs every stream
+ * into pinned host memory (dense F32/Bf16 and ternary streams; the other
+ * profiles are refused as by spm_dense_upload) and keeps only a ring of
+ * device_bytes on the device (0: twice the largest packed stream; less than
+ * the largest is SPM_E_ARG).  spm_sweep_next runs the next stream in file
+ * order on cuda_stream -- dense streams as spm_dense_streamed, ternary ones
+ * as spm_ternary_gemv with x_cols = cols, bit-identical to the reference --
+ * and copies the following streams into the ring meanwhile, as far as it
+ * holds them, on a copy stream of its own.  x_dev holds x_len floats
+ * (positions x cols), y_dev positions x rows; *stream_index receives the
+ * stream run.  Once every stream has run, spm_sweep_next is SPM_E_TRUNCATED
+ * until spm_sweep_rewind; a rewind in mid-sweep drops what was read ahead. */
+typedef struct spm_sweep spm_sweep;
+typedef struct spm_sweep_info {
+    int32_t streams, position;   /* stream count; streams run in this sweep */
+    uint64_t host_bytes;         /* pinned host memory of the packed streams */
+    uint64_t device_bytes;       /* the ring                                 */
+    uint64_t copies, bytes_copied;
+} spm_sweep_info;
+spm_status spm_sweep_open(const uint8_t* spm, uint64_t len, int device, uint64_t device_bytes, spm_sweep** out);
+spm_status spm_sweep_open_file(const char* path, int device, uint64_t device_bytes, spm_sweep** out);
+spm_status spm_sweep_close(spm_sweep* s);
+spm_status spm_sweep_describe(const spm_sweep* s, spm_sweep_info* out);
+spm_status spm_sweep_stream(const spm_sweep* s, int32_t index, uint32_t* rows, uint32_t* cols, uint32_t* encoding);
+spm_status spm_sweep_next(spm_sweep* s, const float* x_dev, uint64_t x_len, int32_t positions, float* y_dev,
+                          void* cuda_stream, int32_t* stream_index);
+spm_status spm_sweep_rewind(spm_sweep* s);
+/* The ring schedule of a sweep on the host, for checking it without a device:
+ * streams regions of region_bytes (256-byte multiples) in a ring of
+ * device_bytes, driven by `script` (SPM_PLAN_NEXT / SPM_PLAN_REWIND); *log_len
+ * receives the number of log records and, when log is not NULL (log_cap
+ * records of 4 int64: kind, stream, ring offset, event pair), the records in
+ * issue order.  The CUDA backend issues exactly these actions for the same
+ * calls: SPM_PLAN_EVENTS creates an event pair, SPM_PLAN_WAIT makes the copy
+ * stream wait for a pair's consumed event, SPM_PLAN_COPY copies a stream then
+ * records its copied event, SPM_PLAN_LAUNCH waits for copied, runs the kernel
+ * and records consumed. */
+enum { SPM_PLAN_NEXT = 1, SPM_PLAN_REWIND = 2 };
+enum { SPM_PLAN_EVENTS = 1, SPM_PLAN_WAIT = 2, SPM_PLAN_COPY = 3, SPM_PLAN_LAUNCH = 4, SPM_PLAN_REFUSED = 5,
+       SPM_PLAN_REWOUND = 6 };
+spm_status spm_sweep_plan(const uint64_t* region_bytes, int32_t streams, uint64_t device_bytes,
+                          const int32_t* script, int32_t script_len, int64_t* log, int64_t log_cap,
+                          int64_t* log_len);
+
 #ifdef __cplusplus
 }
 #endif
