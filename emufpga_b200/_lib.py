@@ -142,6 +142,10 @@ PROTOTYPES = {
     "spm_dense_free": (C.c_int32, [_P]),
     "spm_dense_describe": (C.c_int32, [_P, C.POINTER(DenseInfo)]),
     "spm_dense_streamed": (C.c_int32, [_P, _P, C.c_uint64, C.c_int32, _P, _P]),
+    "spm_qblocks_upload": (C.c_int32, [_P, C.c_uint64, C.c_int32, C.c_int, C.POINTER(_P)]),
+    "spm_qblocks_free": (C.c_int32, [_P]),
+    "spm_qblocks_describe": (C.c_int32, [_P, C.POINTER(DenseInfo)]),
+    "spm_qblocks_gemv": (C.c_int32, [_P, _P, C.c_uint64, C.c_int32, _P, _P]),
     "spm_sweep_open": (C.c_int32, [_P, C.c_uint64, C.c_int, C.c_uint64, C.POINTER(_P)]),
     "spm_sweep_open_file": (C.c_int32, [C.c_char_p, C.c_int, C.c_uint64, C.POINTER(_P)]),
     "spm_sweep_close": (C.c_int32, [_P]),

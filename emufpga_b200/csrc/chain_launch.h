@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include "dense_kernel.cuh"
+#include "qblock_kernel.cuh"
 #include "ternary_kernel.cuh"
 
 namespace spm {
@@ -13,5 +14,7 @@ namespace spm {
 // than 2^31 - 1 blocks.
 cudaError_t launch_ternary_gemv(const TernaryArgs& a, int sms, cudaStream_t stream);
 cudaError_t launch_dense_streamed(const DenseArgs& a, bool bf16, int sms, cudaStream_t stream);
+// encoding: the .spm code of a block profile (SPM_ENC_Q8_0, _Q6K, _Q5K).
+cudaError_t launch_qblock_chain(const QBlockArgs& a, uint8_t encoding, int sms, cudaStream_t stream);
 
 }  // namespace spm

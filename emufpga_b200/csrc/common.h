@@ -134,4 +134,16 @@ struct DenseHost {
 };
 DenseHost pack_dense(const uint8_t* buf, uint64_t len, uint32_t index);
 
+// A Q-profile stream (Q8_0, Q6_K, Q5_K) with the group framing removed: its
+// GGML blocks back to back in source row-major order.  The reference's
+// consumers take exactly one block per group (spm-granite-moe/src/
+// layout.rs:225-227, gemma_smoke.rs:219-221).
+struct QBlockHost {
+    uint32_t rows = 0, cols = 0, group_size = 0;
+    uint8_t encoding = 0;
+    uint64_t groups = 0;
+    std::vector<uint8_t> blocks;
+};
+QBlockHost pack_qblocks(const uint8_t* buf, uint64_t len, uint32_t index);
+
 }  // namespace spm

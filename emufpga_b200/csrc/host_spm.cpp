@@ -218,6 +218,37 @@ DenseHost pack_dense(const uint8_t* buf, uint64_t len, uint32_t index) {
     return h;
 }
 
+QBlockHost pack_qblocks(const uint8_t* buf, uint64_t len, uint32_t index) {
+    const SpmFile f = spm_file_parse(buf, len);
+    if (index >= f.desc.size()) fail(SPM_E_ARG, "stream index out of range");
+    const SpmDesc& d = f.desc[index];
+    uint32_t bv = 0, bb = 0;
+    switch (d.encoding) {
+        case SPM_ENC_Q8_0: bv = 32, bb = 34; break;
+        case SPM_ENC_Q6K: bv = 256, bb = 210; break;
+        case SPM_ENC_Q5K: bv = 256, bb = 176; break;
+        default:
+            fail(SPM_E_STREAM, std::string("stream is ") + encoding_name(d.encoding) +
+                                   ", not a block profile (Q8_0, Q6K or Q5K)");
+    }
+    const uint64_t total = uint64_t(d.rows) * d.cols;
+    // every group must be exactly one block, the last one included
+    if (d.group_size != bv || total % bv)
+        fail(SPM_E_STREAM, std::string("unexpected packed group: ") + encoding_name(d.encoding) +
+                               " streams hold one " + std::to_string(bv) + "-value block per group");
+    const SpmSpan span = spm_file_locate(f, len, index);
+    QBlockHost h;
+    h.rows = d.rows;
+    h.cols = d.cols;
+    h.group_size = d.group_size;
+    h.encoding = d.encoding;
+    h.groups = span.groups;
+    h.blocks.resize(h.groups * bb);
+    const uint8_t* p = buf + span.offset;
+    for (uint64_t g = 0; g < h.groups; ++g, p += 4 + bb) std::memcpy(&h.blocks[g * bb], p + 4, bb);
+    return h;
+}
+
 }  // namespace spm
 
 using namespace spm;

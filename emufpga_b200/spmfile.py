@@ -194,6 +194,27 @@ def dense_file(shapes: Sequence[tuple[int, int]], group_size: int, matrices: Seq
     return out
 
 
+BLOCK = {Q8_0: (32, 34), Q6_K: (256, 210), Q5_K: (256, 176)}
+
+
+def qblock_stream_bytes(blocks: bytes, encoding: int) -> bytes:
+    """The groups of one block-profile stream: one GGML block per group
+    (source row-major order), each behind the inert scale 1.0."""
+    _, bb = BLOCK[encoding]
+    if len(blocks) % bb:
+        raise ValueError("not a whole number of blocks")
+    one = struct.pack("<f", 1.0)
+    return b"".join(one + blocks[i:i + bb] for i in range(0, len(blocks), bb))
+
+
+def qblock_file(rows: int, cols: int, encoding: int, blocks: bytes) -> bytes:
+    """A one-stream .spm file of GGML blocks (rows x cols values, row-major)."""
+    bv, bb = BLOCK[encoding]
+    if rows * cols != len(blocks) // bb * bv:
+        raise ValueError("rows x cols must be the blocks' value count")
+    return render_header(1) + render_descriptor(rows, cols, bv, encoding) + qblock_stream_bytes(blocks, encoding)
+
+
 def ternary_file(rows: int, cols: int, group_size: int, codes: np.ndarray, scales: np.ndarray,
                  lane_count: int = 1) -> bytes:
     """A one-stream ternary .spm file (codes in stream order)."""

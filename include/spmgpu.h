@@ -280,6 +280,23 @@ spm_status spm_dense_describe(const spm_dense* t, spm_dense_info* out);
 spm_status spm_dense_streamed(const spm_dense* t, const float* x_dev, uint64_t x_len, int32_t positions,
                               float* y_dev, void* cuda_stream);
 
+/* The block profiles of .spm files (Encoding::Q8_0, Q6K, Q5K: GGML blocks in
+ * source row-major order, one block per group) as the reference's block
+ * consumers compute them: q6_operation (spm-granite-moe/src/layout.rs:208-242)
+ * and stream_matrix (gemma_smoke.rs:201-236) decode each block with
+ * spm-gguf's decoders and apply value k = W[k / cols][k % cols] to every input
+ * as out = fma(w, x, out).  Bit-identical results; a group that is not one
+ * whole block is refused (SPM_E_STREAM, "unexpected packed group"), as the
+ * reference refuses it.  x_dev holds x_len floats (positions x cols), y_dev
+ * positions x rows; device pointers, enqueued on cuda_stream.  The fast GEMV
+ * over the same blocks is the GGUF model path above. */
+typedef struct spm_qblocks spm_qblocks;
+spm_status spm_qblocks_upload(const uint8_t* spm, uint64_t len, int32_t index, int device, spm_qblocks** out);
+spm_status spm_qblocks_free(spm_qblocks* t);
+spm_status spm_qblocks_describe(const spm_qblocks* t, spm_dense_info* out);
+spm_status spm_qblocks_gemv(const spm_qblocks* t, const float* x_dev, uint64_t x_len, int32_t positions,
+                            float* y_dev, void* cuda_stream);
+
 /* ---- host-to-HBM streaming of a .spm file ----
  * The reference's file-backed weight stream (spm-stream-file/src/prefetch.rs:
  * PrefetchFileWeightStream reads ahead into a bounded buffer) consumed stream

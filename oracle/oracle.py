@@ -82,6 +82,8 @@ def lib() -> C.CDLL:
         L.or_spm_streamed.argtypes = [u8, C.c_uint64, C.c_int32, C.c_uint32, C.c_uint32, fp, C.c_uint64, C.c_int,
                                       fp, C.c_char_p, C.c_int]
         L.or_resident.argtypes = [fp, C.c_uint32, C.c_uint32, fp, C.c_int, fp]
+        L.or_spm_qblocks.restype = C.c_int
+        L.or_spm_qblocks.argtypes = [u8, C.c_uint64, C.c_int32, fp, C.c_uint64, C.c_int, fp, C.c_char_p, C.c_int]
         _lib = L
     return _lib
 
@@ -253,6 +255,21 @@ def spm_streamed(spm, x: np.ndarray, positions: int, index: int = 0, shape: tupl
     err = C.create_string_buffer(256)
     rc = lib().or_spm_streamed(raw.ctypes.data, raw.size, index, rows, cols, _f(x), x.size, positions, _f(out),
                                err, 256)
+    if rc:
+        raise SpmError(rc, err.value.decode())
+    return out[: positions * rows].reshape(positions, rows)
+
+
+def spm_qblocks(spm, x: np.ndarray, positions: int, index: int = 0) -> np.ndarray:
+    """q6_operation / stream_matrix on the block stream `index`: x is the
+    flat positions x cols buffer; returns positions x rows."""
+    raw = _spm_bytes(spm)
+    d = spm_describe(spm, index)
+    rows = d["rows"]
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    out = np.empty(max(1, positions * rows), dtype=np.float32)
+    err = C.create_string_buffer(256)
+    rc = lib().or_spm_qblocks(raw.ctypes.data, raw.size, index, _f(x), x.size, positions, _f(out), err, 256)
     if rc:
         raise SpmError(rc, err.value.decode())
     return out[: positions * rows].reshape(positions, rows)

@@ -1341,3 +1341,72 @@ int or_spm_streamed(const uint8_t* spm, uint64_t len, int32_t index, uint32_t ro
     free(d);
     return 0;
 }
+
+int or_spm_qblocks(const uint8_t* spm, uint64_t len, int32_t index, const float* x, uint64_t x_len,
+                   int positions, float* out, char* err, int errlen) {
+    uint32_t n = 0;
+    or_spm_desc* d = NULL;
+    uint64_t at = 0;
+    char msg[160];
+    int rc = spm_parse(spm, len, &n, &d, &at, err, errlen);
+    if (rc) return rc;
+    if (index < 0 || (uint32_t)index >= n) {
+        free(d);
+        return spm_err(err, errlen, OR_SPM_NO_STREAMS, "stream index out of range");
+    }
+    const uint8_t enc = d[index].encoding;
+    uint32_t type, bv;
+    if (enc == 6) type = OR_Q8_0, bv = 32;
+    else if (enc == 4) type = OR_Q6_K, bv = 256;
+    else if (enc == 5) type = OR_Q5_K, bv = 256;
+    else {
+        free(d);
+        snprintf(msg, sizeof msg, "stream is %s, not a block profile (Q8_0, Q6K or Q5K)", spm_encoding_name(enc));
+        return spm_err(err, errlen, OR_SPM_UNSUPPORTED, msg);
+    }
+    const uint64_t rows = d[index].rows, cols = d[index].cols, total = rows * cols;
+    if (x_len < (uint64_t)positions * cols) {
+        free(d);
+        snprintf(msg, sizeof msg, "need %llu activations, got %llu", (unsigned long long)((uint64_t)positions * cols),
+                 (unsigned long long)x_len);
+        return spm_err(err, errlen, OR_SPM_ACTIVATIONS, msg);
+    }
+    memset(out, 0, sizeof(float) * (size_t)positions * rows);
+    or_cursor cur = {0, 0};
+    cursor_settle(&cur, d, n);
+    float block[256];
+    uint64_t k = 0;
+    while (cur.stream < n && cur.stream <= (uint32_t)index) {
+        const uint32_t stream = cur.stream;
+        const uint64_t count = cursor_group_len(&cur, d);
+        const uint64_t needed = 4 + spm_bytes_for(d[stream].encoding, count), available = len - at;
+        if (available < needed) {
+            free(d);
+            snprintf(msg, sizeof msg, "payload truncated: group needs %llu bytes, %llu remain",
+                     (unsigned long long)needed, (unsigned long long)available);
+            return spm_err(err, errlen, OR_SPM_TRUNCATED, msg);
+        }
+        const uint8_t* p = spm + at + 4;
+        at += needed;
+        cur.group++;
+        cursor_settle(&cur, d, n);
+        if (stream != (uint32_t)index) continue;
+        if (count != bv) { /* layout.rs:225-227, gemma_smoke.rs:219-221 */
+            free(d);
+            snprintf(msg, sizeof msg, "unexpected packed group: %s streams hold one %u-value block per group",
+                     spm_encoding_name(enc), bv);
+            return spm_err(err, errlen, OR_SPM_UNSUPPORTED, msg);
+        }
+        or_decode(type, p, needed - 4, block);
+        for (uint32_t i = 0; i < bv; ++i, ++k) {
+            const uint64_t row = k / cols, col = k % cols;
+            for (int q = 0; q < positions; ++q) {
+                float* slot = out + (uint64_t)q * rows + row;
+                *slot = fmaf(block[i], x[(uint64_t)q * cols + col], *slot);
+            }
+        }
+    }
+    free(d);
+    (void)total;
+    return 0;
+}

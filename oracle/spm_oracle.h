@@ -139,6 +139,14 @@ enum {
 };
 int or_spm_streamed(const uint8_t* spm, uint64_t len, int32_t index, uint32_t rows, uint32_t cols,
                     const float* x, uint64_t x_len, int positions, float* out, char* err, int errlen);
+/* q6_operation (spm-granite-moe/src/layout.rs:208-242) and stream_matrix
+ * (gemma_smoke.rs:201-236) for the block stream `index` (Q8_0, Q6K or Q5K,
+ * one block per group): decode each group's block (or_decode), then apply
+ * value k = W[k / cols][k % cols] to every input as out = fma(w, x, out).
+ * A group that is not one whole block of the stream's profile is
+ * OR_SPM_UNSUPPORTED ("unexpected packed group"). */
+int or_spm_qblocks(const uint8_t* spm, uint64_t len, int32_t index, const float* x, uint64_t x_len,
+                   int positions, float* out, char* err, int errlen);
 /* spm_linear::resident (resident.rs:79-96): the same product with the weights
  * given in stream order (w[k] = W[k % rows][k / rows]). */
 void or_resident(const float* w, uint32_t rows, uint32_t cols, const float* x, int positions, float* out);
