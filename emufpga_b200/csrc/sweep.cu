@@ -29,8 +29,10 @@ using namespace spm;
 
 namespace {
 
+bool block_profile(uint8_t enc) { return enc == SPM_ENC_Q8_0 || enc == SPM_ENC_Q6K || enc == SPM_ENC_Q5K; }
+
 struct SweepStream {
-    uint8_t kind = 0;             // SPM_ENC_TERNARY, SPM_ENC_F32 or SPM_ENC_BF16
+    uint8_t kind = 0;             // the stream's .spm encoding
     uint32_t rows = 0, cols = 0, group = 0;
     uint64_t rows_pad = 0, col_words = 0, groups = 0;
     uint64_t host_off = 0, bytes = 0;  // packed bytes in the pinned image
@@ -115,6 +117,16 @@ struct spm_sweep final : RingBackend {
                 a.last_group = st.groups ? uint32_t(st.groups - 1) : 0u;
                 a.lanes = positions;
                 e = launch_ternary_gemv(a, sms, compute);
+            } else if (block_profile(st.kind)) {
+                QBlockArgs a{};
+                a.blocks = base;
+                a.x = x;
+                a.y = y;
+                a.rows_pad = st.rows_pad;
+                a.rows = st.rows;
+                a.cols = st.cols;
+                a.positions = positions;
+                e = launch_qblock_chain(a, st.kind, sms, compute);
             } else {
                 DenseArgs a{};
                 a.w = base;
@@ -141,6 +153,7 @@ spm_status spm_sweep_open(const uint8_t* spm, uint64_t len, int device, uint64_t
         // pack every stream (host work first, so refusals need no device)
         std::vector<TernaryHost> tern(f.desc.size());
         std::vector<DenseHost> dense(f.desc.size());
+        std::vector<QBlockHost> qb(f.desc.size());
         uint64_t largest = 0;
         for (uint32_t i = 0; i < f.desc.size(); ++i) {
             SweepStream st;
@@ -153,8 +166,15 @@ spm_status spm_sweep_open(const uint8_t* spm, uint64_t len, int device, uint64_t
                 st.scale_off = align256(h.codes.size() * 4);
                 st.bytes = st.scale_off + h.scales.size() * 4;
                 st.payload_bytes = h.payload_bytes;
+            } else if (block_profile(st.kind)) {
+                qb[i] = pack_qblocks(spm, len, i);  // refuses groups that are not one block
+                const QBlockHost& h = qb[i];
+                st.rows = h.rows, st.cols = h.cols, st.group = h.group_size;
+                st.rows_pad = (uint64_t(h.rows) + 31) / 32 * 32, st.groups = h.groups;
+                st.bytes = h.blocks.size();
+                st.payload_bytes = h.blocks.size();
             } else {
-                dense[i] = pack_dense(spm, len, i);  // refuses the profiles without a dense decoder
+                dense[i] = pack_dense(spm, len, i);
                 const DenseHost& h = dense[i];
                 st.rows = h.rows, st.cols = h.cols, st.group = h.group_size;
                 st.rows_pad = h.rows_pad, st.groups = h.groups;
@@ -188,6 +208,8 @@ spm_status spm_sweep_open(const uint8_t* spm, uint64_t len, int device, uint64_t
                 const TernaryHost& h = tern[i];
                 if (!h.codes.empty()) std::memcpy(dst, h.codes.data(), h.codes.size() * 4);
                 if (!h.scales.empty()) std::memcpy(dst + st.scale_off, h.scales.data(), h.scales.size() * 4);
+            } else if (block_profile(st.kind)) {
+                if (!qb[i].blocks.empty()) std::memcpy(dst, qb[i].blocks.data(), qb[i].blocks.size());
             } else if (!dense[i].data.empty()) {
                 std::memcpy(dst, dense[i].data.data(), dense[i].data.size());
             }

@@ -7,8 +7,9 @@ streams in file order with streamed()/run_gemv, rewinding between sweeps
 device as the consumer: every stream stays packed in pinned host memory, the
 device holds a ring of ``device_bytes``, and each ``next`` runs the next
 stream -- dense F32/Bf16 streams as spm_linear::streamed, ternary streams as
-spm_gemv_ref::run_gemv, bit-identical to the reference -- while the streams
-after it are copied into the ring.
+spm_gemv_ref::run_gemv, block-profile streams as q6_operation/stream_matrix,
+bit-identical to the reference -- while the streams after it are copied into
+the ring.
 """
 from __future__ import annotations
 

@@ -302,12 +302,13 @@ spm_status spm_qblocks_gemv(const spm_qblocks* t, const float* x_dev, uint64_t x
  * PrefetchFileWeightStream reads ahead into a bounded buffer) consumed stream
  * by stream in file order by streamed()/run_gemv and rewound between sweeps
  * (spm-stream-groups/src/groups.rs:88-117).  spm_sweep_open packs every stream
- * into pinned host memory (dense F32/Bf16 and ternary streams; the other
- * profiles are refused as by spm_dense_upload) and keeps only a ring of
+ * into pinned host memory (dense F32/Bf16, ternary and block-profile streams,
+ * each refused as its own upload call refuses it) and keeps only a ring of
  * device_bytes on the device (0: twice the largest packed stream; less than
  * the largest is SPM_E_ARG).  spm_sweep_next runs the next stream in file
  * order on cuda_stream -- dense streams as spm_dense_streamed, ternary ones
- * as spm_ternary_gemv with x_cols = cols, bit-identical to the reference --
+ * as spm_ternary_gemv with x_cols = cols, block-profile ones as
+ * spm_qblocks_gemv, bit-identical to the reference --
  * and copies the following streams into the ring meanwhile, as far as it
  * holds them, on a copy stream of its own.  x_dev holds x_len floats
  * (positions x cols), y_dev positions x rows; *stream_index receives the

@@ -99,3 +99,35 @@ def test_open_by_path(cuda, tmp_path):
     path.write_bytes(data)
     with S.Sweep(str(path)) as sw:
         run_sweep(sw, data, rng, cuda, positions=2)
+
+
+def test_sweeps_over_block_streams(cuda):
+    """Block-profile streams (Q6_K, Q8_0) beside a ternary one, through a ring
+    of the largest stream: each bit-identical to the oracle's q6_operation."""
+    import torch
+
+    from tests.test_qblocks import tensor_blocks
+
+    rng = np.random.default_rng(3)
+    q6, r6, c6 = tensor_blocks(sf.Q6_K)
+    q8, r8, c8 = tensor_blocks(sf.Q8_0)
+    tern, _, _ = random_file(rng, 40, 30, 9)
+    data = (sf.render_header(3) + sf.render_descriptor(r6, c6, 256, sf.Q6_K) + sf.render_descriptor(40, 30, 9)
+            + sf.render_descriptor(r8, c8, 32, sf.Q8_0) + sf.qblock_stream_bytes(q6, sf.Q6_K) + tern[64:]
+            + sf.qblock_stream_bytes(q8, sf.Q8_0))
+    shapes = [(r6, c6), (40, 30), (r8, c8)]
+    with S.Sweep(data, device_bytes=largest_stream(data)) as sw:
+        for _ in range(2):
+            for k, (rows, cols) in enumerate(shapes):
+                x = rng.standard_normal(2 * cols).astype(np.float32)
+                index, y = sw.next(torch.from_numpy(x).to(cuda), 2)
+                torch.cuda.synchronize()
+                assert index == k
+                if k == 1:
+                    st = T.file_stream(data, 1)
+                    one = sf.render_header(1) + data[64:96] + data[st.offset:st.offset + st.bytes]
+                    want = O.spm_run_gemv(one, x.reshape(2, cols))
+                else:
+                    want = O.spm_qblocks(data, x, 2, k)
+                assert bits_equal(y.cpu().numpy(), want), f"stream {k}"
+            sw.rewind()

@@ -132,9 +132,9 @@ def test_open_refusals_need_no_device(tmp_path):
     with pytest.raises(eb.SpmError) as e:
         S.Sweep(data, device_bytes=100)
     assert e.value.code == -1 and "cannot hold the largest stream" in str(e.value)
-    q = sf.SpmWriter([(2, 16, 32, sf.Q8_0)])
-    q.write_raw_group(1.0, bytes(sf.bytes_for(sf.Q8_0, 32)), 32)
-    with pytest.raises(eb.SpmError, match="Q8_0 needs a scale-aware engine"):
+    q = sf.SpmWriter([(2, 32, 64, sf.Q8_0)])  # two blocks in one group
+    q.write_raw_group(1.0, bytes(sf.bytes_for(sf.Q8_0, 64)), 64)
+    with pytest.raises(eb.SpmError, match="unexpected packed group"):
         S.Sweep(q.finish())
     with pytest.raises(eb.SpmError) as e:
         S.Sweep(sf.render_header(0))
