@@ -139,9 +139,11 @@ def _tick_tokens(prompts, tick, best):
     return [p[tick + 1] if tick + 1 < len(p) else best[i] for i, p in enumerate(prompts)]
 
 
-def cpu_baseline(recipe, img, prompts, steps, seconds: float):
+def cpu_baseline(recipe, img, prompts, steps, seconds: float, threads: int = 0):
     """The oracle (this repo's C restatement of the reference CPU loop) on all
-    host cores: lockstep ticks until `seconds` of work; tokens/s."""
+    host cores (threads=0) or `threads` of them: lockstep ticks until `seconds`
+    of work; tokens/s.  One thread matches the reference's single-threaded
+    engine; more spread the output rows, leaving every result bit-identical."""
     from oracle import oracle as O
 
     n = len(prompts)
@@ -152,15 +154,17 @@ def cpu_baseline(recipe, img, prompts, steps, seconds: float):
     t0 = time.perf_counter()
     ticks = 0
     while ticks < longest + steps - 1:
-        logits = sess.step(tokens)
+        logits = sess.step(tokens, threads=threads)
         best = [O.argmax_last(logits[i]) for i in range(n)]
         tokens = _tick_tokens(prompts, ticks, best)
         ticks += 1
         if time.perf_counter() - t0 > seconds:
             break
     dt = time.perf_counter() - t0
-    return {"value": n * ticks / dt, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"first {ticks} lockstep ticks x {n} clients of the workload (oracle, OpenMP over rows)"}
+    cores = threads or os.cpu_count()
+    how = "one thread" if cores == 1 else "OpenMP over rows"
+    return {"value": n * ticks / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"first {ticks} lockstep ticks x {n} clients of the workload (oracle, {how})"}
 
 
 def run_reference(a, rank, world):
@@ -371,6 +375,8 @@ def main():
             line["invalid"] = "model truncated with --layers (profiling case, not a bench number)"
         if not a.no_cpu_baseline and img is not None:
             line["cpu_baseline"] = cpu_baseline(recipe, img, prompts, w["steps"], a.cpu_seconds)
+            line["cpu_baseline_1thread"] = cpu_baseline(recipe, img, prompts, w["steps"], a.cpu_seconds / 2,
+                                                        threads=1)
         print(json.dumps(line), flush=True)
     if pg:
         pg.barrier()

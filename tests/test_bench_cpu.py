@@ -34,3 +34,17 @@ def test_reference_arm_other_ranks_exit_quietly():
                           "--steps", "1", "--warmup", "0"], cwd=ROOT, capture_output=True, text=True, timeout=600,
                          env={**os.environ, **env})
     assert out.returncode == 0 and not out.stdout.strip()
+
+
+def test_cpu_baseline_reports_one_thread_and_all_cores():
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    import emufpga_b200 as eb
+
+    w, recipe, prompts = bench._workload("smollm2-b5", layers=2)
+    img = eb.synth_gguf(recipe)
+    one = bench.cpu_baseline(recipe, img, prompts, w["steps"], 0.3, threads=1)
+    every = bench.cpu_baseline(recipe, img, prompts, w["steps"], 0.3)
+    assert one["cores"] == 1 and "one thread" in one["sample"] and one["value"] > 0
+    assert every["cores"] >= 1 and every["value"] > 0 and every["kind"] == one["kind"] == "port"
