@@ -73,7 +73,7 @@ class Recipe:
         return dataclasses.replace(self, **kw)
 
 
-# ---- BASELINE shapes ----
+# ---- benchmark model shapes ----
 SMOLLM2 = Shape(LLAMA, 30, 576, 1536, 9, 3, 64, 49152, tied=True, rope_base=10000.0, eps=1e-5)
 QWEN3_8B = Shape(QWEN3, 36, 4096, 12288, 32, 8, 128, 151936, rope_base=1e6, eps=1e-6)
 OLMOE_1B7B = Shape(OLMOE, 16, 2048, 0, 16, 16, 128, 50304, experts=64, experts_used=8, expert_ff=1024,
@@ -89,7 +89,7 @@ RECIPES = {
     "qwen3-30b-a3b-q5_k": Recipe(QWEN3_30B_A3B, Q5_K, Q5_K, Q5_K, expert_type=Q5_K, zipf_s=1.1),
 }
 
-# The five BASELINE workloads (prompt lengths, generated tokens, clients).
+# The five benchmark workloads (prompt lengths, generated tokens, clients).
 WORKLOADS = {
     "smollm2-b1": dict(recipe="smollm2-q8_0", prompts=[32], steps=64, prompt_seed=1),
     "smollm2-b5": dict(recipe="smollm2-q8_0", prompts=[16, 24, 32, 48, 64], steps=128, prompt_seed=2),

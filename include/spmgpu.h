@@ -73,9 +73,9 @@ typedef struct spm_synth_spec {
     uint32_t embed_type;      /* dtype of token_embd                     */
     uint32_t head_type;       /* dtype of output.weight (untied)         */
     uint64_t seed;
-    float sigma;              /* 0.02 in every BASELINE config           */
+    float sigma;              /* 0.02 in every benchmark configuration */
     float zipf_s;             /* 0 = no router bias                      */
-    float gain_sigma;         /* 0: norm gains are 1 (BASELINE); else 1+N(0,gain_sigma) */
+    float gain_sigma;         /* 0: norm gains are 1 (the benchmark setting); else 1+N(0,gain_sigma) */
     int32_t threads;          /* <=0: all cores                          */
 } spm_synth_spec;
 
@@ -110,9 +110,10 @@ spm_status spm_model_open(const char* gguf_path, const char* order_path,
                           const spm_model_cfg* cfg, int device, spm_model** out);
 spm_status spm_model_open_memory(const uint8_t* gguf, uint64_t len, const char* order_text,
                                  const spm_model_cfg* cfg, int device, spm_model** out);
-/* Packed device image files (the .spm device image of the blueprint's next
- * steps; the reference reads its streams from .spm/.order files,
- * spm-file/src and spm-order/src/order.rs:28-52): spm_pack_image packs a GGUF
+/* Packed device image files (the reference lays a model out once, in
+ * consumption order, in .spm/.order files, spm-file/src and
+ * spm-order/src/order.rs:28-52; here the file holds the packed HBM image
+ * itself): spm_pack_image packs a GGUF
  * model on the host (no GPU) into a file holding the stream table, the norm
  * gains and every matrix's tiles in consumption order; spm_model_open_image
  * uploads it with one sequential read, without re-packing; spm_image_probe

@@ -123,7 +123,7 @@ def test_bad_token_is_refused(cuda, models):
     sess.close()
 
 
-# ---- BASELINE shapes ----
+# ---- benchmark model shapes ----
 def test_smollm2_b5_full_run_matches_the_oracle(cuda):
     """Config 2 (SmolLM2 Q8_0, 5 clients, prompts 16/24/32/48/64, 128 greedy
     tokens each, lockstep): every greedy token identical over the full run."""
