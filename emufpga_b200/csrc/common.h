@@ -110,40 +110,43 @@ struct SpmSpan {
 // with the reference's PayloadTruncated message when the file ends inside one.
 SpmSpan spm_file_locate(const SpmFile& f, uint64_t len, uint32_t index);
 
-// A ternary stream repacked for the device.  codes[w * rows_pad + r] holds the
-// 2-bit codes of row r for columns 16w..16w+15 (column 16w+j at bits 2j, 2j+1;
-// padding rows and columns hold code 0); scales[g] is group g's scale.
-struct TernaryHost {
-    uint32_t rows = 0, cols = 0, group_size = 0;
-    uint64_t groups = 0, col_words = 0, rows_pad = 0;
-    uint64_t payload_bytes = 0;   // packed weight bytes of the stream (scales excluded)
-    uint64_t reserved_codes = 0;  // 0b10 codes: no-ops for the datapath, as in the reference
-    std::vector<uint32_t> codes;
-    std::vector<float> scales;
-};
-TernaryHost pack_ternary(const uint8_t* buf, uint64_t len, uint32_t index);
-
-// A dense (F32 or Bf16) stream repacked for the device: the group framing
-// removed, column-major with rows padded to a multiple of 32 (zeros), element
-// (r, c) at c * rows_pad + r, as f32 or as the raw bf16 bits.
-struct DenseHost {
-    uint32_t rows = 0, cols = 0, group_size = 0;
+// The device form of one .spm stream, in two steps: plan_* validates the
+// stream (the refusals of the matching upload call) and sizes its device
+// form; fill_stream writes that form into memory the caller provides, so a
+// caller can pack straight into pinned or device-bound buffers.
+//   ternary: codes[w * rows_pad + r] holds the 2-bit codes of row r for
+//     columns 16w..16w+15 (column 16w+j at bits 2j, 2j+1; padding holds
+//     code 0), then at scale_off the f32 scale of every group;
+//   dense (F32, Bf16): the group framing removed, column-major with rows
+//     padded to 32 (zeros), element (r, c) at c * rows_pad + r, as f32 or the
+//     raw bf16 bits;
+//   block profiles (Q8_0, Q6K, Q5K): the GGML blocks back to back in source
+//     row-major order (the reference's consumers take exactly one block per
+//     group, spm-granite-moe/src/layout.rs:225-227, gemma_smoke.rs:219-221).
+struct StreamPlan {
     uint8_t encoding = 0;
-    uint64_t rows_pad = 0, groups = 0, payload_bytes = 0;
+    uint32_t rows = 0, cols = 0, group_size = 0;
+    uint64_t groups = 0, rows_pad = 0, col_words = 0;
+    uint64_t offset = 0;         // the stream's first group in the file
+    uint64_t bytes = 0;          // size of the device form
+    uint64_t scale_off = 0;      // ternary: the scales inside the device form
+    uint64_t payload_bytes = 0;  // weight bytes of the stream (scales excluded)
+};
+StreamPlan plan_ternary(const uint8_t* buf, uint64_t len, uint32_t index);
+StreamPlan plan_dense(const uint8_t* buf, uint64_t len, uint32_t index);
+StreamPlan plan_qblocks(const uint8_t* buf, uint64_t len, uint32_t index);
+// Writes the device form (plan.bytes bytes at dst); returns the number of
+// reserved 0b10 codes of a ternary stream (0 otherwise).
+uint64_t fill_stream(const uint8_t* buf, const StreamPlan& plan, uint8_t* dst);
+
+// A stream packed into host memory: its plan and device form.
+struct PackedStream {
+    StreamPlan plan;
     std::vector<uint8_t> data;
+    uint64_t reserved_codes = 0;
 };
-DenseHost pack_dense(const uint8_t* buf, uint64_t len, uint32_t index);
-
-// A Q-profile stream (Q8_0, Q6_K, Q5_K) with the group framing removed: its
-// GGML blocks back to back in source row-major order.  The reference's
-// consumers take exactly one block per group (spm-granite-moe/src/
-// layout.rs:225-227, gemma_smoke.rs:219-221).
-struct QBlockHost {
-    uint32_t rows = 0, cols = 0, group_size = 0;
-    uint8_t encoding = 0;
-    uint64_t groups = 0;
-    std::vector<uint8_t> blocks;
-};
-QBlockHost pack_qblocks(const uint8_t* buf, uint64_t len, uint32_t index);
+PackedStream pack_ternary(const uint8_t* buf, uint64_t len, uint32_t index);
+PackedStream pack_dense(const uint8_t* buf, uint64_t len, uint32_t index);
+PackedStream pack_qblocks(const uint8_t* buf, uint64_t len, uint32_t index);
 
 }  // namespace spm

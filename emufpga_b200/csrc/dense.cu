@@ -66,23 +66,24 @@ spm_status spm_dense_upload(const uint8_t* spm, uint64_t len, int32_t index, int
     return guarded([&] {
         if (!out) fail(SPM_E_ARG, "null output");
         if (index < 0) fail(SPM_E_ARG, "stream index out of range");
-        const DenseHost h = pack_dense(spm, len, uint32_t(index));
+        const PackedStream h = pack_dense(spm, len, uint32_t(index));
+        const StreamPlan& pl = h.plan;
         int ndev = 0;
         if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) fail(SPM_E_NO_DEVICE, "no CUDA device is visible");
         std::unique_ptr<spm_dense> t(new spm_dense());
-        t->rows = h.rows;
-        t->cols = h.cols;
-        t->group_size = h.group_size;
-        t->encoding = h.encoding;
-        t->rows_pad = h.rows_pad;
-        t->groups = h.groups;
-        t->payload_bytes = h.payload_bytes;
+        t->rows = pl.rows;
+        t->cols = pl.cols;
+        t->group_size = pl.group_size;
+        t->encoding = pl.encoding;
+        t->rows_pad = pl.rows_pad;
+        t->groups = pl.groups;
+        t->payload_bytes = pl.payload_bytes;
         t->device = device;
         CUDA_OK(cudaSetDevice(device));
         CUDA_OK(cudaDeviceGetAttribute(&t->sms, cudaDevAttrMultiProcessorCount, device));
-        t->device_bytes = std::max<uint64_t>(h.data.size(), 256);
+        t->device_bytes = std::max<uint64_t>(pl.bytes, 256);
         CUDA_OK(cudaMalloc(&t->mem, t->device_bytes));
-        if (!h.data.empty()) CUDA_OK(cudaMemcpy(t->mem, h.data.data(), h.data.size(), cudaMemcpyHostToDevice));
+        if (pl.bytes) CUDA_OK(cudaMemcpy(t->mem, h.data.data(), pl.bytes, cudaMemcpyHostToDevice));
         *out = t.release();
     });
 }

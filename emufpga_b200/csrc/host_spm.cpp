@@ -113,7 +113,20 @@ SpmSpan spm_file_locate(const SpmFile& f, uint64_t len, uint32_t index) {
     return span;
 }
 
-TernaryHost pack_ternary(const uint8_t* buf, uint64_t len, uint32_t index) {
+static const char* encoding_name(uint8_t enc) {  // Debug names of spm_layout::Encoding
+    switch (enc) {
+        case SPM_ENC_TERNARY: return "Ternary2F32I32";
+        case SPM_ENC_F32: return "F32";
+        case SPM_ENC_BF16: return "Bf16";
+        case SPM_ENC_Q6K: return "Q6K";
+        case SPM_ENC_Q5K: return "Q5K";
+        default: return "Q8_0";
+    }
+}
+
+static uint64_t align256(uint64_t v) { return (v + 255) / 256 * 256; }
+
+StreamPlan plan_ternary(const uint8_t* buf, uint64_t len, uint32_t index) {
     const SpmFile f = spm_file_parse(buf, len);
     if (f.desc.empty()) fail(SPM_E_ARG, "parameter stream declares no operations");
     if (index >= f.desc.size()) fail(SPM_E_ARG, "stream index out of range");
@@ -134,53 +147,22 @@ TernaryHost pack_ternary(const uint8_t* buf, uint64_t len, uint32_t index) {
         break;
     }
     if (span.groups > 0xFFFFFFFFull) fail(SPM_E_ARG, "a ternary stream may hold at most 2^32 - 1 scale groups");
-
-    TernaryHost t;
-    t.rows = d.rows;
-    t.cols = d.cols;
-    t.group_size = d.group_size;
-    t.groups = span.groups;
-    t.rows_pad = (uint64_t(d.rows) + 31) / 32 * 32;
-    t.col_words = (uint64_t(d.cols) + 15) / 16;
-    t.codes.assign(t.col_words * t.rows_pad, 0u);
-    t.scales.resize(t.groups);
-    const uint64_t total = uint64_t(d.rows) * d.cols;
-    const uint8_t* p = buf + span.offset;
-    uint64_t r = 0, c = 0;  // (row, col) of the next weight: stream position c * rows + r
-    for (uint64_t g = 0; g < t.groups; ++g) {
-        const uint64_t count = std::min<uint64_t>(d.group_size, total - g * d.group_size);
-        std::memcpy(&t.scales[g], p, 4);  // f32::from_le_bytes on a little-endian host
-        const uint8_t* packed = p + 4;
-        for (uint64_t local = 0; local < count; ++local) {
-            const uint32_t code = (packed[local >> 2] >> ((local & 3) * 2)) & 3u;
-            if (code) {
-                t.codes[(c >> 4) * t.rows_pad + r] |= code << ((c & 15) * 2);
-                if (code == 2) ++t.reserved_codes;
-            }
-            if (++r == d.rows) {
-                r = 0;
-                ++c;
-            }
-        }
-        const uint64_t payload = uint64_t(bytes_for(SPM_ENC_TERNARY, count));
-        t.payload_bytes += payload;
-        p += 4 + payload;
-    }
-    return t;
+    StreamPlan p;
+    p.encoding = d.encoding;
+    p.rows = d.rows;
+    p.cols = d.cols;
+    p.group_size = d.group_size;
+    p.groups = span.groups;
+    p.offset = span.offset;
+    p.rows_pad = (uint64_t(d.rows) + 31) / 32 * 32;
+    p.col_words = (uint64_t(d.cols) + 15) / 16;
+    p.scale_off = align256(p.col_words * p.rows_pad * 4);
+    p.bytes = p.scale_off + p.groups * 4;
+    p.payload_bytes = span.bytes - 4 * span.groups;
+    return p;
 }
 
-static const char* encoding_name(uint8_t enc) {  // Debug names of spm_layout::Encoding
-    switch (enc) {
-        case SPM_ENC_TERNARY: return "Ternary2F32I32";
-        case SPM_ENC_F32: return "F32";
-        case SPM_ENC_BF16: return "Bf16";
-        case SPM_ENC_Q6K: return "Q6K";
-        case SPM_ENC_Q5K: return "Q5K";
-        default: return "Q8_0";
-    }
-}
-
-DenseHost pack_dense(const uint8_t* buf, uint64_t len, uint32_t index) {
+StreamPlan plan_dense(const uint8_t* buf, uint64_t len, uint32_t index) {
     const SpmFile f = spm_file_parse(buf, len);
     if (index >= f.desc.size()) fail(SPM_E_ARG, "stream index out of range");
     const SpmDesc& d = f.desc[index];
@@ -190,43 +172,28 @@ DenseHost pack_dense(const uint8_t* buf, uint64_t len, uint32_t index) {
         fail(SPM_E_STREAM, std::string("parameter stream: ") + encoding_name(d.encoding) +
                                " needs a scale-aware engine");
     const SpmSpan span = spm_file_locate(f, len, index);
-    DenseHost h;
-    h.rows = d.rows;
-    h.cols = d.cols;
-    h.group_size = d.group_size;
-    h.encoding = d.encoding;
-    h.groups = span.groups;
-    h.rows_pad = (uint64_t(d.rows) + 31) / 32 * 32;
-    const uint32_t es = d.encoding == SPM_ENC_F32 ? 4 : 2;
-    h.data.assign(h.rows_pad * d.cols * es, 0);
-    const uint64_t total = uint64_t(d.rows) * d.cols;
-    const uint8_t* p = buf + span.offset;
-    uint64_t r = 0, c = 0;  // element of the next weight: stream position c * rows + r
-    for (uint64_t g = 0; g < h.groups; ++g) {
-        const uint64_t count = std::min<uint64_t>(d.group_size, total - g * d.group_size);
-        const uint8_t* w = p + 4;  // the group scale is inert for the dense profiles
-        for (uint64_t i = 0; i < count; ++i) {
-            std::memcpy(&h.data[(c * h.rows_pad + r) * es], w + i * es, es);
-            if (++r == d.rows) {
-                r = 0;
-                ++c;
-            }
-        }
-        h.payload_bytes += count * es;
-        p += 4 + count * es;
-    }
-    return h;
+    StreamPlan p;
+    p.encoding = d.encoding;
+    p.rows = d.rows;
+    p.cols = d.cols;
+    p.group_size = d.group_size;
+    p.groups = span.groups;
+    p.offset = span.offset;
+    p.rows_pad = (uint64_t(d.rows) + 31) / 32 * 32;
+    p.bytes = p.rows_pad * d.cols * (d.encoding == SPM_ENC_F32 ? 4 : 2);
+    p.payload_bytes = span.bytes - 4 * span.groups;
+    return p;
 }
 
-QBlockHost pack_qblocks(const uint8_t* buf, uint64_t len, uint32_t index) {
+StreamPlan plan_qblocks(const uint8_t* buf, uint64_t len, uint32_t index) {
     const SpmFile f = spm_file_parse(buf, len);
     if (index >= f.desc.size()) fail(SPM_E_ARG, "stream index out of range");
     const SpmDesc& d = f.desc[index];
-    uint32_t bv = 0, bb = 0;
+    uint32_t bv = 0;
     switch (d.encoding) {
-        case SPM_ENC_Q8_0: bv = 32, bb = 34; break;
-        case SPM_ENC_Q6K: bv = 256, bb = 210; break;
-        case SPM_ENC_Q5K: bv = 256, bb = 176; break;
+        case SPM_ENC_Q8_0: bv = 32; break;
+        case SPM_ENC_Q6K: bv = 256; break;
+        case SPM_ENC_Q5K: bv = 256; break;
         default:
             fail(SPM_E_STREAM, std::string("stream is ") + encoding_name(d.encoding) +
                                    ", not a block profile (Q8_0, Q6K or Q5K)");
@@ -237,16 +204,85 @@ QBlockHost pack_qblocks(const uint8_t* buf, uint64_t len, uint32_t index) {
         fail(SPM_E_STREAM, std::string("unexpected packed group: ") + encoding_name(d.encoding) +
                                " streams hold one " + std::to_string(bv) + "-value block per group");
     const SpmSpan span = spm_file_locate(f, len, index);
-    QBlockHost h;
-    h.rows = d.rows;
-    h.cols = d.cols;
-    h.group_size = d.group_size;
-    h.encoding = d.encoding;
-    h.groups = span.groups;
-    h.blocks.resize(h.groups * bb);
-    const uint8_t* p = buf + span.offset;
-    for (uint64_t g = 0; g < h.groups; ++g, p += 4 + bb) std::memcpy(&h.blocks[g * bb], p + 4, bb);
-    return h;
+    StreamPlan p;
+    p.encoding = d.encoding;
+    p.rows = d.rows;
+    p.cols = d.cols;
+    p.group_size = d.group_size;
+    p.groups = span.groups;
+    p.offset = span.offset;
+    p.rows_pad = (uint64_t(d.rows) + 31) / 32 * 32;
+    p.bytes = span.bytes - 4 * span.groups;
+    p.payload_bytes = p.bytes;
+    return p;
+}
+
+uint64_t fill_stream(const uint8_t* buf, const StreamPlan& pl, uint8_t* dst) {
+    std::memset(dst, 0, pl.bytes);
+    const uint64_t total = uint64_t(pl.rows) * pl.cols;
+    const uint8_t* p = buf + pl.offset;
+    uint64_t reserved = 0;
+    if (pl.encoding == SPM_ENC_TERNARY) {
+        uint32_t* codes = reinterpret_cast<uint32_t*>(dst);
+        uint8_t* scales = dst + pl.scale_off;
+        uint64_t r = 0, c = 0;  // (row, col) of the next weight: stream position c * rows + r
+        for (uint64_t g = 0; g < pl.groups; ++g) {
+            const uint64_t count = std::min<uint64_t>(pl.group_size, total - g * pl.group_size);
+            std::memcpy(scales + 4 * g, p, 4);  // f32::from_le_bytes on a little-endian host
+            const uint8_t* packed = p + 4;
+            for (uint64_t local = 0; local < count; ++local) {
+                const uint32_t code = (packed[local >> 2] >> ((local & 3) * 2)) & 3u;
+                if (code) {
+                    codes[(c >> 4) * pl.rows_pad + r] |= code << ((c & 15) * 2);
+                    if (code == 2) ++reserved;
+                }
+                if (++r == pl.rows) {
+                    r = 0;
+                    ++c;
+                }
+            }
+            p += 4 + uint64_t(bytes_for(SPM_ENC_TERNARY, count));
+        }
+    } else if (pl.encoding == SPM_ENC_F32 || pl.encoding == SPM_ENC_BF16) {
+        const uint32_t es = pl.encoding == SPM_ENC_F32 ? 4 : 2;
+        uint64_t r = 0, c = 0;
+        for (uint64_t g = 0; g < pl.groups; ++g) {
+            const uint64_t count = std::min<uint64_t>(pl.group_size, total - g * pl.group_size);
+            const uint8_t* w = p + 4;  // the group scale is inert for the dense profiles
+            for (uint64_t i = 0; i < count; ++i) {
+                std::memcpy(dst + (c * pl.rows_pad + r) * es, w + i * es, es);
+                if (++r == pl.rows) {
+                    r = 0;
+                    ++c;
+                }
+            }
+            p += 4 + count * es;
+        }
+    } else {
+        const uint64_t bb = pl.groups ? pl.bytes / pl.groups : 0;
+        for (uint64_t g = 0; g < pl.groups; ++g, p += 4 + bb) std::memcpy(dst + g * bb, p + 4, bb);
+    }
+    return reserved;
+}
+
+static PackedStream pack(const uint8_t* buf, StreamPlan plan) {
+    PackedStream out;
+    out.plan = plan;
+    out.data.resize(plan.bytes);
+    out.reserved_codes = plan.bytes ? fill_stream(buf, plan, out.data.data()) : 0;
+    return out;
+}
+
+PackedStream pack_ternary(const uint8_t* buf, uint64_t len, uint32_t index) {
+    return pack(buf, plan_ternary(buf, len, index));
+}
+
+PackedStream pack_dense(const uint8_t* buf, uint64_t len, uint32_t index) {
+    return pack(buf, plan_dense(buf, len, index));
+}
+
+PackedStream pack_qblocks(const uint8_t* buf, uint64_t len, uint32_t index) {
+    return pack(buf, plan_qblocks(buf, len, index));
 }
 
 }  // namespace spm

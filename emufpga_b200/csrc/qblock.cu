@@ -69,22 +69,23 @@ spm_status spm_qblocks_upload(const uint8_t* spm, uint64_t len, int32_t index, i
     return guarded([&] {
         if (!out) fail(SPM_E_ARG, "null output");
         if (index < 0) fail(SPM_E_ARG, "stream index out of range");
-        const QBlockHost h = pack_qblocks(spm, len, uint32_t(index));
+        const PackedStream h = pack_qblocks(spm, len, uint32_t(index));
+        const StreamPlan& pl = h.plan;
         int ndev = 0;
         if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) fail(SPM_E_NO_DEVICE, "no CUDA device is visible");
         std::unique_ptr<spm_qblocks> t(new spm_qblocks());
-        t->rows = h.rows;
-        t->cols = h.cols;
-        t->group_size = h.group_size;
-        t->encoding = h.encoding;
-        t->groups = h.groups;
-        t->payload_bytes = h.blocks.size();
+        t->rows = pl.rows;
+        t->cols = pl.cols;
+        t->group_size = pl.group_size;
+        t->encoding = pl.encoding;
+        t->groups = pl.groups;
+        t->payload_bytes = pl.payload_bytes;
         t->device = device;
         CUDA_OK(cudaSetDevice(device));
         CUDA_OK(cudaDeviceGetAttribute(&t->sms, cudaDevAttrMultiProcessorCount, device));
-        t->device_bytes = std::max<uint64_t>(h.blocks.size(), 256);
+        t->device_bytes = std::max<uint64_t>(pl.bytes, 256);
         CUDA_OK(cudaMalloc(&t->mem, t->device_bytes));
-        if (!h.blocks.empty()) CUDA_OK(cudaMemcpy(t->mem, h.blocks.data(), h.blocks.size(), cudaMemcpyHostToDevice));
+        if (pl.bytes) CUDA_OK(cudaMemcpy(t->mem, h.data.data(), pl.bytes, cudaMemcpyHostToDevice));
         *out = t.release();
     });
 }

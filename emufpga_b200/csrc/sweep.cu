@@ -150,41 +150,27 @@ spm_status spm_sweep_open(const uint8_t* spm, uint64_t len, int device, uint64_t
         if (!out) fail(SPM_E_ARG, "null output");
         const SpmFile f = spm_file_parse(spm, len);
         std::unique_ptr<spm_sweep> s(new spm_sweep());
-        // pack every stream (host work first, so refusals need no device)
-        std::vector<TernaryHost> tern(f.desc.size());
-        std::vector<DenseHost> dense(f.desc.size());
-        std::vector<QBlockHost> qb(f.desc.size());
+        // plan every stream first (host work, so refusals need no device);
+        // each is packed later straight into the pinned image
+        std::vector<StreamPlan> plans;
         uint64_t largest = 0;
         for (uint32_t i = 0; i < f.desc.size(); ++i) {
+            const uint8_t enc = f.desc[i].encoding;
+            const StreamPlan pl = enc == SPM_ENC_TERNARY ? plan_ternary(spm, len, i)
+                                  : block_profile(enc)   ? plan_qblocks(spm, len, i)
+                                                         : plan_dense(spm, len, i);
             SweepStream st;
-            st.kind = f.desc[i].encoding;
-            if (st.kind == SPM_ENC_TERNARY) {
-                tern[i] = pack_ternary(spm, len, i);
-                const TernaryHost& h = tern[i];
-                st.rows = h.rows, st.cols = h.cols, st.group = h.group_size;
-                st.rows_pad = h.rows_pad, st.col_words = h.col_words, st.groups = h.groups;
-                st.scale_off = align256(h.codes.size() * 4);
-                st.bytes = st.scale_off + h.scales.size() * 4;
-                st.payload_bytes = h.payload_bytes;
-            } else if (block_profile(st.kind)) {
-                qb[i] = pack_qblocks(spm, len, i);  // refuses groups that are not one block
-                const QBlockHost& h = qb[i];
-                st.rows = h.rows, st.cols = h.cols, st.group = h.group_size;
-                st.rows_pad = (uint64_t(h.rows) + 31) / 32 * 32, st.groups = h.groups;
-                st.bytes = h.blocks.size();
-                st.payload_bytes = h.blocks.size();
-            } else {
-                dense[i] = pack_dense(spm, len, i);
-                const DenseHost& h = dense[i];
-                st.rows = h.rows, st.cols = h.cols, st.group = h.group_size;
-                st.rows_pad = h.rows_pad, st.groups = h.groups;
-                st.bytes = h.data.size();
-                st.payload_bytes = h.payload_bytes;
-            }
+            st.kind = enc;
+            st.rows = pl.rows, st.cols = pl.cols, st.group = pl.group_size;
+            st.rows_pad = pl.rows_pad, st.col_words = pl.col_words, st.groups = pl.groups;
+            st.scale_off = pl.scale_off;
+            st.bytes = pl.bytes;
+            st.payload_bytes = pl.payload_bytes;
             st.host_off = s->host_bytes;
             s->host_bytes = align256(s->host_bytes + st.bytes);
             largest = std::max(largest, align256(st.bytes));
             s->streams.push_back(st);
+            plans.push_back(pl);
         }
         if (s->streams.empty()) fail(SPM_E_ARG, "parameter stream declares no operations");
         if (device_bytes == 0) device_bytes = 2 * largest;
@@ -201,19 +187,8 @@ spm_status spm_sweep_open(const uint8_t* spm, uint64_t len, int device, uint64_t
         CUDA_OK(cudaDeviceGetAttribute(&s->sms, cudaDevAttrMultiProcessorCount, device));
         CUDA_OK(cudaHostAlloc(reinterpret_cast<void**>(&s->host), std::max<uint64_t>(s->host_bytes, 256),
                               cudaHostAllocDefault));
-        for (uint32_t i = 0; i < s->streams.size(); ++i) {
-            const SweepStream& st = s->streams[i];
-            uint8_t* dst = s->host + st.host_off;
-            if (st.kind == SPM_ENC_TERNARY) {
-                const TernaryHost& h = tern[i];
-                if (!h.codes.empty()) std::memcpy(dst, h.codes.data(), h.codes.size() * 4);
-                if (!h.scales.empty()) std::memcpy(dst + st.scale_off, h.scales.data(), h.scales.size() * 4);
-            } else if (block_profile(st.kind)) {
-                if (!qb[i].blocks.empty()) std::memcpy(dst, qb[i].blocks.data(), qb[i].blocks.size());
-            } else if (!dense[i].data.empty()) {
-                std::memcpy(dst, dense[i].data.data(), dense[i].data.size());
-            }
-        }
+        for (uint32_t i = 0; i < s->streams.size(); ++i)
+            if (plans[i].bytes) fill_stream(spm, plans[i], s->host + s->streams[i].host_off);
         s->cap = device_bytes / 256 * 256;
         CUDA_OK(cudaMalloc(reinterpret_cast<void**>(&s->ring_mem), s->cap));
         CUDA_OK(cudaStreamCreateWithFlags(&s->copy_stream, cudaStreamNonBlocking));

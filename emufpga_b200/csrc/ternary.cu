@@ -75,31 +75,27 @@ spm_status spm_ternary_upload(const uint8_t* spm, uint64_t len, int32_t index, i
     return guarded([&] {
         if (!out) fail(SPM_E_ARG, "null output");
         if (index < 0) fail(SPM_E_ARG, "stream index out of range");
-        const TernaryHost h = pack_ternary(spm, len, uint32_t(index));
+        const PackedStream h = pack_ternary(spm, len, uint32_t(index));
+        const StreamPlan& pl = h.plan;
         int ndev = 0;
         if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) fail(SPM_E_NO_DEVICE, "no CUDA device is visible");
         std::unique_ptr<spm_ternary> t(new spm_ternary());
-        t->rows = h.rows;
-        t->cols = h.cols;
-        t->group_size = h.group_size;
-        t->groups = h.groups;
-        t->col_words = h.col_words;
-        t->rows_pad = h.rows_pad;
-        t->payload_bytes = h.payload_bytes;
+        t->rows = pl.rows;
+        t->cols = pl.cols;
+        t->group_size = pl.group_size;
+        t->groups = pl.groups;
+        t->col_words = pl.col_words;
+        t->rows_pad = pl.rows_pad;
+        t->payload_bytes = pl.payload_bytes;
         t->reserved_codes = h.reserved_codes;
         t->device = device;
         CUDA_OK(cudaSetDevice(device));
         CUDA_OK(cudaDeviceGetAttribute(&t->sms, cudaDevAttrMultiProcessorCount, device));
-        const uint64_t code_bytes = h.codes.size() * sizeof(uint32_t);
-        const uint64_t scale_at = (code_bytes + 255) / 256 * 256;
-        t->device_bytes = std::max<uint64_t>(scale_at + h.scales.size() * sizeof(float), 256);
+        t->device_bytes = std::max<uint64_t>(pl.bytes, 256);
         CUDA_OK(cudaMalloc(&t->mem, t->device_bytes));
-        if (code_bytes) CUDA_OK(cudaMemcpy(t->mem, h.codes.data(), code_bytes, cudaMemcpyHostToDevice));
-        if (!h.scales.empty())
-            CUDA_OK(cudaMemcpy(t->mem + scale_at, h.scales.data(), h.scales.size() * sizeof(float),
-                               cudaMemcpyHostToDevice));
+        if (pl.bytes) CUDA_OK(cudaMemcpy(t->mem, h.data.data(), pl.bytes, cudaMemcpyHostToDevice));
         t->codes = reinterpret_cast<const uint32_t*>(t->mem);
-        t->scales = reinterpret_cast<const float*>(t->mem + scale_at);
+        t->scales = reinterpret_cast<const float*>(t->mem + pl.scale_off);
         *out = t.release();
     });
 }
