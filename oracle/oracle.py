@@ -1,6 +1,7 @@
 """ctypes face of liboracle.so -- TEST INFRASTRUCTURE ONLY.
 
-The CPU restatement of emufpga's token loop (spm_oracle.c).  Only tests/,
+The CPU restatement of emufpga's token loop and of its .spm stream
+operators (spm_oracle.c).  Only tests/,
 __graft_entry__.smoke() and bench.py's CPU-baseline leg use it, as the
 checker or the timed reference; the product (emufpga_b200) never does.
 """

@@ -15,7 +15,11 @@
  * known-answer tests (spm-gguf/tests/decode.rs) and bit-for-bit against the
  * gguf-py 0.19.0 dequantizers on committed fixtures (tests/golden/).  Q2_K has
  * no decoder in the reference; it follows ggml's published block format and is
- * pinned only against gguf-py.
+ * pinned only against gguf-py.  The .spm restatements (run_gemv, streamed,
+ * resident, q6_operation / stream_matrix) are pinned against the reference's
+ * own tests read from their sources: the tiny.spm layout and the header,
+ * descriptor and payload refusals (spm-file, spm-header, spm-layout tests),
+ * the gemv-ref correctness and batch cases, and spm-linear's agreement cases.
  */
 #ifndef SPM_ORACLE_H
 #define SPM_ORACLE_H
