@@ -452,13 +452,23 @@ struct Mapped {
 // ---- packed device image files ----
 // A model already packed for the device: the stream table, the norm gains,
 // then the tiles exactly as they sit in HBM, so that opening it is one
-// sequential read and upload.  Layout (little endian):
-//   "SPMIMG01", u64 data offset (4096-aligned), u64 image bytes, the
+// sequential read and upload.  The file is a .spm container (spm-header,
+// spm-layout) extended with this library's tiled profiles.  Layout (little
+// endian):
+//   the 32-byte .spm header: magic, version 1.1, little-endian, stream count;
+//   one 32-byte .spm descriptor per stream: rows, cols, group_size = values
+//     per GGML block, encoding = kImageProfile + GGML type (this library's
+//     tiled layout of that block type; .spm profiles 1-6 are the reference's,
+//     so a stock .spm reader refuses these as unknown encodings),
+//     lane_count = rows per tile;
+//   "SPMIMG02", u64 data offset (4096-aligned), u64 image bytes, the
 //   spm_model_cfg, u32 streams { u16 name length, name, u32 dtype, u64 rows,
 //   cols, experts, u8 rotating, u64 tiles, tile bytes, u32 planes[4], u64
 //   offset, quant bytes }, u32 gains { u16 name length, name, u64 offset,
 //   length }, u64 floats, the floats; zeros up to the data offset; the image.
-constexpr char kImageMagic[8] = {'S', 'P', 'M', 'I', 'M', 'G', '0', '1'};
+constexpr uint8_t kSpmMagic[8] = {0x89, 'S', 'P', 'M', 0x0D, 0x0A, 0x1A, 0x0A};
+constexpr char kImageMagic[8] = {'S', 'P', 'M', 'I', 'M', 'G', '0', '2'};
+constexpr uint8_t kImageProfile = 0x80;
 constexpr uint64_t kImageAlign = 4096;
 
 struct ImgWriter {
@@ -494,9 +504,31 @@ struct ImgReader {
     }
 };
 
+// The .spm descriptor of one packed stream.
+void image_descriptor(ImgWriter& w, const StreamDesc& s) {
+    uint64_t bv = 0, bb = 0;
+    if (!type_layout(s.pk.dtype, &bv, &bb)) fail(SPM_E_ENCODING, s.name + ": no block layout");
+    if (s.pk.rows > 0xFFFFFFFFull || s.pk.cols > 0xFFFFFFFFull) fail(SPM_E_ARG, s.name + ": too large for .spm");
+    w.put(uint32_t(s.pk.rows));
+    w.put(uint32_t(s.pk.cols));
+    w.put(uint32_t(bv));
+    w.put(uint8_t(kImageProfile + s.pk.dtype));
+    w.put(uint8_t(0));
+    w.put(uint16_t(kTileRows));
+    for (int k = 0; k < 16; k++) w.put(uint8_t(0));
+}
+
 std::vector<uint8_t> image_header(const ModelDesc& d) {
     ImgWriter w;
+    w.b.insert(w.b.end(), kSpmMagic, kSpmMagic + 8);  // .spm header (spm-header/src/lib.rs:3-25)
+    w.put(uint16_t(1));
+    w.put(uint16_t(1));
+    w.put(uint32_t(0));  // little-endian, reserved
+    w.put(uint32_t(d.streams.size()));
+    for (int k = 0; k < 12; k++) w.put(uint8_t(0));
+    for (const StreamDesc& s : d.streams) image_descriptor(w, s);
     w.b.insert(w.b.end(), kImageMagic, kImageMagic + 8);
+    const size_t data_at = w.b.size();
     w.put(uint64_t(0));  // data offset, patched below
     w.put(d.image_bytes);
     w.put(d.cfg);
@@ -523,22 +555,32 @@ std::vector<uint8_t> image_header(const ModelDesc& d) {
     w.put(uint64_t(d.gains.size()));
     for (float f : d.gains) w.put(f);
     const uint64_t data = (w.b.size() + kImageAlign - 1) / kImageAlign * kImageAlign;
-    std::memcpy(w.b.data() + 8, &data, 8);
+    std::memcpy(w.b.data() + data_at, &data, 8);
     w.b.resize(data, 0);
     return w.b;
 }
 
 // The description and data offset of an image file held in memory.
 ModelDesc read_image(const uint8_t* p, uint64_t n, uint64_t* data) {
-    if (n < 8 || std::memcmp(p, kImageMagic, 8) != 0) fail(SPM_E_STREAM, "not a packed image (bad magic)");
-    ImgReader r{p, n, 8};
+    if (n < 32) fail(SPM_E_TRUNCATED, "image header is truncated");
+    if (std::memcmp(p, kSpmMagic, 8) != 0) fail(SPM_E_STREAM, "not a packed image (bad magic)");
+    uint16_t major;
+    std::memcpy(&major, p + 8, 2);
+    if (major != 1 || p[12] != 0) fail(SPM_E_STREAM, "not a packed image (version or byte order)");
+    uint32_t nd;
+    std::memcpy(&nd, p + 16, 4);
+    if (nd > 1u << 20) fail(SPM_E_STREAM, "image stream count is not plausible");
+    const uint64_t dir = 32 + 32 * uint64_t(nd);
+    if (n < dir + 8) fail(SPM_E_TRUNCATED, "image header is truncated");
+    if (std::memcmp(p + dir, kImageMagic, 8) != 0) fail(SPM_E_STREAM, "not a packed image (a .spm file of streams?)");
+    ImgReader r{p, n, dir + 8};
     ModelDesc d;
     *data = r.get<uint64_t>();
     d.image_bytes = r.get<uint64_t>();
     d.cfg = r.get<spm_model_cfg>();
     check_cfg(d.cfg);
     const uint32_t ns = r.get<uint32_t>();
-    if (ns > 1u << 20) fail(SPM_E_STREAM, "image stream count is not plausible");
+    if (ns != nd) fail(SPM_E_STREAM, "image directory and stream table disagree");
     for (uint32_t i = 0; i < ns; i++) {
         StreamDesc s;
         s.name = r.str();
@@ -559,6 +601,10 @@ ModelDesc read_image(const uint8_t* p, uint64_t n, uint64_t* data) {
         if (got.offset > d.image_bytes || got.tiles * got.tile_bytes > d.image_bytes - got.offset)
             fail(SPM_E_STREAM, s.name + ": outside the image");
         s.pk = got;
+        ImgWriter want_desc;  // the descriptor this stream must have in the directory
+        image_descriptor(want_desc, s);
+        if (std::memcmp(p + 32 + 32 * uint64_t(i), want_desc.b.data(), 32) != 0)
+            fail(SPM_E_STREAM, s.name + ": directory entry does not match the stream");
         if (!d.stream_of.emplace(s.name, int(d.streams.size())).second) fail(SPM_E_STREAM, "duplicate stream " + s.name);
         d.streams.push_back(s);
     }

@@ -113,11 +113,15 @@ spm_status spm_model_open_memory(const uint8_t* gguf, uint64_t len, const char* 
 /* Packed device image files (the reference lays a model out once, in
  * consumption order, in .spm/.order files, spm-file/src and
  * spm-order/src/order.rs:28-52; here the file holds the packed HBM image
- * itself): spm_pack_image packs a GGUF
- * model on the host (no GPU) into a file holding the stream table, the norm
- * gains and every matrix's tiles in consumption order; spm_model_open_image
- * uploads it with one sequential read, without re-packing; spm_image_probe
- * validates a file and reports its image bytes and stream count. */
+ * itself): spm_pack_image packs a GGUF model on the host (no GPU) into a .spm
+ * container -- the .spm header and one descriptor per stream, with encoding
+ * 0x80 + GGML type for this library's tiled layout of that block type (group
+ * size = values per block, lane count = rows per tile), then the stream table,
+ * the norm gains and every matrix's tiles in consumption order.  A stock .spm
+ * reader refuses those encodings; spm_model_open_image uploads the file with
+ * one sequential read, without re-packing; spm_image_probe validates a file
+ * (every descriptor must match its stream) and reports its image bytes and
+ * stream count. */
 spm_status spm_pack_image(const uint8_t* gguf, uint64_t len, const char* order_text,
                           const spm_model_cfg* cfg, const char* path);
 spm_status spm_image_probe(const char* path, uint64_t* image_bytes, int32_t* streams);
