@@ -19,6 +19,13 @@
  *                         of spm-batch/examples/serve-demo.rs:72-90
  *   spm_streamed          spm-linear/src/stream.rs:31-55 (streamed) for one stream
  *   spm_dequant_rows      parity hook for the decoders above, run on the device
+ *   spm_file_*            spm-file/src/read.rs:46-101 (SpmReader) over .spm files
+ *   spm_dense_*           spm-linear/src/stream.rs:31-125 (streamed) on dense .spm streams
+ *   spm_qblocks_*         spm-granite-moe/src/layout.rs:208-242 (q6_operation),
+ *                         gemma_smoke.rs:201-236 (stream_matrix) on block-profile streams
+ *   spm_ternary_*         spm-gemv-ref/src/gemv.rs:39-126 (run_gemv)
+ *   spm_sweep_*           spm-stream-file/src/prefetch.rs + spm-stream-groups rewind:
+ *                         .spm files streamed from host memory through a device ring
  */
 #ifndef SPMGPU_H
 #define SPMGPU_H
