@@ -373,7 +373,7 @@ def main():
         if a.layers:
             line["config"]["layers_kept"] = recipe.shape.layers
             line["invalid"] = "model truncated with --layers (profiling case, not a bench number)"
-        if not a.no_cpu_baseline and img is not None:
+        if not a.no_cpu_baseline and img is not None and world == 1:  # rank 0 at N=1 only
             line["cpu_baseline"] = cpu_baseline(recipe, img, prompts, w["steps"], a.cpu_seconds)
             line["cpu_baseline_1thread"] = cpu_baseline(recipe, img, prompts, w["steps"], a.cpu_seconds / 2,
                                                         threads=1)
@@ -615,7 +615,7 @@ def run_ternary(a, rank, world, local):
                                  "requires, not by HBM"},
             "clocks": clocks.summary(),
         }
-        if not a.no_cpu_baseline:
+        if not a.no_cpu_baseline and world == 1:  # rank 0 at N=1 only
             line["cpu_baseline"] = ternary_cpu_baseline(a.workload, data, x, a.cpu_seconds)
         print(json.dumps(line), flush=True)
     m.close()
