@@ -252,7 +252,7 @@ def main():
     n = len(prompts)
     longest = max(len(p) for p in prompts)
     total_ticks = longest + w["steps"] - 1
-    warm, steps = a.warmup, a.steps
+    warm, steps = max(a.warmup, 3), a.steps  # at least three untimed warm-up steps
     if warm + steps > total_ticks:
         steps = max(1, total_ticks - warm)
     context = longest + w["steps"] + 1
