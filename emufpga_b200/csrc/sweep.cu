@@ -14,6 +14,10 @@
 // Prefetch runs cyclically into the next sweep's first streams, so back to
 // back sweeps keep the copy engine busy across the rewind.
 #include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include <cstdio>
 #include <deque>
@@ -201,19 +205,28 @@ spm_status spm_sweep_open(const uint8_t* spm, uint64_t len, int device, uint64_t
 }
 
 spm_status spm_sweep_open_file(const char* path, int device, uint64_t device_bytes, spm_sweep** out) {
-    std::vector<uint8_t> bytes;
+    // The file is mapped, not read into memory: packing reads it once, straight
+    // into the pinned image, so the host holds one copy of the weights.
+    int fd = -1;
+    void* map = MAP_FAILED;
+    uint64_t len = 0;
     const spm_status st = guarded([&] {
         if (!path) fail(SPM_E_ARG, "null path");
-        std::FILE* f = std::fopen(path, "rb");
-        if (!f) fail(SPM_E_STREAM, std::string("cannot open ") + path);
-        std::unique_ptr<std::FILE, int (*)(std::FILE*)> guard(f, std::fclose);
-        uint8_t buf[1 << 16];
-        size_t got;
-        while ((got = std::fread(buf, 1, sizeof buf, f)) > 0) bytes.insert(bytes.end(), buf, buf + got);
-        if (std::ferror(f)) fail(SPM_E_STREAM, std::string("cannot read ") + path);
+        fd = open(path, O_RDONLY);
+        if (fd < 0) fail(SPM_E_STREAM, std::string("cannot open ") + path);
+        struct stat sb;
+        if (fstat(fd, &sb) != 0) fail(SPM_E_STREAM, std::string("cannot stat ") + path);
+        len = uint64_t(sb.st_size);
+        if (len) {
+            map = mmap(nullptr, len, PROT_READ, MAP_PRIVATE, fd, 0);
+            if (map == MAP_FAILED) fail(SPM_E_STREAM, std::string("cannot map ") + path);
+        }
     });
-    if (st != SPM_OK) return st;
-    return spm_sweep_open(bytes.data(), bytes.size(), device, device_bytes, out);
+    spm_status rc = st;
+    if (rc == SPM_OK) rc = spm_sweep_open(len ? static_cast<const uint8_t*>(map) : nullptr, len, device, device_bytes, out);
+    if (map != MAP_FAILED) munmap(map, len);
+    if (fd >= 0) close(fd);
+    return rc;
 }
 
 spm_status spm_sweep_close(spm_sweep* s) {
