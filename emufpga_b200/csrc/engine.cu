@@ -19,7 +19,6 @@
 #include <fstream>
 #include <map>
 #include <memory>
-#include <mutex>
 #include <set>
 #include <sstream>
 #include <thread>
@@ -111,10 +110,25 @@ struct spm_session {
     bool ep_ready = false;
     std::vector<int> lens;
     bool graphs = true, pdl = true;
+    // GEMV launch profile (spm_session_set_profile): steps run eagerly and
+    // every GEMV launch is bracketed by an event pair on the session stream;
+    // a launch's algorithmic bytes are the quantized weight bytes it streams
+    // (for expert launches counted from the step's plans once it has run).
+    struct ProfLaunch {
+        cudaEvent_t a, b;
+        uint64_t bytes;
+        int32_t kind, layer, stream;
+    };
+    bool prof = false;
+    std::vector<ProfLaunch> prof_pending;
+    std::vector<float> prof_ms;
+    std::vector<uint64_t> prof_bytes;
+    std::vector<int32_t> prof_kind;
     std::map<int, cudaGraphExec_t> exec;
     std::map<int, int> launches;
     std::vector<void*> allocs;
     ~spm_session() {
+        for (auto& p : prof_pending) cudaEventDestroy(p.a), cudaEventDestroy(p.b);
         for (auto& kv : exec) cudaGraphExecDestroy(kv.second);
         for (void* p : ep_mapped) cudaIpcCloseMemHandle(p);
         for (void* p : allocs) cudaFree(p);
@@ -274,7 +288,7 @@ void index_layers(ModelDesc& d) {
     d.head = c.tied ? d.embed : check_shape(need_stream("output.weight"), c.vocab, c.hidden);
     d.output_norm = need_gain("output_norm.weight", c.hidden);
     if (d.streams[d.embed].pk.dtype == SPM_F32 && c.hidden % 32) fail(SPM_E_ARG, "bad embedding width");
-    // StepReport::for_sweep (spm-batch/src/session.rs:263-278): descriptor
+    // StepReport::for_sweep (spm-batch/src/session.rs:105-120): descriptor
     // bytes of every matrix one step reads -- here the rotating streams plus
     // the LM head.  MoE steps read only the routed experts; their per-step
     // bytes are counted by the session.
@@ -719,7 +733,31 @@ void enqueue_step(spm_session* s, int n) {
     const int ff = int(c.intermediate);
     const StreamDesc& E = m->streams[m->embed];
     float* part[2] = {s->sumsq, s->sumsq + kMaxParts * 8};
-    CUDA_OK(launch_embed(E.pk.dtype, m->tiles(m->embed), E.pk, s->tokens, n, s->states, part[0], st, false));
+    // Every launch of the step goes through timed(): with the profile on, an
+    // event pair brackets it (kind, layer, the stream it reads and its bytes
+    // are kept for the record).
+    auto timed = [&](int kind, int layer, int idx, uint64_t bytes, auto&& launch) {
+        cudaEvent_t a = nullptr, b = nullptr;
+        if (s->prof) {
+            CUDA_OK(cudaEventCreate(&a));
+            CUDA_OK(cudaEventCreate(&b));
+            CUDA_OK(cudaEventRecord(a, st));
+        }
+        auto r = launch();
+        if (s->prof) {
+            CUDA_OK(cudaEventRecord(b, st));
+            s->prof_pending.push_back({a, b, bytes, kind, layer, idx});
+        }
+        return r;
+    };
+    auto gemv = [&](const GemvLaunch& g, int idx, int kind, int layer, uint64_t bytes) {
+        return timed(kind, layer, idx, bytes, [&] { return run_gemv(m, g, m->streams[idx].pk.dtype, st, pdl); });
+    };
+    auto qbytes = [&](int idx) { return m->streams[idx].pk.quant_bytes; };
+    timed(SPM_KERNEL_OTHER, -1, -1, 0, [&] {
+        CUDA_OK(launch_embed(E.pk.dtype, m->tiles(m->embed), E.pk, s->tokens, n, s->states, part[0], st, false));
+        return 0;
+    });
     int parts = n;
     auto norm_in = [&](GemvLaunch& g, int64_t gain, int which) {
         g.gain = m->gains + gain;
@@ -735,7 +773,7 @@ void enqueue_step(spm_session* s, int n) {
         add_job(g, m, L.q, nullptr, s->q, qw, nullptr, 0, EPI_STORE);
         add_job(g, m, L.k, nullptr, s->k, kvw, nullptr, 0, EPI_STORE);
         add_job(g, m, L.v, nullptr, s->v, kvw, nullptr, 0, EPI_STORE);
-        run_gemv(m, g, m->streams[L.q].pk.dtype, st, pdl);
+        gemv(g, L.q, SPM_GEMV_DENSE, int(l), qbytes(L.q) + qbytes(L.k) + qbytes(L.v));
         AttnParams P{};
         P.q = s->q; P.k = s->k; P.v = s->v; P.out = s->attn;
         P.kcache = s->kc; P.vcache = s->vc; P.pos = s->pos; P.rope = s->rope;
@@ -745,12 +783,15 @@ void enqueue_step(spm_session* s, int n) {
         P.layer = int(l); P.layers = int(c.layers); P.context = s->context;
         P.heads = int(c.heads); P.kv_heads = int(c.kv_heads); P.head_dim = int(c.head_dim);
         P.family = int(c.family); P.eps = c.eps;
-        CUDA_OK(launch_attention(P, n, st, pdl));
+        timed(SPM_KERNEL_ATTENTION, int(l), -1, 0, [&] {
+            CUDA_OK(launch_attention(P, n, st, pdl));
+            return 0;
+        });
         GemvLaunch go = gemv_base(m, L.o, s->attn, n);
         go.status = s->status;
         go.sumsq_out = part[1];
         add_job(go, m, L.o, nullptr, s->states, d, s->states, d, EPI_ADD);
-        parts = run_gemv(m, go, m->streams[L.o].pk.dtype, st, pdl);
+        parts = gemv(go, L.o, SPM_GEMV_DENSE, int(l), qbytes(L.o));
         if (is_moe(c)) {
             // routed feed-forward (spm-granite-moe/src/layout.rs:188-333)
             const int E = int(c.experts), K = int(c.experts_used), eff = int(c.expert_ff);
@@ -758,10 +799,13 @@ void enqueue_step(spm_session* s, int n) {
             gr.status = s->status;
             norm_in(gr, L.ffn_norm, 1);
             add_job(gr, m, L.router, nullptr, s->moe_logits, E, nullptr, 0, EPI_STORE);
-            run_gemv(m, gr, m->streams[L.router].pk.dtype, st, pdl);
+            gemv(gr, L.router, SPM_GEMV_ROUTER, int(l), qbytes(L.router));
             MoePlan* plan = s->plans + l;
-            CUDA_OK(launch_route(s->moe_logits, L.bias >= 0 ? m->gains + L.bias : nullptr, n, E, K, m->world, m->rank,
-                                 plan, st, pdl));
+            timed(SPM_KERNEL_ROUTE, int(l), -1, 0, [&] {
+                CUDA_OK(launch_route(s->moe_logits, L.bias >= 0 ? m->gains + L.bias : nullptr, n, E, K, m->world, m->rank,
+                                     plan, st, pdl));
+                return 0;
+            });
             // active experts of this rank, at most: the expert launches split
             // each over enough chunks to give every SM two CTAs
             const int local_max = std::min(s->moe_max_active, (E + m->world - 1) / m->world);
@@ -778,7 +822,7 @@ void enqueue_step(spm_session* s, int n) {
             ge.expert_tiles = uint32_t(eff / kTileRows);
             ge.total_tiles = ge.expert_tiles;
             ge.xmode = 0;
-            run_gemv(m, ge, m->streams[L.gate_exps].pk.dtype, st, pdl);
+            gemv(ge, L.gate_exps, SPM_GEMV_EXPERT_GATE_UP, int(l), 0);  // bytes from the plan
             const int chunks_d = std::max(1, std::min(d / kTileRows, (2 * m->sms + local_max - 1) / local_max));
             GemvLaunch gx = gemv_base(m, L.down_exps, s->moe_act, kMoeMaxClients);
             gx.status = s->status;
@@ -806,8 +850,11 @@ void enqueue_step(spm_session* s, int n) {
             gx.expert_tiles = uint32_t(d / kTileRows);
             gx.total_tiles = gx.expert_tiles;
             gx.xmode = 1;
-            run_gemv(m, gx, m->streams[L.down_exps].pk.dtype, st, pdl);
-            CUDA_OK(launch_combine(plan, outs, d, s->states, d, n, K, part[0], m->world > 1 ? &ex : nullptr, st, pdl));
+            gemv(gx, L.down_exps, SPM_GEMV_EXPERT_DOWN, int(l), 0);
+            timed(SPM_KERNEL_COMBINE, int(l), -1, 0, [&] {
+                CUDA_OK(launch_combine(plan, outs, d, s->states, d, n, K, part[0], m->world > 1 ? &ex : nullptr, st, pdl));
+                return 0;
+            });
             parts = combine_parts(d, n);
             continue;
         }
@@ -815,20 +862,26 @@ void enqueue_step(spm_session* s, int n) {
         gu.status = s->status;
         norm_in(gu, L.ffn_norm, 1);
         add_job(gu, m, L.gate, m->tiles(L.up), s->act, ff, nullptr, 0, EPI_SWIGLU);
-        run_gemv(m, gu, m->streams[L.gate].pk.dtype, st, pdl);
+        gemv(gu, L.gate, SPM_GEMV_DENSE, int(l), qbytes(L.gate) + qbytes(L.up));
         GemvLaunch gd = gemv_base(m, L.down, s->act, n);
         gd.status = s->status;
         gd.sumsq_out = part[0];
         add_job(gd, m, L.down, nullptr, s->states, d, s->states, d, EPI_ADD);
-        parts = run_gemv(m, gd, m->streams[L.down].pk.dtype, st, pdl);
+        parts = gemv(gd, L.down, SPM_GEMV_DENSE, int(l), qbytes(L.down));
     }
     GemvLaunch gh = gemv_base(m, m->head, s->states, n);
     gh.status = s->status;
     norm_in(gh, m->output_norm, 0);
     add_job(gh, m, m->head, nullptr, s->logits, int(c.vocab), nullptr, 0, EPI_STORE);
-    run_gemv(m, gh, m->streams[m->head].pk.dtype, st, pdl);
-    CUDA_OK(launch_argmax(s->logits, n, int(c.vocab), s->argmax, st, pdl));
-    CUDA_OK(launch_advance(s->pos, n, s->step, st, pdl));
+    gemv(gh, m->head, SPM_GEMV_HEAD, -1, qbytes(m->head));
+    timed(SPM_KERNEL_OTHER, -1, -1, 0, [&] {
+        CUDA_OK(launch_argmax(s->logits, n, int(c.vocab), s->argmax, st, pdl));
+        return 0;
+    });
+    timed(SPM_KERNEL_OTHER, -1, -1, 0, [&] {
+        CUDA_OK(launch_advance(s->pos, n, s->step, st, pdl));
+        return 0;
+    });
 }
 
 // A bounded device wait that gave up leaves a code in the status word; the
@@ -843,6 +896,35 @@ void check_status(spm_session* s) {
     }
 }
 
+// After a profiled step: wait for it, count the expert launches' bytes from
+// the step's plans (this rank's active experts times one expert's matrices),
+// and move the launches' event times into the record.
+void collect_profile(spm_session* s) {
+    spm_model* m = s->m;
+    CUDA_OK(cudaStreamSynchronize(s->stream));
+    std::vector<MoePlan> plans;
+    if (is_moe(m->cfg)) {
+        plans.resize(m->cfg.layers);
+        CUDA_OK(cudaMemcpy(plans.data(), s->plans, plans.size() * sizeof(MoePlan), cudaMemcpyDeviceToHost));
+    }
+    for (auto& p : s->prof_pending) {
+        uint64_t bytes = p.bytes;
+        if (p.kind == SPM_GEMV_EXPERT_GATE_UP || p.kind == SPM_GEMV_EXPERT_DOWN) {
+            const StreamDesc& d = m->streams[p.stream];
+            const uint64_t one = d.pk.quant_bytes / d.experts;
+            bytes = uint64_t(plans[p.layer].nlocal) * one * (p.kind == SPM_GEMV_EXPERT_GATE_UP ? 2 : 1);
+        }
+        float ms = 0.f;
+        CUDA_OK(cudaEventElapsedTime(&ms, p.a, p.b));
+        cudaEventDestroy(p.a);
+        cudaEventDestroy(p.b);
+        s->prof_ms.push_back(ms);
+        s->prof_bytes.push_back(bytes);
+        s->prof_kind.push_back(p.kind);
+    }
+    s->prof_pending.clear();
+}
+
 // Client counts above 8 are not batched into one sweep by this build.
 constexpr int kMaxBatch = 8;
 
@@ -851,7 +933,7 @@ void step(spm_session* s, int n) {
     if (n > kMaxBatch) fail(SPM_E_ARG, "at most 8 clients share one sweep");
     for (int i = 0; i < n; i++)
         if (s->lens[i] >= s->context) fail(SPM_E_CONTEXT, "context " + std::to_string(s->context) + " exhausted");
-    if (s->graphs) {
+    if (s->graphs && !s->prof) {
         auto it = s->exec.find(n);
         if (it == s->exec.end()) {
             cudaGraph_t graph;
@@ -882,12 +964,13 @@ void step(spm_session* s, int n) {
         CUDA_OK(cudaGraphLaunch(it->second, s->stream));
     } else {
         enqueue_step(s, n);
+        if (s->prof) collect_profile(s);
     }
     for (int i = 0; i < n; i++) s->lens[i]++;
 }
 
 // Host-computed rotary table so that cos/sin are the oracle's glibc values:
-// LLAMA spm-ops/src/attention.rs:241-248, others spm-qwen3-slice/src/attention.rs:11-19.
+// LLAMA spm-ops/src/attention.rs:20-27, others spm-qwen3-slice/src/attention.rs:11-19.
 std::vector<float2> rope_table(const spm_model_cfg& c, int context) {
     const int half = int(c.head_dim / 2);
     std::vector<float2> t(size_t(context) * half);
@@ -1364,6 +1447,32 @@ spm_status spm_session_ep_connect(spm_session* s, const void* handles) {
     });
 }
 
+spm_status spm_session_set_profile(spm_session* s, int32_t enable) {
+    return guarded([&] {
+        CUDA_OK(cudaSetDevice(s->m->device));
+        CUDA_OK(cudaStreamSynchronize(s->stream));
+        for (auto& p : s->prof_pending) cudaEventDestroy(p.a), cudaEventDestroy(p.b);
+        s->prof_pending.clear();
+        s->prof_ms.clear();
+        s->prof_bytes.clear();
+        s->prof_kind.clear();
+        s->prof = enable != 0;
+    });
+}
+
+spm_status spm_session_profile(const spm_session* s, int32_t max, float* ms, uint64_t* bytes, int32_t* kind,
+                               int32_t* count) {
+    return guarded([&] {
+        const int32_t have = int32_t(s->prof_ms.size());
+        if (count) *count = have;
+        for (int32_t i = 0; i < std::min(max, have); i++) {
+            if (ms) ms[i] = s->prof_ms[i];
+            if (bytes) bytes[i] = s->prof_bytes[i];
+            if (kind) kind[i] = s->prof_kind[i];
+        }
+    });
+}
+
 spm_status spm_session_launches_per_step(spm_session* s, int32_t n, int32_t* launches) {
     return guarded([&] {
         auto it = s->launches.find(n);
@@ -1391,25 +1500,20 @@ spm_status spm_session_launches_per_step(spm_session* s, int32_t n, int32_t* lau
 // buffer keeps the previous call's contents, but nothing in it needs to start
 // at zero: the kernel writes every float that the call then copies out.
 // Calls that overlap on the GPU (from two host threads, say) use the same
-// buffer and race; serialise them.  The first call on each device resolves the
-// buffer's device address, so make that first call before any stream capture
-// begins on that device.
+// buffer and race; serialise them.  Every call looks up the buffer's device
+// address in the calling thread's current context (cheap once the module is
+// loaded), so an address never outlives the context it belongs to.  The first
+// call on a device loads this library's device code there; make that first
+// call before any stream capture begins on that device.
 constexpr uint64_t kStaticDequantFloats = uint64_t(1) << 20;
 static __device__ __align__(256) float g_static_dequant[kStaticDequantFloats];
 
 namespace {
-std::mutex g_static_dequant_mu;
-std::map<int, float*> g_static_dequant_ptr;  // device address of the buffer, per device
-
-// The calling thread's current device must be `device`.  In host code the
-// array's name is only a stand-in; its device address comes from the runtime.
-float* static_dequant_buffer(int device) {
-    std::lock_guard<std::mutex> lock(g_static_dequant_mu);
-    auto it = g_static_dequant_ptr.find(device);
-    if (it != g_static_dequant_ptr.end()) return it->second;
+// In host code the array's name is only a stand-in; its device address comes
+// from the runtime, for the current device's context.
+float* static_dequant_buffer() {
     float* ptr = nullptr;
     CUDA_OK(cudaGetSymbolAddress((void**)&ptr, g_static_dequant));
-    g_static_dequant_ptr[device] = ptr;
     return ptr;
 }
 }  // namespace
@@ -1427,7 +1531,7 @@ spm_status spm_dequant_rows_static(const spm_model* m, int32_t index, uint64_t r
                                 " cols exceeds the static buffer of " + std::to_string(kStaticDequantFloats) +
                                 " floats; request fewer rows per call");
         CUDA_OK(cudaSetDevice(m->device));
-        float* buf = static_dequant_buffer(m->device);
+        float* buf = static_dequant_buffer();
         CUDA_OK(launch_dequant(p.dtype, m->tiles(index), p, row0, rows, buf, nullptr));
         CUDA_OK(cudaMemcpy(out_host, buf, rows * p.cols * sizeof(float), cudaMemcpyDeviceToHost));
     });

@@ -79,7 +79,7 @@ uint16_t f32_to_f16(float f) {
 }
 
 // ------------------------------------------------------------------
-// GGUF: spm-gguf/src/parse.rs:47-198 and wire.rs:10-91, on a memory image.
+// GGUF: spm-gguf/src/parse.rs:31-182 and wire.rs:10-91, on a memory image.
 // ------------------------------------------------------------------
 static constexpr uint64_t kMaxMetadata = 1000000, kMaxTensors = 1000000;
 static constexpr uint64_t kMaxString = 16ull << 20, kMaxArray = 2000000;

@@ -1,7 +1,7 @@
 // .spm files on the host: the fixed 32-byte header (spm-header/src/parse.rs:
 // 10-62), the 32-byte stream descriptors (spm-layout/src/wire.rs:12-30,
 // model.rs Encoding::bytes_for), the group order (spm-walk/src/cursor.rs,
-// spm-layout/src/tiling.rs:37-55) and the group framing -- an f32 scale, then
+// spm-layout/src/tiling.rs:37-51) and the group framing -- an f32 scale, then
 // the group's payload (spm-file/src/read.rs:69-101).  Plus the device packing
 // of a ternary stream (spm-codec/src/lib.rs: two bits per weight, LSB pair
 // first, bit 0 = nonzero, bit 1 = negative).

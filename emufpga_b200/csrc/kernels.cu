@@ -210,7 +210,7 @@ constexpr int kAttnThreads = 256;
 constexpr int kSub = 64;  // positions staged per pass
 
 __device__ __forceinline__ void rope_pair(float& x, float& y, float c, float s, bool llama) {
-    if (llama) {  // spm-ops/src/attention.rs:249-251
+    if (llama) {  // spm-ops/src/attention.rs:29-30
         const float nx = __fmaf_rn(x, c, -__fmul_rn(y, s));
         const float ny = __fmaf_rn(x, s, __fmul_rn(y, c));
         x = nx;

@@ -86,7 +86,7 @@ def ternary_codes(weights: Sequence[int] | np.ndarray) -> np.ndarray:
 
 class SpmWriter:
     """Builds a .spm file group by group, in stream order (SpmWriter,
-    spm-file/src/write.rs:13-123): the header and directory first, then each
+    spm-file/src/write.rs:15-108): the header and directory first, then each
     group's scale and payload; a group of the wrong length or past the last
     stream is refused, and finish() refuses a file with groups still owed."""
 

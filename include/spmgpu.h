@@ -8,13 +8,13 @@
  * boundary.  Handles are opaque; there is no global model state.
  *
  * Reference interfaces replaced (paths inside the emufpga tree):
- *   spm_gguf_*            spm-gguf/src/parse.rs:169-198 (read), tensor.rs:21-67
+ *   spm_gguf_*            spm-gguf/src/parse.rs:153-182 (read), tensor.rs:21-67
  *   spm_decode_blocks     spm-gguf/src/tensor.rs:69-210 (decode_f32/q8_0/q5_k/q6_k)
  *   spm_order_check       spm-order/src/order.rs:28-111 (parse_order, reorder)
  *   spm_model_open*       spm-stream-groups/src/groups.rs:54-117 (GroupStream::open)
  *                         + spm-smol/src/config.rs (SmolConfig) + the .order layout
- *   spm_model_weight_bytes spm-batch/src/session.rs:255-278 (StepReport::for_sweep)
- *   spm_session_create    spm-batch/src/session.rs:180-237 (Client::new, Scratch::new)
+ *   spm_model_weight_bytes spm-batch/src/session.rs:83-121 (StepReport::for_sweep)
+ *   spm_session_create    spm-batch/src/session.rs:25-34, :64-78 (Client::new, Scratch::new)
  *   spm_decode_step       spm-batch/src/step.rs:19-40 (decode_step) + the greedy pick
  *                         of spm-batch/examples/serve-demo.rs:72-90
  *   spm_streamed          spm-linear/src/stream.rs:31-55 (streamed) for one stream
@@ -152,8 +152,10 @@ spm_status spm_dequant_rows(const spm_model* m, int32_t index, uint64_t row0, ui
  * that is decoding.  Decodes into one static 4 MiB buffer per device, part of
  * the library's device image and held until exit: rows x cols must not exceed
  * 1048576 floats (SPM_E_ARG otherwise).  Calls that overlap on the GPU share
- * the buffer and race, so serialise them.  The first call on a device resolves
- * the buffer's address; make it before any stream capture on that device. */
+ * the buffer and race, so serialise them.  Each call looks the buffer's
+ * address up in the current context, so it stays valid across a context
+ * reset.  The first call on a device loads the library's device code there;
+ * make it before any stream capture on that device. */
 spm_status spm_dequant_rows_static(const spm_model* m, int32_t index, uint64_t row0, uint64_t rows,
                                    float* out_host);
 /* y[p][r] = sum_c W[r][c] * x[p][c] for one stream; x_dev is positions x cols,
@@ -214,9 +216,32 @@ spm_status spm_session_ep_handle(spm_session* s, void* handle64);
 spm_status spm_session_ep_connect(spm_session* s, const void* handles);
 /* Kernel launches issued by one step at client count n (graph nodes). */
 spm_status spm_session_launches_per_step(spm_session* s, int32_t n, int32_t* launches);
+/* Launch profile; no counterpart in the reference (its StepReport counts
+ * weight bytes, spm-batch/src/session.rs:83-121, but times nothing).  While
+ * enabled, steps run without the CUDA graph and every kernel launch of a step
+ * is bracketed by a CUDA event pair on the session stream.  Enabling or
+ * disabling clears the record.  spm_session_profile returns, for up to `max`
+ * recorded launches, the device milliseconds, the algorithmic bytes (for a
+ * GEMV the quantized weight bytes it streams, expert launches counting this
+ * rank's active experts of that step; 0 for the other kernels) and the kind;
+ * *count receives the number recorded. */
+enum {
+    SPM_GEMV_DENSE = 0,          /* GEMV: attention q/k/v, o; dense feed-forward */
+    SPM_GEMV_ROUTER = 1,         /* GEMV: MoE router logits                   */
+    SPM_GEMV_EXPERT_GATE_UP = 2, /* GEMV: gate/up of the active experts       */
+    SPM_GEMV_EXPERT_DOWN = 3,    /* GEMV: down projection of the active experts */
+    SPM_GEMV_HEAD = 4,           /* GEMV: LM head                             */
+    SPM_KERNEL_ATTENTION = 5,    /* QK-norm, RoPE, KV append, decode attention */
+    SPM_KERNEL_ROUTE = 6,        /* router softmax, top-k, expert plan         */
+    SPM_KERNEL_COMBINE = 7,      /* weighted expert combine + residual         */
+    SPM_KERNEL_OTHER = 8         /* embedding gather, greedy pick, positions   */
+};
+spm_status spm_session_set_profile(spm_session* s, int32_t enable);
+spm_status spm_session_profile(const spm_session* s, int32_t max, float* ms, uint64_t* bytes,
+                               int32_t* kind, int32_t* count);
 
 /* ---- .spm files and the ternary profile (Encoding::Ternary2F32I32) ----
- * A .spm file is a 32-byte header (spm-header/src/parse.rs:10-62), one
+ * A .spm file is a 32-byte header (spm-header/src/parse.rs:12-59), one
  * 32-byte descriptor per stream (spm-layout/src/wire.rs:12-30), then every
  * stream's scale groups in order, each an f32 scale followed by its payload
  * (spm-file/src/read.rs:69-101).  Errors follow the reference's:

@@ -70,13 +70,15 @@ int or_type_layout(uint32_t t, uint64_t* bv, uint64_t* bb) {
 }
 
 /* Q8_0: spm-gguf/src/tensor.rs:193-210.  w = d * (float)(int8)q. */
-static void dec_q8_0(const uint8_t* blk, float* out) {
+__attribute__((target_clones("avx2", "default"))) static void dec_q8_0(const uint8_t* blk, float* out) {
     float d = or_f16_to_f32(le16(blk));
     for (int i = 0; i < 32; i++) out[i] = d * (float)(int8_t)blk[2 + i];
 }
 
-/* Q6_K: spm-gguf/src/tensor.rs:103-139.  w = (d * sc) * (q - 32). */
-static void dec_q6_k(const uint8_t* blk, float* out) {
+/* Q6_K: spm-gguf/src/tensor.rs:103-139.  w = (d * sc) * (q - 32); the
+ * product d * sc is formed once per 16 values (the same rounding as forming it
+ * per value, which the reference writes). */
+__attribute__((target_clones("avx2", "default"))) static void dec_q6_k(const uint8_t* blk, float* out) {
     const uint8_t* ql0 = blk;
     const uint8_t* qh0 = blk + 128;
     const uint8_t* sc0 = blk + 192;
@@ -86,18 +88,15 @@ static void dec_q6_k(const uint8_t* blk, float* out) {
         const uint8_t* qh = qh0 + half * 32;
         const uint8_t* sc = sc0 + half * 8;
         float* o = out + half * 128;
-        for (int l = 0; l < 32; l++) {
-            int is = l / 16;
-            uint8_t q[4] = {
-                (uint8_t)((ql[l] & 0x0f) | ((qh[l] & 3) << 4)),
-                (uint8_t)((ql[l + 32] & 0x0f) | (((qh[l] >> 2) & 3) << 4)),
-                (uint8_t)((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)),
-                (uint8_t)((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)),
-            };
-            for (int lane = 0; lane < 4; lane++) {
-                float qf = (float)q[lane] - 32.0f;
-                float scale = (float)(int8_t)sc[is + lane * 2];
-                o[l + lane * 32] = d * scale * qf;
+        for (int lane = 0; lane < 4; lane++) {
+            const uint8_t* qlo = ql + (lane & 1) * 32;
+            const int lshift = (lane >> 1) * 4, hshift = lane * 2;
+            for (int is = 0; is < 2; is++) {
+                const float ds = d * (float)(int8_t)sc[is + lane * 2];
+                for (int l = is * 16; l < is * 16 + 16; l++) {
+                    const int q = ((qlo[l] >> lshift) & 0x0f) | (((qh[l] >> hshift) & 3) << 4);
+                    o[l + lane * 32] = ds * ((float)q - 32.0f);
+                }
             }
         }
     }
@@ -114,25 +113,26 @@ static void scale_min_q5(int index, const uint8_t* p, uint8_t* sc, uint8_t* m) {
     }
 }
 
-/* Q5_K: spm-gguf/src/tensor.rs:144-177.  w = (d*sc)*q - dmin*m. */
-static void dec_q5_k(const uint8_t* blk, float* out) {
+/* Q5_K: spm-gguf/src/tensor.rs:144-177.  w = (d*sc)*q - dmin*m; the two
+ * products d*sc and dmin*m are formed once per 32 values (the same roundings
+ * as forming them per value). */
+__attribute__((target_clones("avx2", "default"))) static void dec_q5_k(const uint8_t* blk, float* out) {
     float d = or_f16_to_f32(le16(blk));
     float dmin = or_f16_to_f32(le16(blk + 2));
     const uint8_t* scales = blk + 4;
     const uint8_t* qh = blk + 16;
     const uint8_t* qs = blk + 48;
-    int k = 0;
     for (int group = 0; group < 4; group++) {
         for (int half = 0; half < 2; half++) {
             int index = group * 2 + half;
             uint8_t sc, mn;
             scale_min_q5(index, scales, &sc, &mn);
-            uint8_t bit = (uint8_t)(1u << index);
+            const float ds = d * (float)sc, dm = dmin * (float)mn;
+            float* o = out + index * 32;
             for (int lane = 0; lane < 32; lane++) {
-                uint8_t packed = qs[group * 32 + lane];
-                uint8_t low = half == 0 ? (packed & 0x0f) : (packed >> 4);
-                uint8_t quant = (uint8_t)(low + ((qh[lane] & bit) ? 16 : 0));
-                out[k++] = d * (float)sc * (float)quant - dmin * (float)mn;
+                const int low = (qs[group * 32 + lane] >> (half * 4)) & 0x0f;
+                const int quant = low + (((qh[lane] >> index) & 1) << 4);
+                o[lane] = ds * (float)quant - dm;
             }
         }
     }
@@ -142,7 +142,7 @@ static void dec_q5_k(const uint8_t* blk, float* out) {
  * Follows ggml's published block_q2_K: scales[16] (low nibble scale, high
  * nibble min), qs[64] (four 2-bit planes per 32 bytes), d, dmin (fp16).
  * w = (d*(sc&15)) * q - (dmin*(sc>>4)).  Pinned against gguf-py 0.19.0. */
-static void dec_q2_k(const uint8_t* blk, float* out) {
+__attribute__((target_clones("avx2", "default"))) static void dec_q2_k(const uint8_t* blk, float* out) {
     const uint8_t* scales = blk;
     const uint8_t* qs = blk + 16;
     float d = or_f16_to_f32(le16(blk + 80));
@@ -195,7 +195,7 @@ int or_decode(uint32_t t, const uint8_t* bytes, uint64_t nbytes, float* out) {
 }
 
 /* ------------------------------------------------------------------ */
-/* GGUF: a bounded restatement of spm-gguf/src/parse.rs:47-198 and     */
+/* GGUF: a bounded restatement of spm-gguf/src/parse.rs:31-182 and     */
 /* wire.rs:10-91, reading from memory instead of a file.               */
 /* ------------------------------------------------------------------ */
 #define OR_MAX_METADATA 1000000ull
@@ -411,7 +411,80 @@ static int nthreads(int threads) {
  * out = fma(w, x[col], out) over col ascending, starting from +0.0:
  * spm-linear/src/resident.rs:124-137 (apply_weight) and
  * spm-granite-moe/src/layout.rs:232-238 (q6_operation).  Rows are
- * independent, so spreading rows over threads leaves every bit unchanged. */
+ * independent, so spreading rows over threads leaves every bit unchanged.
+ *
+ * Speed without changing a bit: R rows x P positions chains advance together
+ * column by column (each chain still adds its columns in ascending order from
+ * +0.0), so the CPU overlaps independent chains instead of waiting on one;
+ * fmaf is the correctly rounded fused multiply-add whether it runs as the FMA
+ * instruction (the "fma" clone, chosen at load time where the CPU has it) or
+ * as the libm call.  The plain-dot form (or_gemv_dot) keeps its separately
+ * rounded multiply and add (-ffp-contract=off). */
+#define OR_STEP_FMA(w, x, a) fmaf((w), (x), (a))
+#define OR_STEP_DOT(w, x, a) ((a) + (x) * (w))
+#define OR_CHAINS(NAME, R, P, STEP)                                                          \
+    __attribute__((target_clones("fma", "default"))) static void NAME(                       \
+        const float* w, uint64_t cols, const float* x, uint64_t xs, float* out) {            \
+        float a[R][P];                                                                       \
+        for (int r = 0; r < R; r++)                                                          \
+            for (int p = 0; p < P; p++) a[r][p] = 0.0f;                                      \
+        for (uint64_t c = 0; c < cols; c++) {                                                \
+            float xv[P];                                                                     \
+            _Pragma("GCC unroll 8") for (int p = 0; p < P; p++) xv[p] = x[(uint64_t)p * xs + c]; \
+            _Pragma("GCC unroll 8") for (int r = 0; r < R; r++) {                            \
+                const float wv = w[(uint64_t)r * cols + c];                                  \
+                _Pragma("GCC unroll 8") for (int p = 0; p < P; p++) a[r][p] = STEP(wv, xv[p], a[r][p]); \
+            }                                                                                \
+        }                                                                                    \
+        for (int r = 0; r < R; r++)                                                          \
+            for (int p = 0; p < P; p++) out[r * P + p] = a[r][p];                            \
+    }
+OR_CHAINS(fma_8x1, 8, 1, OR_STEP_FMA)
+OR_CHAINS(fma_4x2, 4, 2, OR_STEP_FMA)
+OR_CHAINS(fma_3x3, 3, 3, OR_STEP_FMA)
+OR_CHAINS(fma_2x4, 2, 4, OR_STEP_FMA)
+OR_CHAINS(fma_1x1, 1, 1, OR_STEP_FMA)
+OR_CHAINS(fma_1x2, 1, 2, OR_STEP_FMA)
+OR_CHAINS(fma_1x3, 1, 3, OR_STEP_FMA)
+OR_CHAINS(fma_1x4, 1, 4, OR_STEP_FMA)
+OR_CHAINS(dot_8x1, 8, 1, OR_STEP_DOT)
+OR_CHAINS(dot_4x2, 4, 2, OR_STEP_DOT)
+OR_CHAINS(dot_3x3, 3, 3, OR_STEP_DOT)
+OR_CHAINS(dot_2x4, 2, 4, OR_STEP_DOT)
+OR_CHAINS(dot_1x1, 1, 1, OR_STEP_DOT)
+OR_CHAINS(dot_1x2, 1, 2, OR_STEP_DOT)
+OR_CHAINS(dot_1x3, 1, 3, OR_STEP_DOT)
+OR_CHAINS(dot_1x4, 1, 4, OR_STEP_DOT)
+
+typedef void (*or_chain_fn)(const float*, uint64_t, const float*, uint64_t, float*);
+#define OR_ROW_BLOCK 8
+
+/* Rows [r0, r0+nr) decoded in w (nr <= OR_ROW_BLOCK rows of cols values):
+ * every (position, row) chain of them, into y[pos][row]. */
+static void chains_block(const float* w, uint64_t r0, int nr, uint64_t rows, uint64_t cols, const float* x,
+                         int positions, float* y, int fused) {
+    static const or_chain_fn wide_fma[5] = {0, fma_8x1, fma_4x2, fma_3x3, fma_2x4};
+    static const or_chain_fn wide_dot[5] = {0, dot_8x1, dot_4x2, dot_3x3, dot_2x4};
+    static const or_chain_fn one_fma[5] = {0, fma_1x1, fma_1x2, fma_1x3, fma_1x4};
+    static const or_chain_fn one_dot[5] = {0, dot_1x1, dot_1x2, dot_1x3, dot_1x4};
+    static const int wide_rows[5] = {0, 8, 4, 3, 2};
+    float out[8 * 4];
+    for (int p0 = 0; p0 < positions; p0 += 4) {
+        const int pc = positions - p0 < 4 ? positions - p0 : 4;
+        const int R = wide_rows[pc];
+        int r = 0;
+        for (; r + R <= nr; r += R) {
+            (fused ? wide_fma : wide_dot)[pc](w + (uint64_t)r * cols, cols, x + (uint64_t)p0 * cols, cols, out);
+            for (int i = 0; i < R; i++)
+                for (int p = 0; p < pc; p++) y[(uint64_t)(p0 + p) * rows + r0 + (uint64_t)(r + i)] = out[i * pc + p];
+        }
+        for (; r < nr; r++) {
+            (fused ? one_fma : one_dot)[pc](w + (uint64_t)r * cols, cols, x + (uint64_t)p0 * cols, cols, out);
+            for (int p = 0; p < pc; p++) y[(uint64_t)(p0 + p) * rows + r0 + (uint64_t)r] = out[p];
+        }
+    }
+}
+
 static int gemv_impl(uint32_t t, const uint8_t* blocks, uint64_t rows, uint64_t cols,
                      const float* x, int positions, float* y, int threads, int fused) {
     uint64_t bv, bb;
@@ -419,22 +492,17 @@ static int gemv_impl(uint32_t t, const uint8_t* blocks, uint64_t rows, uint64_t 
     if (cols % bv != 0) return -1;
     uint64_t row_bytes = cols / bv * bb;
     int nt = nthreads(threads);
-#pragma omp parallel num_threads(nt)
+    const int64_t nblocks = (int64_t)((rows + OR_ROW_BLOCK - 1) / OR_ROW_BLOCK);
+#pragma omp parallel num_threads(nt) if (nt > 1)
     {
-        float* w = (float*)malloc(cols * sizeof(float));
+        float* w = (float*)malloc(OR_ROW_BLOCK * cols * sizeof(float) + 1);
 #pragma omp for schedule(static)
-        for (int64_t r = 0; r < (int64_t)rows; r++) {
-            or_decode(t, blocks + (uint64_t)r * row_bytes, row_bytes, w);
-            for (int pos = 0; pos < positions; pos++) {
-                const float* xp = x + (uint64_t)pos * cols;
-                float acc = 0.0f;
-                if (fused) {
-                    for (uint64_t c = 0; c < cols; c++) acc = fmaf(w[c], xp[c], acc);
-                } else {
-                    for (uint64_t c = 0; c < cols; c++) acc = acc + xp[c] * w[c];
-                }
-                y[(uint64_t)pos * rows + (uint64_t)r] = acc;
-            }
+        for (int64_t b = 0; b < nblocks; b++) {
+            const uint64_t r0 = (uint64_t)b * OR_ROW_BLOCK;
+            const int nr = (int)(rows - r0 < OR_ROW_BLOCK ? rows - r0 : OR_ROW_BLOCK);
+            for (int i = 0; i < nr; i++)
+                or_decode(t, blocks + (r0 + (uint64_t)i) * row_bytes, row_bytes, w + (uint64_t)i * cols);
+            chains_block(w, r0, nr, rows, cols, x, positions, y, fused);
         }
         free(w);
     }
@@ -446,7 +514,7 @@ int or_gemv_fma(uint32_t t, const uint8_t* blocks, uint64_t rows, uint64_t cols,
     return gemv_impl(t, blocks, rows, cols, x, positions, y, threads, 1);
 }
 
-/* spm-batch/src/inner.rs:150-156 (finish) and spm-qwen3-slice/src/math.rs:12-20
+/* spm-batch/src/inner.rs:89-105 (finish) and spm-qwen3-slice/src/math.rs:12-20
  * (matvec): `zip(a, b).map(|(a, b)| a * b).sum()`, no fused multiply-add. */
 int or_gemv_dot(uint32_t t, const uint8_t* blocks, uint64_t rows, uint64_t cols, const float* x,
                 int positions, float* y, int threads) {
@@ -848,32 +916,58 @@ static void moe_half(or_session* s, const or_layer* L, int threads, int32_t* rou
             for (int j = 0; j < K; j++) routes[(size_t)i * K + j] = sel[(size_t)i * K + j];
     }
     memset(s->combined, 0, sizeof(float) * (size_t)n * d);
-    float* xs = (float*)malloc(sizeof(float) * (size_t)n * d);
-    int* toks = (int*)malloc(sizeof(int) * (size_t)n);
+    /* The active experts run in parallel (one thread each, every GEMV chain
+     * unchanged); the combine below then adds their outputs in ascending
+     * expert id, as the reference's serial loop does. */
+    int* active = (int*)malloc(sizeof(int) * (size_t)E);
+    int* ntok = (int*)malloc(sizeof(int) * (size_t)E);
+    int* toks = (int*)malloc(sizeof(int) * (size_t)E * n);
+    int na = 0;
     for (int e = 0; e < E; e++) {
         int nt = 0;
         for (int i = 0; i < n; i++)
             for (int j = 0; j < K; j++)
-                if (sel[(size_t)i * K + j] == e) { toks[nt++] = i; break; }
+                if (sel[(size_t)i * K + j] == e) { toks[(size_t)na * n + nt++] = i; break; }
         if (nt == 0) continue;
-        for (int t = 0; t < nt; t++) memcpy(xs + (size_t)t * d, s->normed + (size_t)toks[t] * d, sizeof(float) * d);
-        gemv_w(&L->up_exps, (uint64_t)e, xs, nt, s->up, threads);
-        gemv_w(&L->gate_exps, (uint64_t)e, xs, nt, s->gate, threads);
-        for (size_t i = 0; i < (size_t)nt * ff; i++) {
-            float g = s->gate[i];
-            s->act[i] = g / (1.0f + expf(-g)) * s->up[i];
+        ntok[na] = nt;
+        active[na++] = e;
+    }
+    float* proj = (float*)malloc(sizeof(float) * (size_t)na * n * d + 1);
+    int nth = nthreads(threads);
+#pragma omp parallel num_threads(nth)
+    {
+        float* xs = (float*)malloc(sizeof(float) * (size_t)n * d);
+        float* up = (float*)malloc(sizeof(float) * (size_t)n * ff);
+        float* gate = (float*)malloc(sizeof(float) * (size_t)n * ff);
+        float* act = (float*)malloc(sizeof(float) * (size_t)n * ff);
+#pragma omp for schedule(dynamic, 1)
+        for (int a = 0; a < na; a++) {
+            const int e = active[a], nt = ntok[a];
+            for (int t = 0; t < nt; t++)
+                memcpy(xs + (size_t)t * d, s->normed + (size_t)toks[(size_t)a * n + t] * d, sizeof(float) * d);
+            gemv_w(&L->up_exps, (uint64_t)e, xs, nt, up, 1);
+            gemv_w(&L->gate_exps, (uint64_t)e, xs, nt, gate, 1);
+            for (size_t i = 0; i < (size_t)nt * ff; i++) {
+                float g = gate[i];
+                act[i] = g / (1.0f + expf(-g)) * up[i];
+            }
+            gemv_w(&L->down_exps, (uint64_t)e, act, nt, proj + (size_t)a * n * d, 1);
         }
-        gemv_w(&L->down_exps, (uint64_t)e, s->act, nt, s->proj, threads);
-        for (int t = 0; t < nt; t++) {
-            int i = toks[t];
+        free(xs); free(up); free(gate); free(act);
+    }
+    for (int a = 0; a < na; a++) {
+        const int e = active[a];
+        for (int t = 0; t < ntok[a]; t++) {
+            int i = toks[(size_t)a * n + t];
             float pe = s->probs[(size_t)i * E + e];
             float* total = s->combined + (size_t)i * d;
-            const float* lane = s->proj + (size_t)t * d;
+            const float* lane = proj + ((size_t)a * n + t) * d;
             for (size_t col = 0; col < d; col++) total[col] = total[col] + lane[col] * pe / normv[i];
         }
     }
+    free(active); free(ntok); free(proj);
     for (size_t i = 0; i < (size_t)n * d; i++) s->states[i] = s->states[i] + s->combined[i];
-    free(sel); free(selv); free(normv); free(xs); free(toks);
+    free(sel); free(selv); free(normv); free(toks);
 }
 
 int or_decode_step(or_session* s, const uint32_t* tokens, float* logits, int threads, int32_t* routes) {
@@ -958,7 +1052,7 @@ int or_decode_step(or_session* s, const uint32_t* tokens, float* logits, int thr
     }
     /* spm-batch/src/step.rs:34-36 */
     for (int i = 0; i < n; i++) s->len[i] += 1;
-    /* spm-batch/src/inner.rs:142-158 (finish): final norm, then plain dots. */
+    /* spm-batch/src/inner.rs:89-105 (finish): final norm, then plain dots. */
     if (c->family == OR_FAMILY_LLAMA) {
         or_scaled_rms_norm(s->states, m->output_norm, c->eps, (int)d, n);
         memcpy(s->normed, s->states, sizeof(float) * (size_t)n * d);
@@ -1041,7 +1135,7 @@ static uint64_t spm_bytes_for(uint8_t enc, uint64_t count) {
     }
 }
 
-/* spm-header/src/parse.rs:10-62 then the directory loop of
+/* spm-header/src/parse.rs:12-59 then the directory loop of
  * spm-file/src/read.rs:51-60 with spm-layout/src/wire.rs:12-30. */
 static int spm_parse(const uint8_t* src, uint64_t len, uint32_t* count, or_spm_desc** out, uint64_t* payload,
                      char* err, int errlen) {
@@ -1118,7 +1212,7 @@ int or_spm_describe(const uint8_t* spm, uint64_t len, int32_t index, uint32_t* s
     return 0;
 }
 
-/* Cursor (spm-walk/src/cursor.rs:20-68): a (stream, group) position that
+/* Cursor (spm-walk/src/cursor.rs:20-58): a (stream, group) position that
  * skips streams with no groups left. */
 typedef struct {
     uint32_t stream;
@@ -1137,7 +1231,7 @@ static void cursor_settle(or_cursor* c, const or_spm_desc* d, uint32_t n) {
     }
 }
 
-/* spm-layout/src/tiling.rs:37-55 group_len. */
+/* spm-layout/src/tiling.rs:37-51 group_len. */
 static uint64_t cursor_group_len(const or_cursor* c, const or_spm_desc* d) {
     const uint64_t total = spm_total(&d[c->stream]);
     const uint64_t start = (uint64_t)d[c->stream].group_size * c->group;

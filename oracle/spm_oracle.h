@@ -69,7 +69,7 @@ void or_gguf_free(or_gguf* g);
  * (or row-major f32 for OR_F32). threads<=0 means all cores. */
 int or_gemv_fma(uint32_t ggml_type, const uint8_t* blocks, uint64_t rows, uint64_t cols,
                 const float* x, int positions, float* y, int threads);
-/* logits-style plain multiply + sequential sum (spm-batch/src/inner.rs:150-156). */
+/* logits-style plain multiply + sequential sum (spm-batch/src/inner.rs:89-105, finish). */
 int or_gemv_dot(uint32_t ggml_type, const uint8_t* blocks, uint64_t rows, uint64_t cols,
                 const float* x, int positions, float* y, int threads);
 

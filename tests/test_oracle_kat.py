@@ -140,7 +140,7 @@ def test_a_later_position_cannot_see_an_earlier_one_only_the_reverse():
     assert not np.array_equal(first1, second1)
 
 
-# ---- spm-qwen3-slice/src/math.rs:186-203, spm-granite-moe/src/math.rs:38-47 ----
+# ---- spm-qwen3-slice/src/math.rs:54-60, spm-granite-moe/src/math.rs:38-47 ----
 def test_rms_norm_known_vector():
     r = O.rms_norm_slice(np.array([3.0, 4.0]), np.array([1.0, 2.0]), 1e-6)
     assert abs(r[0] - 0.848528) < 1e-5
@@ -185,6 +185,6 @@ def test_gemv_is_a_fused_multiply_add_chain():
     x = np.array([1.0, 1.0 + 2.0**-22], dtype=np.float32)
     y = O.gemv_fma(O.F32, w.view(np.uint8), 1, 2, x, 1)[0, 0]
     assert y == np.float32(3 * 2.0**-23 + 2.0**-45)
-    # the logits path (spm-batch/src/inner.rs:154) is multiply-then-add
+    # the logits path (spm-batch/src/inner.rs:89-105, finish) is multiply-then-add
     y2 = O.gemv_dot(O.F32, w.view(np.uint8), 1, 2, x, 1)[0, 0]
     assert y2 == np.float32(3 * 2.0**-23)
