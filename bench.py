@@ -2,17 +2,28 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
-A step is one lockstep tick of the workload (serve-demo schedule): every
-client decodes one token off one sweep of the weights.  `value` is the
-whole-job tokens/s with the weights resident in HBM, each step timed with
-CUDA events on the session stream and L2 flushed (a 256 MiB write) between
-steps; `e2e` runs the same ticks through spm_decode_step with host token
-buffers (H2D of the tokens and D2H of the greedy picks inside the timed
-region).  Dense models do not shard: N>1 runs N independent replicas
-("replicas only"), and the slowest rank's time sets the job time.  Routed
-(MoE) models over N>1 GPUs run expert parallel: one job serving the same
-clients on every rank, experts dealt round robin over the ranks, expert
-outputs exchanged over NVLink ("scaling": "strong").
+A run follows the serve-demo lockstep schedule (spm-batch/examples/
+serve-demo.rs:59-91): every tick each client decodes one token off one sweep
+of the weights; a client feeds its prompt one token per tick, then its greedy
+picks.  The prompt ticks run untimed; then W warm-up decode ticks, then K
+timed decode ticks (every client feeding back its own greedy token, contexts
+past the prompts).  `value` is the whole-job tokens/s with the weights
+resident in HBM, each tick timed with CUDA events on the session stream and
+L2 flushed (a 256 MiB write) before each tick; `e2e` times the next K ticks
+through spm_decode_step with host token buffers (H2D of the tokens and D2H of
+the greedy picks inside the timed region).  `roofline` is the dominant
+kernel's: every GEMV launch of a few further decode ticks run eagerly with a
+CUDA event pair around each launch (spm_session_set_profile), achieved =
+quantized weight bytes those launches stream / their summed duration.
+
+The default workload is BASELINE configs[4], Qwen3-30B-A3B Q5_K with eight
+clients (the largest configuration; it fits one B200), and the line carries a
+`batch1` sub-record for configs[2]'s batch-1 case (Qwen3-8B Q6_K, one client)
+measured the same way.  Dense models do not shard: N>1 runs N independent
+replicas ("replicas only").  Routed (MoE) models over N>1 GPUs run expert
+parallel: one job serving the same clients on every rank, experts dealt round
+robin over the ranks, expert outputs exchanged over NVLink ("scaling":
+"strong").
 
 `--workload ternary-4096-b8` times the ternary GEMV of spm-gemv-ref instead
 (one launch over a 4096 x 4096 ternary stream with one scale per column and
@@ -20,6 +31,10 @@ outputs exchanged over NVLink ("scaling": "strong").
 useful-weights rate), and `--workload dense-f32-4096-b8` the dense .spm
 streamed GEMV of spm-linear (a 4096 x 4096 F32 stream, 8 positions), with the
 same clocks, L2 flush, e2e and CPU-baseline fields; N>1 runs replicas.
+
+`--impl reference` times the CPU oracle (this repository's C restatement of
+the reference's CPU token loop; the reference itself is Rust and cannot be
+built here) on all host threads, in a process that loads no GPU code.
 """
 from __future__ import annotations
 
@@ -36,20 +51,32 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-DEFAULT_WORKLOAD = "smollm2-b5"
+DEFAULT_WORKLOAD = "qwen3-30b-b8"
+BATCH1_WORKLOAD = "qwen3-8b-b1"
+PROFILE_TICKS = 3
 # .spm operator workloads: rows, cols, group size, lanes (positions)
 TERNARY = {"ternary-4096-b8": (4096, 4096, 4096, 8)}
 DENSE = {"dense-f32-4096-b8": (4096, 4096, 4096, 8)}
+# DRAM bytes (read + write) per algorithmic weight byte of gemv_stream launches
+# in ncu captures (gpu__... dram__bytes_read.sum + dram__bytes_write.sum over
+# the launch's quantized weight bytes); the file named beside each holds the
+# capture.  Used to report `roofline.traffic` per launch.
+TRAFFIC_RATIO = {
+    "qwen3-8b-b1": (1.003, "profiles/gemv_stream_qwen3_8b_b1.md"),
+}
+STAGING = "activations staged per 32-value unit as 22-bit block fixed point (three int8 digit planes), " \
+          "integer products, fp32 scales and sums"
 
 
 def _args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=96)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batch1", action="store_true", help="skip the batch-1 sub-record")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--gguf-dir", default="/dev/shm",
                     help="where rank 0 writes the synthetic GGUF that expert-parallel ranks memory-map")
@@ -134,16 +161,29 @@ def _workload(name, layers=0):
     return w, r, configs.workload_prompts(name)
 
 
-def _tick_tokens(prompts, tick, best):
-    """Next tokens under serve-demo's lockstep rule."""
+def _next_tokens(prompts, tick, best):
+    """Tokens fed at tick+1 under serve-demo's lockstep rule."""
     return [p[tick + 1] if tick + 1 < len(p) else best[i] for i, p in enumerate(prompts)]
+
+
+def _plan(w, prompts, steps, warmup):
+    """Tick ranges of a run: prompt ticks [0, P), warm-up decode ticks, K timed
+    decode ticks, K e2e ticks, PROFILE_TICKS profiled ticks, clamped so that
+    every one is a decode tick of the workload (at most steps - 1 of them)."""
+    longest = max(len(p) for p in prompts)
+    decode = w["steps"] - 1
+    warm = max(warmup, 3)
+    k = max(1, min(steps, (decode - warm - PROFILE_TICKS) // 2))
+    return {"prompt": longest, "warm": warm, "k": k, "ticks": longest + warm + 2 * k + PROFILE_TICKS,
+            "context": longest + w["steps"] + 1}
 
 
 def cpu_baseline(recipe, img, prompts, steps, seconds: float, threads: int = 0):
     """The oracle (this repo's C restatement of the reference CPU loop) on all
-    host cores (threads=0) or `threads` of them: lockstep ticks until `seconds`
-    of work; tokens/s.  One thread matches the reference's single-threaded
-    engine; more spread the output rows, leaving every result bit-identical."""
+    host cores (threads=0) or `threads` of them: lockstep ticks from the first
+    until `seconds` of work (at least one tick); tokens/s.  One thread matches
+    the reference's single-threaded engine; more spread the output rows and the
+    active experts, leaving every result bit-identical."""
     from oracle import oracle as O
 
     n = len(prompts)
@@ -156,24 +196,30 @@ def cpu_baseline(recipe, img, prompts, steps, seconds: float, threads: int = 0):
     while ticks < longest + steps - 1:
         logits = sess.step(tokens, threads=threads)
         best = [O.argmax_last(logits[i]) for i in range(n)]
-        tokens = _tick_tokens(prompts, ticks, best)
+        tokens = _next_tokens(prompts, ticks, best)
         ticks += 1
         if time.perf_counter() - t0 > seconds:
             break
     dt = time.perf_counter() - t0
     cores = threads or os.cpu_count()
-    how = "one thread" if cores == 1 else "OpenMP over rows"
+    how = "one thread" if cores == 1 else "OpenMP over rows and active experts"
     return {"value": n * ticks / dt, "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"first {ticks} lockstep ticks x {n} clients of the workload (oracle, {how})"}
+            "sample": f"first {ticks} lockstep ticks x {n} clients of the workload, contexts 1-{ticks} "
+                      f"(oracle, {how})"}
 
 
 def run_reference(a, rank, world):
+    """The reference arm: the CPU oracle on all host threads, in a process
+    that loads liboracle.so and the synthetic-model writer libspmsynth.so only
+    (no GPU code).  It times lockstep ticks W..W+K of the run (the first
+    ticks: a full run takes the oracle minutes to hours), each tick bounded so
+    the whole arm ends within a few minutes."""
     if rank != 0:
         return 0
     w, recipe, prompts = _workload(a.workload)
-    import emufpga_b200 as eb
+    from emufpga_b200 import synth
 
-    img = eb.synth_gguf(recipe)
+    img = synth.synth_gguf(recipe)
     n = len(prompts)
     from oracle import oracle as O
 
@@ -184,27 +230,214 @@ def run_reference(a, rank, world):
     total = longest + w["steps"] - 1
     steps = min(a.steps, max(1, total - a.warmup))
     times = []
+    t_start = time.perf_counter()
+    first = None
     for tick in range(min(total, a.warmup + steps)):
         t0 = time.perf_counter()
         logits = sess.step(tokens)
         best = [O.argmax_last(logits[i]) for i in range(n)]
         dt = time.perf_counter() - t0
-        tokens = _tick_tokens(prompts, tick, best)
+        tokens = _next_tokens(prompts, tick, best)
         if tick >= a.warmup:
+            first = tick if first is None else first
             times.append(dt)
-        if tick >= a.warmup and sum(times) > 150.0:
+        if time.perf_counter() - t_start > 150.0 and times:
             break
     value = n * len(times) / sum(times)
+    sample = (f"lockstep ticks {first}-{first + len(times) - 1} (contexts {first + 1}-{first + len(times)}) x {n} "
+              f"clients after {first} warm-up ticks; oracle on {os.cpu_count()} host threads")
     line = {"metric": "decode tokens/s", "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": world,
-            "steps": len(times), "warmup": a.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
+            "steps": len(times), "warmup": first, "ms_per_step": 1e3 * sum(times) / len(times),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded N(0,0.02) weights, uniform prompt ids)",
-            "config": {"workload": a.workload, "clients": n},
+            "data": "synthetic (seeded N(0,0.02) weights quantized by this repo's encoder, uniform prompt ids)",
+            "config": {"workload": a.workload, "model": w["recipe"], "clients": n, "prompts": w["prompts"],
+                       "timed_ticks": [first, first + len(times) - 1]},
             "cpu_baseline": {"value": value, "unit": "tokens/s", "kind": "port", "cores": os.cpu_count(),
-                             "sample": f"{len(times)} lockstep ticks after {a.warmup} warm-up ticks"},
+                             "sample": sample},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
+
+
+def _profile_summary(prof: dict, peak: float, how: str, workload: str) -> dict:
+    """Roofline of gemv_stream from the profiled launches, and every kernel
+    kind's share of the profiled ticks."""
+    import numpy as np
+
+    from emufpga_b200.engine import Session
+
+    ms = prof["ms"].astype(np.float64)
+    nbytes = prof["bytes"].astype(np.float64)
+    gemv = prof["kind"] < len(Session.GEMV_KINDS)
+    seconds = ms[gemv].sum() / 1e3
+    ach = nbytes[gemv].sum() / seconds / 1e9
+    launches = int(gemv.sum())
+    kinds = {}
+    for k, name in enumerate(Session.KERNEL_KINDS):
+        sel = prof["kind"] == k
+        if sel.any():
+            kinds[name] = {"launches_per_tick": int(sel.sum()) // PROFILE_TICKS,
+                           "ms_per_tick": float(ms[sel].sum()) / PROFILE_TICKS,
+                           "share": float(ms[sel].sum() / ms.sum())}
+            if k < len(Session.GEMV_KINDS):
+                kinds[name]["gbs"] = float(nbytes[sel].sum() / (ms[sel].sum() / 1e3) / 1e9)
+    traffic = None
+    if workload in TRAFFIC_RATIO:
+        ratio, src = TRAFFIC_RATIO[workload]
+        traffic = {"bytes_per_launch": ratio * nbytes[gemv].sum() / launches, "source": src,
+                   "how": "ncu dram__bytes_read.sum + dram__bytes_write.sum per algorithmic byte, times the "
+                          "average launch's algorithmic bytes"}
+    return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak, "peak_source": how,
+            "traffic": traffic, "kernel": "gemv_stream",
+            "how": f"CUDA events around each of the {launches} GEMV launches of {PROFILE_TICKS} eager decode ticks "
+                   f"(after the timed ticks); achieved = quantized weight bytes streamed / summed launch time",
+            "bytes_per_launch_avg": nbytes[gemv].sum() / launches, "launch_us_avg": 1e3 * ms[gemv].sum() / launches,
+            "gemv_share_of_eager_tick": float(ms[gemv].sum() / ms.sum()), "by_kind": kinds}
+
+
+def run_decode(a, name, rank, world, local, pg, dev, ep_ok=True):
+    """One decode workload; returns its JSON dict on rank 0 (None elsewhere)."""
+    import torch
+
+    import emufpga_b200 as eb
+
+    w, recipe, prompts = _workload(name, a.layers)
+    # Routed models over several GPUs run expert parallel: every rank serves
+    # all clients, and the experts are dealt round robin over the ranks (one
+    # job; tokens/s is not multiplied by the ranks).  Dense models run one
+    # replica per GPU.  Rank 0 writes the synthetic GGUF once; every rank
+    # memory-maps it.
+    ep_mode = ep_ok and world > 1 and recipe.shape.moe
+    img = None
+    if ep_mode:
+        path = f"{a.gguf_dir}/emufpga_{name}_{recipe.shape.layers}l.gguf"
+        if rank == 0:
+            img = eb.synth_gguf(recipe)
+            if not os.path.exists(path) or os.path.getsize(path) != len(img):
+                img.tofile(path + ".part")
+                os.replace(path + ".part", path)
+        pg.barrier()
+        model = eb.Model.from_file(path, recipe.shape, device=local, ep=(world, rank))
+    else:
+        img = eb.synth_gguf(recipe)
+        model = eb.Model(img, recipe.shape, device=local)
+    n = len(prompts)
+    plan = _plan(w, prompts, a.steps, a.warmup)
+    P, warm, K = plan["prompt"], plan["warm"], plan["k"]
+    sess = eb.Session(model, n, plan["context"])
+    if ep_mode:
+        from emufpga_b200 import ep as eplib
+
+        eplib.connect(sess)
+        pg.barrier()
+    stream = torch.cuda.ExternalStream(sess.cuda_stream, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    argmax = torch.zeros(n, dtype=torch.int32, device=dev)
+    total_ticks = P + warm + K
+    feed = torch.tensor([[p[min(t + 1, len(p) - 1)] for p in prompts] for t in range(total_ticks)],
+                        dtype=torch.int32, device=dev)
+    in_prompt = torch.tensor([[t + 1 < len(p) for p in prompts] for t in range(total_ticks)], device=dev)
+    tokens = torch.tensor([p[0] for p in prompts], dtype=torch.int32, device=dev)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
+
+    with torch.cuda.stream(stream):
+        # untimed: the prompt ticks and the warm-up decode ticks
+        for t in range(P + warm):
+            sess.decode_step_device(tokens, n, argmax)
+            tokens = torch.where(in_prompt[t], feed[t], argmax)
+        torch.cuda.synchronize(dev)
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize(dev)
+        with Clocks(local) as clocks:
+            # ---- device-resident timing (value) ----
+            for i in range(K):
+                flush.zero_()
+                starts[i].record(stream)
+                sess.decode_step_device(tokens, n, argmax)
+                ends[i].record(stream)
+                tokens = argmax.clone()
+            torch.cuda.synchronize(dev)
+            step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+            # ---- end to end through the C ABI with host buffers (e2e) ----
+            toks = tokens.cpu().tolist()
+            if pg:
+                pg.barrier()
+            e2e_s = 0.0
+            touched = []  # MoE: experts the step streamed, summed over layers
+            for i in range(K):
+                t0 = time.perf_counter()
+                best, _ = sess.decode_step(toks)
+                e2e_s += time.perf_counter() - t0
+                toks = best
+                if recipe.shape.moe:
+                    r = sess.routes(n)
+                    touched.append(sum(len(set(r[l].ravel().tolist())) for l in range(r.shape[0])))
+    # ---- the GEMV launches of a few eager ticks, each between CUDA events ----
+    sess.set_profile(True)
+    for i in range(PROFILE_TICKS):
+        best, _ = sess.decode_step(toks)
+        toks = best
+    prof = sess.profile()
+    sess.set_profile(False)
+    local_ms = sum(step_ms)
+    job_ms, job_e2e = local_ms, e2e_s
+    if pg:
+        tt = torch.tensor([local_ms, e2e_s], device=dev, dtype=torch.float64)
+        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
+        job_ms, job_e2e = float(tt[0].item()), float(tt[1].item())
+    launches = sess.launches_per_step(n)
+    ranks_agree = None
+    if ep_mode:
+        # every rank serves the same clients: their greedy tokens must agree
+        got = [None] * world
+        pg.all_gather_object(got, list(toks))
+        ranks_agree = all(g == got[0] for g in got)
+    sess.close()
+    tokens_total = n * K * (1 if ep_mode else world)
+    step_bytes = model.weight_bytes
+    if recipe.shape.moe:
+        step_bytes += statistics.mean(touched) * expert_bytes(model)
+    line = None
+    if rank == 0:
+        peak, how = _peaks()
+        line = {
+            "metric": "decode tokens/s", "value": tokens_total / (job_ms / 1e3), "unit": "tokens/s",
+            "n_gpus": world, "steps": K, "warmup": warm, "ms_per_step": job_ms / K,
+            "higher_is_better": True, "scaling": "strong" if ep_mode else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,0.02) weights quantized by this repo's encoder, uniform prompt ids)",
+            "config": {"workload": name, "model": w["recipe"], "clients": n, "prompts": w["prompts"],
+                       "parallelism": (f"expert parallel x{world}" if ep_mode else f"replicas x{world}")
+                       if world > 1 else "single GPU",
+                       "prompt_ticks_untimed": P,
+                       "timed_ticks": [P + warm, P + warm + K - 1],
+                       "timed_context": [P + warm + 1, P + warm + K],
+                       "e2e_ticks": [P + warm + K, P + warm + 2 * K - 1],
+                       "weight_bytes_per_step": round(step_bytes),
+                       "activation_staging": STAGING,
+                       "l2": "flushed before every timed tick (256 MiB write)"},
+            "weight_stream_gbs": step_bytes * K / (job_ms / 1e3) / 1e9,
+            "e2e": {"value": tokens_total / job_e2e, "unit": "tokens/s", "h2d_bytes_per_step": 4 * n,
+                    "d2h_bytes_per_step": 4 * n},
+            "gpu_launches": launches * K,
+            "roofline": _profile_summary(prof, peak, how, name),
+        }
+        line["weight_stream_frac"] = line["weight_stream_gbs"] / peak
+        if recipe.shape.moe:
+            line["config"]["experts_touched_per_step"] = statistics.mean(touched)
+        if ep_mode:
+            line["config"]["ranks_tokens_agree"] = ranks_agree
+        if a.layers:
+            line["config"]["layers_kept"] = recipe.shape.layers
+            line["invalid"] = "model truncated with --layers (profiling case, not a bench number)"
+        line["_clocks"] = clocks
+        line["_img"] = img
+        line["_recipe"] = recipe
+        line["_prompts"] = prompts
+        line["_steps"] = w["steps"]
+    model.close()
+    return line
 
 
 def main():
@@ -220,163 +453,32 @@ def main():
     dev = torch.device("cuda", local)
     pg = None
     if world > 1:
-        import torch.distributed as dist
         import datetime
+
+        import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
         pg = dist
-    import emufpga_b200 as eb
-
-    w, recipe, prompts = _workload(a.workload, a.layers)
-    # Routed models over several GPUs run expert parallel: every rank serves
-    # all clients, and the experts are dealt round robin over the ranks (one
-    # job; tokens/s is not multiplied by the ranks).  Dense models run one
-    # replica per GPU.  Rank 0 writes the synthetic GGUF once; every rank
-    # memory-maps it.
-    ep_mode = world > 1 and recipe.shape.moe
-    img = None
-    if ep_mode:
-        from emufpga_b200 import ep as eplib
-
-        path = f"{a.gguf_dir}/emufpga_{a.workload}_{recipe.shape.layers}l.gguf"
-        if rank == 0:
-            img = eb.synth_gguf(recipe)
-            if not os.path.exists(path) or os.path.getsize(path) != len(img):
-                img.tofile(path + ".part")
-                os.replace(path + ".part", path)
-        pg.barrier()
-        model = eb.Model.from_file(path, recipe.shape, device=local, ep=(world, rank))
-    else:
-        img = eb.synth_gguf(recipe)
-        model = eb.Model(img, recipe.shape, device=local)
-    n = len(prompts)
-    longest = max(len(p) for p in prompts)
-    total_ticks = longest + w["steps"] - 1
-    warm, steps = max(a.warmup, 3), a.steps  # at least three untimed warm-up steps
-    if warm + steps > total_ticks:
-        steps = max(1, total_ticks - warm)
-    context = longest + w["steps"] + 1
-    sess = eb.Session(model, n, context)
-    if ep_mode:
-        eplib.connect(sess)
-        pg.barrier()
-    stream = torch.cuda.ExternalStream(sess.cuda_stream, device=dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    argmax = torch.zeros(n, dtype=torch.int32, device=dev)
-    prompt_dev = torch.tensor([[p[min(t + 1, len(p) - 1)] for p in prompts] for t in range(total_ticks)],
-                              dtype=torch.int32, device=dev)
-    in_prompt = torch.tensor([[t + 1 < len(p) for p in prompts] for t in range(total_ticks)], device=dev)
-    tokens = torch.tensor([p[0] for p in prompts], dtype=torch.int32, device=dev)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-
-    # ---- device-resident timing (value) ----
-    with torch.cuda.stream(stream):
-        for t in range(warm):
-            sess.decode_step_device(tokens, n, argmax)
-            tokens = torch.where(in_prompt[t], prompt_dev[t], argmax)
-        torch.cuda.synchronize(dev)
-        if pg:
-            pg.barrier()
-        torch.cuda.synchronize(dev)
-        with Clocks(local) as clocks:
-            for i in range(steps):
-                t = warm + i
-                flush.zero_()
-                starts[i].record(stream)
-                sess.decode_step_device(tokens, n, argmax)
-                ends[i].record(stream)
-                tokens = torch.where(in_prompt[t], prompt_dev[t], argmax)
-            torch.cuda.synchronize(dev)
-    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    local_ms = sum(step_ms)
-    job_ms = local_ms
-    if pg:
-        tt = torch.tensor([local_ms], device=dev)
-        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
-        job_ms = float(tt.item())
-    launches = sess.launches_per_step(n)
-    sess.close()
-
-    # ---- end to end through the C ABI with host buffers (e2e) ----
-    sess = eb.Session(model, n, context)
-    if ep_mode:
-        eplib.connect(sess)
-        pg.barrier()
-    toks = [p[0] for p in prompts]
-    for t in range(warm):
-        best, _ = sess.decode_step(toks)
-        toks = _tick_tokens(prompts, t, best)
-    if pg:
-        pg.barrier()
-    e2e_s = 0.0
-    touched = []  # MoE: experts the step streamed, summed over layers
-    for i in range(steps):
-        t0 = time.perf_counter()
-        best, _ = sess.decode_step(toks)
-        e2e_s += time.perf_counter() - t0
-        toks = _tick_tokens(prompts, warm + i, best)
-        if recipe.shape.moe:
-            r = sess.routes(n)
-            touched.append(sum(len(set(r[l].ravel().tolist())) for l in range(r.shape[0])))
-    if pg:
-        tt = torch.tensor([e2e_s], device=dev)
-        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
-        e2e_s = float(tt.item())
-    sess.close()
-
-    # ---- roofline of the GEMV: one sweep of every weight stream, graph-captured ----
-    roof = None
+    line = run_decode(a, a.workload, rank, world, local, pg, dev)
     if rank == 0:
-        roof = gemv_roofline(eb, model, n, dev)
-    tokens_total = n * steps * (1 if ep_mode else world)
-    ranks_agree = None
-    if ep_mode:
-        # every rank serves the same clients: their greedy tokens must agree
-        got = [None] * world
-        pg.all_gather_object(got, list(toks))
-        ranks_agree = all(g == got[0] for g in got)
-    step_bytes = model.weight_bytes
-    if recipe.shape.moe:
-        step_bytes += statistics.mean(touched) * expert_bytes(model)
-    line = None
-    if rank == 0:
-        peak, how = _peaks()
-        clk = clocks.summary()
-        line = {
-            "metric": "decode tokens/s", "value": tokens_total / (job_ms / 1e3), "unit": "tokens/s",
-            "n_gpus": world, "steps": steps, "warmup": warm, "ms_per_step": job_ms / steps,
-            "higher_is_better": True, "scaling": "strong" if ep_mode else "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded N(0,0.02) weights quantized by this repo's encoder, uniform prompt ids)",
-            "config": {"workload": a.workload, "model": w["recipe"], "clients": n, "prompts": w["prompts"],
-                       "parallelism": (f"expert parallel x{world}" if ep_mode else f"replicas x{world}")
-                       if world > 1 else "single GPU",
-                       "weight_bytes_per_step": round(step_bytes),
-                       "l2": "flushed between timed steps (256 MiB write)"},
-            "weight_stream_gbs": step_bytes * steps / (job_ms / 1e3) / 1e9,
-            "e2e": {"value": tokens_total / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 4 * n,
-                    "d2h_bytes_per_step": 4 * n},
-            "gpu_launches": launches * steps,
-            "roofline": None, "clocks": clk,
-        }
-        if roof:
-            ach = roof["bytes"] / roof["seconds"] / 1e9
-            line["roofline"] = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
-                                "peak_source": how, "traffic": None,
-                                "kernel": "gemv_stream (one sweep of every dense stream and the LM head)",
-                                "bytes_per_launch_avg": roof["bytes"] / roof["launches"],
-                                "launches_per_sweep": roof["launches"]}
-        if recipe.shape.moe:
-            line["config"]["experts_touched_per_step"] = statistics.mean(touched)
-        if ep_mode:
-            line["config"]["ranks_tokens_agree"] = ranks_agree
-        if a.layers:
-            line["config"]["layers_kept"] = recipe.shape.layers
-            line["invalid"] = "model truncated with --layers (profiling case, not a bench number)"
+        clocks = line.pop("_clocks")
+        img, recipe, prompts, wsteps = line.pop("_img"), line.pop("_recipe"), line.pop("_prompts"), line.pop("_steps")
+        line["clocks"] = clocks.summary()
         if not a.no_cpu_baseline and img is not None and world == 1:  # rank 0 at N=1 only
-            line["cpu_baseline"] = cpu_baseline(recipe, img, prompts, w["steps"], a.cpu_seconds)
-            line["cpu_baseline_1thread"] = cpu_baseline(recipe, img, prompts, w["steps"], a.cpu_seconds / 2,
+            line["cpu_baseline"] = cpu_baseline(recipe, img, prompts, wsteps, a.cpu_seconds)
+            line["cpu_baseline_1thread"] = cpu_baseline(recipe, img, prompts, wsteps, a.cpu_seconds / 2,
                                                         threads=1)
+        del img
+    if world == 1 and not a.no_batch1 and a.workload != BATCH1_WORKLOAD and not a.layers:
+        sub = run_decode(a, BATCH1_WORKLOAD, rank, world, local, pg, dev, ep_ok=False)
+        clk = sub.pop("_clocks").summary()
+        for k in ("_img", "_recipe", "_prompts", "_steps"):
+            sub.pop(k)
+        line["batch1"] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "steps", "warmup", "weight_stream_gbs",
+                                              "weight_stream_frac", "e2e", "roofline", "config", "gpu_launches")}
+        line["batch1"]["workload"] = BATCH1_WORKLOAD
+        line["batch1"]["clocks"] = clk
+    if rank == 0:
         print(json.dumps(line), flush=True)
     if pg:
         pg.barrier()
@@ -397,54 +499,6 @@ def expert_bytes(model):
     sh = model.shape
     return sum(model.stream_info(model.stream_index(f"blk.0.ffn_{k}_exps.weight"))["bytes"]
                for k in ("gate", "up", "down")) / sh.experts
-
-
-def gemv_roofline(eb, model, n, dev):
-    """Graph-capture one sweep of spm_streamed over every rotating stream plus
-    the LM head (the decode step's GEMV launches, same shapes and client
-    count), replay it with L2 flushed between sweeps, and time each replay
-    with CUDA events: achieved = quantized bytes per sweep / sweep time."""
-    import torch
-
-    idx = list(range(model.stream_count))
-    infos = [model.stream_info(i) for i in idx]
-    embd = model.stream_index("token_embd.weight")
-    # every matrix a step sweeps: all streams but the embedding, which is the
-    # LM head itself when tied
-    experts = set(expert_streams(model))
-    keep = [i for i in idx if (i != embd or model.shape.tied) and i not in experts]
-    maxc = max(infos[i]["cols"] for i in keep)
-    maxr = max(infos[i]["rows"] for i in keep)
-    x = torch.randn(n * maxc, device=dev)
-    y = torch.empty(n * maxr, device=dev)
-    s = torch.cuda.Stream(device=dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
-    with torch.cuda.stream(s):
-        for i in keep:
-            eb.streamed(model, i, x, n, y, stream=s.cuda_stream)
-    torch.cuda.synchronize(dev)
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=s):
-        for i in keep:
-            eb.streamed(model, i, x, n, y, stream=s.cuda_stream)
-    total = 0.0
-    reps = 10
-    with torch.cuda.stream(s):
-        for _ in range(3):
-            g.replay()
-        for _ in range(reps):
-            flush.zero_()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(s)
-            g.replay()
-            b.record(s)
-            b.synchronize()
-            total += a.elapsed_time(b) / 1e3
-    nbytes = sum(infos[i]["bytes"] for i in keep)
-    del g
-    return {"bytes": nbytes, "seconds": total / reps, "launches": len(keep)}
-
-
 
 
 # ---------------------------------------------------------------------------

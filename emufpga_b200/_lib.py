@@ -132,6 +132,8 @@ PROTOTYPES = {
     "spm_session_set_graphs": (C.c_int32, [_P, C.c_int32]),
     "spm_session_routes": (C.c_int32, [_P, C.c_int32, _I32P]),
     "spm_session_launches_per_step": (C.c_int32, [_P, C.c_int32, _I32P]),
+    "spm_session_set_profile": (C.c_int32, [_P, C.c_int32]),
+    "spm_session_profile": (C.c_int32, [_P, C.c_int32, _FP, _U64P, _I32P, _I32P]),
     "spm_file_probe": (C.c_int32, [_P, C.c_uint64, _U32P, _U32P, _I32P]),
     "spm_file_stream": (C.c_int32, [_P, C.c_uint64, C.c_int32, C.POINTER(FileStreamInfo)]),
     "spm_ternary_upload": (C.c_int32, [_P, C.c_uint64, C.c_int32, C.c_int, C.POINTER(_P)]),

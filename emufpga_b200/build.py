@@ -1,10 +1,14 @@
-"""Build libspmgpu.so in-tree for sm_100a (and nothing else).
+"""Build libspmgpu.so in-tree for sm_100a (and nothing else), and libspmsynth.so.
 
     python -m emufpga_b200.build          # incremental
     python -m emufpga_b200.build --clean  # from scratch
 
-Objects go to emufpga_b200/_build/ (git-ignored); the shared library lands
-beside this file so that it travels with the source tree.
+Objects go to emufpga_b200/_build/ (git-ignored); the shared libraries land
+beside this file so that they travel with the source tree:
+
+  libspmgpu.so    the engine: kernels, host orchestration, the C ABI
+  libspmsynth.so  the synthetic-model writer alone (host code, no CUDA), for
+                  processes that must not load the engine
 """
 from __future__ import annotations
 
@@ -20,6 +24,8 @@ HERE = Path(__file__).resolve().parent
 SRC = HERE / "csrc"
 OUT = HERE / "_build"
 LIB = HERE / "libspmgpu.so"
+SYNTH_LIB = HERE / "libspmsynth.so"
+SYNTH_SOURCES = ("host_synth.cpp", "host_format.cpp", "synth_only.cpp")
 INCLUDE = HERE.parent / "include"
 
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
@@ -56,13 +62,16 @@ def build(clean: bool = False, verbose: bool = False) -> Path:
     OUT.mkdir(exist_ok=True)
     sources = sorted(SRC.glob("*.cu")) + sorted(SRC.glob("*.cpp"))
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as pool:
-        objs = list(pool.map(lambda s: _compile(s, verbose), sources))
-    newest = max(o.stat().st_mtime for o in objs)
-    if not LIB.exists() or LIB.stat().st_mtime < newest:
-        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lpthread"]
-        if verbose:
-            print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        objs = dict(zip((s.name for s in sources), pool.map(lambda s: _compile(s, verbose), sources)))
+    engine = [o for n, o in objs.items() if n != "synth_only.cpp"]
+    synth = [objs[n] for n in SYNTH_SOURCES]
+    for lib, parts, link in ((LIB, engine, [NVCC, *ARCH, "-shared"]), (SYNTH_LIB, synth, [CXX, "-shared"])):
+        newest = max(o.stat().st_mtime for o in parts)
+        if not lib.exists() or lib.stat().st_mtime < newest:
+            cmd = [*link, "-o", str(lib), *map(str, parts), "-lpthread"]
+            if verbose:
+                print(" ".join(cmd), flush=True)
+            subprocess.run(cmd, check=True)
     return LIB
 
 

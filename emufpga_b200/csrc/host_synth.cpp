@@ -157,15 +157,21 @@ static uint64_t mix64(uint64_t z) {
 }
 // Normal value `i` of stream `key`: pair i/2 of a Box-Muller transform whose
 // uniforms come from mix64(key ^ pair).  Independent of thread layout.
+// Each pair is transformed once and gives both of its values.
 static void normals(uint64_t key, uint64_t first, uint64_t count, float sigma, float* out) {
-    for (uint64_t k = 0; k < count; k++) {
-        uint64_t i = first + k;
-        uint64_t h = mix64(key ^ mix64(i >> 1));
-        float u1 = (float(uint32_t(h >> 40)) + 0.5f) * (1.0f / 16777216.0f);
-        float u2 = float(uint32_t(h & 0xffffffu)) * (1.0f / 16777216.0f);
-        float r = std::sqrt(-2.0f * std::log(u1));
-        float a = 6.28318530718f * u2;
-        out[k] = sigma * r * ((i & 1) ? std::sin(a) : std::cos(a));
+    uint64_t k = 0;
+    while (k < count) {
+        const uint64_t i = first + k, pair = i >> 1;
+        const uint64_t h = mix64(key ^ mix64(pair));
+        const float u1 = (float(uint32_t(h >> 40)) + 0.5f) * (1.0f / 16777216.0f);
+        const float u2 = float(uint32_t(h & 0xffffffu)) * (1.0f / 16777216.0f);
+        const float r = std::sqrt(-2.0f * std::log(u1));
+        const float a = 6.28318530718f * u2;
+        if ((i & 1) == 0) {
+            out[k++] = sigma * r * std::cos(a);
+            if (k == count) break;
+        }
+        out[k++] = sigma * r * std::sin(a);
     }
 }
 

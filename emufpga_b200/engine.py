@@ -38,16 +38,10 @@ def _ptr(buf) -> C.c_void_p:
 
 # ---------------------------------------------------------------- host ----
 def synth_gguf(recipe: Recipe, threads: int = 0) -> np.ndarray:
-    """A synthetic GGUF v3 image (numpy uint8 view of library-owned memory copied out)."""
-    spec = recipe.spec(threads)
-    out = C.POINTER(C.c_uint8)()
-    n = C.c_uint64()
-    call("spm_synth_gguf", C.byref(spec), C.byref(out), C.byref(n))
-    try:
-        arr = np.ctypeslib.as_array(out, shape=(n.value,)).copy()
-    finally:
-        lib().spm_free(C.cast(out, C.c_void_p))
-    return arr
+    """A synthetic GGUF v3 image (numpy uint8 array), written by libspmsynth.so."""
+    from . import synth
+
+    return synth.synth_gguf(recipe, threads)
 
 
 def decode_blocks(dtype: int, data: bytes | np.ndarray) -> np.ndarray:
@@ -345,6 +339,27 @@ class Session:
         v = C.c_int32()
         call("spm_session_launches_per_step", self._h, n, C.byref(v))
         return v.value
+
+    KERNEL_KINDS = ("gemv_dense", "gemv_router", "gemv_expert_gate_up", "gemv_expert_down", "gemv_head",
+                    "attention", "route", "combine", "other")
+    GEMV_KINDS = KERNEL_KINDS[:5]
+
+    def set_profile(self, enable: bool) -> None:
+        """Eager steps with a CUDA event pair around every kernel launch (clears the record)."""
+        call("spm_session_set_profile", self._h, int(enable))
+
+    def profile(self) -> dict:
+        """The recorded launches: {'ms', 'bytes', 'kind'} arrays (kind names in KERNEL_KINDS)."""
+        count = C.c_int32()
+        call("spm_session_profile", self._h, 0, None, None, None, C.byref(count))
+        n = count.value
+        ms = np.zeros(n, np.float32)
+        nbytes = np.zeros(n, np.uint64)
+        kind = np.zeros(n, np.int32)
+        call("spm_session_profile", self._h, n, ms.ctypes.data_as(C.POINTER(C.c_float)),
+             nbytes.ctypes.data_as(C.POINTER(C.c_uint64)), kind.ctypes.data_as(C.POINTER(C.c_int32)),
+             C.byref(count))
+        return {"ms": ms, "bytes": nbytes, "kind": kind}
 
 
 def serve(model: Model, prompts: Sequence[Sequence[int]], steps: int, max_ticks: int | None = None,

@@ -48,3 +48,14 @@ def test_cpu_baseline_reports_one_thread_and_all_cores():
     every = bench.cpu_baseline(recipe, img, prompts, w["steps"], 0.3)
     assert one["cores"] == 1 and "one thread" in one["sample"] and one["value"] > 0
     assert every["cores"] >= 1 and every["value"] > 0 and every["kind"] == one["kind"] == "port"
+
+
+def test_reference_arm_loads_no_gpu_engine():
+    # the reference arm makes its model with libspmsynth.so and runs the
+    # oracle; the GPU engine library must never be mapped into that process
+    code = ("import sys; sys.argv = ['bench.py', '--impl', 'reference', '--workload', 'smollm2-b1', '--steps', '1', "
+            "'--warmup', '0']; import bench; bench.main(); maps = open('/proc/self/maps').read(); "
+            "print('ENGINE' if 'libspmgpu.so' in maps else 'NO-ENGINE', 'ORACLE' if 'liboracle.so' in maps else '')")
+    out = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert out.stdout.strip().splitlines()[-1] == "NO-ENGINE ORACLE"

@@ -115,6 +115,37 @@ def test_graph_and_eager_steps_agree_bit_for_bit(cuda, models):
     assert a.launches_per_step(2) > 0
 
 
+def test_launch_profile_times_every_kernel_and_changes_no_result(cuda, models):
+    # the profiled (eager, event-bracketed) step computes what the graph step does
+    r, img, m, om = models("qwen3moe-q5_k")
+    sh = r.shape
+    a = eb.Session(m, 3, 8, graphs=True)
+    b = eb.Session(m, 3, 8)
+    b.set_profile(True)
+    for t in range(2):
+        _, la = a.decode_step([t, t + 1, t + 2], want_logits=True)
+        _, lb = b.decode_step([t, t + 1, t + 2], want_logits=True)
+        assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
+    prof = b.profile()
+    kinds = [eb.Session.KERNEL_KINDS[k] for k in prof["kind"]]
+    per_step = 1 + sh.layers * 8 + 1 + 2  # embed, 8 per routed layer, head, argmax, advance
+    assert len(kinds) == 2 * per_step
+    assert kinds.count("attention") == 2 * sh.layers and kinds.count("gemv_head") == 2
+    assert (prof["ms"] > 0).all()
+    gemv = prof["kind"] < len(eb.Session.GEMV_KINDS)
+    assert (prof["bytes"][gemv] > 0).all() and (prof["bytes"][~gemv] == 0).all()
+    # expert launches count the plan's active experts: gate+up stream twice the down bytes per expert
+    routes = b.routes(3)
+    active = [len(set(routes[l].ravel().tolist())) for l in range(sh.layers)]
+    one = m.stream_info(m.stream_index("blk.0.ffn_down_exps.weight"))["bytes"] // sh.experts
+    down = [int(x) for x, k in zip(prof["bytes"], kinds) if k == "gemv_expert_down"][-sh.layers:]
+    assert down == [u * one for u in active]
+    b.set_profile(False)
+    assert b.profile()["ms"].size == 0
+    a.close()
+    b.close()
+
+
 def test_bad_token_is_refused(cuda, models):
     r, img, m, om = models("llama-q8_0")
     sess = eb.Session(m, 1, 4)
