@@ -133,6 +133,8 @@ PROTOTYPES = {
     "spm_session_routes": (C.c_int32, [_P, C.c_int32, _I32P]),
     "spm_session_launches_per_step": (C.c_int32, [_P, C.c_int32, _I32P]),
     "spm_session_set_profile": (C.c_int32, [_P, C.c_int32]),
+    "spm_prefill": (C.c_int32, [_P, C.c_int32, _U32P, C.c_int32]),
+    "spm_session_set_wait_limit": (C.c_int32, [_P, C.c_uint64]),
     "spm_session_profile": (C.c_int32, [_P, C.c_int32, _FP, _U64P, _I32P, _I32P]),
     "spm_file_probe": (C.c_int32, [_P, C.c_uint64, _U32P, _U32P, _I32P]),
     "spm_file_stream": (C.c_int32, [_P, C.c_uint64, C.c_int32, C.POINTER(FileStreamInfo)]),

@@ -26,6 +26,7 @@
 #include "abi.h"
 #include "kernels.h"
 #include "moe.h"
+#include "prefill.h"
 
 namespace spm {
 const std::string& last_error();
@@ -108,6 +109,7 @@ struct spm_session {
     uint32_t** ep_peer_flag = nullptr; // device [2][world]
     std::vector<void*> ep_mapped;      // peers' regions opened by IPC
     bool ep_ready = false;
+    uint64_t wait_ns = 1000000000ull;  // limit of the device waits on other ranks (spm_session_set_wait_limit)
     std::vector<int> lens;
     bool graphs = true, pdl = true;
     // GEMV launch profile (spm_session_set_profile): steps run eagerly and
@@ -121,6 +123,18 @@ struct spm_session {
     };
     bool prof = false;
     std::vector<ProfLaunch> prof_pending;
+    // Prompt buffers (spm_prefill), allocated on first use for kPrefillRows rows.
+    struct Prefill {
+        int rows = 0;
+        uint32_t* tokens = nullptr;
+        int32_t* qpos = nullptr;
+        float *x = nullptr, *xn = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
+        float *g = nullptr, *u = nullptr;                          // dense feed-forward
+        float *logits = nullptr, *prob = nullptr, *norm = nullptr, *ge = nullptr, *ue = nullptr, *ye = nullptr;
+        int32_t *sel = nullptr, *counts = nullptr, *offsets = nullptr, *cursor = nullptr, *list = nullptr,
+                *slot = nullptr;
+        int4* groups = nullptr;                                    // routed: expert groups of <= 128 places
+    } pf;
     std::vector<float> prof_ms;
     std::vector<uint64_t> prof_bytes;
     std::vector<int32_t> prof_kind;
@@ -782,7 +796,7 @@ void enqueue_step(spm_session* s, int n) {
         P.k_norm = L.k_norm >= 0 ? m->gains + L.k_norm : nullptr;
         P.layer = int(l); P.layers = int(c.layers); P.context = s->context;
         P.heads = int(c.heads); P.kv_heads = int(c.kv_heads); P.head_dim = int(c.head_dim);
-        P.family = int(c.family); P.eps = c.eps;
+        P.family = int(c.family); P.eps = c.eps; P.status = s->status;
         timed(SPM_KERNEL_ATTENTION, int(l), -1, 0, [&] {
             CUDA_OK(launch_attention(P, n, st, pdl));
             return 0;
@@ -840,7 +854,7 @@ void enqueue_step(spm_session* s, int n) {
                 gx.ep_layers = int32_t(c.layers);
                 gx.ep_layer = int32_t(l);
                 ex = MoeExchange{reinterpret_cast<const uint32_t*>(s->ep_region), s->step, m->world, int32_t(c.layers),
-                                 int32_t(l), s->ep_xbytes / sizeof(float), s->status};
+                                 int32_t(l), s->ep_xbytes / sizeof(float), s->status, s->wait_ns};
                 outs = reinterpret_cast<const float*>(s->ep_region + 512);
             }
             add_job(gx, m, L.down_exps, nullptr, s->moe_out, d, nullptr, 0, EPI_STORE);
@@ -967,6 +981,160 @@ void step(spm_session* s, int n) {
         if (s->prof) collect_profile(s);
     }
     for (int i = 0; i < n; i++) s->lens[i]++;
+}
+
+// ---- prompts on the tensor cores ----
+// Rows per prompt chunk; longer prompts run chunk after chunk (a chunk's
+// attention reads the earlier chunks' keys and values from the cache).
+constexpr int kPrefillRows = 1024;
+
+void prefill_buffers(spm_session* s) {
+    auto& P = s->pf;
+    if (P.rows) return;
+    const spm_model_cfg& c = s->m->cfg;
+    const size_t T = kPrefillRows, d = c.hidden, qw = size_t(c.heads) * c.head_dim, kvw = size_t(c.kv_heads) * c.head_dim;
+    P.tokens = s->alloc<uint32_t>(T);
+    P.qpos = s->alloc<int32_t>(T);
+    P.x = s->alloc<float>(T * d);
+    P.xn = s->alloc<float>(T * d);
+    P.q = s->alloc<float>(T * qw);
+    P.k = s->alloc<float>(T * kvw);
+    P.v = s->alloc<float>(T * kvw);
+    P.attn = s->alloc<float>(T * qw);
+    if (is_moe(c)) {
+        const size_t E = c.experts, K = c.experts_used, R = T * K;
+        P.logits = s->alloc<float>(T * E);
+        P.sel = s->alloc<int32_t>(R);
+        P.prob = s->alloc<float>(R);
+        P.norm = s->alloc<float>(T);
+        P.counts = s->alloc<int32_t>(E);
+        P.offsets = s->alloc<int32_t>(E);
+        P.cursor = s->alloc<int32_t>(E);
+        P.list = s->alloc<int32_t>(R);
+        P.slot = s->alloc<int32_t>(R);
+        P.groups = s->alloc<int4>(R / 128 + E + 1);
+        P.ge = s->alloc<float>(R * c.expert_ff);
+        P.ue = s->alloc<float>(R * c.expert_ff);
+        P.ye = s->alloc<float>(R * d);
+    } else {
+        P.g = s->alloc<float>(T * c.intermediate);
+        P.u = s->alloc<float>(T * c.intermediate);
+    }
+    P.rows = int(T);
+}
+
+// y = x W^T for T rows on the tensor cores (plain or with residual / SwiGLU input).
+void gemm_rows(spm_session* s, int idx, const float* x, const float* x2, int T, float* y, int epi) {
+    spm_model* m = s->m;
+    const Packed& p = m->streams[idx].pk;
+    GemmArgs a{};
+    a.w = m->tiles(idx);
+    a.pk = p;
+    a.x = x;
+    a.x2 = x2;
+    a.x_stride = int32_t(p.cols);
+    a.tokens = T;
+    a.y = y;
+    a.y_stride = int32_t(p.rows);
+    a.aux = y;
+    a.aux_stride = int32_t(p.rows);
+    a.epi = epi;
+    a.status = s->status;
+    CUDA_OK(launch_prefill_gemm(a, s->stream));
+}
+
+// One chunk of a prompt: T tokens of `client` at positions pos0.. (the
+// decode step's layer schedule, every position of the chunk at once).
+void prefill_chunk(spm_session* s, int client, const uint32_t* tokens, int T, int pos0) {
+    spm_model* m = s->m;
+    const spm_model_cfg& c = m->cfg;
+    auto& P = s->pf;
+    cudaStream_t st = s->stream;
+    const int d = int(c.hidden);
+    std::vector<int32_t> qpos(T);
+    for (int t = 0; t < T; t++) qpos[t] = pos0 + t;
+    CUDA_OK(cudaMemcpyAsync(P.tokens, tokens, size_t(T) * sizeof(uint32_t), cudaMemcpyHostToDevice, st));
+    CUDA_OK(cudaMemcpyAsync(P.qpos, qpos.data(), size_t(T) * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    const StreamDesc& E = m->streams[m->embed];
+    CUDA_OK(launch_embed_rows(E.pk.dtype, m->tiles(m->embed), E.pk, P.tokens, T, P.x, st));
+    std::vector<int32_t> counts, offsets;
+    std::vector<int4> groups;
+    for (uint32_t l = 0; l < c.layers; l++) {
+        const LayerIdx& L = m->layers[l];
+        CUDA_OK(launch_norm_rows(P.x, m->gains + L.attn_norm, c.eps, d, T, P.xn, st));
+        gemm_rows(s, L.q, P.xn, nullptr, T, P.q, EPI_STORE);
+        gemm_rows(s, L.k, P.xn, nullptr, T, P.k, EPI_STORE);
+        gemm_rows(s, L.v, P.xn, nullptr, T, P.v, EPI_STORE);
+        QkArgs q{};
+        q.q = P.q; q.k = P.k; q.v = P.v; q.kcache = s->kc; q.vcache = s->vc; q.rope = s->rope;
+        q.q_norm = L.q_norm >= 0 ? m->gains + L.q_norm : nullptr;
+        q.k_norm = L.k_norm >= 0 ? m->gains + L.k_norm : nullptr;
+        q.client = client; q.layer = int(l); q.layers = int(c.layers); q.context = s->context; q.pos0 = pos0;
+        q.heads = int(c.heads); q.kv_heads = int(c.kv_heads); q.head_dim = int(c.head_dim); q.family = int(c.family);
+        q.eps = c.eps;
+        CUDA_OK(launch_qk_rope_append(q, T, st));
+        AttnParams A{};
+        A.q = P.q; A.out = P.attn; A.kcache = s->kc; A.vcache = s->vc; A.rope = s->rope;
+        A.layer = int(l); A.layers = int(c.layers); A.context = s->context;
+        A.heads = int(c.heads); A.kv_heads = int(c.kv_heads); A.head_dim = int(c.head_dim);
+        A.family = int(c.family); A.eps = c.eps; A.status = s->status;
+        A.qpos = P.qpos; A.cache_client = client;
+        CUDA_OK(launch_attention_queries(A, T, st));
+        gemm_rows(s, L.o, P.attn, nullptr, T, P.x, EPI_ADD);
+        CUDA_OK(launch_norm_rows(P.x, m->gains + L.ffn_norm, c.eps, d, T, P.xn, st));
+        if (!is_moe(c)) {
+            gemm_rows(s, L.gate, P.xn, nullptr, T, P.g, EPI_STORE);
+            gemm_rows(s, L.up, P.xn, nullptr, T, P.u, EPI_STORE);
+            gemm_rows(s, L.down, P.g, P.u, T, P.x, EPI_ADD);
+            continue;
+        }
+        // routed feed-forward: route every row, group the rows by expert, run
+        // each expert over its group, combine in ascending expert id
+        const int Ex = int(c.experts), K = int(c.experts_used), eff = int(c.expert_ff);
+        gemm_rows(s, L.router, P.xn, nullptr, T, P.logits, EPI_STORE);
+        CUDA_OK(cudaMemsetAsync(P.counts, 0, size_t(Ex) * sizeof(int32_t), st));
+        CUDA_OK(launch_route_rows(P.logits, L.bias >= 0 ? m->gains + L.bias : nullptr, T, Ex, K, P.sel, P.prob,
+                                  P.norm, P.counts, st));
+        counts.resize(Ex);
+        CUDA_OK(cudaMemcpyAsync(counts.data(), P.counts, size_t(Ex) * sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+        CUDA_OK(cudaStreamSynchronize(st));
+        offsets.assign(Ex, 0);
+        groups.clear();
+        int run = 0;
+        for (int e = 0; e < Ex; e++) {
+            offsets[e] = run;
+            for (int g0 = 0; g0 < counts[e]; g0 += 128) groups.push_back(make_int4(e, run + g0, std::min(128, counts[e] - g0), 0));
+            run += counts[e];
+        }
+        if (run != T * K) fail(SPM_E_CUDA, "prefill routing lost rows");
+        CUDA_OK(cudaMemcpyAsync(P.offsets, offsets.data(), size_t(Ex) * sizeof(int32_t), cudaMemcpyHostToDevice, st));
+        CUDA_OK(cudaMemcpyAsync(P.groups, groups.data(), groups.size() * sizeof(int4), cudaMemcpyHostToDevice, st));
+        CUDA_OK(cudaMemsetAsync(P.cursor, 0, size_t(Ex) * sizeof(int32_t), st));
+        CUDA_OK(launch_scatter_rows(P.sel, T, K, P.offsets, P.cursor, P.list, P.slot, st));
+        auto grouped = [&](int idx, const float* x, const float* x2, const int32_t* xi, float* y) {
+            const StreamDesc& S = m->streams[idx];
+            GemmArgs a{};
+            a.w = m->tiles(idx);
+            a.pk = packed_shape(S.pk.dtype, S.pk.rows / S.experts, S.pk.cols);  // one expert's matrix
+            a.w_stride = a.pk.tiles * a.pk.tile_bytes;
+            a.x = x;
+            a.x2 = x2;
+            a.x_index = xi;
+            a.x_stride = int32_t(S.pk.cols);
+            a.y = y;
+            a.y_stride = int32_t(a.pk.rows);
+            a.epi = EPI_STORE;
+            a.status = s->status;
+            a.groups = P.groups;
+            a.ngroups = int32_t(groups.size());
+            CUDA_OK(launch_prefill_gemm(a, st));
+        };
+        grouped(L.gate_exps, P.xn, nullptr, P.list, P.ge);
+        grouped(L.up_exps, P.xn, nullptr, P.list, P.ue);
+        grouped(L.down_exps, P.ge, P.ue, nullptr, P.ye);
+        (void)eff;
+        CUDA_OK(launch_combine_rows(P.sel, P.prob, P.norm, P.slot, P.ye, P.x, T, K, d, st));
+    }
 }
 
 // Host-computed rotary table so that cos/sin are the oracle's glibc values:
@@ -1170,6 +1338,28 @@ spm_status spm_dequant_rows(const spm_model* m, int32_t index, uint64_t row0, ui
     });
 }
 
+// Positions from which a product over one matrix runs on the tensor cores
+// (prefill_gemm.cu) instead of streaming GEMVs of up to eight positions.
+static constexpr int32_t kTensorPositions = 16;
+
+// y = x W^T for `positions` rows of x on the tensor cores, when the shapes allow.
+static bool tensor_product(const uint8_t* tiles, const Packed& p, const float* x, int32_t positions, float* y,
+                    cudaStream_t st, int32_t* status) {
+    if (positions < kTensorPositions || p.cols % 64 || (reinterpret_cast<uintptr_t>(x) & 15)) return false;
+    GemmArgs a{};
+    a.w = tiles;
+    a.pk = p;
+    a.x = x;
+    a.x_stride = int32_t(p.cols);
+    a.tokens = positions;
+    a.y = y;
+    a.y_stride = int32_t(p.rows);
+    a.epi = EPI_STORE;
+    a.status = status;
+    CUDA_OK(launch_prefill_gemm(a, st));
+    return true;
+}
+
 spm_status spm_streamed(const spm_model* m, int32_t index, const float* x_dev, int32_t positions, float* y_dev,
                         void* cuda_stream) {
     return guarded([&] {
@@ -1178,6 +1368,9 @@ spm_status spm_streamed(const spm_model* m, int32_t index, const float* x_dev, i
         if (positions > 0 && (!x_dev || !y_dev)) fail(SPM_E_ARG, "null activation or output pointer");
         CUDA_OK(cudaSetDevice(m->device));
         const Packed& p = m->streams[index].pk;
+        if (tensor_product(m->tiles(index), p, x_dev, positions, y_dev, static_cast<cudaStream_t>(cuda_stream),
+                           nullptr))
+            return;
         for (int32_t p0 = 0; p0 < positions; p0 += kMaxBatch) {
             const int n = std::min(kMaxBatch, positions - p0);
             GemvLaunch L = gemv_base(m, index, x_dev + size_t(p0) * p.cols, n);
@@ -1215,6 +1408,8 @@ spm_status spm_weights_gemv(const spm_weights* w, const float* x_dev, int32_t po
         if (positions < 0) fail(SPM_E_ACTIVATION_LEN, "negative position count");
         CUDA_OK(cudaSetDevice(w->device));
         const Packed& p = w->pk;
+        if (tensor_product(w->dev, p, x_dev, positions, y_dev, static_cast<cudaStream_t>(cuda_stream), nullptr))
+            return;
         for (int32_t p0 = 0; p0 < positions; p0 += kMaxBatch) {
             const int n = std::min(kMaxBatch, positions - p0);
             GemvLaunch L{};
@@ -1280,7 +1475,10 @@ spm_status spm_session_create(spm_model* m, int32_t max_clients, int32_t max_con
         s->status = s->alloc<int32_t>(1);
         const size_t chunks = (size_t(max_context) + kAttnMinChunk - 1) / kAttnMinChunk;
         const size_t group = c.heads / c.kv_heads;
-        if (group * c.head_dim > 1024) fail(SPM_E_ARG, "attention supports at most 1024 query values per kv head");
+        // the attention kernel splits a score over 8 / group warps, four values at a time
+        if (group > 8 || group * c.head_dim > 1024 || c.head_dim > 256 || c.head_dim % (4 * (8 / group)))
+            fail(SPM_E_ARG, "attention supports at most 8 query heads and 1024 query values per kv head, "
+                            "head_dim up to 256 and a multiple of 4 * (8 / group)");
         s->attn_scratch = s->alloc<float>(n * c.kv_heads * chunks * group * (c.head_dim + 2));
         s->attn_counters = s->alloc<int32_t>(n * c.kv_heads);
         if (is_moe(c)) {
@@ -1374,6 +1572,32 @@ spm_status spm_decode_step_device(spm_session* s, const uint32_t* tokens_dev, in
     });
 }
 
+spm_status spm_prefill(spm_session* s, int32_t client, const uint32_t* tokens, int32_t len) {
+    return guarded([&] {
+        spm_model* m = s->m;
+        if (client < 0 || client >= s->max_clients) fail(SPM_E_ARG, "client index out of range");
+        if (len < 0 || (len > 0 && !tokens)) fail(SPM_E_ARG, "bad prompt");
+        if (m->world > 1) fail(SPM_E_ARG, "prefill runs on single-GPU models");
+        for (int32_t t = 0; t < len; t++)
+            if (tokens[t] >= m->cfg.vocab) fail(SPM_E_ARG, "token id out of range");
+        if (int64_t(s->lens[client]) + len > s->context)
+            fail(SPM_E_CONTEXT, "context " + std::to_string(s->context) + " exhausted");
+        if (m->streams[m->embed].pk.cols % 64) fail(SPM_E_ARG, "prefill needs hidden a multiple of 64");
+        CUDA_OK(cudaSetDevice(m->device));
+        prefill_buffers(s);
+        for (int32_t t0 = 0; t0 < len; t0 += kPrefillRows) {
+            const int T = std::min(kPrefillRows, len - t0);
+            prefill_chunk(s, client, tokens + t0, T, s->lens[client]);
+            s->lens[client] += T;
+        }
+        const int32_t pos = s->lens[client];
+        CUDA_OK(cudaMemcpyAsync(s->pos + client, &pos, sizeof(int32_t), cudaMemcpyHostToDevice, s->stream));
+        CUDA_OK(cudaMemcpyAsync(s->h_status, s->status, sizeof(int32_t), cudaMemcpyDeviceToHost, s->stream));
+        CUDA_OK(cudaStreamSynchronize(s->stream));
+        check_status(s);
+    });
+}
+
 spm_status spm_session_sync(spm_session* s) {
     return guarded([&] {
         CUDA_OK(cudaMemcpyAsync(s->h_status, s->status, sizeof(int32_t), cudaMemcpyDeviceToHost, s->stream));
@@ -1422,13 +1646,17 @@ spm_status spm_session_ep_connect(spm_session* s, const void* handles) {
         if (s->ep_ready) fail(SPM_E_ARG, "the session is already connected");
         CUDA_OK(cudaSetDevice(s->m->device));
         std::vector<uint8_t*> base(world);
+        cudaIpcMemHandle_t own;
+        CUDA_OK(cudaIpcGetMemHandle(&own, s->ep_region));
         for (int p = 0; p < world; p++) {
-            if (p == rank) {
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, static_cast<const uint8_t*>(handles) + size_t(p) * 64, sizeof(h));
+            // this session's own handle (its own rank, or a rank slot a caller
+            // points back at this buffer) maps its own region
+            if (p == rank || std::memcmp(&h, &own, sizeof(h)) == 0) {
                 base[p] = s->ep_region;
                 continue;
             }
-            cudaIpcMemHandle_t h;
-            std::memcpy(&h, static_cast<const uint8_t*>(handles) + size_t(p) * 64, sizeof(h));
             void* q = nullptr;
             CUDA_OK(cudaIpcOpenMemHandle(&q, h, cudaIpcMemLazyEnablePeerAccess));
             s->ep_mapped.push_back(q);
@@ -1444,6 +1672,17 @@ spm_status spm_session_ep_connect(spm_session* s, const void* handles) {
         CUDA_OK(cudaMemcpy(s->ep_peer_y, y.data(), y.size() * sizeof(float*), cudaMemcpyHostToDevice));
         CUDA_OK(cudaMemcpy(s->ep_peer_flag, f.data(), f.size() * sizeof(uint32_t*), cudaMemcpyHostToDevice));
         s->ep_ready = true;
+    });
+}
+
+spm_status spm_session_set_wait_limit(spm_session* s, uint64_t nanoseconds) {
+    return guarded([&] {
+        if (nanoseconds == 0) fail(SPM_E_ARG, "the wait limit must be positive");
+        CUDA_OK(cudaSetDevice(s->m->device));
+        CUDA_OK(cudaStreamSynchronize(s->stream));
+        s->wait_ns = nanoseconds;
+        for (auto& kv : s->exec) cudaGraphExecDestroy(kv.second);  // captured steps hold the old limit
+        s->exec.clear();
     });
 }
 

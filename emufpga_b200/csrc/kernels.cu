@@ -1,81 +1,11 @@
 // sm_100a kernels of the decode token loop besides the GEMV (gemv.cu):
 // exact dequantization (parity hook and embedding lookup), attention over the
 // device KV cache, greedy selection, position bookkeeping.
-#include "device.cuh"
+#include "dequant.cuh"
 
 namespace spm {
 namespace {
 using namespace dev;
-
-// ---------------------------------------------------------------- decode ----
-// Exact dequantization of unit u of a packed row, in the reference's
-// arithmetic order (spm-gguf/src/tensor.rs:103-210; ggml Q2_K):
-// Q8_0 d*q;  Q6_K (d*sc)*(q-32);  Q5_K (d*sc)*q - dmin*m;  Q2_K (d*sc)*q - dmin*m.
-__device__ void dequant_unit(uint32_t dtype, const uint8_t* tile, const Packed& p, uint32_t rt, uint32_t u,
-                             float* out) {
-    const uint32_t U = uint32_t(p.cols >> 5), B = uint32_t(p.cols >> 8);
-    const size_t unit = size_t(rt) * U + u;
-    switch (dtype) {
-        case SPM_F32: {
-            const float* w = reinterpret_cast<const float*>(tile) + size_t(rt) * p.cols + 32 * size_t(u);
-            for (int i = 0; i < 32; i++) out[i] = w[i];
-            break;
-        }
-        case SPM_Q8_0: {
-            const float d = h2f(tile[p.plane[1] + unit * 2] | (tile[p.plane[1] + unit * 2 + 1] << 8));
-            for (int i = 0; i < 32; i++) out[i] = __fmul_rn(d, float(int8_t(tile[unit * 32 + i])));
-            break;
-        }
-        case SPM_Q6_K: {
-            const uint8_t* ql = tile + unit * 16;
-            const uint8_t* qh = tile + p.plane[1] + unit * 8;
-            const uint8_t* sc = tile + p.plane[2] + unit * 2;
-            const size_t bo = p.plane[3] + (size_t(rt) * B + (u >> 3)) * 2;
-            const float d = h2f(tile[bo] | (tile[bo + 1] << 8));
-            for (int l = 0; l < 32; l++) {
-                const int i = l & 15, half = l >> 4, t = i >> 2, b = i & 3;
-                const uint32_t lo = half ? (ql[i] >> 4) : (ql[i] & 15);
-                const uint32_t hi = (qh[4 * half + b] >> (2 * t)) & 3;
-                const float q = float(lo | (hi << 4));
-                out[l] = __fmul_rn(__fmul_rn(d, float(int8_t(sc[half]))), __fsub_rn(q, 32.0f));
-            }
-            break;
-        }
-        case SPM_Q5_K: {
-            const uint8_t* m = tile + (size_t(rt) * B + (u >> 3)) * 16;
-            const uint8_t* qs = tile + p.plane[1] + unit * 16;
-            const uint8_t* qhp = tile + p.plane[2] + unit * 4;
-            const uint32_t qh = qhp[0] | (qhp[1] << 8) | (qhp[2] << 16) | (uint32_t(qhp[3]) << 24);
-            const float d = h2f(m[0] | (m[1] << 8)), dmin = h2f(m[2] | (m[3] << 8));
-            const uint8_t* s = m + 4;
-            const int j = int(u & 7);
-            int sc, mn;
-            if (j < 4) { sc = s[j] & 63; mn = s[j + 4] & 63; }
-            else { sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4); mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4); }
-            for (int l = 0; l < 32; l++) {
-                const int i = l & 15;
-                const uint32_t lo = (l >> 4) ? (qs[i] >> 4) : (qs[i] & 15);
-                const float q = float(lo | (((qh >> l) & 1) << 4));
-                out[l] = __fsub_rn(__fmul_rn(__fmul_rn(d, float(sc)), q), __fmul_rn(dmin, float(mn)));
-            }
-            break;
-        }
-        case SPM_Q2_K: {
-            const uint8_t* qs = tile + unit * 8;
-            const uint8_t* sc = tile + p.plane[1] + unit * 2;
-            const size_t bo = p.plane[2] + (size_t(rt) * B + (u >> 3)) * 4;
-            const float d = h2f(tile[bo] | (tile[bo + 1] << 8)), dmin = h2f(tile[bo + 2] | (tile[bo + 3] << 8));
-            for (int l = 0; l < 32; l++) {
-                const int h = l >> 4, i = l & 15, t = i >> 2, b = i & 3;
-                const float q = float((qs[4 * h + b] >> (2 * t)) & 3);
-                const float dl = __fmul_rn(d, float(sc[h] & 15)), ml = __fmul_rn(dmin, float(sc[h] >> 4));
-                out[l] = __fsub_rn(__fmul_rn(dl, q), ml);
-            }
-            break;
-        }
-    }
-}
-
 
 __global__ void dequant_kernel(uint32_t dtype, const uint8_t* tiles, const Packed p, uint64_t row0, uint64_t rows,
                                float* out) {
@@ -197,17 +127,22 @@ __global__ void advance_kernel(int32_t* pos, int n, uint32_t* step) {
 // Grid (kv head, client, position chunk of P.chunk).  Every CTA applies the
 // QK-norm and RoPE (host-computed cos/sin table) to its group's queries and
 // the new key; the CTA whose chunk holds the new position appends k, v to the
-// cache (spm-kv/src/cache.rs:49-58).  Each CTA scores its positions for all
-// query heads of the group (keys staged in shared memory, shared by the
-// group), forms its chunk's softmax partials (max, sum, unnormalised value
-// sum), and the last CTA of a (kv head, client) to finish combines the chunks
-// in chunk order.  The scores, the mask (diagonal included) and the GQA head
+// cache (spm-kv/src/cache.rs:49-58).  The chunk's cached keys and values move
+// through a two-stage shared-memory ring of kAttnTile positions with 16-byte
+// asynchronous copies (every thread a share of the tile's rows, one copy group
+// per tile); the first two tiles come from earlier steps and are requested
+// before waiting for the kernel that produces this step's q, k, v.  Per tile every query head of the
+// group scores the positions, the running softmax (max, sum) is updated and
+// the unnormalised value sum rescaled and accumulated (online softmax); the
+// last CTA of a (kv head, client) to finish combines the chunks' partials in
+// chunk order.  The scores, the mask (diagonal included) and the GQA head
 // mapping are the reference's:
 //   LLAMA  : spm-kv/src/attend.rs:37-94   (dot * (1/sqrt hd))
 //   others : spm-qwen3-slice/src/attention.rs:36-79 (dot / sqrt hd), with
 //            per-head (Qwen3) or full-width (OLMoE) QK RMSNorm.
 constexpr int kAttnThreads = 256;
-constexpr int kSub = 64;  // positions staged per pass
+constexpr int kAttnTile = 32;    // positions per staged tile
+constexpr int kAttnStages = 2;
 
 __device__ __forceinline__ void rope_pair(float& x, float& y, float c, float s, bool llama) {
     if (llama) {  // spm-ops/src/attention.rs:29-30
@@ -223,45 +158,73 @@ __device__ __forceinline__ void rope_pair(float& x, float& y, float c, float s, 
     }
 }
 
+// Shared memory of the attention kernel, in floats (mbarriers at the end).
+struct AttnSmem {
+    int qs, kn, vn, kt, vt, part, prob, stat, total;
+    __host__ __device__ AttnSmem(int group, int hd) {
+        const int ld = hd + 4;
+        const int R = 8 / group;  // warps per head in the scores (group <= 8)
+        qs = 0;
+        kn = qs + group * hd;
+        vn = kn + hd;
+        kt = (vn + hd + 31) & ~31;                   // [stage][tile][ld]
+        vt = kt + kAttnStages * kAttnTile * ld;
+        part = vt + kAttnStages * kAttnTile * ld;    // [R][group][tile] partial dots
+        prob = part + R * group * kAttnTile;          // [tile][group] probabilities
+        stat = prob + kAttnTile * group;              // [group]: alpha, m, l (3 arrays) + 64 reduction
+        total = stat + 3 * group + 64;
+    }
+};
+
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParams P) {
-    extern __shared__ __align__(16) float sm[];
+    extern __shared__ __align__(128) float sm[];
     const int kvh = blockIdx.x, i = blockIdx.y, chunk = blockIdx.z, S = gridDim.z;
     const int hd = P.head_dim, group = P.heads / P.kv_heads;
     const int qw = P.heads * hd, kvw = P.kv_heads * hd, ld = hd + 4;
     const bool llama = P.family == SPM_FAMILY_LLAMA;
-    float* qs = sm;                         // group * hd
-    float* kn = qs + group * hd;            // hd (new key)
-    float* vn = kn + hd;                    // hd (new value)
-    float* kv = vn + hd;                    // kSub * ld (staged keys; values of later passes)
-    float* vb = kv + kSub * ld;             // kSub * ld (values of the first pass)
-    float* sc = vb + kSub * ld;             // group * kChunk scores
-    float* red = sc + group * kAttnChunk;   // 64
-    // The position and the cached rows before it come from earlier steps, so
-    // the first pass's keys and values are fetched before waiting for the
-    // kernel that produces this step's q, k, v.
-    const int pos = P.pos[i];
+    const AttnSmem L(group, hd);
+    float* qs = sm + L.qs;
+    float* kn = sm + L.kn;
+    float* vn = sm + L.vn;
+    float* red = sm + L.stat + 3 * group;
+    const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
+    const bool qmode = P.qpos != nullptr;
+    const int pos = qmode ? P.qpos[i] : P.pos[i];
     const int p0 = chunk * P.chunk;
     const int p1 = min(pos + 1, p0 + P.chunk);
-    const size_t base = (size_t(i) * P.layers + P.layer) * P.context * size_t(kvw) + size_t(kvh) * hd;
+    const int npos = max(0, p1 - p0), ntiles = (npos + kAttnTile - 1) / kAttnTile;
+    const size_t cc = qmode ? size_t(P.cache_client) : size_t(i);
+    const size_t base = (cc * P.layers + P.layer) * P.context * size_t(kvw) + size_t(kvh) * hd;
     float* kc = P.kcache + base;
     float* vc = P.vcache + base;
-    {
-        const int pre = max(0, min(min(pos, p1), p0 + kSub) - p0);  // cached rows of the first pass
-        for (int t = threadIdx.x; t < pre * (hd / 4); t += kAttnThreads) {
-            const int p = t / (hd / 4), c4 = t % (hd / 4);
-            *reinterpret_cast<float4*>(kv + p * ld + 4 * c4) = *reinterpret_cast<const float4*>(kc + size_t(p0 + p) * kvw + 4 * c4);
-            *reinterpret_cast<float4*>(vb + p * ld + 4 * c4) = *reinterpret_cast<const float4*>(vc + size_t(p0 + p) * kvw + 4 * c4);
+    // every thread copies its share of tile j's key and value rows into stage
+    // j % kAttnStages (16 bytes per copy), as one copy group
+    const int q4 = hd / 4;
+    auto request = [&](int j) {
+        const int s = j % kAttnStages, t0 = p0 + j * kAttnTile, nr = min(kAttnTile, p1 - t0);
+        for (int e = threadIdx.x; e < 2 * nr * q4; e += kAttnThreads) {
+            const int kv = e / (nr * q4), r = (e / q4) % nr, c4 = e % q4;
+            const float* src = (kv ? vc : kc) + size_t(t0 + r) * kvw + 4 * c4;
+            cp_async16(sm + (kv ? L.vt : L.kt) + (s * kAttnTile + r) * ld + 4 * c4, src);
         }
+        cp_async_commit();
+    };
+    for (int j = 0; j < kAttnStages; j++) {
+        if (j < ntiles) request(j);
+        else cp_async_commit();  // empty group: the wait counts below stay uniform
     }
     pdl_wait();
     const float* qg = P.q + size_t(i) * qw + size_t(kvh) * group * hd;
     for (int t = threadIdx.x; t < group * hd; t += kAttnThreads) qs[t] = qg[t];
-    for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
-        kn[t] = P.k[size_t(i) * kvw + size_t(kvh) * hd + t];
-        vn[t] = P.v[size_t(i) * kvw + size_t(kvh) * hd + t];
-    }
+    if (!qmode)
+        for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
+            kn[t] = P.k[size_t(i) * kvw + size_t(kvh) * hd + t];
+            vn[t] = P.v[size_t(i) * kvw + size_t(kvh) * hd + t];
+        }
     __syncthreads();
-    if (P.family == SPM_FAMILY_OLMOE) {
+    if (qmode) {
+        // the query is normed and rotated, the cache rows are in place
+    } else if (P.family == SPM_FAMILY_OLMOE) {
         float sq = 0.f, sk = 0.f;
         for (int t = threadIdx.x; t < qw; t += kAttnThreads) sq = fmaf(P.q[size_t(i) * qw + t], P.q[size_t(i) * qw + t], sq);
         for (int t = threadIdx.x; t < kvw; t += kAttnThreads) sk = fmaf(P.k[size_t(i) * kvw + t], P.k[size_t(i) * kvw + t], sk);
@@ -275,8 +238,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         __syncthreads();
     } else if (!llama) {
         // per-head RMSNorm, one warp per head (spm-qwen3-slice/src/attention.rs:27-34)
-        const int lane = threadIdx.x & 31;
-        for (int h = threadIdx.x >> 5; h <= group; h += kAttnThreads / 32) {
+        for (int h = warp; h <= group; h += kAttnThreads / 32) {
             float* x = h < group ? qs + h * hd : kn;
             const float* g = h < group ? P.q_norm : P.k_norm;
             float ss = 0.f;
@@ -290,123 +252,140 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     }
     const int half = hd / 2;
     const float2* rt = P.rope + size_t(pos) * half;
-    for (int t = threadIdx.x; t < (group + 1) * half; t += kAttnThreads) {
+    for (int t = threadIdx.x; !qmode && t < (group + 1) * half; t += kAttnThreads) {
         const int h = t / half, j = t % half;
         float* x = h < group ? qs + h * hd : kn;
         const float2 cs = rt[j];
         rope_pair(x[j], x[j + half], cs.x, cs.y, llama);
     }
     __syncthreads();
-    if (pos >= p0 && pos < p0 + P.chunk)
+    if (!qmode && pos >= p0 && pos < p0 + P.chunk)
         for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
             kc[size_t(pos) * kvw + t] = kn[t];
             vc[size_t(pos) * kvw + t] = vn[t];
-            if (pos < p0 + kSub) {  // the new row of the first pass
-                kv[(pos - p0) * ld + t] = kn[t];
-                vb[(pos - p0) * ld + t] = vn[t];
-            }
         }
-    __syncthreads();
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(float(hd)));
     const float denom = __fsqrt_rn(float(hd));
-    const int npos = max(0, p1 - p0);
-    // ---- scores for this chunk, all heads of the group ----
-    for (int b0 = 0; b0 < npos; b0 += kSub) {
-        const int nb = min(kSub, npos - b0);
-        if (b0 > 0) {  // the first pass was staged before the wait
+    // scores: warp w takes head w % group (R = 8 / group warps per head, each
+    // over hd / R dimensions), lane = position in the tile
+    const int R = 8 / group;  // group <= 8 (the session checks)
+    const int sh = warp % group, sr = warp / group;  // score head, dimension part
+    const bool scorer = warp < group * R;
+    const int dlen = hd / R, d0 = sr * dlen;
+    // values: thread t owns dimension t % hd of the hpt consecutive heads
+    // (t / hd) * hpt + k
+    const int vd = int(threadIdx.x) % hd, vslot = int(threadIdx.x) / hd, vstep = kAttnThreads / hd;
+    const int hpt = (group + vstep - 1) / vstep, h0 = vslot * hpt;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float m_run = -INFINITY, l_run = 0.f;  // softmax state of head `warp` (warps < group)
+    float* part = sm + L.part;
+    float* prob = sm + L.prob;
+    float* alpha = sm + L.stat;
+    for (int j = 0; j < ntiles; j++) {
+        const int s = j % kAttnStages, t0 = p0 + j * kAttnTile, nr = min(kAttnTile, p1 - t0);
+        cp_async_wait<kAttnStages - 1>();  // this thread's copies of tile j have landed
+        __syncthreads();                   // and every other thread's
+        const float* kt = sm + L.kt + s * kAttnTile * ld;
+        const float* vt = sm + L.vt + s * kAttnTile * ld;
+        if (!qmode && pos >= t0 && pos < t0 + nr) {
+            // the new row: the copy brought the cache's old contents
             __syncthreads();
-            for (int t = threadIdx.x; t < nb * (hd / 4); t += kAttnThreads) {
-                const int p = t / (hd / 4), c4 = t % (hd / 4);
-                const float4 v = *reinterpret_cast<const float4*>(kc + size_t(p0 + b0 + p) * kvw + 4 * c4);
-                *reinterpret_cast<float4*>(kv + p * ld + 4 * c4) = v;
+            for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
+                sm[L.kt + (s * kAttnTile + pos - t0) * ld + t] = kn[t];
+                sm[L.vt + (s * kAttnTile + pos - t0) * ld + t] = vn[t];
             }
             __syncthreads();
         }
-        for (int t = threadIdx.x; t < nb * group; t += kAttnThreads) {
-            const int p = t % nb, h = t / nb;
-            const float* q = qs + h * hd;
-            const float* k = kv + p * ld;
+        if (scorer) {
             float d = 0.f;
-            for (int c = 0; c < hd; c += 4) {
-                const float4 kk = *reinterpret_cast<const float4*>(k + c);
-                d = fmaf(q[c], kk.x, d);
-                d = fmaf(q[c + 1], kk.y, d);
-                d = fmaf(q[c + 2], kk.z, d);
-                d = fmaf(q[c + 3], kk.w, d);
+            if (lane < nr) {
+                const float4* q = reinterpret_cast<const float4*>(qs + sh * hd + d0);
+                const float4* k = reinterpret_cast<const float4*>(kt + lane * ld + d0);
+#pragma unroll 8
+                for (int c = 0; c < dlen / 4; c++) {
+                    const float4 qq = q[c], kk = k[c];
+                    d = fmaf(qq.x, kk.x, d);
+                    d = fmaf(qq.y, kk.y, d);
+                    d = fmaf(qq.z, kk.z, d);
+                    d = fmaf(qq.w, kk.w, d);
+                }
             }
-            sc[h * kAttnChunk + b0 + p] = llama ? __fmul_rn(d, scale) : __fdiv_rn(d, denom);
+            part[(sr * group + sh) * kAttnTile + lane] = d;
         }
         __syncthreads();
-    }
-    // ---- chunk softmax partials per head (one warp per head): m, l ----
-    float* part = P.scratch + ((size_t(i) * P.kv_heads + kvh) * S + chunk) * group * (hd + 2);
-    float* ml = red;  // [group][2]: max, sum of exp
-    {
-        const int lane = threadIdx.x & 31;
-        for (int h = threadIdx.x >> 5; h < group; h += kAttnThreads / 32) {
-            float mx = -INFINITY;
-            for (int p = lane; p < npos; p += 32) mx = fmaxf(mx, sc[h * kAttnChunk + p]);
+        if (warp < group) {
+            // running softmax of head `warp`: lane = position
+            float sc = -INFINITY;
+            if (lane < nr) {
+                float d = 0.f;
+                for (int r = 0; r < R; r++) d += part[(r * group + warp) * kAttnTile + lane];
+                sc = llama ? __fmul_rn(d, scale) : __fdiv_rn(d, denom);
+            }
+            float mx = sc;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            float tot = 0.f;
-            for (int p = lane; p < npos; p += 32) {
-                const float e = expf(sc[h * kAttnChunk + p] - mx);
-                sc[h * kAttnChunk + p] = e;
-                tot += e;
-            }
-            tot = warp_sum(tot);
-            if (lane == 0) {
-                ml[2 * h] = mx;
-                ml[2 * h + 1] = tot;
-            }
+            const float m_new = fmaxf(m_run, mx);
+            const float a = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
+            const float e = lane < nr ? expf(sc - m_new) : 0.f;
+            l_run = fmaf(l_run, a, warp_sum(e));
+            m_run = m_new;
+            prob[lane * group + warp] = e;
+            if (lane == 0) alpha[warp] = a;
         }
-    }
-    __syncthreads();
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};  // (head, dim) pairs t, t+256, ... (group*hd <= 1024)
-    for (int b0 = 0; b0 < npos; b0 += kSub) {
-        const int nb = min(kSub, npos - b0);
-        const float* vv = b0 == 0 ? vb : kv;
-        if (b0 > 0) {
-            for (int t = threadIdx.x; t < nb * (hd / 4); t += kAttnThreads) {
-                const int p = t / (hd / 4), c4 = t % (hd / 4);
-                *reinterpret_cast<float4*>(kv + p * ld + 4 * c4) =
-                    *reinterpret_cast<const float4*>(vc + size_t(p0 + b0 + p) * kvw + 4 * c4);
-            }
-            __syncthreads();
-        }
+        __syncthreads();
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
-            const int t = threadIdx.x + r * kAttnThreads;
-            if (t < group * hd) {
-                const int h = t / hd, dd = t % hd;
-                float a = acc[r];
-                for (int p = 0; p < nb; p++) a = fmaf(sc[h * kAttnChunk + b0 + p], vv[p * ld + dd], a);
-                acc[r] = a;
+        for (int k = 0; k < 4; k++)
+            if (k < hpt && h0 + k < group) acc[k] *= alpha[h0 + k];
+        if (hpt == 4 && h0 + 4 <= group) {
+            // four heads: their probabilities of a position are one vector
+            for (int p = 0; p < nr; p++) {
+                const float v = vt[p * ld + vd];
+                const float4 pr = *reinterpret_cast<const float4*>(prob + p * group + h0);
+                acc[0] = fmaf(pr.x, v, acc[0]);
+                acc[1] = fmaf(pr.y, v, acc[1]);
+                acc[2] = fmaf(pr.z, v, acc[2]);
+                acc[3] = fmaf(pr.w, v, acc[3]);
+            }
+        } else {
+            for (int p = 0; p < nr; p++) {
+                const float v = vt[p * ld + vd];
+#pragma unroll
+                for (int k = 0; k < 4; k++)
+                    if (k < hpt && h0 + k < group) acc[k] = fmaf(prob[p * group + h0 + k], v, acc[k]);
             }
         }
         __syncthreads();
+        // stage s is free: request tile j + kAttnStages into it
+        if (j + kAttnStages < ntiles) request(j + kAttnStages);
+        else cp_async_commit();
     }
+    cp_async_wait<0>();
+    float* m_sh = sm + L.stat + group;  // [group] max, then [group] sum
+    if (warp < group && lane == 0) {
+        m_sh[warp] = m_run;
+        m_sh[group + warp] = l_run;
+    }
+    __syncthreads();
     if (S == 1) {
         // the whole prefix is in this CTA: finish here (no partials)
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
-            const int t = threadIdx.x + r * kAttnThreads;
-            if (t < group * hd) {
-                const int h = t / hd, dd = t % hd;
-                P.out[size_t(i) * qw + (size_t(kvh) * group + h) * hd + dd] = __fdiv_rn(acc[r], ml[2 * h + 1]);
-            }
+        for (int k = 0; k < 4; k++) {
+            const int h = h0 + k;
+            if (k < hpt && h < group)
+                P.out[size_t(i) * qw + (size_t(kvh) * group + h) * hd + vd] = __fdiv_rn(acc[k], m_sh[group + h]);
         }
         pdl_trigger();
         return;
     }
+    float* outp = P.scratch + ((size_t(i) * P.kv_heads + kvh) * S + chunk) * group * (hd + 2);
 #pragma unroll
-    for (int r = 0; r < 4; r++) {
-        const int t = threadIdx.x + r * kAttnThreads;
-        if (t < group * hd) part[(t / hd) * (hd + 2) + (t % hd)] = acc[r];
+    for (int k = 0; k < 4; k++) {
+        const int h = h0 + k;
+        if (k < hpt && h < group) outp[h * (hd + 2) + vd] = acc[k];
     }
     if (threadIdx.x < group) {
-        part[threadIdx.x * (hd + 2) + hd] = ml[2 * threadIdx.x];
-        part[threadIdx.x * (hd + 2) + hd + 1] = ml[2 * threadIdx.x + 1];
+        outp[threadIdx.x * (hd + 2) + hd] = m_sh[threadIdx.x];
+        outp[threadIdx.x * (hd + 2) + hd + 1] = m_sh[group + threadIdx.x];
     }
     // ---- the last chunk CTA of this (kv head, client) combines ----
     __shared__ int last;
@@ -444,9 +423,8 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
 }  // namespace
 
 size_t attention_smem(const AttnParams& P) {
-    const int group = P.heads / P.kv_heads;
-    return (size_t(group) * P.head_dim + 2 * P.head_dim + 2 * size_t(kSub) * (P.head_dim + 4) +
-            size_t(group) * kAttnChunk + 64) * sizeof(float);
+    const AttnSmem L(P.heads / P.kv_heads, P.head_dim);
+    return size_t(L.total) * sizeof(float);
 }
 
 static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
@@ -478,13 +456,30 @@ cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t s, bool pd
     if (dev < 64 && !sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
     const int target = dev < 64 && sms[dev] ? sms[dev] : 148;
     int chunk = kAttnChunk;
-    while (chunk > kAttnMinChunk && ((P.context + chunk - 1) / chunk) * P.kv_heads * n < target) chunk /= 2;
+    while (chunk > kAttnMinChunk && ((P.context + chunk - 1) / chunk) * P.kv_heads * n < 3 * target) chunk /= 2;
     const int chunks = (P.context + chunk - 1) / chunk;
     AttnParams p = P;
     p.chunk = chunk;
     void* args[] = {&p};
     return launch_pdl(reinterpret_cast<const void*>(attention_kernel), dim3(P.kv_heads, n, chunks),
                       dim3(kAttnThreads), smem, s, pdl, args);
+}
+
+cudaError_t launch_attention_queries(const AttnParams& P, int n, cudaStream_t s) {
+    const size_t smem = attention_smem(P);
+    static int configured_for = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (smem > 48 * 1024 && configured_for != dev) {
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+        if (e != cudaSuccess) return e;
+        configured_for = dev;
+    }
+    AttnParams p = P;
+    p.chunk = P.context;  // one CTA covers the whole prefix: S == 1, no partials
+    void* args[] = {&p};
+    return launch_pdl(reinterpret_cast<const void*>(attention_kernel), dim3(P.kv_heads, n, 1), dim3(kAttnThreads),
+                      smem, s, false, args);
 }
 
 cudaError_t launch_embed(uint32_t dtype, const uint8_t* tiles, const Packed& p, const uint32_t* tokens, int n,

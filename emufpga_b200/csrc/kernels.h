@@ -79,6 +79,34 @@ GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms, int per = 0)
 // `grid_out` receives the grid size (= sum-of-squares parts written by EPI_ADD).
 cudaError_t launch_gemv(uint32_t dtype, GemvLaunch L, int sms, cudaStream_t stream, bool pdl, int* grid_out = nullptr);
 
+// Many-position product on the tensor cores (prefill_gemm.cu):
+// y[t * y_stride + f] (+= aux for EPI_ADD) = sum_k W[f][k] * x_t[k] for every
+// row f of one packed matrix and t < tokens, where x_t is row x_index[t] (or
+// t) of x; with x2 set the input is silu(x) * x2 (a SwiGLU pair) instead.
+// cols must be a multiple of 64, x 16-byte aligned with x_stride % 4 == 0.
+struct GemmArgs {
+    const uint8_t* w;      // tile 0 of the packed matrix
+    Packed pk;
+    const float* x;
+    const float* x2;
+    const int32_t* x_index;
+    int32_t x_stride, tokens;
+    float* y;
+    int32_t y_stride;
+    const float* aux;      // residual for EPI_ADD (may alias y)
+    int32_t aux_stride, epi;
+    int32_t* status;       // device error word (code 7: a bounded wait gave up)
+    // Grouped mode (groups != nullptr; routed experts): CTA row y takes group
+    // groups[y] = {expert e, first place, count <= 128, 0}: the matrix is the
+    // pk.rows rows starting e * w_stride bytes after w, its positions are
+    // places first..first+count-1 (x row x_index[place], or place itself
+    // without x_index) and its outputs go to y rows of those places.
+    const int4* groups;
+    int32_t ngroups;
+    uint64_t w_stride;
+};
+cudaError_t launch_prefill_gemm(const GemmArgs& a, cudaStream_t stream);
+
 // Positions per attention CTA, at most and at least; a (kv head, client) is
 // split over ceil(context / chunk) CTAs whose softmax partials are combined,
 // with the chunk halved from the maximum while the grid has fewer CTAs than
@@ -98,9 +126,19 @@ struct AttnParams {
     int32_t layer, layers, context, heads, kv_heads, head_dim, family;
     float eps;
     int32_t chunk;                 // positions per CTA (set by launch_attention)
+    int32_t* status;               // device error word: a bounded wait that gave up sets it (code 6)
+    // Query mode (qpos != nullptr; prefill): row i of q is a query already
+    // QK-normed and rotated, at position qpos[i], over the cache of client
+    // cache_client, whose rows up to that position are already written; no
+    // append.  Launched without programmatic dependent launch.
+    const int32_t* qpos;
+    int32_t cache_client;
 };
 size_t attention_smem(const AttnParams& P);
 cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t stream, bool pdl);
+// Query mode over n query rows, one CTA per (kv head, query) covering the
+// whole prefix (no split, no partials).
+cudaError_t launch_attention_queries(const AttnParams& P, int n, cudaStream_t stream);
 
 // Gather-and-decode one packed row per client (embedding lookup).
 // Also writes sumsq_out[i*8 + c] = (i == c) ? sum of squares of row i : 0.

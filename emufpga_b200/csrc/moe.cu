@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(kCombineCols) combine_kernel(const MoePlan* pl
             if (ld_acquire_sys(f) != E) {
                 const uint64_t t0 = now_ns();
                 while (ld_acquire_sys(f) != E)
-                    if (now_ns() - t0 > kWaitLimitNs) {
+                    if (now_ns() - t0 > ex.wait_ns) {
                         flag(ex.status, 5);
                         break;
                     }

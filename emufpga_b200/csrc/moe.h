@@ -37,13 +37,14 @@ cudaError_t launch_route(const float* logits, const float* bias, int n, int expe
 // every rank has raised its flag for this layer (flag value E = *step *
 // layers + layer + 1, in flags[(E & 1) * 64 + rank]); the outputs are in the
 // buffer of parity E & 1, xstride floats after the parity-0 one.  A wait that
-// gives up after 1 s sets *status and goes on.
+// gives up after wait_ns sets *status and goes on.
 struct MoeExchange {
     const uint32_t* flags;
     const uint32_t* step;
     int32_t world, layers, layer;
     size_t xstride;
     int32_t* status;
+    uint64_t wait_ns;  // give up after this long (the session's wait limit)
 };
 
 // states[i] += sum over client i's experts in ascending id of

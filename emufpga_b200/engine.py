@@ -301,6 +301,16 @@ class Session:
              logits.ctypes.data_as(C.POINTER(C.c_float)) if want_logits else None, arg)
         return list(arg), logits
 
+    def set_wait_limit(self, nanoseconds: int) -> None:
+        """How long device waits on other ranks spin before the step reports SPM_E_TIMEOUT."""
+        call("spm_session_set_wait_limit", self._h, int(nanoseconds))
+
+    def prefill(self, client: int, tokens: Sequence[int]) -> None:
+        """Run a prompt for `client` on the tensor cores (KV appended, no logits)."""
+        n = len(tokens)
+        tok = (C.c_uint32 * max(1, n))(*tokens)
+        call("spm_prefill", self._h, client, tok, n)
+
     def decode_step_device(self, tokens_dev, n: int, argmax_dev, logits_dev=None) -> None:
         call("spm_decode_step_device", self._h, _dev_ptr(tokens_dev), n,
              _dev_ptr(logits_dev) if logits_dev is not None else None, _dev_ptr(argmax_dev))

@@ -159,7 +159,10 @@ spm_status spm_dequant_rows(const spm_model* m, int32_t index, uint64_t row0, ui
 spm_status spm_dequant_rows_static(const spm_model* m, int32_t index, uint64_t row0, uint64_t rows,
                                    float* out_host);
 /* y[p][r] = sum_c W[r][c] * x[p][c] for one stream; x_dev is positions x cols,
- * y_dev positions x rows (device pointers); cuda_stream may be NULL. */
+ * y_dev positions x rows (device pointers); cuda_stream may be NULL.  Up to 15
+ * positions stream the weights through GEMVs of at most eight positions; 16 or
+ * more (a prompt's positions) run as one product on the tensor cores when cols
+ * is a multiple of 64 and x_dev 16-byte aligned.  spm_weights_gemv likewise. */
 spm_status spm_streamed(const spm_model* m, int32_t index, const float* x_dev, int32_t positions,
                         float* y_dev, void* cuda_stream);
 
@@ -188,6 +191,18 @@ spm_status spm_decode_step(spm_session* s, const uint32_t* tokens, int32_t n, fl
 spm_status spm_decode_step_device(spm_session* s, const uint32_t* tokens_dev, int32_t n,
                                   float* logits_dev, uint32_t* argmax_dev);
 spm_status spm_session_sync(spm_session* s);
+/* Run a prompt through the model for `client`: its next `len` positions take
+ * tokens[0..len), their keys and values are appended to the client's cache,
+ * and the client's length grows by `len`.  The layers' products over all the
+ * prompt's positions run on the tensor cores (tcgen05, weights decoded exactly
+ * and split into bf16 parts, fp32 accumulation); each position computes what
+ * a decode step computes for it, up to the rounding of sums.  No logits are
+ * produced: feed the prompt's last token through spm_decode_step for the
+ * first greedy pick.  Single-GPU models; prompts longer than 1024 tokens run
+ * in chunks of 1024.  The reference feeds prompts one token per decode tick
+ * (spm-batch/examples/serve-demo.rs:84-89); its Qwen3 slice runs a whole
+ * prompt in one forward pass (spm-qwen3-slice/src/model.rs:10-171). */
+spm_status spm_prefill(spm_session* s, int32_t client, const uint32_t* tokens, int32_t len);
 /* The session's CUDA stream (cudaStream_t as void*). */
 spm_status spm_session_stream(const spm_session* s, void** cuda_stream);
 /* Capture steps as a CUDA graph per client count (1) or launch eagerly (0). */
@@ -213,6 +228,8 @@ spm_status spm_model_open_memory_ep(const uint8_t* gguf, uint64_t len, const cha
                                     const spm_model_cfg* cfg, int device, int32_t world, int32_t rank,
                                     spm_model** out);
 spm_status spm_session_ep_handle(spm_session* s, void* handle64);
+/* handles: the world ranks' 64-byte handles in rank order; a handle equal to
+ * this session's own maps this session's own buffer. */
 spm_status spm_session_ep_connect(spm_session* s, const void* handles);
 /* Kernel launches issued by one step at client count n (graph nodes). */
 spm_status spm_session_launches_per_step(spm_session* s, int32_t n, int32_t* launches);
@@ -237,6 +254,13 @@ enum {
     SPM_KERNEL_OTHER = 8         /* embedding gather, greedy pick, positions   */
 };
 spm_status spm_session_set_profile(spm_session* s, int32_t enable);
+/* How long a device wait on other ranks (the expert-parallel combine waiting
+ * for every rank's expert rows) may spin before it gives up, sets the
+ * session's status word and goes on; the step then returns SPM_E_TIMEOUT and
+ * its outputs are not to be used.  Default 1 s.  No counterpart in the
+ * reference, which runs its experts in one process and reports typed errors
+ * instead of panicking (spm-linear/src/stream.rs:31-55). */
+spm_status spm_session_set_wait_limit(spm_session* s, uint64_t nanoseconds);
 spm_status spm_session_profile(const spm_session* s, int32_t max, float* ms, uint64_t* bytes,
                                int32_t* kind, int32_t* count);
 

@@ -147,3 +147,21 @@ def test_gemv_reuses_ring_slots(cuda, rows, cols, positions):
     # several times (slot counts of 2, 4 and 8 with 2 or 4 consuming warps)
     got, want, scale = gemv_case(cuda, O.Q6_K, rows, cols, positions, seed=rows + cols)
     assert np.all(np.abs(got - want) <= 1e-5 * scale)
+
+
+@pytest.mark.parametrize("dtype", [O.Q8_0, O.Q6_K, O.Q5_K, O.Q2_K, O.F32])
+@pytest.mark.parametrize("positions", [16, 37, 130])
+def test_many_positions_on_tensor_cores_match_the_fma_chain(cuda, dtype, positions):
+    # 16 or more positions run as one tcgen05 product (exact weights, three-part
+    # bf16 splits, fp32 accumulation): the same summation-order bar as the GEMV
+    rows, cols = (203, 1536) if dtype != O.Q8_0 else (203, 576)
+    got, want, scale = gemv_case(cuda, dtype, rows, cols, positions, seed=positions * 3 + dtype)
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-5 * scale + 1e-30), float((err / (scale + 1e-30)).max())
+
+
+def test_tensor_core_product_large_shape(cuda):
+    # several 128-row and 128-position tiles, k split over many stages
+    got, want, scale = gemv_case(cuda, O.Q5_K, 600, 4096, 300, seed=123)
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-5 * scale + 1e-30), float((err / (scale + 1e-30)).max())
