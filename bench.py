@@ -21,9 +21,10 @@ clients (the largest configuration; it fits one B200), and the line carries a
 `batch1` sub-record for configs[2]'s batch-1 case (Qwen3-8B Q6_K, one client)
 measured the same way.  Dense models do not shard: N>1 runs N independent
 replicas ("replicas only").  Routed (MoE) models over N>1 GPUs run expert
-parallel: one job serving the same clients on every rank, experts dealt round
-robin over the ranks, expert outputs exchanged over NVLink ("scaling":
-"strong").
+parallel: one job of n clients, rank r running the attention block of clients
+r*n/N .. (r+1)*n/N - 1 and the experts dealt to it (round robin) for every
+client; the attention outputs, the expert outputs and the greedy picks are
+exchanged over NVLink ("scaling": "strong").
 
 `--workload ternary-4096-b8` times the ternary GEMV of spm-gemv-ref instead
 (one launch over a 4096 x 4096 ternary stream with one scale per column and
@@ -57,6 +58,9 @@ PROFILE_TICKS = 3
 # .spm operator workloads: rows, cols, group size, lanes (positions)
 TERNARY = {"ternary-4096-b8": (4096, 4096, 4096, 8)}
 DENSE = {"dense-f32-4096-b8": (4096, 4096, 4096, 8)}
+# host-to-HBM sweeps of a multi-stream .spm file: kind, streams, rows, cols, lanes
+SWEEP = {"sweep-ternary-32x4096-b8": ("ternary", 32, 4096, 4096, 8),
+         "sweep-f32-8x4096-b8": ("f32", 8, 4096, 4096, 8)}
 # DRAM bytes (read + write) per algorithmic weight byte of gemv_stream launches
 # in ncu captures (gpu__... dram__bytes_read.sum + dram__bytes_write.sum over
 # the launch's quantized weight bytes); the file named beside each holds the
@@ -77,11 +81,16 @@ def _args():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch1", action="store_true", help="skip the batch-1 sub-record")
+    ap.add_argument("--prompt-ticks", action="store_true",
+                    help="feed prompts one token per tick (serve-demo) instead of spm_prefill on the tensor cores")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--gguf-dir", default="/dev/shm",
                     help="where rank 0 writes the synthetic GGUF that expert-parallel ranks memory-map")
     ap.add_argument("--layers", type=int, default=0,
                     help="keep only the first N layers (small cases for profiler captures; not a bench number)")
+    ap.add_argument("--profile-region", choices=["decode", "prefill"], default=None,
+                    help="bracket the timed decode ticks or the prefill with cudaProfilerStart/Stop "
+                         "(for ncu --profile-from-start off)")
     return ap.parse_args()
 
 
@@ -302,9 +311,10 @@ def run_decode(a, name, rank, world, local, pg, dev, ep_ok=True):
     import emufpga_b200 as eb
 
     w, recipe, prompts = _workload(name, a.layers)
-    # Routed models over several GPUs run expert parallel: every rank serves
-    # all clients, and the experts are dealt round robin over the ranks (one
-    # job; tokens/s is not multiplied by the ranks).  Dense models run one
+    # Routed models over several GPUs run expert parallel: each rank runs the
+    # attention block of its share of the clients and the experts dealt to it
+    # (round robin) for all clients (one job; tokens/s is not multiplied by
+    # the ranks).  Dense models run one
     # replica per GPU.  Rank 0 writes the synthetic GGUF once; every rank
     # memory-maps it.
     ep_mode = ep_ok and world > 1 and recipe.shape.moe
@@ -341,9 +351,31 @@ def run_decode(a, name, rank, world, local, pg, dev, ep_ok=True):
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
 
+    prefill = None
+    first = 0
+    if not a.prompt_ticks and not ep_mode and len({len(p) for p in prompts}) == 1:
+        # every prompt but its last token through spm_prefill (tensor cores),
+        # timed on its own; the decode ticks then start at the prompts' last tick
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if a.profile_region == "prefill":
+            torch.cuda.cudart().cudaProfilerStart()
+        e0.record(stream)
+        for i, p in enumerate(prompts):
+            sess.prefill(i, p[:-1])
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        if a.profile_region == "prefill":
+            torch.cuda.cudart().cudaProfilerStop()
+        pms = e0.elapsed_time(e1)
+        ptoks = sum(len(p) - 1 for p in prompts)
+        prefill = {"value": ptoks / (pms / 1e3), "unit": "tokens/s", "ms": pms, "tokens": ptoks,
+                   "how": "spm_prefill of every client's prompt but its last token (tcgen05 products), CUDA events"}
+        first = P - 1
+        tokens = torch.tensor([p[-1] for p in prompts], dtype=torch.int32, device=dev)
     with torch.cuda.stream(stream):
-        # untimed: the prompt ticks and the warm-up decode ticks
-        for t in range(P + warm):
+        # untimed: the prompt ticks (or the prompts' last tick) and the warm-up decode ticks
+        for t in range(first, P + warm):
             sess.decode_step_device(tokens, n, argmax)
             tokens = torch.where(in_prompt[t], feed[t], argmax)
         torch.cuda.synchronize(dev)
@@ -352,6 +384,8 @@ def run_decode(a, name, rank, world, local, pg, dev, ep_ok=True):
         torch.cuda.synchronize(dev)
         with Clocks(local) as clocks:
             # ---- device-resident timing (value) ----
+            if a.profile_region == "decode":
+                torch.cuda.cudart().cudaProfilerStart()
             for i in range(K):
                 flush.zero_()
                 starts[i].record(stream)
@@ -359,6 +393,8 @@ def run_decode(a, name, rank, world, local, pg, dev, ep_ok=True):
                 ends[i].record(stream)
                 tokens = argmax.clone()
             torch.cuda.synchronize(dev)
+            if a.profile_region == "decode":
+                torch.cuda.cudart().cudaProfilerStop()
             step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
             # ---- end to end through the C ABI with host buffers (e2e) ----
             toks = tokens.cpu().tolist()
@@ -390,7 +426,7 @@ def run_decode(a, name, rank, world, local, pg, dev, ep_ok=True):
     launches = sess.launches_per_step(n)
     ranks_agree = None
     if ep_mode:
-        # every rank serves the same clients: their greedy tokens must agree
+        # the greedy picks are gathered on every rank: they must agree
         got = [None] * world
         pg.all_gather_object(got, list(toks))
         ranks_agree = all(g == got[0] for g in got)
@@ -410,7 +446,9 @@ def run_decode(a, name, rank, world, local, pg, dev, ep_ok=True):
             "config": {"workload": name, "model": w["recipe"], "clients": n, "prompts": w["prompts"],
                        "parallelism": (f"expert parallel x{world}" if ep_mode else f"replicas x{world}")
                        if world > 1 else "single GPU",
-                       "prompt_ticks_untimed": P,
+                       "prompt_ticks_untimed": P - first,
+                       "prompt_phase": "spm_prefill (tensor cores), then the prompts' last tick" if prefill else
+                                       "one prompt token per tick (serve-demo schedule)",
                        "timed_ticks": [P + warm, P + warm + K - 1],
                        "timed_context": [P + warm + 1, P + warm + K],
                        "e2e_ticks": [P + warm + K, P + warm + 2 * K - 1],
@@ -424,6 +462,8 @@ def run_decode(a, name, rank, world, local, pg, dev, ep_ok=True):
             "roofline": _profile_summary(prof, peak, how, name),
         }
         line["weight_stream_frac"] = line["weight_stream_gbs"] / peak
+        if prefill:
+            line["prefill"] = prefill
         if recipe.shape.moe:
             line["config"]["experts_touched_per_step"] = statistics.mean(touched)
         if ep_mode:
@@ -440,9 +480,121 @@ def run_decode(a, name, rank, world, local, pg, dev, ep_ok=True):
     return line
 
 
+def sweep_file(name, seed=0):
+    """The workload's .spm file: `streams` streams of rows x cols (ternary
+    weights uniform over {0,+1,-1} with one scale per column, or f32 in
+    sixteenths), and the activations."""
+    import numpy as np
+
+    from emufpga_b200 import spmfile as sf
+
+    kind, streams, rows, cols, lanes = SWEEP[name]
+    rng = np.random.default_rng(seed)
+    descs, bodies = [], []
+    for _ in range(streams):
+        if kind == "ternary":
+            codes = np.array([0, 1, 3], np.uint8)[rng.integers(0, 3, rows * cols)]
+            scales = (rng.integers(0, 32, -(-rows * cols // rows)) / 16 + 0.0625).astype(np.float32)
+            descs.append(sf.render_descriptor(rows, cols, rows))
+            bodies.append(sf.ternary_stream_bytes(codes, scales, rows))
+        else:
+            w = (rng.integers(0, 64, rows * cols) / 16 - 2.0).astype(np.float32)
+            descs.append(sf.render_descriptor(rows, cols, rows, sf.F32))
+            bodies.append(sf.dense_stream_bytes(w, rows, sf.F32))
+    x = (rng.integers(0, 64, (lanes, cols)) / 16 - 2.0).astype(np.float32)
+    return sf.render_header(streams) + b"".join(descs) + b"".join(bodies), x
+
+
+def run_sweep(a, rank, world, local):
+    """One step = one sweep of every stream of the file through the device
+    ring (the streams after the running one are copied in from pinned host
+    memory on a copy stream meanwhile).  Beside the streaming sweep the same
+    file runs with a ring holding every stream (after the first sweep nothing
+    is copied: the compute alone) and the packed bytes are copied once with a
+    plain host-to-device copy (the link alone); overlap = the share of the
+    shorter of the two that the streaming sweep hides."""
+    import torch
+
+    from emufpga_b200 import sweep as S
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    kind, streams, rows, cols, lanes = SWEEP[a.workload]
+    data, x = sweep_file(a.workload)
+    xd = torch.from_numpy(x).to(dev).reshape(-1)
+    stream = torch.cuda.current_stream(dev)
+    warm, steps = max(a.warmup, 3), a.steps
+
+    def timed(sw, n):
+        y = torch.empty((lanes, rows), dtype=torch.float32, device=dev)
+        for _ in range(warm):
+            for _ in range(streams):
+                sw.next(xd, lanes, out=y)
+            sw.rewind()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            for _ in range(streams):
+                sw.next(xd, lanes, out=y)
+            sw.rewind()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / 1e3 / n
+
+    with S.Sweep(data, local) as sw:
+        info = sw.describe()
+        packed, ring = int(info["host_bytes"]), int(info["device_bytes"])
+        with Clocks(local) as clocks:
+            before = sw.describe()["bytes_copied"]
+            t_stream = timed(sw, steps)
+            copied = (sw.describe()["bytes_copied"] - before) / (warm + steps)
+    with S.Sweep(data, local, device_bytes=len(data) * 2) as sw:
+        t_compute = timed(sw, steps)
+    nbytes = packed
+    host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    devbuf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        devbuf.copy_(host, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        devbuf.copy_(host, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    t_copy = e0.elapsed_time(e1) / 1e3 / steps
+    hidden = (t_compute + t_copy - t_stream) / min(t_compute, t_copy)
+    apps = rows * cols * lanes * streams
+    if rank == 0:
+        line = {"metric": ("ternary" if kind == "ternary" else "dense") + " weight applications/s, streamed from host",
+                "value": apps * world / t_stream, "unit": "weights/s", "n_gpus": world, "steps": steps, "warmup": warm,
+                "ms_per_step": 1e3 * t_stream, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic (weights and activations as the reference's generators draw them)",
+                "config": {"workload": a.workload, "streams": streams, "rows": rows, "cols": cols, "lanes": lanes,
+                           "file_bytes": len(data), "ring_bytes": ring, "packed_bytes": nbytes},
+                "bytes_copied_per_sweep": copied,
+                "h2d_gbs_streaming": copied / t_stream / 1e9,
+                "h2d_gbs_plain_copy": nbytes / t_copy / 1e9,
+                "sweep_ms_resident": 1e3 * t_compute, "copy_ms": 1e3 * t_copy,
+                "overlap_hidden": hidden,
+                "e2e": {"value": apps * world / t_stream, "unit": "weights/s", "h2d_bytes_per_step": nbytes,
+                        "d2h_bytes_per_step": 0},
+                "gpu_launches": streams * steps, "clocks": clocks.summary()}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     a = _args()
     rank, world, local = _dist()
+    if a.workload in SWEEP:
+        if a.impl == "ours":
+            return run_sweep(a, rank, world, local)
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "sweep workloads measure the host link; the "
+                              "reference arm times the operators (ternary-4096-b8, dense-f32-4096-b8)"}), flush=True)
+        return 0
     if a.workload in TERNARY or a.workload in DENSE:
         return run_ternary_reference(a, rank, world) if a.impl == "reference" else run_ternary(a, rank, world, local)
     if a.impl == "reference":
@@ -475,7 +627,8 @@ def main():
         for k in ("_img", "_recipe", "_prompts", "_steps"):
             sub.pop(k)
         line["batch1"] = {k: sub[k] for k in ("value", "unit", "ms_per_step", "steps", "warmup", "weight_stream_gbs",
-                                              "weight_stream_frac", "e2e", "roofline", "config", "gpu_launches")}
+                                              "weight_stream_frac", "e2e", "roofline", "config", "gpu_launches",
+                                              "prefill") if k in sub}
         line["batch1"]["workload"] = BATCH1_WORKLOAD
         line["batch1"]["clocks"] = clk
     if rank == 0:

@@ -108,6 +108,19 @@ struct spm_session {
     float** ep_peer_y = nullptr;       // device [2][world]
     uint32_t** ep_peer_flag = nullptr; // device [2][world]
     std::vector<void*> ep_mapped;      // peers' regions opened by IPC
+    // Data-parallel attention (world > 1): rank r runs the attention block
+    // of its own clients; the area after the expert buffers in ep_region
+    // holds the all-gather flags [2][64] and the greedy-pick flags [64]
+    // (dp_flags), then this session's greedy picks, states and sums of
+    // squares, which the other ranks write into.
+    size_t dp_off = 0, dp_states_bytes = 0;
+    uint32_t* dp_flags = nullptr;
+    uint32_t* ep_done2 = nullptr;       // CTA counter of the o launch
+    float** dp_peer_states = nullptr;   // device [world]: every rank's states
+    float** dp_peer_sumsq = nullptr;    // device [world]: every rank's second sums-of-squares array
+    uint32_t** dp_peer_flag = nullptr;  // device [2][world]: this rank's all-gather flag on every rank
+    uint32_t** dp_peer_argmax = nullptr;  // device [world]
+    uint32_t** dp_peer_gflag = nullptr;   // device [world]: every rank's greedy-pick flags
     bool ep_ready = false;
     uint64_t wait_ns = 1000000000ull;  // limit of the device waits on other ranks (spm_session_set_wait_limit)
     std::vector<int> lens;
@@ -747,6 +760,10 @@ void enqueue_step(spm_session* s, int n) {
     const int ff = int(c.intermediate);
     const StreamDesc& E = m->streams[m->embed];
     float* part[2] = {s->sumsq, s->sumsq + kMaxParts * 8};
+    // data-parallel attention: this rank's clients f0..f0+nl-1 run the
+    // attention block; the routed feed-forward sees every client
+    const bool dp = m->world > 1;
+    const int nl = dp ? n / m->world : n, f0 = dp ? m->rank * nl : 0;
     // Every launch of the step goes through timed(): with the profile on, an
     // event pair brackets it (kind, layer, the stream it reads and its bytes
     // are kept for the record).
@@ -769,10 +786,11 @@ void enqueue_step(spm_session* s, int n) {
     };
     auto qbytes = [&](int idx) { return m->streams[idx].pk.quant_bytes; };
     timed(SPM_KERNEL_OTHER, -1, -1, 0, [&] {
-        CUDA_OK(launch_embed(E.pk.dtype, m->tiles(m->embed), E.pk, s->tokens, n, s->states, part[0], st, false));
+        CUDA_OK(launch_embed(E.pk.dtype, m->tiles(m->embed), E.pk, s->tokens + f0, nl, s->states + size_t(f0) * d,
+                             part[0], st, false, f0));
         return 0;
     });
-    int parts = n;
+    int parts = nl;
     auto norm_in = [&](GemvLaunch& g, int64_t gain, int which) {
         g.gain = m->gains + gain;
         g.sumsq = part[which];
@@ -781,8 +799,9 @@ void enqueue_step(spm_session* s, int n) {
     };
     for (uint32_t l = 0; l < c.layers; l++) {
         const LayerIdx& L = m->layers[l];
-        GemvLaunch g = gemv_base(m, L.q, s->states, n);
+        GemvLaunch g = gemv_base(m, L.q, s->states + size_t(f0) * d, nl);
         g.status = s->status;
+        g.c0 = f0;
         norm_in(g, L.attn_norm, 0);
         add_job(g, m, L.q, nullptr, s->q, qw, nullptr, 0, EPI_STORE);
         add_job(g, m, L.k, nullptr, s->k, kvw, nullptr, 0, EPI_STORE);
@@ -790,7 +809,7 @@ void enqueue_step(spm_session* s, int n) {
         gemv(g, L.q, SPM_GEMV_DENSE, int(l), qbytes(L.q) + qbytes(L.k) + qbytes(L.v));
         AttnParams P{};
         P.q = s->q; P.k = s->k; P.v = s->v; P.out = s->attn;
-        P.kcache = s->kc; P.vcache = s->vc; P.pos = s->pos; P.rope = s->rope;
+        P.kcache = s->kc; P.vcache = s->vc; P.pos = s->pos + f0; P.rope = s->rope; P.cache_client = f0;
         P.scratch = s->attn_scratch; P.counters = s->attn_counters;
         P.q_norm = L.q_norm >= 0 ? m->gains + L.q_norm : nullptr;
         P.k_norm = L.k_norm >= 0 ? m->gains + L.k_norm : nullptr;
@@ -798,13 +817,29 @@ void enqueue_step(spm_session* s, int n) {
         P.heads = int(c.heads); P.kv_heads = int(c.kv_heads); P.head_dim = int(c.head_dim);
         P.family = int(c.family); P.eps = c.eps; P.status = s->status;
         timed(SPM_KERNEL_ATTENTION, int(l), -1, 0, [&] {
-            CUDA_OK(launch_attention(P, n, st, pdl));
+            CUDA_OK(launch_attention(P, nl, st, pdl));
             return 0;
         });
-        GemvLaunch go = gemv_base(m, L.o, s->attn, n);
+        GemvLaunch go = gemv_base(m, L.o, s->attn, nl);
         go.status = s->status;
         go.sumsq_out = part[1];
-        add_job(go, m, L.o, nullptr, s->states, d, s->states, d, EPI_ADD);
+        go.c0 = f0;
+        if (dp) {
+            // rows and sums of squares of this rank's clients to every rank,
+            // then this rank's all-gather flag up on every rank
+            if (!s->ep_ready) fail(SPM_E_ARG, "expert parallel session: call spm_session_ep_connect first");
+            go.ep_dense = 1;
+            go.world = m->world;
+            go.rank = m->rank;
+            go.ep_peer_y = s->dp_peer_states;
+            go.ep_peer_sumsq = s->dp_peer_sumsq;
+            go.ep_peer_flag = s->dp_peer_flag;
+            go.ep_done = s->ep_done2;
+            go.ep_step = s->step;
+            go.ep_layers = int32_t(c.layers);
+            go.ep_layer = int32_t(l);
+        }
+        add_job(go, m, L.o, nullptr, s->states + size_t(f0) * d, d, s->states + size_t(f0) * d, d, EPI_ADD);
         parts = gemv(go, L.o, SPM_GEMV_DENSE, int(l), qbytes(L.o));
         if (is_moe(c)) {
             // routed feed-forward (spm-granite-moe/src/layout.rs:188-333)
@@ -812,6 +847,15 @@ void enqueue_step(spm_session* s, int n) {
             GemvLaunch gr = gemv_base(m, L.router, s->states, n);
             gr.status = s->status;
             norm_in(gr, L.ffn_norm, 1);
+            if (dp) {
+                // every rank's rows of this layer must be in place
+                gr.world = m->world;
+                gr.ep_wait_flags = s->dp_flags;
+                gr.ep_step = s->step;
+                gr.ep_layers = int32_t(c.layers);
+                gr.ep_layer = int32_t(l);
+                gr.wait_ns = s->wait_ns;
+            }
             add_job(gr, m, L.router, nullptr, s->moe_logits, E, nullptr, 0, EPI_STORE);
             gemv(gr, L.router, SPM_GEMV_ROUTER, int(l), qbytes(L.router));
             MoePlan* plan = s->plans + l;
@@ -820,8 +864,10 @@ void enqueue_step(spm_session* s, int n) {
                                      plan, st, pdl));
                 return 0;
             });
-            // active experts of this rank, at most: the expert launches split
-            // each over enough chunks to give every SM two CTAs
+            // active experts of this rank, at most; the expert launches fill
+            // the SMs once and split the active experts over them (at least
+            // the chunks that would give every SM two CTAs with all possible
+            // experts active, which bounds a CTA's tiles)
             const int local_max = std::min(s->moe_max_active, (E + m->world - 1) / m->world);
             const int chunks_gu = std::max(1, std::min(eff / kTileRows, (2 * m->sms + local_max - 1) / local_max));
             GemvLaunch ge = gemv_base(m, L.gate_exps, s->states, kMoeMaxClients);
@@ -866,10 +912,11 @@ void enqueue_step(spm_session* s, int n) {
             gx.xmode = 1;
             gemv(gx, L.down_exps, SPM_GEMV_EXPERT_DOWN, int(l), 0);
             timed(SPM_KERNEL_COMBINE, int(l), -1, 0, [&] {
-                CUDA_OK(launch_combine(plan, outs, d, s->states, d, n, K, part[0], m->world > 1 ? &ex : nullptr, st, pdl));
+                CUDA_OK(launch_combine(plan, outs, d, s->states, d, nl, K, part[0], m->world > 1 ? &ex : nullptr, st, pdl,
+                                       f0));
                 return 0;
             });
-            parts = combine_parts(d, n);
+            parts = combine_parts(d, nl);
             continue;
         }
         GemvLaunch gu = gemv_base(m, L.gate, s->states, n);
@@ -883,15 +930,22 @@ void enqueue_step(spm_session* s, int n) {
         add_job(gd, m, L.down, nullptr, s->states, d, s->states, d, EPI_ADD);
         parts = gemv(gd, L.down, SPM_GEMV_DENSE, int(l), qbytes(L.down));
     }
-    GemvLaunch gh = gemv_base(m, m->head, s->states, n);
+    GemvLaunch gh = gemv_base(m, m->head, s->states + size_t(f0) * d, nl);
     gh.status = s->status;
+    gh.c0 = f0;
     norm_in(gh, m->output_norm, 0);
-    add_job(gh, m, m->head, nullptr, s->logits, int(c.vocab), nullptr, 0, EPI_STORE);
+    add_job(gh, m, m->head, nullptr, s->logits + size_t(f0) * c.vocab, int(c.vocab), nullptr, 0, EPI_STORE);
     gemv(gh, m->head, SPM_GEMV_HEAD, -1, qbytes(m->head));
     timed(SPM_KERNEL_OTHER, -1, -1, 0, [&] {
-        CUDA_OK(launch_argmax(s->logits, n, int(c.vocab), s->argmax, st, pdl));
+        CUDA_OK(launch_argmax(s->logits + size_t(f0) * c.vocab, nl, int(c.vocab), s->argmax + f0, st, pdl));
         return 0;
     });
+    if (dp)
+        timed(SPM_KERNEL_OTHER, -1, -1, 0, [&] {
+            CUDA_OK(launch_ep_gather(s->argmax, s->dp_peer_argmax, s->dp_peer_gflag, s->dp_flags + 128, s->step, f0,
+                                     nl, m->world, m->rank, s->status, s->wait_ns, st, pdl));
+            return 0;
+        });
     timed(SPM_KERNEL_OTHER, -1, -1, 0, [&] {
         CUDA_OK(launch_advance(s->pos, n, s->step, st, pdl));
         return 0;
@@ -945,6 +999,7 @@ constexpr int kMaxBatch = 8;
 void step(spm_session* s, int n) {
     if (n < 1 || n > s->max_clients) fail(SPM_E_ARG, "client count out of range");
     if (n > kMaxBatch) fail(SPM_E_ARG, "at most 8 clients share one sweep");
+    if (n % s->m->world) fail(SPM_E_ARG, "expert parallel: the client count must be a multiple of the ranks");
     for (int i = 0; i < n; i++)
         if (s->lens[i] >= s->context) fail(SPM_E_CONTEXT, "context " + std::to_string(s->context) + " exhausted");
     if (s->graphs && !s->prof) {
@@ -1460,7 +1515,6 @@ spm_status spm_session_create(spm_model* m, int32_t max_clients, int32_t max_con
         CUDA_OK(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
         s->kc = s->alloc<float>(n * c.layers * size_t(max_context) * kvw);
         s->vc = s->alloc<float>(n * c.layers * size_t(max_context) * kvw);
-        s->states = s->alloc<float>(n * d);
         s->normed = s->alloc<float>(n * d);
         s->q = s->alloc<float>(n * qw);
         s->k = s->alloc<float>(n * kvw);
@@ -1470,8 +1524,6 @@ spm_status spm_session_create(spm_model* m, int32_t max_clients, int32_t max_con
         s->logits = s->alloc<float>(n * c.vocab);
         s->pos = s->alloc<int32_t>(n);
         s->tokens = s->alloc<uint32_t>(n);
-        s->argmax = s->alloc<uint32_t>(n);
-        s->sumsq = s->alloc<float>(2 * size_t(kMaxParts) * 8);
         s->status = s->alloc<int32_t>(1);
         const size_t chunks = (size_t(max_context) + kAttnMinChunk - 1) / kAttnMinChunk;
         const size_t group = c.heads / c.kv_heads;
@@ -1492,11 +1544,34 @@ spm_status spm_session_create(spm_model* m, int32_t max_clients, int32_t max_con
             s->moe_out = s->alloc<float>(size_t(s->moe_max_active) * kMoeMaxClients * c.hidden);
             if (m->world > 1) {
                 s->ep_xbytes = (size_t(s->moe_max_active) * kMoeMaxClients * c.hidden * sizeof(float) + 255) & ~size_t(255);
-                s->ep_region = s->alloc<uint8_t>(512 + 2 * s->ep_xbytes);
+                // after the exchange: flags [2][64] + [64], greedy picks,
+                // states, sums of squares (every rank writes into them)
+                s->dp_off = 512 + 2 * s->ep_xbytes;
+                const size_t pick_off = 1024, states_off = pick_off + ((n * sizeof(uint32_t) + 255) & ~size_t(255));
+                s->dp_states_bytes = (n * d * sizeof(float) + 255) & ~size_t(255);
+                const size_t sumsq_off = states_off + s->dp_states_bytes;
+                const size_t dp_bytes = sumsq_off + 2 * size_t(kMaxParts) * 8 * sizeof(float);
+                s->ep_region = s->alloc<uint8_t>(s->dp_off + dp_bytes);
+                uint8_t* dp = s->ep_region + s->dp_off;
+                s->dp_flags = reinterpret_cast<uint32_t*>(dp);
+                s->argmax = reinterpret_cast<uint32_t*>(dp + pick_off);
+                s->states = reinterpret_cast<float*>(dp + states_off);
+                s->sumsq = reinterpret_cast<float*>(dp + sumsq_off);
                 s->ep_done = s->alloc<uint32_t>(1);
+                s->ep_done2 = s->alloc<uint32_t>(1);
                 s->ep_peer_y = s->alloc<float*>(2 * size_t(m->world));
                 s->ep_peer_flag = s->alloc<uint32_t*>(2 * size_t(m->world));
+                s->dp_peer_states = s->alloc<float*>(m->world);
+                s->dp_peer_sumsq = s->alloc<float*>(m->world);
+                s->dp_peer_flag = s->alloc<uint32_t*>(2 * size_t(m->world));
+                s->dp_peer_argmax = s->alloc<uint32_t*>(m->world);
+                s->dp_peer_gflag = s->alloc<uint32_t*>(m->world);
             }
+        }
+        if (!s->states) {
+            s->states = s->alloc<float>(n * d);
+            s->argmax = s->alloc<uint32_t>(n);
+            s->sumsq = s->alloc<float>(2 * size_t(kMaxParts) * 8);
         }
         s->step = s->alloc<uint32_t>(1);
         auto table = rope_table(c, max_context);
@@ -1671,6 +1746,25 @@ spm_status spm_session_ep_connect(spm_session* s, const void* handles) {
             }
         CUDA_OK(cudaMemcpy(s->ep_peer_y, y.data(), y.size() * sizeof(float*), cudaMemcpyHostToDevice));
         CUDA_OK(cudaMemcpy(s->ep_peer_flag, f.data(), f.size() * sizeof(uint32_t*), cudaMemcpyHostToDevice));
+        // data-parallel attention: the same offsets in every rank's region
+        const uint8_t* own_base = s->ep_region;
+        auto at = [&](int p, const void* own_ptr) {
+            return base[p] + (static_cast<const uint8_t*>(own_ptr) - own_base);
+        };
+        std::vector<float*> st(world), sq(world);
+        std::vector<uint32_t*> df(2 * size_t(world)), am(world), gf(world);
+        for (int p = 0; p < world; p++) {
+            st[p] = reinterpret_cast<float*>(at(p, s->states));
+            sq[p] = reinterpret_cast<float*>(at(p, s->sumsq + kMaxParts * 8));
+            am[p] = reinterpret_cast<uint32_t*>(at(p, s->argmax));
+            gf[p] = reinterpret_cast<uint32_t*>(at(p, s->dp_flags + 128));
+            for (int k = 0; k < 2; k++) df[k * world + p] = reinterpret_cast<uint32_t*>(at(p, s->dp_flags)) + k * 64 + rank;
+        }
+        CUDA_OK(cudaMemcpy(s->dp_peer_states, st.data(), st.size() * sizeof(float*), cudaMemcpyHostToDevice));
+        CUDA_OK(cudaMemcpy(s->dp_peer_sumsq, sq.data(), sq.size() * sizeof(float*), cudaMemcpyHostToDevice));
+        CUDA_OK(cudaMemcpy(s->dp_peer_flag, df.data(), df.size() * sizeof(uint32_t*), cudaMemcpyHostToDevice));
+        CUDA_OK(cudaMemcpy(s->dp_peer_argmax, am.data(), am.size() * sizeof(uint32_t*), cudaMemcpyHostToDevice));
+        CUDA_OK(cudaMemcpy(s->dp_peer_gflag, gf.data(), gf.size() * sizeof(uint32_t*), cudaMemcpyHostToDevice));
         s->ep_ready = true;
     });
 }

@@ -45,8 +45,10 @@ GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms, int per_fixe
     // work items: tiles, or pairs of tiles for the tensor-core loop (whose
     // warps take whole units of a slot instead of lanes taking units)
     const bool pair = L.tc && !dual;
-    const uint32_t work = pair ? (L.total_tiles + 1) / 2 : L.total_tiles;
-    if (per_fixed > 0 && pair) per_fixed = (per_fixed + 1) / 2;
+    // tiles of rows per work item (slot): tc2 four (two gate/up pairs), pair two
+    const uint32_t tps = L.tc2 ? (dual ? 2u : 4u) : pair ? 2u : 1u;
+    const uint32_t work = (L.total_tiles + tps - 1) / tps;
+    if (per_fixed > 0 && tps > 1) per_fixed = int((uint32_t(per_fixed) + tps - 1) / tps);
     GemvGeometry best{};
     double best_score = -1.0;
     for (int per_sm = 2; per_sm >= 1; per_sm--) {
@@ -60,7 +62,8 @@ GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms, int per_fixe
         }
         for (int gw = 1; gw <= Wmax; gw *= 2) {
             // at most four units per lane (tensor cores: 32 units per warp)
-            const uint32_t lanes = L.tc ? uint32_t(gw) : 32u * gw, most = L.tc ? 32u : 4u;
+            const bool warps_take_units = L.tc || L.tc2;
+            const uint32_t lanes = warps_take_units ? uint32_t(gw) : 32u * gw, most = warps_take_units ? 32u : 4u;
             if ((U + lanes - 1) / lanes > most && gw < Wmax) continue;
             const double busy = std::min(1.0, double(U) / double(lanes));
             for (int G = Wmax / gw; G >= 1; G--) {
@@ -91,6 +94,7 @@ GemvGeometry gemv_geometry(const GemvLaunch& L, bool dual, int sms, int per_fixe
 static void prepare(GemvLaunch& L, uint32_t dtype) {
     L.xrec = unit_bytes(int(dtype));
     L.tc = use_tc(int(dtype), L.n) && !L.plan ? 1 : 0;
+    L.tc2 = use_tc2(int(dtype), L.n) ? 1 : 0;
 }
 
 // Geometry with the grid capped at the CTAs that can be resident at once
@@ -109,9 +113,12 @@ static cudaError_t launch_one(uint32_t dtype, GemvLaunch L, int sms, cudaStream_
     prepare(L, dtype);
     GemvGeometry g;
     if (L.plan) {
-        // expert mode: a CTA owns 1/expert_chunks of one active expert's tiles
+        // expert mode: a CTA owns 1/expert_chunks of one active expert's
+        // tiles at most; the grid fills the SMs once (the kernel splits the
+        // active experts over it), every possible active expert has a CTA
         g = gemv_geometry(L, dual, sms, int((L.expert_tiles + L.expert_chunks - 1) / L.expert_chunks));
-        g.grid = L.expert_max * L.expert_chunks;
+        const int occ = occupancy(dtype, L, dual, g.warps * 32, g.smem);
+        g.grid = std::max(L.expert_max, std::max(1, occ) * sms);
     } else {
         g = geometry_resident(dtype, L, dual, sms);
     }
@@ -140,7 +147,7 @@ cudaError_t launch_gemv(uint32_t dtype, GemvLaunch L, int sms, cudaStream_t s, b
     prepare(one, dtype);
     if (smem_bytes(one, dual, 1, kMaxWarps) > kSmemMax) return cudaErrorInvalidValue;
     const bool fits = smem_bytes(L, dual, 1, kMaxWarps) <= kSmemMax;
-    if (L.plan && !fits) return cudaErrorInvalidValue;
+    if ((L.plan || L.ep_done) && !fits) return cudaErrorInvalidValue;  // one launch raises the flag
     if (!fits) {
         // The clients' activations do not fit beside one tile: one launch per
         // half of the clients (the weights are read twice), on a common grid

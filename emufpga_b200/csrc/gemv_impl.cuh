@@ -54,7 +54,9 @@ constexpr int kMaxWarps = 16;             // warps of a CTA that has an SM to it
 constexpr int kPairWarps = 8;             // warps of each of two CTAs sharing an SM
 constexpr int kMaxSlots = 16;
 constexpr size_t kSmemMax = 200 * 1024;   // dynamic shared memory of a CTA alone on its SM
-constexpr size_t kHalfSm = 100 * 1024;    // dynamic shared memory of each of two CTAs per SM
+// Dynamic shared memory of each of two CTAs per SM: half of the SM's 228 KB,
+// less each CTA's static arrays (5.25 KB) and the 1 KB the system reserves.
+constexpr size_t kHalfSm = 107 * 1024;
 constexpr int kAuxPrefetch = 1024;        // residual values prefetched per CTA, at most
 // Staged activations of the integer block types: per client one 112-byte
 // record per 32-value unit -- three planes of 32 signed 8-bit digits (8 words
@@ -78,6 +80,16 @@ inline __host__ __device__ constexpr uint32_t unit_bytes(int enc) { return enc =
 // values, the per-sub-block fp32 work that the tensor-core loop keeps on the
 // CUDA cores makes it no faster than the dp4a loop even with eight clients.)
 inline __host__ __device__ constexpr bool use_tc(int enc, int n) { return enc == SPM_Q8_0 && n >= 4; }
+// The K-quants with four or more clients (dense and expert launches) take the
+// other tensor-core loop (gemv_tc.cuh: codes as the A operand, sixteen rows
+// per product, the clients as the eight columns); a slot then holds four
+// tiles, or two gate and two up tiles.
+// Tiles of a TC2 slot start kTc2Skew bytes after the previous one ends, so
+// that rows of different tiles read by one instruction fall on different banks.
+constexpr uint32_t kTc2Skew = 64;
+inline __host__ __device__ constexpr bool use_tc2(int enc, int n) {
+    return (enc == SPM_Q5_K || enc == SPM_Q6_K || enc == SPM_Q2_K) && n >= 4;
+}
 // Bytes between two clients' records.  The tensor-core loop reads 8 bytes of
 // eight clients at once; a stride of 32 mod 128 bytes keeps them on
 // different banks.
@@ -439,9 +451,9 @@ struct Shape {
 // of partial sums per slot, warp of the group and matrix.
 inline size_t smem_bytes(const GemvLaunch& L, bool dual, int slots, int group_warps) {
     // a tensor-core slot holds eight rows: two tiles, or one gate/up pair
-    const size_t slot = size_t(L.tile_bytes) * (dual || L.tc ? 2 : 1);
-    const size_t xb = size_t(L.n) * client_stride(L.xrec, L.tc != 0, L.cols / 32);
-    const size_t rec = L.tc ? 256 : (dual ? 256 : 128);  // partials per slot and warp
+    const size_t slot = L.tc2 ? 4 * (size_t(L.tile_bytes) + kTc2Skew) : size_t(L.tile_bytes) * (dual || L.tc ? 2 : 1);
+    const size_t xb = size_t(L.n) * client_stride(L.xrec, L.tc != 0 || L.tc2 != 0, L.cols / 32);
+    const size_t rec = L.tc2 ? 512 : L.tc ? 256 : (dual ? 256 : 128);  // partials per slot and warp
     const size_t pb = group_warps > 1 ? size_t(slots) * group_warps * rec : 0;
     return slot * size_t(slots) + xb + pb;
 }
@@ -455,6 +467,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     constexpr int VR = S::VR, PASSES = S::PASSES, M = S::M, NCP = S::NCP, V = S::V, SH = S::SH;
     constexpr bool TC = TCX && use_tc(ENC, NC);
     constexpr bool PAIR = TC && !DUAL;  // slot = two consecutive tiles
+    constexpr bool TC2 = TCX && use_tc2(ENC, NC);
+    // tiles of rows per slot: TC2 four (two gate/up pairs), PAIR two, else one
+    constexpr uint32_t TPS = TC2 ? (DUAL ? 2u : 4u) : PAIR ? 2u : 1u;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t full[kMaxSlots], ready[kMaxSlots];
     __shared__ float nscale[8];
@@ -472,8 +487,13 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     if (L.plan) {
         // expert mode: the plan comes from the previous kernel
         pdl_wait();
-        // CTA b works on chunk b % chunks of this rank's active expert b / chunks
-        const int la = int(blockIdx.x) / L.expert_chunks, chunk = int(blockIdx.x) % L.expert_chunks;
+        // The grid is one wave of CTAs; with nl active experts on this rank
+        // each expert's tiles split into C = grid / nl chunks (at least
+        // expert_chunks, at most one tile each), and CTA b works on chunk
+        // b % C of active expert b / C.
+        const int nl = L.plan->nlocal;
+        const int C = max(L.expert_chunks, min(int(L.expert_tiles), int(gridDim.x) / max(nl, 1)));
+        const int la = int(blockIdx.x) / C, chunk = int(blockIdx.x) % C;
         if (la >= L.plan->nlocal) {
             pdl_trigger();
             if (L.ep_done && threadIdx.x == 0) ep_arrive(L);
@@ -484,11 +504,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
             const uint32_t E = *L.ep_step * uint32_t(L.ep_layers) + uint32_t(L.ep_layer) + 1;
             ep_y[threadIdx.x] = L.ep_peer_y[(E & 1u) * L.world + threadIdx.x];
         }
-        const uint32_t e = uint32_t(L.plan->expert[a]), Te = L.expert_tiles, C = uint32_t(L.expert_chunks);
+        const uint32_t e = uint32_t(L.plan->expert[a]), Te = L.expert_tiles;
         rbase = e * Te * kTileRows;
         rlim = Te * kTileRows;
-        t0 = e * Te + uint32_t(uint64_t(Te) * chunk / C);
-        t1 = e * Te + uint32_t(uint64_t(Te) * (chunk + 1) / C);
+        t0 = e * Te + uint32_t(uint64_t(Te) * chunk / uint32_t(C));
+        t1 = e * Te + uint32_t(uint64_t(Te) * (chunk + 1) / uint32_t(C));
         n_act = L.plan->ntok[a];
         if (threadIdx.x < 8) {
             const int c = int(threadIdx.x);
@@ -499,10 +519,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
         }
     } else {
         const uint32_t T = L.total_tiles, Gd = gridDim.x;
-        if (PAIR) {  // whole pairs per CTA
-            const uint32_t P = (T + 1) / 2;
-            t0 = 2 * uint32_t(uint64_t(P) * blockIdx.x / Gd);
-            t1 = min(T, 2 * uint32_t(uint64_t(P) * (blockIdx.x + 1) / Gd));
+        if (TPS > 1) {  // whole slots per CTA
+            const uint32_t P = (T + TPS - 1) / TPS;
+            t0 = TPS * uint32_t(uint64_t(P) * blockIdx.x / Gd);
+            t1 = min(T, TPS * uint32_t(uint64_t(P) * (blockIdx.x + 1) / Gd));
         } else {
             t0 = uint32_t(uint64_t(T) * blockIdx.x / Gd);
             t1 = uint32_t(uint64_t(T) * (blockIdx.x + 1) / Gd);
@@ -512,20 +532,38 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
             yrows[threadIdx.x] = int(threadIdx.x);
             srows[threadIdx.x] = L.c0 + int(threadIdx.x);
         }
+        // data-parallel attention: every rank's copy of the output rows
+        // (one job; ep_peer_y[p] is rank p's output base, rows from client c0)
+        if (L.ep_dense && threadIdx.x < uint32_t(L.world))
+            ep_y[threadIdx.x] = L.ep_peer_y[threadIdx.x] + size_t(L.c0) * L.job[0].y_stride;
     }
-    const uint32_t nt = PAIR ? (t1 - t0 + 1) / 2 : t1 - t0, NS = uint32_t(L.slots);  // work items (slots to fill)
+    const uint32_t nt = (t1 - t0 + TPS - 1) / TPS, NS = uint32_t(L.slots);  // work items (slots to fill)
     // Slot s belongs to group s % G alone (NS is a multiple of G), so each
     // group waits for its slots' phases in order and refills them itself.
     if (NS % uint32_t(G) != 0 || NS > uint32_t(kMaxSlots) || W * 32 != int(blockDim.x) || G * gw != W) {
         if (threadIdx.x == 0) flag(L.status, 3);
         return;
     }
-    const uint32_t tile_bytes = L.tile_bytes, slot_bytes = tile_bytes * (DUAL || PAIR ? 2u : 1u);
+    const uint32_t tile_bytes = L.tile_bytes;
+    const uint32_t tile_step = TC2 ? tile_bytes + kTc2Skew : tile_bytes;  // distance between a slot's tiles
+    const uint32_t slot_bytes = TC2 ? 4u * tile_step : tile_bytes * (DUAL || PAIR ? 2u : 1u);
     constexpr uint32_t XREC = unit_bytes(ENC);
-    const uint32_t U = L.cols >> 5, cstride = client_stride(XREC, TC, U);
+    const uint32_t U = L.cols >> 5, cstride = client_stride(XREC, TC || TC2, U);
     const uint32_t xoff = NS * slot_bytes, poff = xoff + NC * cstride;  // activations, group partials
     auto issue = [&](uint32_t i) {
         const uint32_t s = i % NS;
+        if (TC2) {
+            // tiles g.. of the slot (gate/up: the gate tiles, then the up tiles two further on)
+            const uint32_t g = t0 + TPS * i, h = min(TPS, t1 - g);
+            mbar_expect_tx(&full[s], tile_bytes * h * (DUAL ? 2u : 1u));
+            for (uint32_t k = 0; k < h; k++) {
+                const GemvJob& J = pick(jobs, L.njobs, g + k);
+                const size_t off = size_t(g + k - J.tile_begin) * tile_bytes;
+                bulk_g2s(smem + size_t(s) * slot_bytes + k * tile_step, J.a + off, tile_bytes, &full[s]);
+                if (DUAL) bulk_g2s(smem + size_t(s) * slot_bytes + (2 + k) * tile_step, J.b + off, tile_bytes, &full[s]);
+            }
+            return;
+        }
         if (PAIR) {
             const uint32_t g = t0 + 2 * i, h = g + 1 < t1 ? 2u : 1u;
             mbar_expect_tx(&full[s], tile_bytes * h);
@@ -557,6 +595,22 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
         pdl_trigger();
     }
     pdl_wait();  // activations and norm partials come from the previous kernel
+    if (L.ep_wait_flags) {
+        // the other ranks' rows and sums of squares of this layer must be in place
+        const uint32_t E = *L.ep_step * uint32_t(L.ep_layers) + uint32_t(L.ep_layer) + 1;
+        if (threadIdx.x < uint32_t(L.world)) {
+            const uint32_t* f = L.ep_wait_flags + (E & 1u) * 64 + threadIdx.x;
+            if (ld_acquire_sys(f) != E) {
+                const uint64_t w0 = now_ns();
+                while (ld_acquire_sys(f) != E)
+                    if (now_ns() - w0 > L.wait_ns) {
+                        flag(L.status, 8);
+                        break;
+                    }
+            }
+        }
+        __syncthreads();
+    }
 
     // ---- prologue: norm scales, staged activations, residual prefetch ----
     for (int cw = warp; L.gain && cw < NC; cw += W) {
@@ -653,7 +707,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
                 uint8_t* rec = smem + xoff + c * cstride + u * XREC;
 #pragma unroll
                 for (int j = 0; j < 3; j++) {
-                    if (TC) {  // word w = 4*half + k at (w % 4) * 8 + (w / 4) * 4
+                    if (TC || TC2) {  // word w = 4*half + k at (w % 4) * 8 + (w / 4) * 4
 #pragma unroll
                         for (int k = 0; k < 4; k++) *reinterpret_cast<uint32_t*>(rec + j * 32 + k * 8 + half * 4) = dw[j][k];
                     } else {
@@ -695,7 +749,90 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
     float* part = reinterpret_cast<float*>(smem + poff);  // [NS][gw][M][32]
     float sq = 0.f;
     const uint32_t B = L.cols >> 8;
-    if constexpr (TC) {
+    float sq2[2] = {0.f, 0.f};  // TC2: sums of squares of the lane's two clients
+    if constexpr (TC2) {
+        // lane (g, t): A rows g (slot row g, or gate row g) and g + 8 (slot
+        // row g + 8, or up row g); outputs for clients 2t and 2t + 1
+        const int g = lane >> 2, t = lane & 3;
+        const uint32_t xg = smem_s + xoff + uint32_t(g < NC ? g : 0) * cstride;
+        const uint32_t xc[2] = {smem_s + xoff + uint32_t(min(2 * t, NC - 1)) * cstride,
+                                smem_s + xoff + uint32_t(min(2 * t + 1, NC - 1)) * cstride};
+        for (uint32_t i = uint32_t(grp); i < nt; i += uint32_t(G)) {
+            const uint32_t s = i % NS, par = (i / NS) & 1;
+            if (!mbar_wait(&full[s], par)) {
+                flag(L.status, 2);
+                break;
+            }
+            const uint32_t tb = smem_s + s * slot_bytes;
+            const uint32_t gt = t0 + TPS * i;  // the slot's first tile
+            const Tc2Row ra{tb + uint32_t(g >> 2) * tile_step, uint32_t(g & 3)};
+            const Tc2Row rb{tb + (2u + uint32_t(g >> 2)) * tile_step, uint32_t(g & 3)};
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+            for (uint32_t u = uint32_t(wig); u < U; u += uint32_t(gw)) tc2_unit<ENC>(ra, rb, u, t, xg, xc, L, acc);
+            bool fin = true;
+            if (gw == 1) {
+                // this warp alone read the slot: refill it
+                __syncwarp();
+                if (lane == 0 && i + NS < nt) {
+                    fence_proxy_async();
+                    issue(i + NS);
+                }
+            } else {
+                // the group's first warp adds the warps' totals in warp order
+                float* pr = part + (s * gw + wig) * 128 + lane * 4;
+#pragma unroll
+                for (int k = 0; k < 4; k++) pr[k] = acc[k];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&ready[s]);
+                fin = wig == 0;
+                if (fin) {
+                    if (!mbar_wait(&ready[s], par)) {
+                        flag(L.status, 4);
+                        break;
+                    }
+#pragma unroll
+                    for (int k = 0; k < 4; k++) acc[k] = 0.f;
+                    for (int w = 0; w < gw; w++) {
+                        const float* q = part + (s * gw + w) * 128 + lane * 4;
+#pragma unroll
+                        for (int k = 0; k < 4; k++) acc[k] += q[k];
+                    }
+                    __syncwarp();
+                    if (lane == 0 && i + NS < nt) {
+                        fence_proxy_async();
+                        issue(i + NS);
+                    }
+                }
+            }
+            if (fin) {
+                // (row g, row g + 8) x (clients 2t, 2t + 1); gate/up: row g's SwiGLU for both clients
+#pragma unroll
+                for (int k = 0; k < (DUAL ? 2 : 4); k++) {
+                    const int c = 2 * t + (k & 1);
+                    const uint32_t sr = DUAL ? uint32_t(g) : uint32_t(g + 8 * (k >> 1));  // slot row
+                    const uint32_t tile = gt + (sr >> 2), e = sr & 3;
+                    if (tile >= t1 || c >= n_act) continue;
+                    const GemvJob& J = pick(jobs, L.njobs, tile);
+                    const uint32_t grow = (tile - J.tile_begin) * kTileRows + e;
+                    const uint32_t row = grow - rbase;
+                    if (grow >= J.rows || row >= rlim) continue;
+                    const float fs = L.gain ? nscale[c] : 1.0f;
+                    float r = acc[k] * fs;
+                    if constexpr (DUAL) r = silu_mul(r, acc[k + 2] * fs);
+                    if (J.epi == EPI_ADD)
+                        r = (aux_pre ? auxs[((tile - t0) * kTileRows + e) * NC + c]
+                                     : J.aux[size_t(yrows[c]) * J.aux_stride + row]) + r;
+                    if (L.ep_peer_y) {
+                        for (int p = 0; p < L.world; p++) ep_y[p][size_t(yrows[c]) * J.y_stride + row] = r;
+                    } else {
+                        J.y[size_t(yrows[c]) * J.y_stride + row] = r;
+                    }
+                    sq2[k & 1] = fmaf(r, r, sq2[k & 1]);
+                }
+            }
+        }
+    } else if constexpr (TC) {
         // lane (g, t): client g; codes of slot row g; totals of slot rows 2t, 2t+1
         const int g = lane >> 2, t = lane & 3;
         TcLane z;
@@ -880,7 +1017,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
         // per-CTA sum of squares of the rows written, reduced in a fixed order
 #pragma unroll
         for (int c = 0; c < NC; c++) {
-            const float t = warp_sum(fc == c ? sq : 0.f);
+            const int t2 = 2 * (lane & 3);
+            const float mine = TC2 ? (c == t2 ? sq2[0] : 0.f) + (c == t2 + 1 ? sq2[1] : 0.f) : (fc == c ? sq : 0.f);
+            const float t = warp_sum(mine);
             if (lane == 0) sqw[warp][c] = t;
         }
         __syncthreads();
@@ -888,6 +1027,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_stream(const __grid_co
             float t = 0.f;
             for (int w = 0; w < W; w++) t += sqw[w][threadIdx.x];
             L.sumsq_out[blockIdx.x * 8 + L.c0 + threadIdx.x] = t;
+            if (L.ep_peer_sumsq)
+                for (int p = 0; p < L.world; p++) L.ep_peer_sumsq[p][blockIdx.x * 8 + L.c0 + threadIdx.x] = t;
         }
     }
     if (L.ep_done) {
@@ -937,15 +1078,15 @@ cudaError_t launch_t(const GemvLaunch& L, int grid, int threads, size_t smem, cu
 // launches never do.
 template <int ENC, int NC, bool DUAL>
 cudaError_t launch_n(const GemvLaunch& L, int grid, int threads, size_t smem, cudaStream_t s, bool pdl) {
-    if constexpr (use_tc(ENC, NC))
-        if (L.tc) return launch_t<ENC, NC, DUAL, true>(L, grid, threads, smem, s, pdl);
+    if constexpr (use_tc(ENC, NC) || use_tc2(ENC, NC))
+        if (L.tc || L.tc2) return launch_t<ENC, NC, DUAL, true>(L, grid, threads, smem, s, pdl);
     return launch_t<ENC, NC, DUAL, false>(L, grid, threads, smem, s, pdl);
 }
 
 template <int ENC, int NC, bool DUAL>
 cudaError_t configure_n(const GemvLaunch& L, int* occ, int threads, size_t smem) {
-    if constexpr (use_tc(ENC, NC))
-        if (L.tc) return configure<ENC, NC, DUAL, true>(occ, threads, smem);
+    if constexpr (use_tc(ENC, NC) || use_tc2(ENC, NC))
+        if (L.tc || L.tc2) return configure<ENC, NC, DUAL, true>(occ, threads, smem);
     return configure<ENC, NC, DUAL, false>(occ, threads, smem);
 }
 

@@ -210,3 +210,141 @@ __device__ __forceinline__ void tc_slot(const TcLane& z, uint32_t u0, uint32_t s
         tc_apply<ENC>(x, w, acc);
     }
 }
+
+// ---------------------------------------------------------------------------
+// Tensor-core loop of the K-quants (Q5_K, Q6_K, Q2_K) for four or more
+// clients, the other way round: A (16 x k) holds the codes of sixteen matrix
+// rows (unsigned), B (k x 8) one digit plane of the eight clients' staged
+// activations, so one unit of sixteen rows is three products (Q5_K: one per
+// plane, k = 32) or six (Q6_K, Q2_K: k = 16 per half, their scales change
+// every 16 values).  Lane (g, t) holds rows g and g + 8 of the slot for
+// clients 2t and 2t + 1 and applies the block scales in fp32 per (sub-)block,
+// as the CUDA-core loop does.  A gate/up slot puts gate row g in A row g and
+// up row g in A row g + 8, so each lane holds both halves of its SwiGLU.
+
+// D = A x B for m16n8k32 / m16n8k16 with unsigned A (codes), signed B (digits).
+__device__ __forceinline__ void mma_us_k32(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void mma_us_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                 : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+}
+
+// sum_c q_c m_c of output k from the three planes' products.
+__device__ __forceinline__ float tc2_total(const int (&d0)[4], const int (&d1)[4], const int (&d2)[4], int k) {
+    return fmaf(__int2float_rn(d2[k]), 65536.0f, __int2float_rn(d1[k] * 256 + d0[k]));
+}
+
+// One row of the slot: shared address of its tile and its row in the tile.
+struct Tc2Row {
+    uint32_t t, e;
+};
+
+// Unit u of rows ra (A rows g) and rb (A rows g + 8): products with every
+// client's digits and scaling into acc[k] (k: (ra, 2t), (ra, 2t+1), (rb, 2t),
+// (rb, 2t+1)).  xg: client g's records; xc[2]: clients 2t, 2t+1's records.
+template <int ENC>
+__device__ __forceinline__ void tc2_unit(const Tc2Row& ra, const Tc2Row& rb, uint32_t u, int t, uint32_t xg,
+                                         const uint32_t (&xc)[2], const GemvLaunch& L, float (&acc)[4]) {
+    const uint32_t U = L.cols >> 5, B = L.cols >> 8;
+    uint2 p[3];
+#pragma unroll
+    for (int j = 0; j < 3; j++) p[j] = lds64(xg + u * kDigitUnit + j * 32 + 8 * t);
+    float s[2], xs0[2], xs1[2];
+#pragma unroll
+    for (int c = 0; c < 2; c++) {
+        const uint4 r = lds128(xc[c] + u * kDigitUnit + 96);
+        s[c] = __uint_as_float(r.x);
+        xs0[c] = __uint_as_float(r.y);
+        xs1[c] = __uint_as_float(r.z);
+    }
+    const Tc2Row rows[2] = {ra, rb};
+    if constexpr (ENC == SPM_Q5_K) {
+        uint32_t lo[2], hi[2];
+        float ds[2], dm[2];
+        const int jj = int(u & 7);
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const uint32_t unit = rows[r].e * U + u;
+            const uint32_t qs = lds32(rows[r].t + L.plane1 + unit * 16 + 4 * t);
+            const uint32_t qh = lds32(rows[r].t + L.plane2 + unit * 4);
+            lo[r] = (qs & 0x0F0F0F0Fu) | ((((qh >> (4 * t)) & 0xfu) * 0x02040810u) & 0x10101010u);
+            hi[r] = ((qs >> 4) & 0x0F0F0F0Fu) | ((((qh >> (16 + 4 * t)) & 0xfu) * 0x02040810u) & 0x10101010u);
+            const uint4 m = lds128(rows[r].t + (rows[r].e * B + (u >> 3)) * 16);
+            uint32_t sc, mn;
+            if (jj < 4) {
+                sc = sbyte(m, jj) & 63;
+                mn = sbyte(m, jj + 4) & 63;
+            } else {
+                sc = (sbyte(m, jj + 4) & 15) | ((sbyte(m, jj - 4) >> 6) << 4);
+                mn = (sbyte(m, jj + 4) >> 4) | ((sbyte(m, jj) >> 6) << 4);
+            }
+            ds[r] = h2f(m.x) * (bytef<0>(sc) - 8388608.0f);
+            dm[r] = h2f(m.x >> 16) * (bytef<0>(mn) - 8388608.0f);
+        }
+        int d0[4], d1[4], d2[4];
+        mma_us_k32(d0, lo[0], lo[1], hi[0], hi[1], p[0].x, p[0].y);
+        mma_us_k32(d1, lo[0], lo[1], hi[0], hi[1], p[1].x, p[1].y);
+        mma_us_k32(d2, lo[0], lo[1], hi[0], hi[1], p[2].x, p[2].y);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int r = k >> 1, c = k & 1;
+            acc[k] = fmaf(-dm[r], xs0[c] + xs1[c], fmaf(ds[r], tc2_total(d0, d1, d2, k) * s[c], acc[k]));
+        }
+    } else {
+        // k = 16 per half: Q6_K (d * sc) * (q - 32), Q2_K (d * sc) * q - dmin * m
+        uint32_t q[2][2];  // [row][half]
+        float sa[2][2], sm[2][2];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const uint32_t unit = rows[r].e * U + u;
+            if constexpr (ENC == SPM_Q6_K) {
+                const uint32_t ql = lds32(rows[r].t + unit * 16 + 4 * t);
+                const uint2 qh = lds64(rows[r].t + L.plane1 + unit * 8);
+#pragma unroll
+                for (int h = 0; h < 2; h++)
+                    q[r][h] = ((h ? (ql >> 4) : ql) & 0x0F0F0F0Fu) |
+                              ((((h ? qh.y : qh.x) >> (2 * t)) << 4) & 0x30303030u);
+                const uint32_t sc = lds16(rows[r].t + L.plane2 + unit * 2);
+                const float d = h2f(lds16(rows[r].t + L.plane3 + (rows[r].e * B + (u >> 3)) * 2));
+                sa[r][0] = d * i8f(sc & 0xffu);
+                sa[r][1] = d * i8f(sc >> 8);
+            } else {
+                const uint2 qs = lds64(rows[r].t + unit * 8);
+#pragma unroll
+                for (int h = 0; h < 2; h++) q[r][h] = ((h ? qs.y : qs.x) >> (2 * t)) & 0x03030303u;
+                const uint32_t sc = lds16(rows[r].t + L.plane1 + unit * 2);
+                const uint32_t dd = lds32(rows[r].t + L.plane2 + (rows[r].e * B + (u >> 3)) * 4);
+                const float d = h2f(dd), dmin = h2f(dd >> 16);
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const uint32_t b = (sc >> (8 * h)) & 0xffu;
+                    sa[r][h] = d * (bytef<0>(b & 15u) - 8388608.0f);
+                    sm[r][h] = dmin * (bytef<0>(b >> 4) - 8388608.0f);
+                }
+            }
+        }
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            int d0[4], d1[4], d2[4];
+            mma_us_k16(d0, q[0][h], q[1][h], h ? p[0].y : p[0].x);
+            mma_us_k16(d1, q[0][h], q[1][h], h ? p[1].y : p[1].x);
+            mma_us_k16(d2, q[0][h], q[1][h], h ? p[2].y : p[2].x);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int r = k >> 1, c = k & 1;
+                const float xs = h ? xs1[c] : xs0[c];
+                if constexpr (ENC == SPM_Q6_K)
+                    acc[k] = fmaf(sa[r][h], fmaf(tc2_total(d0, d1, d2, k), s[c], -32.0f * xs), acc[k]);
+                else
+                    acc[k] = fmaf(-sm[r][h], xs, fmaf(sa[r][h], tc2_total(d0, d1, d2, k) * s[c], acc[k]));
+            }
+        }
+    }
+}

@@ -59,7 +59,7 @@ __device__ float block_max(float v, float* red) {
 // Embedding gather (spm-batch/src/step.rs:27-30): decode the token's row,
 // exactly; also the row's sum of squares for the first layer's fused norm.
 __global__ void __launch_bounds__(128) embed_kernel(uint32_t dtype, const uint8_t* tiles, const Packed p,
-                                                    const uint32_t* tokens, float* out, float* sumsq) {
+                                                    const uint32_t* tokens, float* out, float* sumsq, int c0) {
     __shared__ float red[33];
     pdl_wait();
     const uint32_t U = uint32_t(p.cols >> 5);
@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(128) embed_kernel(uint32_t dtype, const uint8_
     }
     ss = block_sum<128>(ss, red);
     pdl_trigger();
-    if (threadIdx.x < 8) sumsq[blockIdx.x * 8 + threadIdx.x] = threadIdx.x == blockIdx.x ? ss : 0.f;
+    if (threadIdx.x < 8) sumsq[blockIdx.x * 8 + threadIdx.x] = int(threadIdx.x) == c0 + int(blockIdx.x) ? ss : 0.f;
 }
 
 // Greedy selection: largest logit, LAST index among equals
@@ -193,19 +193,21 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
     const int p0 = chunk * P.chunk;
     const int p1 = min(pos + 1, p0 + P.chunk);
     const int npos = max(0, p1 - p0), ntiles = (npos + kAttnTile - 1) / kAttnTile;
-    const size_t cc = qmode ? size_t(P.cache_client) : size_t(i);
+    const size_t cc = size_t(P.cache_client) + (qmode ? 0 : size_t(i));
     const size_t base = (cc * P.layers + P.layer) * P.context * size_t(kvw) + size_t(kvh) * hd;
     float* kc = P.kcache + base;
     float* vc = P.vcache + base;
     // every thread copies its share of tile j's key and value rows into stage
     // j % kAttnStages (16 bytes per copy), as one copy group
-    const int q4 = hd / 4;
+    // thread t copies 16-byte column c4 of rows r0, r0 + rstep, ... (hd / 4 divides 256)
+    const int q4 = hd / 4, c4 = int(threadIdx.x) % q4, r0 = int(threadIdx.x) / q4, rstep = kAttnThreads / q4;
     auto request = [&](int j) {
         const int s = j % kAttnStages, t0 = p0 + j * kAttnTile, nr = min(kAttnTile, p1 - t0);
-        for (int e = threadIdx.x; e < 2 * nr * q4; e += kAttnThreads) {
-            const int kv = e / (nr * q4), r = (e / q4) % nr, c4 = e % q4;
-            const float* src = (kv ? vc : kc) + size_t(t0 + r) * kvw + 4 * c4;
-            cp_async16(sm + (kv ? L.vt : L.kt) + (s * kAttnTile + r) * ld + 4 * c4, src);
+        for (int r = r0; r < nr; r += rstep) {
+            const size_t g = size_t(t0 + r) * kvw + 4 * c4;
+            const int o = (s * kAttnTile + r) * ld + 4 * c4;
+            cp_async16(sm + L.kt + o, kc + g);
+            cp_async16(sm + L.vt + o, vc + g);
         }
         cp_async_commit();
     };
@@ -483,9 +485,9 @@ cudaError_t launch_attention_queries(const AttnParams& P, int n, cudaStream_t s)
 }
 
 cudaError_t launch_embed(uint32_t dtype, const uint8_t* tiles, const Packed& p, const uint32_t* tokens, int n,
-                         float* out, float* sumsq, cudaStream_t s, bool pdl) {
+                         float* out, float* sumsq, cudaStream_t s, bool pdl, int c0) {
     Packed pk = p;
-    void* args[] = {&dtype, &tiles, &pk, &tokens, &out, &sumsq};
+    void* args[] = {&dtype, &tiles, &pk, &tokens, &out, &sumsq, &c0};
     return launch_pdl(reinterpret_cast<const void*>(embed_kernel), dim3(n), dim3(128), 0, s, pdl, args);
 }
 

@@ -42,14 +42,17 @@ struct GemvLaunch {
     int32_t group_warps;  // warps that share a tile (set by gemv_geometry)
     uint32_t xrec;        // bytes of one client's staged 32-value unit (set by launch_gemv)
     int32_t tc;           // tensor-core inner loop (integer codes, four or more clients; set by launch_gemv)
+    int32_t tc2;          // K-quant tensor-core loop, codes as A, sixteen rows a slot (set by launch_gemv)
     int32_t c0;           // index of client 0 of this launch in the sum-of-squares arrays
     // Expert mode (plan != nullptr): one job over a [experts][rows][cols]
-    // tensor; CTA b works on active expert b / expert_chunks of the plan and
-    // streams only that expert's tiles; client slot p of the expert reads x
-    // row plan->tok[a][p] (xmode 0) or a*8+p (xmode 1) and writes y row a*8+p.
+    // tensor; the grid is one wave of resident CTAs (at least expert_max),
+    // and with nl active experts in the plan each expert's tiles split into
+    // C = max(expert_chunks, grid / nl) chunks: CTA b streams chunk b % C of
+    // active expert b / C; client slot p of the expert reads x row
+    // plan->tok[a][p] (xmode 0) or a*8+p (xmode 1) and writes y row a*8+p.
     const MoePlan* plan;
-    int32_t expert_max;   // grid = expert_max * expert_chunks CTAs
-    int32_t expert_chunks;
+    int32_t expert_max;     // active experts of this rank, at most
+    int32_t expert_chunks;  // chunks per expert, at least (sizes the ring)
     uint32_t expert_tiles;
     int32_t xmode;
     // Expert parallel (world > 1, expert mode): experts e with e % world ==
@@ -65,6 +68,17 @@ struct GemvLaunch {
     uint32_t* ep_done;
     const uint32_t* ep_step;
     int32_t ep_layers, ep_layer;
+    // Data-parallel attention (world > 1, dense launches of one job): with
+    // ep_dense set, ep_peer_y holds every rank's output base (no parity; the
+    // launch's rows go from client c0 on, job[0].y_stride apart) and each
+    // output row goes to all of them; ep_peer_sumsq, when set, holds every rank's
+    // sum-of-squares array and the per-CTA sums go to all of them too.  With
+    // ep_wait_flags set the launch first waits (bounded by wait_ns, status 8)
+    // until ep_wait_flags[(E & 1) * 64 + p] == E for every rank p, E as above.
+    int32_t ep_dense;
+    float* const* ep_peer_sumsq;
+    const uint32_t* ep_wait_flags;
+    uint64_t wait_ns;
 };
 
 // Grid, ring slots and dynamic shared memory of a streaming GEMV launch.
@@ -130,7 +144,8 @@ struct AttnParams {
     // Query mode (qpos != nullptr; prefill): row i of q is a query already
     // QK-normed and rotated, at position qpos[i], over the cache of client
     // cache_client, whose rows up to that position are already written; no
-    // append.  Launched without programmatic dependent launch.
+    // append.  Launched without programmatic dependent launch.  In decode
+    // mode row i is client cache_client + i's (the cache's client index).
     const int32_t* qpos;
     int32_t cache_client;
 };
@@ -142,8 +157,9 @@ cudaError_t launch_attention_queries(const AttnParams& P, int n, cudaStream_t st
 
 // Gather-and-decode one packed row per client (embedding lookup).
 // Also writes sumsq_out[i*8 + c] = (i == c) ? sum of squares of row i : 0.
+// Client c0 + i's row goes to out row i; sumsq_out[i*8 + c] = (c == c0 + i) ? ss : 0.
 cudaError_t launch_embed(uint32_t dtype, const uint8_t* tiles, const Packed& p, const uint32_t* tokens, int n,
-                         float* out, float* sumsq_out, cudaStream_t stream, bool pdl);
+                         float* out, float* sumsq_out, cudaStream_t stream, bool pdl, int c0 = 0);
 // Decode rows [row0, row0+rows) into out (rows x cols floats), exact.
 cudaError_t launch_dequant(uint32_t dtype, const uint8_t* tiles, const Packed& p, uint64_t row0, uint64_t rows,
                            float* out, cudaStream_t stream);

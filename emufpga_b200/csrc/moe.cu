@@ -151,7 +151,7 @@ constexpr int kCombineCols = 128;
 
 __global__ void __launch_bounds__(kCombineCols) combine_kernel(const MoePlan* plan, const float* out, int out_stride,
                                                                float* states, int width, int K, float* sumsq,
-                                                               MoeExchange ex) {
+                                                               MoeExchange ex, int c0) {
     __shared__ float red[kCombineCols / 32];
     pdl_wait();
     if (ex.world > 1) {
@@ -171,7 +171,7 @@ __global__ void __launch_bounds__(kCombineCols) combine_kernel(const MoePlan* pl
         __syncthreads();
         out += (E & 1u) * ex.xstride;
     }
-    const int i = blockIdx.y, col = blockIdx.x * kCombineCols + threadIdx.x;
+    const int i = c0 + int(blockIdx.y), col = blockIdx.x * kCombineCols + threadIdx.x;
     float ss = 0.f;
     if (col < width) {
         const float norm = plan->norm[i];
@@ -191,7 +191,7 @@ __global__ void __launch_bounds__(kCombineCols) combine_kernel(const MoePlan* pl
     if (threadIdx.x < 8) {
         float t = 0.f;
         for (int w = 0; w < kCombineCols / 32; w++) t += red[w];
-        sumsq[(size_t(i) * gridDim.x + blockIdx.x) * 8 + threadIdx.x] = int(threadIdx.x) == i ? t : 0.f;
+        sumsq[(size_t(blockIdx.y) * gridDim.x + blockIdx.x) * 8 + threadIdx.x] = int(threadIdx.x) == i ? t : 0.f;
     }
 }
 
@@ -208,7 +208,42 @@ cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, cudaStream_t s, bo
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
+// Data-parallel attention: each rank picked the greedy tokens of its own
+// clients c0..c0+n-1.  Thread p copies them into rank p's array and raises
+// this rank's flag there (value *step + 1), then thread p waits until rank
+// p's flag is up here (bounded; status 9), so every rank ends the step with
+// every client's pick.
+__global__ void ep_gather_kernel(const uint32_t* argmax, uint32_t* const* peer_argmax, uint32_t* const* peer_flags,
+                                 const uint32_t* own_flags, const uint32_t* step, int c0, int n, int world, int rank,
+                                 int32_t* status, uint64_t wait_ns) {
+    pdl_wait();
+    const uint32_t E = *step + 1;
+    const int p = int(threadIdx.x);
+    if (p < world) {
+        for (int c = 0; c < n; c++) peer_argmax[p][c0 + c] = argmax[c0 + c];
+        __threadfence_system();
+        st_release_sys(peer_flags[p] + rank, E);
+        if (ld_acquire_sys(own_flags + p) != E) {
+            const uint64_t t0 = now_ns();
+            while (ld_acquire_sys(own_flags + p) != E)
+                if (now_ns() - t0 > wait_ns) {
+                    flag(status, 9);
+                    break;
+                }
+        }
+    }
+    __syncthreads();
+    pdl_trigger();
+}
+
 }  // namespace
+
+cudaError_t launch_ep_gather(const uint32_t* argmax, uint32_t* const* peer_argmax, uint32_t* const* peer_flags,
+                             const uint32_t* own_flags, const uint32_t* step, int c0, int n, int world, int rank,
+                             int32_t* status, uint64_t wait_ns, cudaStream_t s, bool pdl) {
+    void* args[] = {&argmax, &peer_argmax, &peer_flags, &own_flags, &step, &c0, &n, &world, &rank, &status, &wait_ns};
+    return launch_pdl(reinterpret_cast<const void*>(ep_gather_kernel), dim3(1), dim3(32), s, pdl, args);
+}
 
 cudaError_t launch_route(const float* logits, const float* bias, int n, int experts, int used, int world, int rank,
                          MoePlan* plan, cudaStream_t s, bool pdl) {
@@ -223,10 +258,10 @@ cudaError_t launch_route(const float* logits, const float* bias, int n, int expe
 int combine_parts(int width, int n) { return ((width + kCombineCols - 1) / kCombineCols) * n; }
 
 cudaError_t launch_combine(const MoePlan* plan, const float* out, int out_stride, float* states, int width, int n,
-                           int used, float* sumsq, const MoeExchange* ex, cudaStream_t s, bool pdl) {
+                           int used, float* sumsq, const MoeExchange* ex, cudaStream_t s, bool pdl, int c0) {
     MoeExchange e = ex ? *ex : MoeExchange{};
     if (!ex) e.world = 1;
-    void* args[] = {&plan, &out, &out_stride, &states, &width, &used, &sumsq, &e};
+    void* args[] = {&plan, &out, &out_stride, &states, &width, &used, &sumsq, &e, &c0};
     return launch_pdl(reinterpret_cast<const void*>(combine_kernel), dim3((width + kCombineCols - 1) / kCombineCols, n),
                       dim3(kCombineCols), s, pdl, args);
 }

@@ -52,7 +52,13 @@ struct MoeExchange {
 // sums of squares of the new state rows, in combine_parts(width, n) parts:
 // part (i * chunks + chunk) holds [c == i ? ss : 0 for c < 8].
 int combine_parts(int width, int n);
+// Clients c0..c0+n-1 (their plan rows and state rows); the sums of squares go
+// to parts blockIdx.y * chunks + chunk with the value at client c0 + blockIdx.y.
 cudaError_t launch_combine(const MoePlan* plan, const float* out, int out_stride, float* states, int width, int n,
-                           int used, float* sumsq, const MoeExchange* ex, cudaStream_t s, bool pdl);
+                           int used, float* sumsq, const MoeExchange* ex, cudaStream_t s, bool pdl, int c0 = 0);
+// Data-parallel attention: gather every rank's greedy picks (ep_gather_kernel).
+cudaError_t launch_ep_gather(const uint32_t* argmax, uint32_t* const* peer_argmax, uint32_t* const* peer_flags,
+                             const uint32_t* own_flags, const uint32_t* step, int c0, int n, int world, int rank,
+                             int32_t* status, uint64_t wait_ns, cudaStream_t s, bool pdl);
 
 }  // namespace spm

@@ -12,6 +12,12 @@ tokens -- the same tokens it would produce served alone.
 A step runs clients 0..n-1 where n-1 is the highest busy slot; a free slot
 below that decodes a filler token and is reset before a request takes it
 (or when its cache would otherwise fill).
+
+With `prefill=True` a joining request's prompt, all but its last token, runs
+at once through the session's `prefill` (the tensor-core prompt path) when
+it takes its slot; it then feeds its last prompt token in the next step and
+decodes from there -- the batched prefill for late joiners that the
+reference's lockstep server lacks (docs/results.md:1189-1191).
 """
 from __future__ import annotations
 
@@ -38,12 +44,18 @@ class DecodeSession(Protocol):
 
     def decode_step(self, tokens: Sequence[int], want_logits: bool = False): ...
 
+    # only with prefill=True: run tokens for `client` at its next positions
+    def prefill(self, client: int, tokens: Sequence[int]) -> None: ...
 
-def serve_continuous(session: DecodeSession, requests: Sequence[Request], filler: int = 0) -> list[list[int]]:
+
+def serve_continuous(session: DecodeSession, requests: Sequence[Request], filler: int = 0,
+                     prefill: bool = False) -> list[list[int]]:
     """Serve `requests` on `session`; returns each request's produced tokens.
 
     Requests start in arrival order (ties in list order) as slots free up.
-    Raises ValueError when a request cannot fit the session's context."""
+    With prefill, a starting request's prompt but its last token is run at
+    once by session.prefill.  Raises ValueError when a request cannot fit the
+    session's context."""
     for r in requests:
         if not r.prompt or r.max_new < 1:
             raise ValueError("a request needs a prompt and at least one new token")
@@ -61,7 +73,12 @@ def serve_continuous(session: DecodeSession, requests: Sequence[Request], filler
                 continue
             r = waiting.pop(0)
             session.reset(s)
-            active[s] = [r, 0, requests[r].prompt[0]]
+            prompt = requests[r].prompt
+            if prefill and len(prompt) > 1:
+                session.prefill(s, list(prompt[:-1]))
+                active[s] = [r, len(prompt) - 1, prompt[-1]]
+            else:
+                active[s] = [r, 0, prompt[0]]
         if not active:
             step = requests[waiting[0]].arrival
             continue

@@ -315,12 +315,13 @@ def test_continuous_batching_matches_the_oracle_served_alone(cuda, models):
     v = r.shape.vocab
     reqs = [Request(configs.prompt_tokens(50 + i, 0, ln, v), new, arr)
             for i, (ln, new, arr) in enumerate([(3, 6, 0), (5, 4, 0), (2, 7, 1), (4, 5, 3), (6, 3, 4), (1, 8, 9)])]
-    sess = eb.Session(m, 3, 24)
-    got = serve_continuous(sess, reqs)
-    sess.close()
-    for q, g in zip(reqs, got):
-        want, _ = om.serve([list(q.prompt)], q.max_new)
-        assert g == want[0]
+    for prefill in (False, True):
+        sess = eb.Session(m, 3, 24)
+        got = serve_continuous(sess, reqs, prefill=prefill)
+        sess.close()
+        for q, g in zip(reqs, got):
+            want, _ = om.serve([list(q.prompt)], q.max_new)
+            assert g == want[0], (prefill, q)
 
 
 @pytest.mark.parametrize("name", ["qwen3-q5_k", "olmoe-q2_k"])

@@ -3,9 +3,10 @@ SPM_E_TIMEOUT, and leaves the CUDA context usable.
 
 One process, one GPU: the model is rank 0 of an expert-parallel pair, and the
 session's rank-1 slot is pointed back at its own exchange buffer, so rank 1's
-flag is never raised.  The exchange wait is shortened to 1 ms; every routed
-layer's combine then waits that long on the missing flag, flags the session's
-status word and goes on (no trap, no fault).  The same context then serves a
+flags are never raised.  The waits are shortened to 1 ms; every routed
+layer's router (for rank 1's rows) and combine (for rank 1's expert rows), and
+the gather of the greedy picks, then wait that long on a missing flag, flag
+the session's status word and go on (no trap, no fault).  The same context then serves a
 single-GPU model whose step matches the oracle.
 """
 import numpy as np

@@ -13,12 +13,18 @@ class ToySession:
         self.max_clients, self.context, self.vocab = max_clients, context, vocab
         self.hist = [[] for _ in range(max_clients)]
         self.steps = []
+        self.prefills = []
 
     def reset(self, client):
         self.hist[client] = []
 
     def length(self, client):
         return len(self.hist[client])
+
+    def prefill(self, client, tokens):
+        # the prompt path: the same history as feeding the tokens one per step
+        self.prefills.append((client, len(tokens)))
+        self.hist[client].extend(tokens)
 
     def decode_step(self, tokens, want_logits=False):
         self.steps.append(len(tokens))
@@ -69,3 +75,14 @@ def test_requests_that_cannot_fit_are_refused():
         serve_continuous(ToySession(2, 8), [Request([1] * 5, 4)])
     with pytest.raises(ValueError):
         serve_continuous(ToySession(2, 8), [Request([], 2)])
+
+
+def test_prefill_of_joining_requests_changes_no_token():
+    reqs = [Request([1, 2, 3, 9, 9], 5), Request([7], 9, arrival=2), Request([4, 4, 4, 4], 3, arrival=2),
+            Request([5, 6, 7, 8, 1, 2], 4, arrival=6)]
+    plain = ToySession(2, 32)
+    fast = ToySession(2, 32)
+    assert serve_continuous(fast, reqs, prefill=True) == serve_continuous(plain, reqs)
+    # every prompt longer than one token went through prefill, all but its last token
+    assert sorted(n for _, n in fast.prefills) == sorted(len(r.prompt) - 1 for r in reqs if len(r.prompt) > 1)
+    assert len(fast.steps) < len(plain.steps)
