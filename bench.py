@@ -95,6 +95,8 @@ def _args():
 
 
 def _dist():
+    # NCCL's version banner would land on stdout beside the JSON line
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

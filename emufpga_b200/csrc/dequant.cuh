@@ -41,16 +41,12 @@ __device__ __forceinline__ void dequant_unit(uint32_t dtype, const uint8_t* tile
             break;
         }
         case SPM_Q5_K: {
-            const uint8_t* m = tile + (size_t(rt) * B + (u >> 3)) * 16;
-            const uint8_t* qs = tile + p.plane[1] + unit * 16;
-            const uint8_t* qhp = tile + p.plane[2] + unit * 4;
+            const uint8_t* m = tile + p.plane[3] + (size_t(rt) * B + (u >> 3)) * 4;
+            const uint8_t* qs = tile + unit * 16;
+            const uint8_t* qhp = tile + p.plane[1] + unit * 4;
             const uint32_t qh = qhp[0] | (qhp[1] << 8) | (qhp[2] << 16) | (uint32_t(qhp[3]) << 24);
             const float d = h2f(m[0] | (m[1] << 8)), dmin = h2f(m[2] | (m[3] << 8));
-            const uint8_t* s = m + 4;
-            const int j = int(u & 7);
-            int sc, mn;
-            if (j < 4) { sc = s[j] & 63; mn = s[j + 4] & 63; }
-            else { sc = (s[j + 4] & 15) | ((s[j - 4] >> 6) << 4); mn = (s[j + 4] >> 4) | ((s[j] >> 6) << 4); }
+            const int sc = tile[p.plane[2] + unit * 2], mn = tile[p.plane[2] + unit * 2 + 1];
             for (int l = 0; l < 32; l++) {
                 const int i = l & 15;
                 const uint32_t lo = (l >> 4) ? (qs[i] >> 4) : (qs[i] & 15);

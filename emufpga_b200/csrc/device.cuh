@@ -103,7 +103,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
         if (now_ns() - t0 > kWaitLimitNs) return false;
     return true;
 }
-// One bulk copy global -> shared (no multicast), completing on `bar`.
+// One bulk copy global -> shared into this CTA alone, completing on `bar`.
 // Source, destination and size must be multiples of 16 bytes.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(

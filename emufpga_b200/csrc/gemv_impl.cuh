@@ -257,33 +257,21 @@ __device__ __forceinline__ void unit_q6_k(const RowRef (&rr)[R], uint32_t u, con
 }
 
 // ------------------------------------------------------------------ Q5_K --
-__device__ __forceinline__ uint32_t sbyte(const uint4& m, int k) {  // scales byte k (0..11)
-    const uint32_t w = k < 4 ? m.y : k < 8 ? m.z : m.w;
-    return (w >> (8 * (k & 3))) & 0xffu;
-}
 
 template <int NC, int R>
 __device__ __forceinline__ void unit_q5_k(const RowRef (&rr)[R], uint32_t u, const GemvLaunch& L, const XDig<NC>& X,
                                           float (&acc)[R][NC]) {
-    const int j = int(u & 7);
     uint32_t q[R][8];  // 5-bit codes as bytes
     float ds[R], dm[R];
 #pragma unroll
     for (int v = 0; v < R; v++) {
         const uint32_t unit = rr[v].ru + u;
-        const uint4 m = lds128(rr[v].t + (rr[v].rb + (u >> 3)) * 16);
-        const uint4 qs = lds128(rr[v].t + L.plane1 + unit * 16);
-        const uint32_t qh = lds32(rr[v].t + L.plane2 + unit * 4);
-        uint32_t sc, mn;
-        if (j < 4) {
-            sc = sbyte(m, j) & 63;
-            mn = sbyte(m, j + 4) & 63;
-        } else {
-            sc = (sbyte(m, j + 4) & 15) | ((sbyte(m, j - 4) >> 6) << 4);
-            mn = (sbyte(m, j + 4) >> 4) | ((sbyte(m, j) >> 6) << 4);
-        }
-        ds[v] = h2f(m.x) * (bytef<0>(sc) - 8388608.0f);
-        dm[v] = h2f(m.x >> 16) * (bytef<0>(mn) - 8388608.0f);
+        const uint4 qs = lds128(rr[v].t + unit * 16);
+        const uint32_t qh = lds32(rr[v].t + L.plane1 + unit * 4);
+        const uint32_t sm = lds16(rr[v].t + L.plane2 + unit * 2);
+        const uint32_t dd = lds32(rr[v].t + L.plane3 + (rr[v].rb + (u >> 3)) * 4);
+        ds[v] = h2f(dd) * (bytef<0>(sm) - 8388608.0f);
+        dm[v] = h2f(dd >> 16) * (bytef<1>(sm) - 8388608.0f);
 #pragma unroll
         for (int run = 0; run < 2; run++)
 #pragma unroll

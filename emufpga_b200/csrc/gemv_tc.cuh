@@ -1,6 +1,5 @@
-// Tensor-core inner loop of the streaming GEMV for four or more clients of a
-// Q8_0 matrix (included by gemv_impl.cuh; the K-quant forms are kept for
-// experiments with other client counts and block sizes).
+// Tensor-core inner loops of the streaming GEMV for four or more clients
+// (included by gemv_impl.cuh): the Q8_0 loop first, the K-quant loop below.
 //
 // With several clients the integer dot products outgrow the CUDA cores, so
 // one 32-value unit of eight matrix rows is one small integer matrix product
@@ -10,8 +9,7 @@
 //                 plane 1 in rows 8..15, plane 2 in a second product;
 //     B (k x 8):  the codes of the slot's eight rows (four rows of two tiles,
 //                 or the four gate and four up rows of one tile);
-// k = 32 for block types with one scale per 32 values (Q8_0, Q5_K) and 16,
-// one product per half, for those with one per 16 (Q6_K, Q2_K).  The integer
+// k = 32 (one scale per 32 values).  The integer
 // sums are exact; lane (g, t) of the warp then holds client g's totals for
 // slot rows 2t and 2t+1 and applies the block scales in fp32, as the CUDA-core
 // loop does per lane.  Fragment layouts are those of the PTX mma.sync m16n8k16
@@ -33,12 +31,6 @@ __device__ __forceinline__ void mma_k32(int (&d)[4], uint32_t a0, uint32_t a1, u
             "mma.sync.aligned.m16n8k32.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
             : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
             : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
-}
-// D = A x B + 0 for the m16n8k16 integer shape (B unsigned codes).
-__device__ __forceinline__ void mma_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-    asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.u8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
-                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-                 : "r"(a0), "r"(a1), "r"(b0), "r"(0));
 }
 
 // sum_c q_c m_c for the lane's client and slot row 2t + j from the products
@@ -77,110 +69,33 @@ __device__ __forceinline__ void tc_load_x(const TcLane& z, uint32_t u, TcX& x) {
     }
 }
 
-// Codes (the slot row's two code words per half-or-run) and the two output
-// rows' scale terms of one unit, loaded before any product is formed.
+// Codes (the slot row's two code words) and the two output rows' scales of
+// one unit, loaded before any product is formed.
 struct TcW {
-    uint32_t q[2];       // B operands: k32 -> words t, 4+t; k16 -> half 0, half 1
-    float sa[2][2];      // per output row j and half (or [j][0] for per-unit types): scale
-    float sm[2][2];      // min terms (Q5_K, Q2_K)
+    uint32_t q[2];  // B operand: words t, 4+t
+    float sa[2];    // per output row j: the block scale
 };
 
 template <int ENC>
 __device__ __forceinline__ void tc_load_w(const TcLane& z, uint32_t u, const GemvLaunch& L, TcW& w) {
-    const uint32_t U = L.cols >> 5, B = L.cols >> 8;
+    static_assert(ENC == SPM_Q8_0, "the Q8_0 tensor-core loop");
+    const uint32_t U = L.cols >> 5;
     const int t = z.t;
     const uint32_t unit = z.cr * U + u;
-    if constexpr (ENC == SPM_Q8_0) {
-        w.q[0] = lds32(z.cb + unit * 32 + 4 * t);
-        w.q[1] = lds32(z.cb + unit * 32 + 16 + 4 * t);
+    w.q[0] = lds32(z.cb + unit * 32 + 4 * t);
+    w.q[1] = lds32(z.cb + unit * 32 + 16 + 4 * t);
 #pragma unroll
-        for (int j = 0; j < 2; j++) w.sa[j][0] = h2f(lds16(z.ob + L.plane1 + ((z.or0 + j) * U + u) * 2));
-    } else if constexpr (ENC == SPM_Q6_K) {
-        const uint32_t ql = lds32(z.cb + unit * 16 + 4 * t);
-        const uint2 qh = lds64(z.cb + L.plane1 + unit * 8);
-#pragma unroll
-        for (int h = 0; h < 2; h++)
-            w.q[h] = ((h ? (ql >> 4) : ql) & 0x0F0F0F0Fu) | ((((h ? qh.y : qh.x) >> (2 * t)) << 4) & 0x30303030u);
-#pragma unroll
-        for (int j = 0; j < 2; j++) {
-            const uint32_t sc = lds16(z.ob + L.plane2 + ((z.or0 + j) * U + u) * 2);
-            const float d = h2f(lds16(z.ob + L.plane3 + ((z.or0 + j) * B + (u >> 3)) * 2));
-            w.sa[j][0] = d * i8f(sc & 0xffu);
-            w.sa[j][1] = d * i8f(sc >> 8);
-        }
-    } else if constexpr (ENC == SPM_Q5_K) {
-        const uint32_t qs = lds32(z.cb + L.plane1 + unit * 16 + 4 * t);
-        const uint32_t qh = lds32(z.cb + L.plane2 + unit * 4);
-#pragma unroll
-        for (int run = 0; run < 2; run++)
-            w.q[run] = ((run ? (qs >> 4) : qs) & 0x0F0F0F0Fu) |
-                       ((((qh >> (16 * run + 4 * t)) & 0xfu) * 0x02040810u) & 0x10101010u);
-        const int jj = int(u & 7);
-#pragma unroll
-        for (int j = 0; j < 2; j++) {
-            const uint4 m = lds128(z.ob + ((z.or0 + j) * B + (u >> 3)) * 16);
-            uint32_t sc, mn;
-            if (jj < 4) {
-                sc = sbyte(m, jj) & 63;
-                mn = sbyte(m, jj + 4) & 63;
-            } else {
-                sc = (sbyte(m, jj + 4) & 15) | ((sbyte(m, jj - 4) >> 6) << 4);
-                mn = (sbyte(m, jj + 4) >> 4) | ((sbyte(m, jj) >> 6) << 4);
-            }
-            w.sa[j][0] = h2f(m.x) * (bytef<0>(sc) - 8388608.0f);
-            w.sm[j][0] = h2f(m.x >> 16) * (bytef<0>(mn) - 8388608.0f);
-        }
-    } else if constexpr (ENC == SPM_Q2_K) {
-        const uint2 qs = lds64(z.cb + unit * 8);
-#pragma unroll
-        for (int h = 0; h < 2; h++) w.q[h] = ((h ? qs.y : qs.x) >> (2 * t)) & 0x03030303u;
-#pragma unroll
-        for (int j = 0; j < 2; j++) {
-            const uint32_t sc = lds16(z.ob + L.plane1 + ((z.or0 + j) * U + u) * 2);
-            const uint32_t dd = lds32(z.ob + L.plane2 + ((z.or0 + j) * B + (u >> 3)) * 4);
-            const float d = h2f(dd), dmin = h2f(dd >> 16);
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const uint32_t b = (sc >> (8 * h)) & 0xffu;
-                w.sa[j][h] = d * (bytef<0>(b & 15u) - 8388608.0f);
-                w.sm[j][h] = dmin * (bytef<0>(b >> 4) - 8388608.0f);
-            }
-        }
-    }
+    for (int j = 0; j < 2; j++) w.sa[j] = h2f(lds16(z.ob + L.plane1 + ((z.or0 + j) * U + u) * 2));
 }
 
 // Products and fp32 scaling of one unit whose operands are loaded.
 template <int ENC>
 __device__ __forceinline__ void tc_apply(const TcX& x, const TcW& w, float (&acc)[2]) {
-    if constexpr (ENC == SPM_Q8_0 || ENC == SPM_Q5_K) {
-        int d01[4], d2[4];
-        mma_k32<ENC == SPM_Q8_0>(d01, x.p[0].x, x.p[1].x, x.p[0].y, x.p[1].y, w.q[0], w.q[1]);
-        mma_k32<ENC == SPM_Q8_0>(d2, x.p[2].x, 0u, x.p[2].y, 0u, w.q[0], w.q[1]);
-        if constexpr (ENC == SPM_Q8_0) {
+    int d01[4], d2[4];
+    mma_k32<true>(d01, x.p[0].x, x.p[1].x, x.p[0].y, x.p[1].y, w.q[0], w.q[1]);
+    mma_k32<true>(d2, x.p[2].x, 0u, x.p[2].y, 0u, w.q[0], w.q[1]);
 #pragma unroll
-            for (int j = 0; j < 2; j++) acc[j] = fmaf(w.sa[j][0] * x.s, tc_total(d01, d2, j), acc[j]);
-        } else {
-            const float xsum = x.sum0 + x.sum1;
-#pragma unroll
-            for (int j = 0; j < 2; j++)
-                acc[j] = fmaf(-w.sm[j][0], xsum, fmaf(w.sa[j][0], tc_total(d01, d2, j) * x.s, acc[j]));
-        }
-    } else {
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-            int d01[4], d2[4];
-            mma_k16(d01, h ? x.p[0].y : x.p[0].x, h ? x.p[1].y : x.p[1].x, w.q[h]);
-            mma_k16(d2, h ? x.p[2].y : x.p[2].x, 0u, w.q[h]);
-            const float xs = h ? x.sum1 : x.sum0;
-#pragma unroll
-            for (int j = 0; j < 2; j++) {
-                if constexpr (ENC == SPM_Q6_K)
-                    acc[j] = fmaf(w.sa[j][h], fmaf(tc_total(d01, d2, j), x.s, -32.0f * xs), acc[j]);
-                else
-                    acc[j] = fmaf(-w.sm[j][h], xs, fmaf(w.sa[j][h], tc_total(d01, d2, j) * x.s, acc[j]));
-            }
-        }
-    }
+    for (int j = 0; j < 2; j++) acc[j] = fmaf(w.sa[j] * x.s, tc_total(d01, d2, j), acc[j]);
 }
 
 // The group's share of a slot: warp wig takes units wig, wig + gw, ...; two
@@ -268,25 +183,17 @@ __device__ __forceinline__ void tc2_unit(const Tc2Row& ra, const Tc2Row& rb, uin
     if constexpr (ENC == SPM_Q5_K) {
         uint32_t lo[2], hi[2];
         float ds[2], dm[2];
-        const int jj = int(u & 7);
 #pragma unroll
         for (int r = 0; r < 2; r++) {
             const uint32_t unit = rows[r].e * U + u;
-            const uint32_t qs = lds32(rows[r].t + L.plane1 + unit * 16 + 4 * t);
-            const uint32_t qh = lds32(rows[r].t + L.plane2 + unit * 4);
+            const uint32_t qs = lds32(rows[r].t + unit * 16 + 4 * t);
+            const uint32_t qh = lds32(rows[r].t + L.plane1 + unit * 4);
             lo[r] = (qs & 0x0F0F0F0Fu) | ((((qh >> (4 * t)) & 0xfu) * 0x02040810u) & 0x10101010u);
             hi[r] = ((qs >> 4) & 0x0F0F0F0Fu) | ((((qh >> (16 + 4 * t)) & 0xfu) * 0x02040810u) & 0x10101010u);
-            const uint4 m = lds128(rows[r].t + (rows[r].e * B + (u >> 3)) * 16);
-            uint32_t sc, mn;
-            if (jj < 4) {
-                sc = sbyte(m, jj) & 63;
-                mn = sbyte(m, jj + 4) & 63;
-            } else {
-                sc = (sbyte(m, jj + 4) & 15) | ((sbyte(m, jj - 4) >> 6) << 4);
-                mn = (sbyte(m, jj + 4) >> 4) | ((sbyte(m, jj) >> 6) << 4);
-            }
-            ds[r] = h2f(m.x) * (bytef<0>(sc) - 8388608.0f);
-            dm[r] = h2f(m.x >> 16) * (bytef<0>(mn) - 8388608.0f);
+            const uint32_t sm = lds16(rows[r].t + L.plane2 + unit * 2);
+            const uint32_t dd = lds32(rows[r].t + L.plane3 + (rows[r].e * B + (u >> 3)) * 4);
+            ds[r] = h2f(dd) * (bytef<0>(sm) - 8388608.0f);
+            dm[r] = h2f(dd >> 16) * (bytef<1>(sm) - 8388608.0f);
         }
         int d0[4], d1[4], d2[4];
         mma_us_k32(d0, lo[0], lo[1], hi[0], hi[1], p[0].x, p[0].y);

@@ -4,7 +4,11 @@
 // holds one fixed-size record per unit (or per 256-weight block), so a warp's
 // loads of a plane are contiguous.  The records hold exactly the bits of the
 // GGML block -- only their positions change -- so the bytes streamed per weight
-// equal the GGUF bytes per weight.  Inside a unit, weights l and l+16 share a
+// equal the GGUF bytes per weight, with one exception: Q5_K's twelve bytes of
+// 6-bit scales and mins are stored unpacked, one byte each per unit (sixteen
+// bytes per block, 180 instead of 176 per 256 weights), so that a unit's scale
+// and min are one 2-byte load instead of a selection among twelve bytes that
+// depends on the unit's place in the block.  Inside a unit, weights l and l+16 share a
 // byte (low / high nibble) and the high bits of weights 4t..4t+3 sit in the
 // same bit slot of four consecutive bytes: one shift and one mask then yield
 // four codes, one per byte, ready for the byte-to-float conversion.
@@ -12,8 +16,7 @@
 // Per tile of kTileRows rows (U = cols/32 units, B = cols/256 blocks per row):
 //   Q8_0 : QS[TR][U][32]  D[TR][U][2]
 //   Q6_K : QL[TR][U][16]  QH[TR][U][8]   SC[TR][U][2]  D[TR][B][2]
-//   Q5_K : META[TR][B][16] (bytes 0..15 of the block: d, dmin, scales[12])
-//          QS[TR][U][16]  QH[TR][U][4]
+//   Q5_K : QS[TR][U][16]  QH[TR][U][4]   SM[TR][U][2] (scale, min)  DM[TR][B][4] (d, dmin)
 //   Q2_K : QS[TR][U][8]   SC[TR][U][2]   DD[TR][B][4]  (d, dmin)
 //   F32  : W[TR][cols][4]
 #include "common.h"
@@ -51,9 +54,10 @@ Packed packed_shape(uint32_t dtype, uint64_t rows, uint64_t cols) {
             break;
         case SPM_Q5_K:
             if (cols % 256) fail(SPM_E_ARG, "Q5_K rows must be whole blocks");
-            p.plane[1] = uint32_t(TR * B * 16);
-            p.plane[2] = uint32_t(p.plane[1] + TR * U * 16);
-            p.tile_bytes = a16(p.plane[2] + TR * U * 4);
+            p.plane[1] = uint32_t(TR * U * 16);
+            p.plane[2] = uint32_t(p.plane[1] + TR * U * 4);
+            p.plane[3] = uint32_t(a16(p.plane[2] + TR * U * 2));
+            p.tile_bytes = a16(p.plane[3] + TR * B * 4);
             break;
         case SPM_Q2_K:
             if (cols % 256) fail(SPM_E_ARG, "Q2_K rows must be whole blocks");
@@ -154,14 +158,24 @@ void pack_matrix(const Packed& p, const uint8_t* src, uint8_t* dst) {
                 for (uint64_t b = 0; b < B; b++) {
                     const uint8_t* blk = row + b * 176;
                     q5_codes(blk, q);
-                    std::memcpy(tile + (rt * B + b) * 16, blk, 16);
+                    std::memcpy(tile + p.plane[3] + (rt * B + b) * 4, blk, 4);
+                    const uint8_t* s = blk + 4;
                     for (int j = 0; j < 8; j++) {
                         uint64_t u = b * 8 + j;
                         const uint8_t* qq = q + 32 * j;
-                        put_nibbles(qq, tile + p.plane[1] + (rt * U + u) * 16);
+                        put_nibbles(qq, tile + (rt * U + u) * 16);
                         uint32_t hb = 0;
                         for (int l = 0; l < 32; l++) hb |= uint32_t((qq[l] >> 4) & 1) << l;
-                        std::memcpy(tile + p.plane[2] + (rt * U + u) * 4, &hb, 4);
+                        std::memcpy(tile + p.plane[1] + (rt * U + u) * 4, &hb, 4);
+                        // sub-block j's 6-bit scale and min (spm-gguf/src/tensor.rs:141-156)
+                        uint8_t* sm = tile + p.plane[2] + (rt * U + u) * 2;
+                        if (j < 4) {
+                            sm[0] = uint8_t(s[j] & 63);
+                            sm[1] = uint8_t(s[j + 4] & 63);
+                        } else {
+                            sm[0] = uint8_t((s[j + 4] & 15) | ((s[j - 4] >> 6) << 4));
+                            sm[1] = uint8_t((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
+                        }
                     }
                 }
                 break;

@@ -1,6 +1,8 @@
 // sm_100a kernels of the decode token loop besides the GEMV (gemv.cu):
 // exact dequantization (parity hook and embedding lookup), attention over the
 // device KV cache, greedy selection, position bookkeeping.
+#include <algorithm>
+
 #include "dequant.cuh"
 
 namespace spm {
@@ -158,6 +160,111 @@ __device__ __forceinline__ void rope_pair(float& x, float& y, float c, float s, 
     }
 }
 
+// The inputs of one (kv head, client): the group's queries into qs and, in
+// decode mode, the new key and value into kn, vn, QK-normed and rotated (in
+// query mode the queries are ready as they are); the CTA whose chunk
+// [p0, p0 + P.chunk) holds the new position appends the key and value to the
+// cache (spm-kv/src/cache.rs:49-58).  Waits for the kernel that produced q, k, v.
+template <int NT>
+__device__ void attn_prepare(const AttnParams& P, int i, int kvh, int pos, int p0, bool qmode, float* qs, float* kn,
+                             float* vn, float* red, float* kc, float* vc) {
+    const int hd = P.head_dim, group = P.heads / P.kv_heads;
+    const int qw = P.heads * hd, kvw = P.kv_heads * hd;
+    const bool llama = P.family == SPM_FAMILY_LLAMA;
+    const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
+    pdl_wait();
+    const float* qg = P.q + size_t(i) * qw + size_t(kvh) * group * hd;
+    for (int t = threadIdx.x; t < group * hd; t += NT) qs[t] = qg[t];
+    if (!qmode)
+        for (int t = threadIdx.x; t < hd; t += NT) {
+            kn[t] = P.k[size_t(i) * kvw + size_t(kvh) * hd + t];
+            vn[t] = P.v[size_t(i) * kvw + size_t(kvh) * hd + t];
+        }
+    __syncthreads();
+    if (qmode) {
+        // the query is normed and rotated, the cache rows are in place
+    } else if (P.family == SPM_FAMILY_OLMOE) {
+        float sq = 0.f, sk = 0.f;
+        for (int t = threadIdx.x; t < qw; t += NT) sq = fmaf(P.q[size_t(i) * qw + t], P.q[size_t(i) * qw + t], sq);
+        for (int t = threadIdx.x; t < kvw; t += NT) sk = fmaf(P.k[size_t(i) * kvw + t], P.k[size_t(i) * kvw + t], sk);
+        sq = block_sum<NT>(sq, red);
+        sk = block_sum<NT>(sk, red);
+        const float scq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, float(qw)), P.eps)));
+        const float sck = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sk, float(kvw)), P.eps)));
+        for (int t = threadIdx.x; t < group * hd; t += NT)
+            qs[t] = __fmul_rn(__fmul_rn(qs[t], scq), P.q_norm[kvh * group * hd + t]);
+        for (int t = threadIdx.x; t < hd; t += NT) kn[t] = __fmul_rn(__fmul_rn(kn[t], sck), P.k_norm[kvh * hd + t]);
+        __syncthreads();
+    } else if (!llama) {
+        // per-head RMSNorm, one warp per head (spm-qwen3-slice/src/attention.rs:27-34)
+        for (int h = warp; h <= group; h += NT / 32) {
+            float* x = h < group ? qs + h * hd : kn;
+            const float* g = h < group ? P.q_norm : P.k_norm;
+            float ss = 0.f;
+            for (int t = lane; t < hd; t += 32) ss = fmaf(x[t], x[t], ss);
+            ss = warp_sum(ss);
+            const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(hd)), P.eps)));
+            __syncwarp();
+            for (int t = lane; t < hd; t += 32) x[t] = __fmul_rn(__fmul_rn(x[t], s), g[t]);
+        }
+        __syncthreads();
+    }
+    const int half = hd / 2;
+    const float2* rt = P.rope + size_t(pos) * half;
+    for (int t = threadIdx.x; !qmode && t < (group + 1) * half; t += NT) {
+        const int h = t / half, j = t % half;
+        float* x = h < group ? qs + h * hd : kn;
+        const float2 cs = rt[j];
+        rope_pair(x[j], x[j + half], cs.x, cs.y, llama);
+    }
+    __syncthreads();
+    if (!qmode && pos >= p0 && pos < p0 + P.chunk)
+        for (int t = threadIdx.x; t < hd; t += NT) {
+            kc[size_t(pos) * kvw + t] = kn[t];
+            vc[size_t(pos) * kvw + t] = vn[t];
+        }
+}
+
+// Once every CTA of a (kv head, client) has written its chunk's partial to
+// P.scratch (unnormalised value sums, then the max and the sum of
+// exponentials of each head): the last one to finish combines the partials
+// in chunk order into the output.
+template <int NT>
+__device__ void attn_combine(const AttnParams& P, int i, int kvh, int S) {
+    const int hd = P.head_dim, group = P.heads / P.kv_heads, qw = P.heads * hd;
+    // ---- the last chunk CTA of this (kv head, client) combines ----
+    __shared__ int last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int* ctr = P.counters + i * P.kv_heads + kvh;
+        last = atomicAdd(ctr, 1) == S - 1;
+        if (last) *ctr = 0;
+    }
+    __syncthreads();
+    pdl_trigger();
+    if (!last) return;
+    __threadfence();
+    const float* parts = P.scratch + (size_t(i) * P.kv_heads + kvh) * S * group * (hd + 2);
+    for (int t = threadIdx.x; t < group * hd; t += NT) {
+        const int h = t / hd, dd = t % hd;
+        float M = -INFINITY;
+#pragma unroll 4
+        for (int s = 0; s < S; s++) M = fmaxf(M, __ldcg(parts + (size_t(s) * group + h) * (hd + 2) + hd));
+        // chunks in order; the loads of four chunks are in flight together
+        float Lsum = 0.f, O = 0.f;
+#pragma unroll 4
+        for (int s = 0; s < S; s++) {
+            const float* ps = parts + (size_t(s) * group + h) * (hd + 2);
+            const float m = __ldcg(ps + hd), l = __ldcg(ps + hd + 1), o = __ldcg(ps + dd);
+            const float w = m == -INFINITY ? 0.f : expf(m - M);
+            Lsum = fmaf(l, w, Lsum);
+            O = fmaf(o, w, O);
+        }
+        P.out[size_t(i) * qw + (size_t(kvh) * group + h) * hd + dd] = __fdiv_rn(O, Lsum);
+    }
+}
+
 // Shared memory of the attention kernel, in floats (mbarriers at the end).
 struct AttnSmem {
     int qs, kn, vn, kt, vt, part, prob, stat, total;
@@ -215,57 +322,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         if (j < ntiles) request(j);
         else cp_async_commit();  // empty group: the wait counts below stay uniform
     }
-    pdl_wait();
-    const float* qg = P.q + size_t(i) * qw + size_t(kvh) * group * hd;
-    for (int t = threadIdx.x; t < group * hd; t += kAttnThreads) qs[t] = qg[t];
-    if (!qmode)
-        for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
-            kn[t] = P.k[size_t(i) * kvw + size_t(kvh) * hd + t];
-            vn[t] = P.v[size_t(i) * kvw + size_t(kvh) * hd + t];
-        }
-    __syncthreads();
-    if (qmode) {
-        // the query is normed and rotated, the cache rows are in place
-    } else if (P.family == SPM_FAMILY_OLMOE) {
-        float sq = 0.f, sk = 0.f;
-        for (int t = threadIdx.x; t < qw; t += kAttnThreads) sq = fmaf(P.q[size_t(i) * qw + t], P.q[size_t(i) * qw + t], sq);
-        for (int t = threadIdx.x; t < kvw; t += kAttnThreads) sk = fmaf(P.k[size_t(i) * kvw + t], P.k[size_t(i) * kvw + t], sk);
-        sq = block_sum<kAttnThreads>(sq, red);
-        sk = block_sum<kAttnThreads>(sk, red);
-        const float scq = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sq, float(qw)), P.eps)));
-        const float sck = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sk, float(kvw)), P.eps)));
-        for (int t = threadIdx.x; t < group * hd; t += kAttnThreads)
-            qs[t] = __fmul_rn(__fmul_rn(qs[t], scq), P.q_norm[kvh * group * hd + t]);
-        for (int t = threadIdx.x; t < hd; t += kAttnThreads) kn[t] = __fmul_rn(__fmul_rn(kn[t], sck), P.k_norm[kvh * hd + t]);
-        __syncthreads();
-    } else if (!llama) {
-        // per-head RMSNorm, one warp per head (spm-qwen3-slice/src/attention.rs:27-34)
-        for (int h = warp; h <= group; h += kAttnThreads / 32) {
-            float* x = h < group ? qs + h * hd : kn;
-            const float* g = h < group ? P.q_norm : P.k_norm;
-            float ss = 0.f;
-            for (int t = lane; t < hd; t += 32) ss = fmaf(x[t], x[t], ss);
-            ss = warp_sum(ss);
-            const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(hd)), P.eps)));
-            __syncwarp();
-            for (int t = lane; t < hd; t += 32) x[t] = __fmul_rn(__fmul_rn(x[t], s), g[t]);
-        }
-        __syncthreads();
-    }
-    const int half = hd / 2;
-    const float2* rt = P.rope + size_t(pos) * half;
-    for (int t = threadIdx.x; !qmode && t < (group + 1) * half; t += kAttnThreads) {
-        const int h = t / half, j = t % half;
-        float* x = h < group ? qs + h * hd : kn;
-        const float2 cs = rt[j];
-        rope_pair(x[j], x[j + half], cs.x, cs.y, llama);
-    }
-    __syncthreads();
-    if (!qmode && pos >= p0 && pos < p0 + P.chunk)
-        for (int t = threadIdx.x; t < hd; t += kAttnThreads) {
-            kc[size_t(pos) * kvw + t] = kn[t];
-            vc[size_t(pos) * kvw + t] = vn[t];
-        }
+    attn_prepare<kAttnThreads>(P, i, kvh, pos, p0, qmode, qs, kn, vn, red, kc, vc);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(float(hd)));
     const float denom = __fsqrt_rn(float(hd));
     // scores: warp w takes head w % group (R = 8 / group warps per head, each
@@ -389,37 +446,320 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         outp[threadIdx.x * (hd + 2) + hd] = m_sh[threadIdx.x];
         outp[threadIdx.x * (hd + 2) + hd + 1] = m_sh[group + threadIdx.x];
     }
-    // ---- the last chunk CTA of this (kv head, client) combines ----
-    __shared__ int last;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int* ctr = P.counters + i * P.kv_heads + kvh;
-        last = atomicAdd(ctr, 1) == S - 1;
-        if (last) *ctr = 0;
+    attn_combine<kAttnThreads>(P, i, kvh, S);
+}
+
+// ------------------------------------------------ attention on tensor cores ----
+// Decode attention of the grouped-query models (4 to 8 query heads per kv
+// head, head_dim 64 or 128) with the products on the tensor cores
+// (mma.sync m16n8k16, bf16 operands, fp32 accumulation).  Every fp32 operand
+// is split exactly into three bf16 parts by truncation, x = hi + mid + lo
+// (8 + 8 + 8 significant bits), and a product takes the six part products
+// hi*hi, hi*mid, mid*hi, hi*lo, mid*mid, lo*hi (the three left out are below
+// 2^-32 of it), smallest first.  Per warp and 16 cached positions:
+//   scores  S^T (16 positions x 8 heads) = K (16 x hd) . Q^T (hd x 8 heads)
+//   softmax of each head over the positions: running max and sum, as in
+//           attention_kernel (the reference's scores, scale and mask)
+//   values  O^T (hd x 8 heads) += V^T (hd x 16) . P^T (16 x 8 heads)
+// The probability fragments become the B operand of the value product by a
+// transpose of each 8 x 8 block (movmatrix); heads beyond the group are zero
+// columns.  Grid (kv head, client, chunk) as attention_kernel, one CTA of
+// four warps per SM: warp w streams sub-tiles w, w + 4, ... of its chunk
+// (16 positions each) through its own two-stage ring of bulk row copies,
+// the warps' softmax states are merged through shared memory, and the
+// chunks' partials as in attention_kernel.
+constexpr int kTcWarps = 4, kTcThreads = 32 * kTcWarps, kTcStages = 2, kTcSub = 16;
+
+template <int HD>
+struct AttnTcSmem {  // in floats
+    // row strides: the key fragments (8-byte loads of rows g, 2t) and the
+    // value fragments (4-byte loads of rows 2t, column g) hit distinct banks
+    static constexpr int ldk = HD + 8, ldv = HD + 4;
+    static constexpr int stage = kTcSub * (ldk + ldv);
+    static constexpr int qs = 0, kn = 8 * HD, vn = kn + HD, red = vn + HD, ring = red + 64;
+    static constexpr int total = ring + kTcWarps * kTcStages * stage;
+    // after the loop the ring holds the warps' states: [warp][8 heads][HD + 2]
+    static_assert(kTcWarps * 8 * (HD + 2) <= kTcWarps * kTcStages * stage, "warp states fit in the ring");
+};
+
+// x0, x1 -> three bf16x2 words (hi, mid, lo), x0 in the low halves.
+__device__ __forceinline__ void split3(float x0, float x1, uint32_t (&p)[3]) {
+    const uint32_t b0 = __float_as_uint(x0), b1 = __float_as_uint(x1);
+    const float r0 = __fsub_rn(x0, __uint_as_float(b0 & 0xffff0000u));
+    const float r1 = __fsub_rn(x1, __uint_as_float(b1 & 0xffff0000u));
+    const uint32_t c0 = __float_as_uint(r0), c1 = __float_as_uint(r1);
+    const float l0 = __fsub_rn(r0, __uint_as_float(c0 & 0xffff0000u));
+    const float l1 = __fsub_rn(r1, __uint_as_float(c1 & 0xffff0000u));
+    p[0] = __byte_perm(b0, b1, 0x7632);
+    p[1] = __byte_perm(c0, c1, 0x7632);
+    p[2] = __byte_perm(__float_as_uint(l0), __float_as_uint(l1), 0x7632);
+}
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// d += A . B over the six part products, smallest first.
+__device__ __forceinline__ void mma_split(float (&d)[4], const uint32_t (&a)[3][4], const uint32_t (&b)[3][2]) {
+    mma_bf16(d, a[2], b[0][0], b[0][1]);  // lo  x hi
+    mma_bf16(d, a[1], b[1][0], b[1][1]);  // mid x mid
+    mma_bf16(d, a[0], b[2][0], b[2][1]);  // hi  x lo
+    mma_bf16(d, a[1], b[0][0], b[0][1]);  // mid x hi
+    mma_bf16(d, a[0], b[1][0], b[1][1]);  // hi  x mid
+    mma_bf16(d, a[0], b[0][0], b[0][1]);  // hi  x hi
+}
+
+__device__ __forceinline__ uint32_t movtrans(uint32_t a) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnParams P) {
+    using L = AttnTcSmem<HD>;
+    constexpr int KS = HD / 16;  // k-steps of the scores, m-tiles of the values
+    extern __shared__ __align__(128) float sm[];
+    __shared__ uint64_t full[kTcWarps][kTcStages];
+    const int kvh = blockIdx.x, i = blockIdx.y, chunk = blockIdx.z, S = gridDim.z;
+    const int group = P.heads / P.kv_heads, kvw = P.kv_heads * HD, qw = P.heads * HD;
+    const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31), g = lane >> 2, t = lane & 3;
+    const int pos = P.pos[i];
+    const int p0 = chunk * P.chunk, p1 = min(pos + 1, p0 + P.chunk);
+    const int npos = max(0, p1 - p0), nsub = (npos + kTcSub - 1) / kTcSub;
+    const int mine = nsub > warp ? (nsub - warp + kTcWarps - 1) / kTcWarps : 0;  // this warp's sub-tiles
+    const size_t cc = size_t(P.cache_client) + size_t(i);
+    const size_t base = (cc * P.layers + P.layer) * P.context * size_t(kvw) + size_t(kvh) * HD;
+    float* kc = P.kcache + base;
+    float* vc = P.vcache + base;
+    float* ring = sm + L::ring + warp * kTcStages * L::stage;
+    if (lane == 0) {
+        for (int s = 0; s < kTcStages; s++) mbar_init(&full[warp][s], 1);
+        mbar_fence_init();
     }
-    __syncthreads();
-    pdl_trigger();
-    if (!last) return;
-    __threadfence();
-    const float* parts = P.scratch + (size_t(i) * P.kv_heads + kvh) * S * group * (hd + 2);
-    for (int t = threadIdx.x; t < group * hd; t += kAttnThreads) {
-        const int h = t / hd, dd = t % hd;
-        float M = -INFINITY;
-#pragma unroll 4
-        for (int s = 0; s < S; s++) M = fmaxf(M, __ldcg(parts + (size_t(s) * group + h) * (hd + 2) + hd));
-        // chunks in order; the loads of four chunks are in flight together
-        float Lsum = 0.f, O = 0.f;
-#pragma unroll 4
-        for (int s = 0; s < S; s++) {
-            const float* ps = parts + (size_t(s) * group + h) * (hd + 2);
-            const float m = __ldcg(ps + hd), l = __ldcg(ps + hd + 1), o = __ldcg(ps + dd);
-            const float w = m == -INFINITY ? 0.f : expf(m - M);
-            Lsum = fmaf(l, w, Lsum);
-            O = fmaf(o, w, O);
+    __syncwarp();
+    // sub-tile j of this warp: positions s0 .. s0 + nr - 1 into stage j % 2,
+    // lanes 0-15 copying the key rows and lanes 16-31 the value rows
+    auto issue = [&](int j) {
+        const int st = j % kTcStages, s0 = p0 + (warp + kTcWarps * j) * kTcSub, nr = min(kTcSub, p1 - s0);
+        float* kt = ring + st * L::stage;
+        if (lane == 0) mbar_expect_tx(&full[warp][st], uint32_t(nr) * 2u * HD * 4u);
+        __syncwarp();
+        const int r = lane & 15;
+        if (r < nr) {
+            if (lane < 16) bulk_g2s(kt + r * L::ldk, kc + size_t(s0 + r) * kvw, HD * 4, &full[warp][st]);
+            else bulk_g2s(kt + kTcSub * L::ldk + r * L::ldv, vc + size_t(s0 + r) * kvw, HD * 4, &full[warp][st]);
         }
-        P.out[size_t(i) * qw + (size_t(kvh) * group + h) * hd + dd] = __fdiv_rn(O, Lsum);
+    };
+    // the cached rows come from earlier steps: requested before the wait for q, k, v
+    for (int j = 0; j < kTcStages && j < mine; j++) issue(j);
+    float* qs = sm + L::qs;
+    float* kn = sm + L::kn;
+    float* vn = sm + L::vn;
+    attn_prepare<kTcThreads>(P, i, kvh, pos, p0, false, qs, kn, vn, sm + L::red, kc, vc);
+    const bool llama = P.family == SPM_FAMILY_LLAMA;
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(float(HD)));
+    const float denom = __fsqrt_rn(float(HD));
+    // Q^T as the B operand: lane (g, t) holds head g's dims 2t, 2t+1 (+8) of each k-step
+    uint32_t bq[KS][3][2];
+#pragma unroll
+    for (int ks = 0; ks < KS; ks++) {
+        const bool on = g < group;
+        const float* qr = qs + (on ? g : 0) * HD + ks * 16 + 2 * t;
+        uint32_t lo[3], hi[3];
+        split3(on ? qr[0] : 0.f, on ? qr[1] : 0.f, lo);
+        split3(on ? qr[8] : 0.f, on ? qr[9] : 0.f, hi);
+#pragma unroll
+        for (int q = 0; q < 3; q++) {
+            bq[ks][q][0] = lo[q];
+            bq[ks][q][1] = hi[q];
+        }
     }
+    // softmax state of heads 2t, 2t+1 (the sums per lane, added up at the end)
+    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+    float o[KS][4];  // O^T m-tile mt: dims mt*16 + g (+8) x heads 2t, 2t+1
+#pragma unroll
+    for (int mt = 0; mt < KS; mt++) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    // copy phase issued into stage 0 / 1 and not yet waited for (-1: none)
+    int out0 = mine > 0 ? 0 : -1, out1 = mine > 1 ? 1 : -1;
+    bool ok = true;
+    for (int j = 0; j < mine; j++) {
+        const int st = j % kTcStages, s0 = p0 + (warp + kTcWarps * j) * kTcSub, nr = min(kTcSub, p1 - s0);
+        float* kt = ring + st * L::stage;
+        float* vt = kt + kTcSub * L::ldk;
+        if (!mbar_wait(&full[warp][st], uint32_t(j / kTcStages) & 1u)) {
+            flag(P.status, 6);
+            ok = false;
+            break;
+        }
+        (st ? out1 : out0) = -1;
+        if (nr < kTcSub)  // rows past the chunk: zero (probability 0, value finite)
+            for (int e = lane; e < (kTcSub - nr) * HD; e += 32) {
+                const int r = nr + e / HD, c = e % HD;
+                kt[r * L::ldk + c] = 0.f;
+                vt[r * L::ldv + c] = 0.f;
+            }
+        if (pos >= s0 && pos < s0 + nr)  // the new row: the copy brought the cache's old contents
+            for (int c = lane; c < HD; c += 32) {
+                kt[(pos - s0) * L::ldk + c] = kn[c];
+                vt[(pos - s0) * L::ldv + c] = vn[c];
+            }
+        __syncwarp();
+        // ---- scores: two accumulators over alternate k-steps ----
+        float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int ks = 0; ks < KS; ks++) {
+            const float* k0 = kt + g * L::ldk + ks * 16 + 2 * t;
+            const float2 x0 = *reinterpret_cast<const float2*>(k0);
+            const float2 x1 = *reinterpret_cast<const float2*>(k0 + 8 * L::ldk);
+            const float2 x2 = *reinterpret_cast<const float2*>(k0 + 8);
+            const float2 x3 = *reinterpret_cast<const float2*>(k0 + 8 * L::ldk + 8);
+            uint32_t a[3][4], p[3];
+            split3(x0.x, x0.y, p);
+            a[0][0] = p[0], a[1][0] = p[1], a[2][0] = p[2];
+            split3(x1.x, x1.y, p);
+            a[0][1] = p[0], a[1][1] = p[1], a[2][1] = p[2];
+            split3(x2.x, x2.y, p);
+            a[0][2] = p[0], a[1][2] = p[1], a[2][2] = p[2];
+            split3(x3.x, x3.y, p);
+            a[0][3] = p[0], a[1][3] = p[1], a[2][3] = p[2];
+            if (ks & 1) mma_split(sb, a, bq[ks]);
+            else mma_split(sa, a, bq[ks]);
+        }
+        // ---- softmax: sc[0], sc[1] position g, heads 2t, 2t+1; sc[2], sc[3] position g + 8 ----
+        float sc[4], pr[4], mx[2], alpha[2];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float d = sa[e] + sb[e];
+            const bool valid = (e < 2 ? g : g + 8) < nr;
+            sc[e] = !valid ? -INFINITY : llama ? __fmul_rn(d, scale) : __fdiv_rn(d, denom);
+        }
+        mx[0] = fmaxf(sc[0], sc[2]);
+        mx[1] = fmaxf(sc[1], sc[3]);
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+            mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], off));
+            mx[1] = fmaxf(mx[1], __shfl_xor_sync(0xffffffffu, mx[1], off));
+        }
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const float m_new = fmaxf(m_run[h], mx[h]);
+            alpha[h] = m_run[h] == -INFINITY ? 0.f : expf(m_run[h] - m_new);
+            m_run[h] = m_new;
+        }
+#pragma unroll
+        for (int e = 0; e < 4; e++) pr[e] = sc[e] == -INFINITY ? 0.f : expf(sc[e] - m_run[e & 1]);
+#pragma unroll
+        for (int h = 0; h < 2; h++) l_run[h] = fmaf(l_run[h], alpha[h], pr[h] + pr[h + 2]);
+#pragma unroll
+        for (int mt = 0; mt < KS; mt++) {
+            o[mt][0] *= alpha[0];
+            o[mt][1] *= alpha[1];
+            o[mt][2] *= alpha[0];
+            o[mt][3] *= alpha[1];
+        }
+        // ---- P^T as the B operand: positions 2t, 2t+1 (+8) of head g ----
+        uint32_t bp[3][2];
+        {
+            uint32_t pa[3], pb[3];
+            split3(pr[0], pr[1], pa);
+            split3(pr[2], pr[3], pb);
+#pragma unroll
+            for (int q = 0; q < 3; q++) {
+                bp[q][0] = movtrans(pa[q]);
+                bp[q][1] = movtrans(pb[q]);
+            }
+        }
+        // ---- values: V^T m-tile mt (dims mt*16 ..) times P^T ----
+#pragma unroll
+        for (int mt = 0; mt < KS; mt++) {
+            const float* v0 = vt + (2 * t) * L::ldv + mt * 16 + g;
+            uint32_t a[3][4], p[3];
+            split3(v0[0], v0[L::ldv], p);
+            a[0][0] = p[0], a[1][0] = p[1], a[2][0] = p[2];
+            split3(v0[8], v0[L::ldv + 8], p);
+            a[0][1] = p[0], a[1][1] = p[1], a[2][1] = p[2];
+            split3(v0[8 * L::ldv], v0[9 * L::ldv], p);
+            a[0][2] = p[0], a[1][2] = p[1], a[2][2] = p[2];
+            split3(v0[8 * L::ldv + 8], v0[9 * L::ldv + 8], p);
+            a[0][3] = p[0], a[1][3] = p[1], a[2][3] = p[2];
+            mma_split(o[mt], a, bp);
+        }
+        __syncwarp();
+        if (j + kTcStages < mine) {
+            fence_proxy_async();  // this stage's reads and writes before the copies that refill it
+            issue(j + kTcStages);
+            (st ? out1 : out0) = j + kTcStages;
+        }
+    }
+    if (!ok) {
+        // a wait gave up: the copies still in flight land before the CTA ends
+        // (each phase waited for once more, bounded), and this warp adds nothing
+        if (out0 >= 0) mbar_wait(&full[warp][0], uint32_t(out0 / kTcStages) & 1u);
+        if (out1 >= 0) mbar_wait(&full[warp][1], uint32_t(out1 / kTcStages) & 1u);
+        m_run[0] = m_run[1] = -INFINITY;
+        l_run[0] = l_run[1] = 0.f;
+#pragma unroll
+        for (int mt = 0; mt < KS; mt++) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+    }
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int off = 4; off < 32; off <<= 1) l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], off);
+    __syncthreads();  // every warp is done with its ring: it holds the warps' states now
+    {
+        float* ws = sm + L::ring + warp * 8 * (HD + 2);
+#pragma unroll
+        for (int mt = 0; mt < KS; mt++) {
+            ws[(2 * t) * (HD + 2) + mt * 16 + g] = o[mt][0];
+            ws[(2 * t + 1) * (HD + 2) + mt * 16 + g] = o[mt][1];
+            ws[(2 * t) * (HD + 2) + mt * 16 + g + 8] = o[mt][2];
+            ws[(2 * t + 1) * (HD + 2) + mt * 16 + g + 8] = o[mt][3];
+        }
+        if (g == 0) {
+            ws[(2 * t) * (HD + 2) + HD] = m_run[0];
+            ws[(2 * t + 1) * (HD + 2) + HD] = m_run[1];
+            ws[(2 * t) * (HD + 2) + HD + 1] = l_run[0];
+            ws[(2 * t + 1) * (HD + 2) + HD + 1] = l_run[1];
+        }
+    }
+    __syncthreads();
+    // the warps' states merged in warp order: this chunk's partial, or the output
+    float* outp = P.scratch + ((size_t(i) * P.kv_heads + kvh) * S + chunk) * group * (HD + 2);
+    for (int e = threadIdx.x; e < group * HD; e += kTcThreads) {
+        const int h = e / HD, d = e % HD;
+        const float* st = sm + L::ring + h * (HD + 2);
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kTcWarps; w++) M = fmaxf(M, st[w * 8 * (HD + 2) + HD]);
+        float Lsum = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < kTcWarps; w++) {
+            const float* ws = st + w * 8 * (HD + 2);
+            const float m = ws[HD];
+            const float wt = m == -INFINITY ? 0.f : expf(m - M);
+            Lsum = fmaf(ws[HD + 1], wt, Lsum);
+            O = fmaf(ws[d], wt, O);
+        }
+        if (S == 1) {
+            P.out[size_t(i) * qw + (size_t(kvh) * group + h) * HD + d] = __fdiv_rn(O, Lsum);
+        } else {
+            outp[h * (HD + 2) + d] = O;
+            if (d == 0) {
+                outp[h * (HD + 2) + HD] = M;
+                outp[h * (HD + 2) + HD + 1] = Lsum;
+            }
+        }
+    }
+    if (S == 1) {
+        pdl_trigger();
+        return;
+    }
+    attn_combine<kTcThreads>(P, i, kvh, S);
 }
 
 }  // namespace
@@ -444,7 +784,48 @@ static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
+// The tensor-core kernel takes decode steps of 4 to 8 query heads per kv head
+// and head_dim 64 or 128.
+static bool attention_tc_fits(const AttnParams& P) {
+    const int group = P.heads / P.kv_heads;
+    return P.qpos == nullptr && group >= 4 && group <= 8 && (P.head_dim == 64 || P.head_dim == 128);
+}
+
+template <int HD>
+static cudaError_t launch_attention_tc(const AttnParams& P, int n, int sms, cudaStream_t s, bool pdl) {
+    const size_t smem = size_t(AttnTcSmem<HD>::total) * sizeof(float);
+    static int configured_for = -1;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_for != dev) {
+        cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             int(smem));
+        if (e != cudaSuccess) return e;
+        configured_for = dev;
+    }
+    // one CTA per SM: about as many (kv head, client, chunk) CTAs as SMs,
+    // chunks a multiple of the four warps' 16 positions
+    const int pairs = P.kv_heads * n;
+    const int want = std::max(1, sms / pairs);
+    int chunk = (P.context + want - 1) / want;
+    chunk = std::max(kAttnMinChunk, (chunk + kAttnMinChunk - 1) / kAttnMinChunk * kAttnMinChunk);
+    const int chunks = (P.context + chunk - 1) / chunk;
+    AttnParams p = P;
+    p.chunk = chunk;
+    void* args[] = {&p};
+    return launch_pdl(reinterpret_cast<const void*>(attention_tc_kernel<HD>), dim3(P.kv_heads, n, chunks),
+                      dim3(kTcThreads), smem, s, pdl, args);
+}
+
 cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t s, bool pdl) {
+    if (attention_tc_fits(P)) {
+        static int tc_sms[64] = {};
+        int d = 0;
+        cudaGetDevice(&d);
+        if (d < 64 && !tc_sms[d]) cudaDeviceGetAttribute(&tc_sms[d], cudaDevAttrMultiProcessorCount, d);
+        const int sms = d < 64 && tc_sms[d] ? tc_sms[d] : 148;
+        return P.head_dim == 128 ? launch_attention_tc<128>(P, n, sms, s, pdl) : launch_attention_tc<64>(P, n, sms, s, pdl);
+    }
     const size_t smem = attention_smem(P);
     static int configured_for = -1;
     int dev = 0;

@@ -22,7 +22,7 @@
 // which the producers wait on before refilling it.  The epilogue reads the
 // 128 x 128 fp32 accumulator from TMEM (each warp its quarter of the lanes and
 // half of the columns) and stores y (plus a residual for EPI_ADD).  All
-// operands come from this GPU's own memory; no multicast, no clusters.
+// operands come from this GPU's own memory, each CTA loading its own tiles; no clusters.
 #include <cuda_runtime.h>
 
 #include "dequant.cuh"

@@ -14,7 +14,7 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 LOGIT_TOL = 1e-3
-DENSE = ["llama-q8_0", "llama-q6_k", "qwen3-q6_k", "qwen3-q5_k", "qwen3-q2_k"]
+DENSE = ["llama-q8_0", "llama-q6_k", "qwen3-q6_k", "qwen3-q5_k", "qwen3-q2_k", "qwen3-g8-q6_k"]
 
 
 def logits_close(got, want):
@@ -209,10 +209,11 @@ def test_qwen3_8b_shape_two_layers_matches_the_oracle(cuda):
     m.close()
 
 
-@pytest.mark.parametrize("name", ["llama-q8_0", "qwen3-q6_k"])
+@pytest.mark.parametrize("name", ["llama-q8_0", "qwen3-q6_k", "qwen3-q5_k", "qwen3-g8-q6_k"])
 def test_long_context_attention_matches_the_oracle(cuda, models, name):
-    # past kAttnChunk (256) positions the attention splits a client's prefix
-    # over several CTAs and combines their softmax partials
+    # a client's prefix splits over several CTAs whose softmax partials are
+    # combined (qwen3-q5_k, qwen3-g8-q6_k: the tensor-core kernel, four and
+    # eight query heads per kv head)
     r, img, m, om = models(name)
     n, steps = 2, 600
     sess = eb.Session(m, n, steps)

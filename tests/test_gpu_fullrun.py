@@ -3,12 +3,17 @@ full runs (tests/golden/runs/*.npz, made by tests/golden/make_runs.py).
 
 The schedule is serve-demo's lockstep (spm-batch/examples/serve-demo.rs:
 59-91): every tick one decode step for every client, prompt tokens fed one
-per tick, then each client's own greedy picks.  At every tick of the whole
-run -- prompt ticks included -- the device's greedy pick must equal the
-oracle's, and its logits at the oracle's eight largest must lie within
-1e-3 * max|logit| of the oracle's values.  The synthetic model is made here
-from its seeded recipe; the golden file records a digest of the bytes it was
-made from.
+per tick, then the greedy picks.  The device follows the oracle's run: its
+next token is the oracle's pick, so one tick's result cannot move the
+following ticks off the oracle's path.  At every tick of the whole run --
+prompt ticks included -- the device's greedy pick must equal the oracle's,
+and its logits at the oracle's eight largest must lie within
+1e-3 * max|logit| of the oracle's values.  The one exception is a near tie:
+where the oracle's best and the device's pick lie within TIE * max|logit| in
+the oracle's own logits (the order of the fp32 sums decides between them;
+the golden files hold a handful of such ticks among thousands), either is
+accepted.  The synthetic model is made here from its seeded recipe; the
+golden file records a digest of the bytes it was made from.
 """
 import dataclasses
 from pathlib import Path
@@ -23,6 +28,7 @@ pytestmark = pytest.mark.gpu
 
 RUNS = Path(__file__).resolve().parent / "golden" / "runs"
 LOGIT_TOL = 1e-3
+TIE = 1e-4
 
 
 def _digest(img):
@@ -42,11 +48,19 @@ def _load(name):
 
 
 def _check_tick(t, best, logits, g):
-    assert best == g["argmax"][t].tolist(), f"tick {t}: greedy picks {best} != {g['argmax'][t].tolist()}"
+    """Returns the number of near ties the device decided the other way."""
     ids, vals, scale = g["top_ids"][t], g["top_vals"][t], g["maxabs"][t]
+    ties = 0
     for i in range(len(best)):
+        want = int(g["argmax"][t][i])
+        if best[i] != want:
+            where = np.nonzero(ids[i] == best[i])[0]
+            assert where.size and vals[i][0] - vals[i][where[0]] <= TIE * scale[i], \
+                f"tick {t} client {i}: greedy pick {best[i]} != {want} (not a near tie)"
+            ties += 1
         err = np.abs(logits[i, ids[i]] - vals[i]).max()
         assert err <= LOGIT_TOL * scale[i], (t, i, float(err), float(scale[i]))
+    return ties
 
 
 def _model(name):
@@ -69,12 +83,16 @@ def test_full_run_matches_the_oracle(cuda, name):
     assert g["argmax"].shape == (ticks, n)
     s = eb.Session(m, n, longest + w["steps"] + 1)
     toks = [p[0] for p in prompts]
+    ties = 0
     for t in range(ticks):
         best, logits = s.decode_step(toks, want_logits=True)
-        _check_tick(t, best, logits, g)
-        toks = [p[t + 1] if t + 1 < len(p) else best[i] for i, p in enumerate(prompts)]
+        ties += _check_tick(t, best, logits, g)
+        oracle = g["argmax"][t].tolist()
+        toks = [p[t + 1] if t + 1 < len(p) else oracle[i] for i, p in enumerate(prompts)]
     s.close()
     m.close()
+    near = int((g["margin"] <= TIE * g["maxabs"]).sum())
+    assert ties <= near, (ties, near)
 
 
 def test_full_run_with_tensor_core_prompts(cuda):
@@ -96,7 +114,7 @@ def test_full_run_with_tensor_core_prompts(cuda):
     for t in range(L - 1, L + w["steps"] - 1):
         best, logits = s.decode_step(toks, want_logits=True)
         _check_tick(t, best, logits, g)
-        toks = best
+        toks = g["argmax"][t].tolist()
     s.close()
     m.close()
 
