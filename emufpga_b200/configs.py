@@ -110,8 +110,11 @@ TINY = {
                          gain_sigma=0.1),
     "qwen3-q2_k": Recipe(Shape(QWEN3, 2, 256, 512, 4, 2, 64, 160, rope_base=1e6, eps=1e-6), Q2_K, Q2_K, Q6_K, seed=11,
                          gain_sigma=0.1),
-    # eight query heads of 128 per kv head (the Qwen3-30B-A3B grouping)
-    "qwen3-g8-q6_k": Recipe(Shape(QWEN3, 2, 256, 512, 8, 1, 128, 160, rope_base=1e6, eps=1e-6), Q6_K, Q6_K, Q6_K,
+    # four query heads of 64 per kv head, two kv heads
+    "qwen3-g4-q5_k": Recipe(Shape(QWEN3, 2, 256, 512, 8, 2, 64, 160, rope_base=1e6, eps=1e-6), Q5_K, Q5_K, Q5_K,
+                            seed=16, gain_sigma=0.1),
+    # eight query heads of 128 per kv head (the Qwen3-30B-A3B grouping), two kv heads
+    "qwen3-g8-q6_k": Recipe(Shape(QWEN3, 2, 256, 512, 16, 2, 128, 160, rope_base=1e6, eps=1e-6), Q6_K, Q6_K, Q6_K,
                             seed=15, gain_sigma=0.1),
     "olmoe-q6_k": Recipe(Shape(OLMOE, 2, 256, 0, 4, 4, 64, 128, experts=8, experts_used=2, expert_ff=256),
                          Q6_K, Q6_K, Q6_K, expert_type=Q6_K, seed=12, zipf_s=1.1, gain_sigma=0.1),

@@ -64,6 +64,27 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+// x = hi + mid + lo exactly, each part a bf16 (its bits returned): hi the
+// top 16 bits of x, mid those of x - hi, lo those of x - hi - mid (x's 24
+// significant bits are 8 + 8 + 8; every subtraction is exact).
+__device__ __forceinline__ void split3_bits(float x, uint16_t (&p)[3]) {
+    const uint32_t b = __float_as_uint(x);
+    const float r = __fsub_rn(x, __uint_as_float(b & 0xffff0000u));
+    const uint32_t c = __float_as_uint(r);
+    const float l = __fsub_rn(r, __uint_as_float(c & 0xffff0000u));
+    p[0] = uint16_t(b >> 16);
+    p[1] = uint16_t(c >> 16);
+    p[2] = uint16_t(__float_as_uint(l) >> 16);
+}
+// Row c of a plane row [3][hd] of bf16 bits.
+__device__ __forceinline__ void store_planes(uint16_t* row, int hd, int c, float x) {
+    uint16_t p[3];
+    split3_bits(x, p);
+    row[c] = p[0];
+    row[hd + c] = p[1];
+    row[2 * hd + c] = p[2];
+}
+
 // ---- time, errors ----
 __device__ __forceinline__ uint64_t now_ns() {
     uint64_t t;

@@ -82,6 +82,9 @@ struct spm_session {
     int max_clients = 0, context = 0;
     cudaStream_t stream = nullptr;
     float *kc = nullptr, *vc = nullptr;
+    // the cache rows split into three bf16 planes, for the tensor-core
+    // attention (models with 4-8 query heads per kv head, head_dim 64 or 128)
+    uint16_t *kp = nullptr, *vp = nullptr;
     float *states = nullptr, *normed = nullptr, *q = nullptr, *k = nullptr, *v = nullptr, *attn = nullptr;
     float *act = nullptr, *logits = nullptr;
     float2* rope = nullptr;
@@ -810,6 +813,7 @@ void enqueue_step(spm_session* s, int n) {
         AttnParams P{};
         P.q = s->q; P.k = s->k; P.v = s->v; P.out = s->attn;
         P.kcache = s->kc; P.vcache = s->vc; P.pos = s->pos + f0; P.rope = s->rope; P.cache_client = f0;
+        P.kplanes = s->kp; P.vplanes = s->vp;
         P.scratch = s->attn_scratch; P.counters = s->attn_counters;
         P.q_norm = L.q_norm >= 0 ? m->gains + L.q_norm : nullptr;
         P.k_norm = L.k_norm >= 0 ? m->gains + L.k_norm : nullptr;
@@ -1122,6 +1126,7 @@ void prefill_chunk(spm_session* s, int client, const uint32_t* tokens, int T, in
         gemm_rows(s, L.v, P.xn, nullptr, T, P.v, EPI_STORE);
         QkArgs q{};
         q.q = P.q; q.k = P.k; q.v = P.v; q.kcache = s->kc; q.vcache = s->vc; q.rope = s->rope;
+        q.kplanes = s->kp; q.vplanes = s->vp;
         q.q_norm = L.q_norm >= 0 ? m->gains + L.q_norm : nullptr;
         q.k_norm = L.k_norm >= 0 ? m->gains + L.k_norm : nullptr;
         q.client = client; q.layer = int(l); q.layers = int(c.layers); q.context = s->context; q.pos0 = pos0;
@@ -1515,6 +1520,13 @@ spm_status spm_session_create(spm_model* m, int32_t max_clients, int32_t max_con
         CUDA_OK(cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking));
         s->kc = s->alloc<float>(n * c.layers * size_t(max_context) * kvw);
         s->vc = s->alloc<float>(n * c.layers * size_t(max_context) * kvw);
+        {
+            const uint32_t grp = c.heads / c.kv_heads;
+            if (grp >= 4 && grp <= 8 && (c.head_dim == 64 || c.head_dim == 128)) {
+                s->kp = s->alloc<uint16_t>(3 * n * c.layers * size_t(max_context) * kvw);
+                s->vp = s->alloc<uint16_t>(3 * n * c.layers * size_t(max_context) * kvw);
+            }
+        }
         s->normed = s->alloc<float>(n * d);
         s->q = s->alloc<float>(n * qw);
         s->k = s->alloc<float>(n * kvw);

@@ -167,7 +167,7 @@ __device__ __forceinline__ void rope_pair(float& x, float& y, float c, float s, 
 // cache (spm-kv/src/cache.rs:49-58).  Waits for the kernel that produced q, k, v.
 template <int NT>
 __device__ void attn_prepare(const AttnParams& P, int i, int kvh, int pos, int p0, bool qmode, float* qs, float* kn,
-                             float* vn, float* red, float* kc, float* vc) {
+                             float* vn, float* red, float* kc, float* vc, uint16_t* kp, uint16_t* vp) {
     const int hd = P.head_dim, group = P.heads / P.kv_heads;
     const int qw = P.heads * hd, kvw = P.kv_heads * hd;
     const bool llama = P.family == SPM_FAMILY_LLAMA;
@@ -222,6 +222,10 @@ __device__ void attn_prepare(const AttnParams& P, int i, int kvh, int pos, int p
         for (int t = threadIdx.x; t < hd; t += NT) {
             kc[size_t(pos) * kvw + t] = kn[t];
             vc[size_t(pos) * kvw + t] = vn[t];
+            if (kp) {  // the plane rows of the same position
+                store_planes(kp + size_t(pos) * kvw * 3, hd, t, kn[t]);
+                store_planes(vp + size_t(pos) * kvw * 3, hd, t, vn[t]);
+            }
         }
 }
 
@@ -322,7 +326,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         if (j < ntiles) request(j);
         else cp_async_commit();  // empty group: the wait counts below stay uniform
     }
-    attn_prepare<kAttnThreads>(P, i, kvh, pos, p0, qmode, qs, kn, vn, red, kc, vc);
+    uint16_t* kp = P.kplanes ? P.kplanes + base * 3 : nullptr;
+    uint16_t* vp = P.vplanes ? P.vplanes + base * 3 : nullptr;
+    attn_prepare<kAttnThreads>(P, i, kvh, pos, p0, qmode, qs, kn, vn, red, kc, vc, kp, vp);
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(float(hd)));
     const float denom = __fsqrt_rn(float(hd));
     // scores: warp w takes head w % group (R = 8 / group warps per head, each
@@ -456,30 +462,39 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
 // is split exactly into three bf16 parts by truncation, x = hi + mid + lo
 // (8 + 8 + 8 significant bits), and a product takes the six part products
 // hi*hi, hi*mid, mid*hi, hi*lo, mid*mid, lo*hi (the three left out are below
-// 2^-32 of it), smallest first.  Per warp and 16 cached positions:
+// 2^-32 of it), smallest first.  The cached keys and values are split once,
+// when they are appended: the session keeps them as plane rows [3][hd] of
+// bf16 beside the fp32 cache (6 bytes per value).  Per warp and 16 cached
+// positions:
 //   scores  S^T (16 positions x 8 heads) = K (16 x hd) . Q^T (hd x 8 heads)
 //   softmax of each head over the positions: running max and sum, as in
 //           attention_kernel (the reference's scores, scale and mask)
 //   values  O^T (hd x 8 heads) += V^T (hd x 16) . P^T (16 x 8 heads)
-// The probability fragments become the B operand of the value product by a
-// transpose of each 8 x 8 block (movmatrix); heads beyond the group are zero
-// columns.  Grid (kv head, client, chunk) as attention_kernel, one CTA of
-// four warps per SM: warp w streams sub-tiles w, w + 4, ... of its chunk
-// (16 positions each) through its own two-stage ring of bulk row copies,
-// the warps' softmax states are merged through shared memory, and the
-// chunks' partials as in attention_kernel.
-constexpr int kTcWarps = 4, kTcThreads = 32 * kTcWarps, kTcStages = 2, kTcSub = 16;
+// The key and value fragments come straight from the staged plane rows with
+// ldmatrix (transposed for the values); the queries are split once per CTA
+// and the probabilities per sub-tile, whose fragments become the B operand
+// of the value product by a transpose of each 8 x 8 block (movmatrix);
+// heads beyond the group are zero columns.  Grid (kv head, client, chunk)
+// as attention_kernel, one CTA of eight warps per SM: warp w streams
+// sub-tiles w, w + 8, ... of its chunk (16 positions each) through its own
+// ring slot of bulk row copies (the next sub-tile's copies go out once the
+// current one is read), the warps' softmax states are merged through shared
+// memory, and the chunks' partials as in attention_kernel.
+constexpr int kTcWarps = 8, kTcThreads = 32 * kTcWarps, kTcStages = 1, kTcSub = 16;
+static_assert(kTcStages == 1 || kTcStages == 2, "one or two ring stages per warp");
 
 template <int HD>
-struct AttnTcSmem {  // in floats
-    // row strides: the key fragments (8-byte loads of rows g, 2t) and the
-    // value fragments (4-byte loads of rows 2t, column g) hit distinct banks
-    static constexpr int ldk = HD + 8, ldv = HD + 4;
-    static constexpr int stage = kTcSub * (ldk + ldv);
-    static constexpr int qs = 0, kn = 8 * HD, vn = kn + HD, red = vn + HD, ring = red + 64;
+struct AttnTcSmem {  // in bytes
+    // a staged row is one position's [3][HD] bf16 planes; rows 16 bytes
+    // apart beyond their size, so the 8 rows an ldmatrix reads fall on
+    // distinct banks
+    static constexpr int row = 3 * HD * 2 + 16;
+    static constexpr int stage = 2 * kTcSub * row;  // keys, then values
+    static constexpr int qs = 0, kn = 4 * 8 * HD, vn = kn + 4 * HD, red = vn + 4 * HD, ring = red + 4 * 64;
     static constexpr int total = ring + kTcWarps * kTcStages * stage;
-    // after the loop the ring holds the warps' states: [warp][8 heads][HD + 2]
-    static_assert(kTcWarps * 8 * (HD + 2) <= kTcWarps * kTcStages * stage, "warp states fit in the ring");
+    // after the loop the ring holds the warps' states: [warp][8 heads][HD + 2] floats
+    static_assert(kTcWarps * 8 * (HD + 2) * 4 <= kTcWarps * kTcStages * stage, "warp states fit in the ring");
+    static_assert(ring % 16 == 0 && row % 16 == 0, "bulk copy destinations 16-byte aligned");
 };
 
 // x0, x1 -> three bf16x2 words (hi, mid, lo), x0 in the low halves.
@@ -519,11 +534,26 @@ __device__ __forceinline__ uint32_t movtrans(uint32_t a) {
     return d;
 }
 
+// Four 8 x 8 bf16 matrices from shared memory (lane l gives the address of
+// row l % 8 of matrix l / 8), as the A fragment of m16n8k16; .trans
+// transposes each matrix on the way.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&a)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&a)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(a[0]), "=r"(a[1]), "=r"(a[2]), "=r"(a[3])
+                 : "r"(addr));
+}
+
 template <int HD>
 __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnParams P) {
     using L = AttnTcSmem<HD>;
     constexpr int KS = HD / 16;  // k-steps of the scores, m-tiles of the values
-    extern __shared__ __align__(128) float sm[];
+    constexpr int RW = 3 * HD;   // a plane row, in bf16
+    extern __shared__ __align__(128) uint8_t smb[];
     __shared__ uint64_t full[kTcWarps][kTcStages];
     const int kvh = blockIdx.x, i = blockIdx.y, chunk = blockIdx.z, S = gridDim.z;
     const int group = P.heads / P.kv_heads, kvw = P.kv_heads * HD, qw = P.heads * HD;
@@ -536,7 +566,9 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
     const size_t base = (cc * P.layers + P.layer) * P.context * size_t(kvw) + size_t(kvh) * HD;
     float* kc = P.kcache + base;
     float* vc = P.vcache + base;
-    float* ring = sm + L::ring + warp * kTcStages * L::stage;
+    uint16_t* kp = P.kplanes + base * 3;  // position p's plane row at p * kvw * 3
+    uint16_t* vp = P.vplanes + base * 3;
+    uint8_t* ring = smb + L::ring + warp * kTcStages * L::stage;
     if (lane == 0) {
         for (int s = 0; s < kTcStages; s++) mbar_init(&full[warp][s], 1);
         mbar_fence_init();
@@ -546,21 +578,22 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
     // lanes 0-15 copying the key rows and lanes 16-31 the value rows
     auto issue = [&](int j) {
         const int st = j % kTcStages, s0 = p0 + (warp + kTcWarps * j) * kTcSub, nr = min(kTcSub, p1 - s0);
-        float* kt = ring + st * L::stage;
-        if (lane == 0) mbar_expect_tx(&full[warp][st], uint32_t(nr) * 2u * HD * 4u);
+        uint8_t* kt = ring + st * L::stage;
+        if (lane == 0) mbar_expect_tx(&full[warp][st], uint32_t(nr) * 2u * RW * 2u);
         __syncwarp();
         const int r = lane & 15;
         if (r < nr) {
-            if (lane < 16) bulk_g2s(kt + r * L::ldk, kc + size_t(s0 + r) * kvw, HD * 4, &full[warp][st]);
-            else bulk_g2s(kt + kTcSub * L::ldk + r * L::ldv, vc + size_t(s0 + r) * kvw, HD * 4, &full[warp][st]);
+            if (lane < 16) bulk_g2s(kt + r * L::row, kp + size_t(s0 + r) * kvw * 3, RW * 2, &full[warp][st]);
+            else bulk_g2s(kt + (kTcSub + r) * L::row, vp + size_t(s0 + r) * kvw * 3, RW * 2, &full[warp][st]);
         }
     };
     // the cached rows come from earlier steps: requested before the wait for q, k, v
     for (int j = 0; j < kTcStages && j < mine; j++) issue(j);
-    float* qs = sm + L::qs;
-    float* kn = sm + L::kn;
-    float* vn = sm + L::vn;
-    attn_prepare<kTcThreads>(P, i, kvh, pos, p0, false, qs, kn, vn, sm + L::red, kc, vc);
+    float* qs = reinterpret_cast<float*>(smb + L::qs);
+    float* kn = reinterpret_cast<float*>(smb + L::kn);
+    float* vn = reinterpret_cast<float*>(smb + L::vn);
+    attn_prepare<kTcThreads>(P, i, kvh, pos, p0, false, qs, kn, vn, reinterpret_cast<float*>(smb + L::red), kc, vc,
+                             kp, vp);
     const bool llama = P.family == SPM_FAMILY_LLAMA;
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(float(HD)));
     const float denom = __fsqrt_rn(float(HD));
@@ -579,18 +612,23 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
             bq[ks][q][1] = hi[q];
         }
     }
+    // ldmatrix addresses of this lane: keys (A = K, rows = positions) row
+    // (l & 7) + 8 ((l >> 3) & 1), column 8 (l >> 4); values (A = V^T via
+    // .trans, rows of the stage = positions) row (l & 7) + 8 (l >> 4),
+    // column 8 ((l >> 3) & 1)
+    const uint32_t k_off = uint32_t(((lane & 7) + 8 * ((lane >> 3) & 1)) * L::row + 16 * (lane >> 4));
+    const uint32_t v_off = uint32_t((kTcSub + (lane & 7) + 8 * (lane >> 4)) * L::row + 16 * ((lane >> 3) & 1));
     // softmax state of heads 2t, 2t+1 (the sums per lane, added up at the end)
     float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
     float o[KS][4];  // O^T m-tile mt: dims mt*16 + g (+8) x heads 2t, 2t+1
 #pragma unroll
     for (int mt = 0; mt < KS; mt++) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
     // copy phase issued into stage 0 / 1 and not yet waited for (-1: none)
-    int out0 = mine > 0 ? 0 : -1, out1 = mine > 1 ? 1 : -1;
+    int out0 = mine > 0 ? 0 : -1, out1 = kTcStages > 1 && mine > 1 ? 1 : -1;
     bool ok = true;
     for (int j = 0; j < mine; j++) {
         const int st = j % kTcStages, s0 = p0 + (warp + kTcWarps * j) * kTcSub, nr = min(kTcSub, p1 - s0);
-        float* kt = ring + st * L::stage;
-        float* vt = kt + kTcSub * L::ldk;
+        uint8_t* kt = ring + st * L::stage;
         if (!mbar_wait(&full[warp][st], uint32_t(j / kTcStages) & 1u)) {
             flag(P.status, 6);
             ok = false;
@@ -598,35 +636,25 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
         }
         (st ? out1 : out0) = -1;
         if (nr < kTcSub)  // rows past the chunk: zero (probability 0, value finite)
-            for (int e = lane; e < (kTcSub - nr) * HD; e += 32) {
-                const int r = nr + e / HD, c = e % HD;
-                kt[r * L::ldk + c] = 0.f;
-                vt[r * L::ldv + c] = 0.f;
+            for (int e = lane; e < (kTcSub - nr) * RW; e += 32) {
+                const int r = nr + e / RW, c = e % RW;
+                reinterpret_cast<uint16_t*>(kt + r * L::row)[c] = 0;
+                reinterpret_cast<uint16_t*>(kt + (kTcSub + r) * L::row)[c] = 0;
             }
         if (pos >= s0 && pos < s0 + nr)  // the new row: the copy brought the cache's old contents
             for (int c = lane; c < HD; c += 32) {
-                kt[(pos - s0) * L::ldk + c] = kn[c];
-                vt[(pos - s0) * L::ldv + c] = vn[c];
+                store_planes(reinterpret_cast<uint16_t*>(kt + (pos - s0) * L::row), HD, c, kn[c]);
+                store_planes(reinterpret_cast<uint16_t*>(kt + (kTcSub + pos - s0) * L::row), HD, c, vn[c]);
             }
         __syncwarp();
+        const uint32_t ks_base = saddr(kt) + k_off, vs_base = saddr(kt) + v_off;
         // ---- scores: two accumulators over alternate k-steps ----
         float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int ks = 0; ks < KS; ks++) {
-            const float* k0 = kt + g * L::ldk + ks * 16 + 2 * t;
-            const float2 x0 = *reinterpret_cast<const float2*>(k0);
-            const float2 x1 = *reinterpret_cast<const float2*>(k0 + 8 * L::ldk);
-            const float2 x2 = *reinterpret_cast<const float2*>(k0 + 8);
-            const float2 x3 = *reinterpret_cast<const float2*>(k0 + 8 * L::ldk + 8);
-            uint32_t a[3][4], p[3];
-            split3(x0.x, x0.y, p);
-            a[0][0] = p[0], a[1][0] = p[1], a[2][0] = p[2];
-            split3(x1.x, x1.y, p);
-            a[0][1] = p[0], a[1][1] = p[1], a[2][1] = p[2];
-            split3(x2.x, x2.y, p);
-            a[0][2] = p[0], a[1][2] = p[1], a[2][2] = p[2];
-            split3(x3.x, x3.y, p);
-            a[0][3] = p[0], a[1][3] = p[1], a[2][3] = p[2];
+            uint32_t a[3][4];
+#pragma unroll
+            for (int q = 0; q < 3; q++) ldsm_x4(a[q], ks_base + uint32_t(q * HD * 2 + ks * 32));
             if (ks & 1) mma_split(sb, a, bq[ks]);
             else mma_split(sa, a, bq[ks]);
         }
@@ -677,16 +705,9 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
         // ---- values: V^T m-tile mt (dims mt*16 ..) times P^T ----
 #pragma unroll
         for (int mt = 0; mt < KS; mt++) {
-            const float* v0 = vt + (2 * t) * L::ldv + mt * 16 + g;
-            uint32_t a[3][4], p[3];
-            split3(v0[0], v0[L::ldv], p);
-            a[0][0] = p[0], a[1][0] = p[1], a[2][0] = p[2];
-            split3(v0[8], v0[L::ldv + 8], p);
-            a[0][1] = p[0], a[1][1] = p[1], a[2][1] = p[2];
-            split3(v0[8 * L::ldv], v0[9 * L::ldv], p);
-            a[0][2] = p[0], a[1][2] = p[1], a[2][2] = p[2];
-            split3(v0[8 * L::ldv + 8], v0[9 * L::ldv + 8], p);
-            a[0][3] = p[0], a[1][3] = p[1], a[2][3] = p[2];
+            uint32_t a[3][4];
+#pragma unroll
+            for (int q = 0; q < 3; q++) ldsm_x4_trans(a[q], vs_base + uint32_t(q * HD * 2 + mt * 32));
             mma_split(o[mt], a, bp);
         }
         __syncwarp();
@@ -700,7 +721,7 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
         // a wait gave up: the copies still in flight land before the CTA ends
         // (each phase waited for once more, bounded), and this warp adds nothing
         if (out0 >= 0) mbar_wait(&full[warp][0], uint32_t(out0 / kTcStages) & 1u);
-        if (out1 >= 0) mbar_wait(&full[warp][1], uint32_t(out1 / kTcStages) & 1u);
+        if (kTcStages > 1 && out1 >= 0) mbar_wait(&full[warp][kTcStages - 1], uint32_t(out1 / kTcStages) & 1u);
         m_run[0] = m_run[1] = -INFINITY;
         l_run[0] = l_run[1] = 0.f;
 #pragma unroll
@@ -712,7 +733,7 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
         for (int off = 4; off < 32; off <<= 1) l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], off);
     __syncthreads();  // every warp is done with its ring: it holds the warps' states now
     {
-        float* ws = sm + L::ring + warp * 8 * (HD + 2);
+        float* ws = reinterpret_cast<float*>(smb + L::ring) + warp * 8 * (HD + 2);
 #pragma unroll
         for (int mt = 0; mt < KS; mt++) {
             ws[(2 * t) * (HD + 2) + mt * 16 + g] = o[mt][0];
@@ -732,7 +753,7 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
     float* outp = P.scratch + ((size_t(i) * P.kv_heads + kvh) * S + chunk) * group * (HD + 2);
     for (int e = threadIdx.x; e < group * HD; e += kTcThreads) {
         const int h = e / HD, d = e % HD;
-        const float* st = sm + L::ring + h * (HD + 2);
+        const float* st = reinterpret_cast<const float*>(smb + L::ring) + h * (HD + 2);
         float M = -INFINITY;
 #pragma unroll
         for (int w = 0; w < kTcWarps; w++) M = fmaxf(M, st[w * 8 * (HD + 2) + HD]);
@@ -785,15 +806,20 @@ static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem
 }
 
 // The tensor-core kernel takes decode steps of 4 to 8 query heads per kv head
-// and head_dim 64 or 128.
-static bool attention_tc_fits(const AttnParams& P) {
+// and head_dim 64 or 128 with at least 16 (kv head, client) pairs.  (With
+// fewer pairs -- Qwen3-8B with one client: 8 -- a step's attention is a
+// latency chain of prologue, one sub-tile per warp and the chunk combine,
+// and the 256-thread CUDA-core kernel measured shorter: 23 against 32 us
+// per layer.)
+static bool attention_tc_fits(const AttnParams& P, int n) {
     const int group = P.heads / P.kv_heads;
-    return P.qpos == nullptr && group >= 4 && group <= 8 && (P.head_dim == 64 || P.head_dim == 128);
+    return P.qpos == nullptr && P.kplanes && P.vplanes && group >= 4 && group <= 8 &&
+           (P.head_dim == 64 || P.head_dim == 128) && P.kv_heads * n >= 16;
 }
 
 template <int HD>
 static cudaError_t launch_attention_tc(const AttnParams& P, int n, int sms, cudaStream_t s, bool pdl) {
-    const size_t smem = size_t(AttnTcSmem<HD>::total) * sizeof(float);
+    const size_t smem = size_t(AttnTcSmem<HD>::total);
     static int configured_for = -1;
     int dev = 0;
     cudaGetDevice(&dev);
@@ -804,11 +830,13 @@ static cudaError_t launch_attention_tc(const AttnParams& P, int n, int sms, cuda
         configured_for = dev;
     }
     // one CTA per SM: about as many (kv head, client, chunk) CTAs as SMs,
-    // chunks a multiple of the four warps' 16 positions
+    // chunks a multiple of the warps' 16 positions each (and of the 64 the
+    // session's partials are sized for)
+    constexpr int step = kTcWarps * kTcSub > kAttnMinChunk ? kTcWarps * kTcSub : kAttnMinChunk;
     const int pairs = P.kv_heads * n;
     const int want = std::max(1, sms / pairs);
     int chunk = (P.context + want - 1) / want;
-    chunk = std::max(kAttnMinChunk, (chunk + kAttnMinChunk - 1) / kAttnMinChunk * kAttnMinChunk);
+    chunk = std::max(step, (chunk + step - 1) / step * step);
     const int chunks = (P.context + chunk - 1) / chunk;
     AttnParams p = P;
     p.chunk = chunk;
@@ -818,7 +846,7 @@ static cudaError_t launch_attention_tc(const AttnParams& P, int n, int sms, cuda
 }
 
 cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t s, bool pdl) {
-    if (attention_tc_fits(P)) {
+    if (attention_tc_fits(P, n)) {
         static int tc_sms[64] = {};
         int d = 0;
         cudaGetDevice(&d);

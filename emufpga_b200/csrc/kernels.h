@@ -132,6 +132,11 @@ struct AttnParams {
     const float *q, *k, *v;        // [n][q_width], [n][kv_width]
     float* out;                    // [n][q_width]
     float *kcache, *vcache;        // [client][layer][context][kv_width]
+    // The same rows split exactly into three bf16 parts (hi, mid, lo; section
+    // "attention on tensor cores" of kernels.cu), [client][layer][context]
+    // [kv_heads][3][head_dim], or nullptr: written at every append when set,
+    // read by the tensor-core kernel.
+    uint16_t *kplanes, *vplanes;
     const int32_t* pos;            // [n] position of the token being decoded
     const float2* rope;            // [context][head_dim/2] (cos, sin)
     const float *q_norm, *k_norm;  // QK-norm gains or nullptr

@@ -132,8 +132,15 @@ __global__ void __launch_bounds__(256) qk_rope_append_kernel(const QkArgs a) {
     for (int c = threadIdx.x; c < qw; c += blockDim.x) qo[c] = q[c];
     const size_t row = ((size_t(a.client) * a.layers + a.layer) * a.context + pos) * kvw;
     for (int c = threadIdx.x; c < kvw; c += blockDim.x) {
+        const float vv = a.v[size_t(t) * kvw + c];
         a.kcache[row + c] = k[c];
-        a.vcache[row + c] = a.v[size_t(t) * kvw + c];
+        a.vcache[row + c] = vv;
+        if (a.kplanes) {
+            // head h's [3][hd] plane row
+            const int h = c / hd, d = c % hd;
+            store_planes(a.kplanes + (row + size_t(h) * hd) * 3, hd, d, k[c]);
+            store_planes(a.vplanes + (row + size_t(h) * hd) * 3, hd, d, vv);
+        }
     }
 }
 

@@ -19,6 +19,7 @@ struct QkArgs {
     float* q;                      // [T][heads * head_dim], normed and rotated in place
     const float *k, *v;            // [T][kv_heads * head_dim]
     float *kcache, *vcache;        // [client][layer][context][kv_width]
+    uint16_t *kplanes, *vplanes;   // the rows as three bf16 parts (AttnParams), or nullptr
     const float2* rope;            // [context][head_dim / 2]
     const float *q_norm, *k_norm;  // QK-norm gains or nullptr (LLAMA)
     int32_t client, layer, layers, context, pos0;

@@ -14,7 +14,7 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 LOGIT_TOL = 1e-3
-DENSE = ["llama-q8_0", "llama-q6_k", "qwen3-q6_k", "qwen3-q5_k", "qwen3-q2_k", "qwen3-g8-q6_k"]
+DENSE = ["llama-q8_0", "llama-q6_k", "qwen3-q6_k", "qwen3-q5_k", "qwen3-q2_k", "qwen3-g8-q6_k", "qwen3-g4-q5_k"]
 
 
 def logits_close(got, want):
@@ -209,13 +209,15 @@ def test_qwen3_8b_shape_two_layers_matches_the_oracle(cuda):
     m.close()
 
 
-@pytest.mark.parametrize("name", ["llama-q8_0", "qwen3-q6_k", "qwen3-q5_k", "qwen3-g8-q6_k"])
-def test_long_context_attention_matches_the_oracle(cuda, models, name):
+@pytest.mark.parametrize("name,n", [("llama-q8_0", 2), ("qwen3-q6_k", 2), ("qwen3-g8-q6_k", 2), ("qwen3-g8-q6_k", 8),
+                                    ("qwen3-g4-q5_k", 8)])
+def test_long_context_attention_matches_the_oracle(cuda, models, name, n):
     # a client's prefix splits over several CTAs whose softmax partials are
-    # combined (qwen3-q5_k, qwen3-g8-q6_k: the tensor-core kernel, four and
-    # eight query heads per kv head)
+    # combined (qwen3-g8-q6_k and qwen3-g4-q5_k with 8 clients: 16 kv head x
+    # client pairs, the tensor-core kernel at head_dim 128 and 64; otherwise
+    # the CUDA-core kernel)
     r, img, m, om = models(name)
-    n, steps = 2, 600
+    steps = 600
     sess = eb.Session(m, n, steps)
     osess = om.session(n, steps)
     for step in range(steps):
