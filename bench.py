@@ -67,6 +67,7 @@ SWEEP = {"sweep-ternary-32x4096-b8": ("ternary", 32, 4096, 4096, 8),
 # capture.  Used to report `roofline.traffic` per launch.
 TRAFFIC_RATIO = {
     "qwen3-8b-b1": (1.003, "profiles/gemv_stream_qwen3_8b_b1.md"),
+    "qwen3-30b-b8": (1.053, "profiles/gemv_stream_qwen3_30b_b8.md"),
 }
 STAGING = "activations staged per 32-value unit as 22-bit block fixed point (three int8 digit planes), " \
           "integer products, fp32 scales and sums"
