@@ -133,6 +133,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                  : "memory");
 }
 
+// Asks for `bytes` of global memory to be brought into L2 (no completion
+// to wait for).  Address and size must be multiples of 16 bytes.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // ---- 16-byte asynchronous copies global -> shared (no mbarrier) ----
 // Both addresses 16-byte aligned; cp_async_commit closes the thread's current
 // group and cp_async_wait<N> waits until at most N of its groups are pending.

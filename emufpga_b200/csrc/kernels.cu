@@ -477,11 +477,12 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
 // heads beyond the group are zero columns.  Grid (kv head, client, chunk)
 // as attention_kernel, one CTA of eight warps per SM: warp w streams
 // sub-tiles w, w + 8, ... of its chunk (16 positions each) through its own
-// ring slot of bulk row copies (the next sub-tile's copies go out once the
-// current one is read), the warps' softmax states are merged through shared
-// memory, and the chunks' partials as in attention_kernel.
+// slot of bulk row copies, keys and values on separate barriers (the next
+// sub-tile's keys go out once the scores have read this one's, its values
+// once the value products have; later sub-tiles are asked into L2 at the
+// start), the warps' softmax states are merged through shared memory, and
+// the chunks' partials as in attention_kernel.
 constexpr int kTcWarps = 8, kTcThreads = 32 * kTcWarps, kTcStages = 1, kTcSub = 16;
-static_assert(kTcStages == 1 || kTcStages == 2, "one or two ring stages per warp");
 
 template <int HD>
 struct AttnTcSmem {  // in bytes
@@ -554,7 +555,7 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
     constexpr int KS = HD / 16;  // k-steps of the scores, m-tiles of the values
     constexpr int RW = 3 * HD;   // a plane row, in bf16
     extern __shared__ __align__(128) uint8_t smb[];
-    __shared__ uint64_t full[kTcWarps][kTcStages];
+    __shared__ uint64_t kbar[kTcWarps], vbar[kTcWarps];  // this warp's key rows, value rows landed
     const int kvh = blockIdx.x, i = blockIdx.y, chunk = blockIdx.z, S = gridDim.z;
     const int group = P.heads / P.kv_heads, kvw = P.kv_heads * HD, qw = P.heads * HD;
     const int warp = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31), g = lane >> 2, t = lane & 3;
@@ -570,25 +571,35 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
     uint16_t* vp = P.vplanes + base * 3;
     uint8_t* ring = smb + L::ring + warp * kTcStages * L::stage;
     if (lane == 0) {
-        for (int s = 0; s < kTcStages; s++) mbar_init(&full[warp][s], 1);
+        mbar_init(&kbar[warp], 1);
+        mbar_init(&vbar[warp], 1);
         mbar_fence_init();
     }
     __syncwarp();
-    // sub-tile j of this warp: positions s0 .. s0 + nr - 1 into stage j % 2,
-    // lanes 0-15 copying the key rows and lanes 16-31 the value rows
-    auto issue = [&](int j) {
-        const int st = j % kTcStages, s0 = p0 + (warp + kTcWarps * j) * kTcSub, nr = min(kTcSub, p1 - s0);
-        uint8_t* kt = ring + st * L::stage;
-        if (lane == 0) mbar_expect_tx(&full[warp][st], uint32_t(nr) * 2u * RW * 2u);
+    // the key (v = false) or value rows of sub-tile j of this warp, positions
+    // s0 .. s0 + nr - 1, one row per lane; the keys of the next sub-tile are
+    // requested once the scores have read this one's, the values once the
+    // value products have
+    auto issue = [&](int j, bool v) {
+        const int s0 = p0 + (warp + kTcWarps * j) * kTcSub, nr = min(kTcSub, p1 - s0);
+        uint64_t* bar = v ? &vbar[warp] : &kbar[warp];
+        if (lane == 0) mbar_expect_tx(bar, uint32_t(nr) * RW * 2u);
         __syncwarp();
-        const int r = lane & 15;
-        if (r < nr) {
-            if (lane < 16) bulk_g2s(kt + r * L::row, kp + size_t(s0 + r) * kvw * 3, RW * 2, &full[warp][st]);
-            else bulk_g2s(kt + (kTcSub + r) * L::row, vp + size_t(s0 + r) * kvw * 3, RW * 2, &full[warp][st]);
-        }
+        if (lane < nr)
+            bulk_g2s(ring + (v ? kTcSub + lane : lane) * L::row, (v ? vp : kp) + size_t(s0 + lane) * kvw * 3, RW * 2,
+                     bar);
     };
-    // the cached rows come from earlier steps: requested before the wait for q, k, v
-    for (int j = 0; j < kTcStages && j < mine; j++) issue(j);
+    // the cached rows come from earlier steps: requested before the wait for
+    // q, k, v, the first sub-tile into the ring and the warp's later ones
+    // toward L2, so that their copies find them there
+    if (mine > 0) {
+        issue(0, false);
+        issue(0, true);
+    }
+    for (int j = 1; j < mine; j++) {
+        const int s0 = p0 + (warp + kTcWarps * j) * kTcSub, r = lane & 15;
+        if (r < min(kTcSub, p1 - s0)) prefetch_l2((lane < 16 ? kp : vp) + size_t(s0 + r) * kvw * 3, RW * 2);
+    }
     float* qs = reinterpret_cast<float*>(smb + L::qs);
     float* kn = reinterpret_cast<float*>(smb + L::kn);
     float* vn = reinterpret_cast<float*>(smb + L::vn);
@@ -623,29 +634,24 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
     float o[KS][4];  // O^T m-tile mt: dims mt*16 + g (+8) x heads 2t, 2t+1
 #pragma unroll
     for (int mt = 0; mt < KS; mt++) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
-    // copy phase issued into stage 0 / 1 and not yet waited for (-1: none)
-    int out0 = mine > 0 ? 0 : -1, out1 = kTcStages > 1 && mine > 1 ? 1 : -1;
+    // copy phases issued and not yet waited for (-1: none): keys, values
+    int kout = mine > 0 ? 0 : -1, vout = kout;
     bool ok = true;
+    uint8_t* const kt = ring;
     for (int j = 0; j < mine; j++) {
-        const int st = j % kTcStages, s0 = p0 + (warp + kTcWarps * j) * kTcSub, nr = min(kTcSub, p1 - s0);
-        uint8_t* kt = ring + st * L::stage;
-        if (!mbar_wait(&full[warp][st], uint32_t(j / kTcStages) & 1u)) {
+        const int s0 = p0 + (warp + kTcWarps * j) * kTcSub, nr = min(kTcSub, p1 - s0);
+        if (!mbar_wait(&kbar[warp], uint32_t(j) & 1u)) {
             flag(P.status, 6);
             ok = false;
             break;
         }
-        (st ? out1 : out0) = -1;
-        if (nr < kTcSub)  // rows past the chunk: zero (probability 0, value finite)
-            for (int e = lane; e < (kTcSub - nr) * RW; e += 32) {
-                const int r = nr + e / RW, c = e % RW;
-                reinterpret_cast<uint16_t*>(kt + r * L::row)[c] = 0;
-                reinterpret_cast<uint16_t*>(kt + (kTcSub + r) * L::row)[c] = 0;
-            }
+        kout = -1;
+        if (nr < kTcSub)  // key rows past the chunk: zero (their scores are masked)
+            for (int e = lane; e < (kTcSub - nr) * RW; e += 32)
+                reinterpret_cast<uint16_t*>(kt + (nr + e / RW) * L::row)[e % RW] = 0;
         if (pos >= s0 && pos < s0 + nr)  // the new row: the copy brought the cache's old contents
-            for (int c = lane; c < HD; c += 32) {
+            for (int c = lane; c < HD; c += 32)
                 store_planes(reinterpret_cast<uint16_t*>(kt + (pos - s0) * L::row), HD, c, kn[c]);
-                store_planes(reinterpret_cast<uint16_t*>(kt + (kTcSub + pos - s0) * L::row), HD, c, vn[c]);
-            }
         __syncwarp();
         const uint32_t ks_base = saddr(kt) + k_off, vs_base = saddr(kt) + v_off;
         // ---- scores: two accumulators over alternate k-steps ----
@@ -657,6 +663,12 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
             for (int q = 0; q < 3; q++) ldsm_x4(a[q], ks_base + uint32_t(q * HD * 2 + ks * 32));
             if (ks & 1) mma_split(sb, a, bq[ks]);
             else mma_split(sa, a, bq[ks]);
+        }
+        __syncwarp();
+        if (j + 1 < mine) {
+            fence_proxy_async();  // the key rows' reads and writes before the copies that refill them
+            issue(j + 1, false);
+            kout = j + 1;
         }
         // ---- softmax: sc[0], sc[1] position g, heads 2t, 2t+1; sc[2], sc[3] position g + 8 ----
         float sc[4], pr[4], mx[2], alpha[2];
@@ -702,6 +714,19 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
                 bp[q][1] = movtrans(pb[q]);
             }
         }
+        if (!mbar_wait(&vbar[warp], uint32_t(j) & 1u)) {
+            flag(P.status, 6);
+            ok = false;
+            break;
+        }
+        vout = -1;
+        if (nr < kTcSub)  // value rows past the chunk: zero (probability 0, value finite)
+            for (int e = lane; e < (kTcSub - nr) * RW; e += 32)
+                reinterpret_cast<uint16_t*>(kt + (kTcSub + nr + e / RW) * L::row)[e % RW] = 0;
+        if (pos >= s0 && pos < s0 + nr)
+            for (int c = lane; c < HD; c += 32)
+                store_planes(reinterpret_cast<uint16_t*>(kt + (kTcSub + pos - s0) * L::row), HD, c, vn[c]);
+        __syncwarp();
         // ---- values: V^T m-tile mt (dims mt*16 ..) times P^T ----
 #pragma unroll
         for (int mt = 0; mt < KS; mt++) {
@@ -711,17 +736,17 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
             mma_split(o[mt], a, bp);
         }
         __syncwarp();
-        if (j + kTcStages < mine) {
-            fence_proxy_async();  // this stage's reads and writes before the copies that refill it
-            issue(j + kTcStages);
-            (st ? out1 : out0) = j + kTcStages;
+        if (j + 1 < mine) {
+            fence_proxy_async();  // the value rows' reads and writes before the copies that refill them
+            issue(j + 1, true);
+            vout = j + 1;
         }
     }
     if (!ok) {
         // a wait gave up: the copies still in flight land before the CTA ends
         // (each phase waited for once more, bounded), and this warp adds nothing
-        if (out0 >= 0) mbar_wait(&full[warp][0], uint32_t(out0 / kTcStages) & 1u);
-        if (kTcStages > 1 && out1 >= 0) mbar_wait(&full[warp][kTcStages - 1], uint32_t(out1 / kTcStages) & 1u);
+        if (kout >= 0) mbar_wait(&kbar[warp], uint32_t(kout) & 1u);
+        if (vout >= 0) mbar_wait(&vbar[warp], uint32_t(vout) & 1u);
         m_run[0] = m_run[1] = -INFINITY;
         l_run[0] = l_run[1] = 0.f;
 #pragma unroll
