@@ -64,3 +64,29 @@ def test_golden_script_is_reproducible():
         assert sorted(fresh.files) == sorted(ref.files)
         for k in ref.files:
             assert np.array_equal(fresh[k].view(np.uint8), ref[k].view(np.uint8)), k
+
+
+def test_golden_runs_cover_the_benchmark_workloads():
+    """Every workload of the full-run parity tests has its oracle run on file,
+    made from the same synthetic model recipe (tests/golden/make_runs.py)."""
+    import sys
+    from pathlib import Path
+
+    here = Path(__file__).resolve().parent / "golden"
+    sys.path.insert(0, str(here))
+    from make_runs import RUNS
+
+    from emufpga_b200 import configs
+
+    for name in RUNS:
+        path = here / "runs" / f"{name}.npz"
+        assert path.exists(), f"no golden run for {name}: python tests/golden/make_runs.py {name}"
+        g = np.load(path)
+        w = configs.WORKLOADS[name]
+        prompts = configs.workload_prompts(name)
+        ticks = max(len(p) for p in prompts) + w["steps"] - 1
+        assert g["argmax"].shape == (ticks, len(prompts))
+        assert g["top_ids"].shape == (ticks, len(prompts), 8)
+        # the oracle's pick is its largest logit (where there is no exact tie)
+        strict = g["margin"] > 0
+        assert np.array_equal(g["argmax"][strict], g["top_ids"][:, :, 0][strict])
