@@ -95,6 +95,23 @@ def _args():
     return ap.parse_args()
 
 
+def _init_nccl(dist, dev):
+    """The NCCL process group, with anything the library prints while it sets
+    up its communicator sent to stderr: stdout carries only the JSON line."""
+    import datetime
+
+    sys.stdout.flush()
+    saved = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        dist.barrier()
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved, 1)
+        os.close(saved)
+
+
 def _dist():
     # NCCL's version banner would land on stdout beside the JSON line
     os.environ.setdefault("NCCL_DEBUG", "WARN")
@@ -612,7 +629,7 @@ def main():
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        _init_nccl(dist, dev)
         pg = dist
     line = run_decode(a, a.workload, rank, world, local, pg, dev)
     if rank == 0:
@@ -730,7 +747,7 @@ def run_ternary(a, rank, world, local):
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        _init_nccl(dist, dev)
         pg = dist
     from emufpga_b200 import linear as L
     from emufpga_b200 import ternary as T

@@ -131,6 +131,7 @@ PROTOTYPES = {
     "spm_session_stream": (C.c_int32, [_P, C.POINTER(_P)]),
     "spm_session_set_graphs": (C.c_int32, [_P, C.c_int32]),
     "spm_session_routes": (C.c_int32, [_P, C.c_int32, _I32P]),
+    "spm_session_route_gaps": (C.c_int32, [_P, C.c_int32, C.POINTER(C.c_float)]),
     "spm_session_launches_per_step": (C.c_int32, [_P, C.c_int32, _I32P]),
     "spm_session_set_profile": (C.c_int32, [_P, C.c_int32]),
     "spm_prefill": (C.c_int32, [_P, C.c_int32, _U32P, C.c_int32]),

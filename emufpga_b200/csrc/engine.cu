@@ -1715,6 +1715,18 @@ spm_status spm_session_routes(const spm_session* s, int32_t n, int32_t* routes_h
     });
 }
 
+spm_status spm_session_route_gaps(const spm_session* s, int32_t n, float* gaps_host) {
+    return guarded([&] {
+        const spm_model_cfg& c = s->m->cfg;
+        if (!is_moe(c)) fail(SPM_E_ARG, "the model has no routed layers");
+        if (n < 1 || n > s->max_clients || n > kMoeMaxClients) fail(SPM_E_ARG, "client count out of range");
+        std::vector<MoePlan> plans(c.layers);
+        CUDA_OK(cudaMemcpy(plans.data(), s->plans, c.layers * sizeof(MoePlan), cudaMemcpyDeviceToHost));
+        for (uint32_t l = 0; l < c.layers; l++)
+            for (int i = 0; i < n; i++) gaps_host[size_t(l) * n + i] = plans[l].gap[i];
+    });
+}
+
 spm_status spm_session_ep_handle(spm_session* s, void* handle) {
     return guarded([&] {
         if (s->m->world < 2) fail(SPM_E_ARG, "the model is not expert parallel");

@@ -67,6 +67,22 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
             else taken4 |= bit;
             if (lane == 0) sel[i][j] = bi;
         }
+        // the largest probability left out, for the routing's margin
+        {
+            float best = -INFINITY;
+            for (int e = lane; e < E; e += 32) {
+                const uint64_t bit = 1ull << (e & 63);
+                const uint64_t t = e < 64 ? taken : e < 128 ? taken2 : e < 192 ? taken3 : taken4;
+                if (!(t & bit)) best = fmaxf(best, prob[i][e]);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
+            __syncwarp();
+            if (lane == 0) {
+                const float pk = prob[i][sel[i][K - 1]];
+                plan->gap[i] = best == -INFINITY ? 1.0f : (pk - best) / pk;
+            }
+        }
         __syncwarp();
         if (lane == 0) {
             float s = 0.f;  // in route order (layout.rs:289-293)
@@ -77,13 +93,23 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
     }
     __syncthreads();
     // ---- plan: active experts ascending, their clients ascending ----
+    // Every thread holds the selection table in registers (-1 beyond n
+    // clients and K routes), so the scans below run without memory waits.
+    int32_t S[kMoeMaxClients][kMoeMaxUsed];
+#pragma unroll
+    for (int i = 0; i < kMoeMaxClients; i++)
+#pragma unroll
+        for (int j = 0; j < kMoeMaxUsed; j++) S[i][j] = i < n && j < K ? sel[i][j] : -1;
     // Thread e counts expert e's routes and records, for each of them, its
-    // position among the expert's clients (clients ascending).
+    // position among the expert's clients (clients ascending; a client
+    // routes to an expert at most once).
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         int c = 0;
-        for (int i = 0; i < n; i++)
-            for (int j = 0; j < K; j++)
-                if (sel[i][j] == e) pos_of[i][j] = c++;
+#pragma unroll
+        for (int i = 0; i < kMoeMaxClients; i++)
+#pragma unroll
+            for (int j = 0; j < kMoeMaxUsed; j++)
+                if (S[i][j] == e) pos_of[i][j] = c++;
         cnt[e] = c;
     }
     __syncthreads();
@@ -120,26 +146,31 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
         plan->expert[a] = e;
         plan->ntok[a] = cnt[e];
         int p = 0;
-        for (int i = 0; i < n; i++)
-            for (int j = 0; j < K; j++)
-                if (sel[i][j] == e) plan->tok[a][p++] = i;
+#pragma unroll
+        for (int i = 0; i < kMoeMaxClients; i++) {
+            bool hit = false;
+#pragma unroll
+            for (int j = 0; j < kMoeMaxUsed; j++) hit |= S[i][j] == e;
+            if (hit) plan->tok[a][p++] = i;
+        }
         for (; p < kMoeMaxClients; p++) plan->tok[a][p] = 0;
     }
     if (threadIdx.x < n) {
+        // this client's routes in ascending expert id: route j goes to place
+        // rank_j = the number of its routes with a lower expert id
         const int i = threadIdx.x;
-        // this client's routes in ascending expert id
-        int ids[kMoeMaxUsed], js[kMoeMaxUsed];
-        for (int j = 0; j < K; j++) ids[j] = sel[i][j], js[j] = j;
-        for (int x = 1; x < K; x++)
-            for (int y = x; y > 0 && ids[y - 1] > ids[y]; y--) {
-                const int t = ids[y], tj = js[y];
-                ids[y] = ids[y - 1], js[y] = js[y - 1];
-                ids[y - 1] = t, js[y - 1] = tj;
-            }
-        for (int j = 0; j < K; j++) {
-            plan->slot_a[i][j] = base[ids[j]];
-            plan->slot_pos[i][j] = pos_of[i][js[j]];
-            plan->slot_p[i][j] = prob[i][ids[j]];
+        int32_t ids[kMoeMaxUsed];
+#pragma unroll
+        for (int j = 0; j < kMoeMaxUsed; j++) ids[j] = sel[i][j < K ? j : 0];
+#pragma unroll
+        for (int j = 0; j < kMoeMaxUsed; j++) {
+            if (j >= K) break;
+            int rank = 0;
+#pragma unroll
+            for (int x = 0; x < kMoeMaxUsed; x++) rank += (x < K && ids[x] < ids[j]) ? 1 : 0;
+            plan->slot_a[i][rank] = base[ids[j]];
+            plan->slot_pos[i][rank] = pos_of[i][j];
+            plan->slot_p[i][rank] = prob[i][ids[j]];
         }
     }
     pdl_trigger();
@@ -175,11 +206,23 @@ __global__ void __launch_bounds__(kCombineCols) combine_kernel(const MoePlan* pl
     float ss = 0.f;
     if (col < width) {
         const float norm = plan->norm[i];
-        float total = 0.f;
-        for (int j = 0; j < K; j++) {
-            const float* lane = out + size_t(plan->slot_a[i][j] * kMoeMaxClients + plan->slot_pos[i][j]) * out_stride;
-            total = total + __fdiv_rn(__fmul_rn(__ldcg(lane + col), plan->slot_p[i][j]), norm);
+        // the K expert rows' values first (their loads in flight together),
+        // then the sum in ascending expert id
+        float vals[kMoeMaxUsed], ps[kMoeMaxUsed];
+#pragma unroll
+        for (int j = 0; j < kMoeMaxUsed; j++) {
+            vals[j] = ps[j] = 0.f;
+            if (j < K) {
+                const float* lane =
+                    out + size_t(plan->slot_a[i][j] * kMoeMaxClients + plan->slot_pos[i][j]) * out_stride;
+                vals[j] = __ldcg(lane + col);
+                ps[j] = plan->slot_p[i][j];
+            }
         }
+        float total = 0.f;
+#pragma unroll
+        for (int j = 0; j < kMoeMaxUsed; j++)
+            if (j < K) total = total + __fdiv_rn(__fmul_rn(vals[j], ps[j]), norm);
         const float v = states[size_t(i) * width + col] + total;
         states[size_t(i) * width + col] = v;
         ss = v * v;

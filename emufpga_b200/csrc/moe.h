@@ -23,6 +23,10 @@ struct MoePlan {
     int32_t slot_pos[kMoeMaxClients][kMoeMaxUsed];       // position among that expert's clients
     float slot_p[kMoeMaxClients][kMoeMaxUsed];           // routing probability
     float norm[kMoeMaxClients];                          // sum of the selected probabilities
+    // how close the routing came to a different expert set: (p_K - p_K+1) / p_K
+    // for the K-th largest probability and the largest one left out (1 when
+    // every expert is selected)
+    float gap[kMoeMaxClients];
     // the active experts this rank computes (expert parallel: e % world ==
     // rank; one GPU: all), as active indices ascending
     int32_t nlocal;

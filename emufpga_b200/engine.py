@@ -331,6 +331,12 @@ class Session:
         call("spm_session_routes", self._h, n, out.ctypes.data_as(C.POINTER(C.c_int32)))
         return out
 
+    def route_gaps(self, n: int) -> np.ndarray:
+        """Routing margins of the last step, layers x clients: (p_K - p_K+1) / p_K."""
+        out = np.zeros((self.model.shape.layers, n), dtype=np.float32)
+        call("spm_session_route_gaps", self._h, n, out.ctypes.data_as(C.POINTER(C.c_float)))
+        return out
+
     def ep_handle(self) -> bytes:
         """This rank's exchange buffer as a 64-byte CUDA IPC handle."""
         buf = (C.c_uint8 * 64)()

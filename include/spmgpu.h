@@ -209,14 +209,27 @@ spm_status spm_session_stream(const spm_session* s, void** cuda_stream);
 spm_status spm_session_set_graphs(spm_session* s, int32_t enable);
 /* Routes of the last step (MoE): layers x n x experts_used expert ids. */
 spm_status spm_session_routes(const spm_session* s, int32_t n, int32_t* routes_host);
+/* Margins of the last step's routing (MoE), layers x n floats: for each
+ * client and routed layer (p_K - p_K+1) / p_K, p_K the smallest selected
+ * routing probability and p_K+1 the largest left out (1 when every expert is
+ * selected).  A margin near zero marks a near tie between two experts, which
+ * the order of fp32 sums can decide either way (spm-granite-moe/src/moe.rs:
+ * 17-35 selects by the same order, ties to the lower id). */
+spm_status spm_session_route_gaps(const spm_session* s, int32_t n, float* gaps_host);
 /* ---- expert parallel (routed models over 1..8 GPUs of one node) ----
  * Replaces the reference's single-process expert loop
- * (spm-granite-moe/src/layout.rs:244-304) across GPUs: each rank runs the
- * whole step for every client (attention, router, norms and LM head are
- * replicated), but computes only the experts e with e % world == rank and
- * writes their output rows over NVLink into every rank's exchange buffer;
- * the combine waits (1 s bound) for all ranks' rows and sums them in
- * ascending expert id, so every rank's results equal the single-GPU ones.
+ * (spm-granite-moe/src/layout.rs:244-304) across GPUs, with data-parallel
+ * attention.  The client count n of a step must be a multiple of world;
+ * rank r owns clients r*n/world .. (r+1)*n/world - 1 and their KV cache.
+ * Per layer each rank runs the attention block of its own clients and the O
+ * projection stores their rows (and norm partials) over NVLink into every
+ * rank's states; the router waits (bounded) until every rank's rows are in,
+ * so every rank routes every client; each rank computes only the experts e
+ * with e % world == rank, writes their output rows into every rank's
+ * exchange buffer, and the combine waits (bounded) for all ranks' rows and
+ * adds them, in ascending expert id, into its own clients' states.  Each
+ * rank runs the LM head for its own clients (their logits alone are
+ * written) and the greedy picks are gathered, so every rank returns all n.
  * Open the model with spm_model_open_ep (only this rank's experts are
  * uploaded; the file is memory-mapped, so ranks share its pages), create
  * the session, exchange the 64-byte handles of spm_session_ep_handle between
