@@ -58,7 +58,7 @@ def _load(name):
     return np.load(path)
 
 
-def _check_tick(t, best, logits, g, route_tie=None):
+def _check_tick(t, best, logits, g, route_tie=None, gaps=None):
     """Returns (near ties the device decided the other way, clients exempted
     for a routing near tie).  route_tie[i]: in this tick client i's routing
     had a near tie in some layer on the device (spm_session_route_gaps)."""
@@ -76,7 +76,8 @@ def _check_tick(t, best, logits, g, route_tie=None):
         err = np.abs(logits[i, ids[i]] - vals[i]).max()
         if err > LOGIT_TOL * scale[i]:
             # an expert set that differs from the oracle's at a routing near tie
-            assert rt and err <= ROUTE_SLACK * scale[i], (t, i, float(err), float(scale[i]))
+            gap = None if gaps is None else float(gaps[i])
+            assert rt and err <= ROUTE_SLACK * scale[i], (t, i, float(err), float(scale[i]), gap)
             exempt += 1
     return ties, exempt
 
@@ -104,8 +105,8 @@ def test_full_run_matches_the_oracle(cuda, name):
     ties = exempt = 0
     for t in range(ticks):
         best, logits = s.decode_step(toks, want_logits=True)
-        rt = (s.route_gaps(n).min(axis=0) < ROUTE_TIE) if recipe.shape.moe else None
-        a, b = _check_tick(t, best, logits, g, rt)
+        gaps = s.route_gaps(n).min(axis=0) if recipe.shape.moe else None
+        a, b = _check_tick(t, best, logits, g, None if gaps is None else gaps < ROUTE_TIE, gaps)
         ties, exempt = ties + a, exempt + b
         oracle = g["argmax"][t].tolist()
         toks = [p[t + 1] if t + 1 < len(p) else oracle[i] for i, p in enumerate(prompts)]
