@@ -3,6 +3,8 @@
 // device KV cache, greedy selection, position bookkeeping.
 #include <algorithm>
 
+#include <cooperative_groups.h>
+
 #include "dequant.cuh"
 
 namespace spm {
@@ -442,7 +444,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         pdl_trigger();
         return;
     }
-    float* outp = P.scratch + ((size_t(i) * P.kv_heads + kvh) * S + chunk) * group * (hd + 2);
+    // this chunk's partial: in the scratch, or (cluster) in the tile ring,
+    // which the loop no longer uses
+    float* outp = P.cluster ? sm + L.kt : P.scratch + ((size_t(i) * P.kv_heads + kvh) * S + chunk) * group * (hd + 2);
 #pragma unroll
     for (int k = 0; k < 4; k++) {
         const int h = h0 + k;
@@ -452,7 +456,36 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         outp[threadIdx.x * (hd + 2) + hd] = m_sh[threadIdx.x];
         outp[threadIdx.x * (hd + 2) + hd + 1] = m_sh[group + threadIdx.x];
     }
-    attn_combine<kAttnThreads>(P, i, kvh, S);
+    if (!P.cluster) {
+        attn_combine<kAttnThreads>(P, i, kvh, S);
+        return;
+    }
+    // Cluster of the S chunks (rank = chunk): once every partial is in
+    // place, CTA r combines the outputs r * per .. (r + 1) * per - 1, reading
+    // the partials from the other CTAs' shared memory in chunk order -- the
+    // arithmetic of attn_combine, without the global round trip and the
+    // counter.  A second cluster barrier keeps every partial alive until all
+    // have been read.
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    cl.sync();
+    pdl_trigger();
+    const int per = (group * hd + S - 1) / S;
+    for (int t = chunk * per + int(threadIdx.x); t < min(group * hd, (chunk + 1) * per); t += kAttnThreads) {
+        const int h = t / hd, dd = t % hd;
+        float M = -INFINITY;
+        for (int s = 0; s < S; s++) M = fmaxf(M, cl.map_shared_rank(outp, s)[h * (hd + 2) + hd]);
+        float Lsum = 0.f, O = 0.f;
+        for (int s = 0; s < S; s++) {
+            const float* ps = cl.map_shared_rank(outp, s) + h * (hd + 2);
+            const float m = ps[hd], l = ps[hd + 1], o = ps[dd];
+            const float w = m == -INFINITY ? 0.f : expf(m - M);
+            Lsum = fmaf(l, w, Lsum);
+            O = fmaf(o, w, O);
+        }
+        P.out[size_t(i) * qw + (size_t(kvh) * group + h) * hd + dd] = __fdiv_rn(O, Lsum);
+    }
+    cl.sync();
 }
 
 // ------------------------------------------------ attention on tensor cores ----
@@ -893,12 +926,42 @@ cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t s, bool pd
     const int target = dev < 64 && sms[dev] ? sms[dev] : 148;
     int chunk = kAttnChunk;
     while (chunk > kAttnMinChunk && ((P.context + chunk - 1) / chunk) * P.kv_heads * n < 3 * target) chunk /= 2;
-    const int chunks = (P.context + chunk - 1) / chunk;
+    int chunks = (P.context + chunk - 1) / chunk;
     AttnParams p = P;
+    p.cluster = 0;
+    if (P.kv_heads * n < 16) {
+        // Few (kv head, client) pairs (one client of Qwen3-8B: 8): the step's
+        // attention is a latency chain, so each pair's prefix is split into
+        // at most 8 chunks that form one cluster and combine on chip.
+        int c8 = (P.context + 7) / 8;
+        c8 = std::max(kAttnMinChunk, (c8 + kAttnMinChunk - 1) / kAttnMinChunk * kAttnMinChunk);
+        const int s8 = (P.context + c8 - 1) / c8;
+        if (s8 > 1) {
+            chunk = c8;
+            chunks = s8;
+            p.cluster = 1;
+        }
+    }
     p.chunk = chunk;
     void* args[] = {&p};
-    return launch_pdl(reinterpret_cast<const void*>(attention_kernel), dim3(P.kv_heads, n, chunks),
-                      dim3(kAttnThreads), smem, s, pdl, args);
+    if (!p.cluster)
+        return launch_pdl(reinterpret_cast<const void*>(attention_kernel), dim3(P.kv_heads, n, chunks),
+                          dim3(kAttnThreads), smem, s, pdl, args);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(P.kv_heads, n, chunks);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = unsigned(chunks);
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(attention_kernel), args);
 }
 
 cudaError_t launch_attention_queries(const AttnParams& P, int n, cudaStream_t s) {
@@ -912,6 +975,7 @@ cudaError_t launch_attention_queries(const AttnParams& P, int n, cudaStream_t s)
         configured_for = dev;
     }
     AttnParams p = P;
+    p.cluster = 0;
     p.chunk = P.context;  // one CTA covers the whole prefix: S == 1, no partials
     void* args[] = {&p};
     return launch_pdl(reinterpret_cast<const void*>(attention_kernel), dim3(P.kv_heads, n, 1), dim3(kAttnThreads),

@@ -153,6 +153,10 @@ struct AttnParams {
     // mode row i is client cache_client + i's (the cache's client index).
     const int32_t* qpos;
     int32_t cache_client;
+    // Set by launch_attention: the chunks of a (kv head, client) form one
+    // thread-block cluster and combine their partials through distributed
+    // shared memory instead of the scratch and the last-CTA counter.
+    int32_t cluster;
 };
 size_t attention_smem(const AttnParams& P);
 cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t stream, bool pdl);
