@@ -271,6 +271,38 @@ __device__ void attn_combine(const AttnParams& P, int i, int kvh, int S) {
     }
 }
 
+// The chunks of a (kv head, client) as one cluster of S CTAs (rank =
+// chunk), each with its partial [group][hd + 2] in its own shared memory at
+// `part`: once every partial is in place, CTA r combines the outputs
+// r * per .. (r + 1) * per - 1, reading the partials from the other CTAs'
+// shared memory in chunk order -- attn_combine's arithmetic, without the
+// global round trip and the counter.  A second cluster barrier keeps every
+// partial alive until all have been read.
+template <int NT>
+__device__ void attn_cluster_combine(const AttnParams& P, int i, int kvh, int S, int chunk, float* part) {
+    namespace cg = cooperative_groups;
+    const int hd = P.head_dim, group = P.heads / P.kv_heads, qw = P.heads * hd;
+    cg::cluster_group cl = cg::this_cluster();
+    cl.sync();
+    pdl_trigger();
+    const int per = (group * hd + S - 1) / S;
+    for (int t = chunk * per + int(threadIdx.x); t < min(group * hd, (chunk + 1) * per); t += NT) {
+        const int h = t / hd, dd = t % hd;
+        float M = -INFINITY;
+        for (int s = 0; s < S; s++) M = fmaxf(M, cl.map_shared_rank(part, s)[h * (hd + 2) + hd]);
+        float Lsum = 0.f, O = 0.f;
+        for (int s = 0; s < S; s++) {
+            const float* ps = cl.map_shared_rank(part, s) + h * (hd + 2);
+            const float m = ps[hd], l = ps[hd + 1], o = ps[dd];
+            const float w = m == -INFINITY ? 0.f : expf(m - M);
+            Lsum = fmaf(l, w, Lsum);
+            O = fmaf(o, w, O);
+        }
+        P.out[size_t(i) * qw + (size_t(kvh) * group + h) * hd + dd] = __fdiv_rn(O, Lsum);
+    }
+    cl.sync();
+}
+
 // Shared memory of the attention kernel, in floats (mbarriers at the end).
 struct AttnSmem {
     int qs, kn, vn, kt, vt, part, prob, stat, total;
@@ -460,32 +492,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const AttnParam
         attn_combine<kAttnThreads>(P, i, kvh, S);
         return;
     }
-    // Cluster of the S chunks (rank = chunk): once every partial is in
-    // place, CTA r combines the outputs r * per .. (r + 1) * per - 1, reading
-    // the partials from the other CTAs' shared memory in chunk order -- the
-    // arithmetic of attn_combine, without the global round trip and the
-    // counter.  A second cluster barrier keeps every partial alive until all
-    // have been read.
-    namespace cg = cooperative_groups;
-    cg::cluster_group cl = cg::this_cluster();
-    cl.sync();
-    pdl_trigger();
-    const int per = (group * hd + S - 1) / S;
-    for (int t = chunk * per + int(threadIdx.x); t < min(group * hd, (chunk + 1) * per); t += kAttnThreads) {
-        const int h = t / hd, dd = t % hd;
-        float M = -INFINITY;
-        for (int s = 0; s < S; s++) M = fmaxf(M, cl.map_shared_rank(outp, s)[h * (hd + 2) + hd]);
-        float Lsum = 0.f, O = 0.f;
-        for (int s = 0; s < S; s++) {
-            const float* ps = cl.map_shared_rank(outp, s) + h * (hd + 2);
-            const float m = ps[hd], l = ps[hd + 1], o = ps[dd];
-            const float w = m == -INFINITY ? 0.f : expf(m - M);
-            Lsum = fmaf(l, w, Lsum);
-            O = fmaf(o, w, O);
-        }
-        P.out[size_t(i) * qw + (size_t(kvh) * group + h) * hd + dd] = __fdiv_rn(O, Lsum);
-    }
-    cl.sync();
+    attn_cluster_combine<kAttnThreads>(P, i, kvh, S, chunk, outp);
 }
 
 // ------------------------------------------------ attention on tensor cores ----
@@ -807,8 +814,11 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
         }
     }
     __syncthreads();
-    // the warps' states merged in warp order: this chunk's partial, or the output
-    float* outp = P.scratch + ((size_t(i) * P.kv_heads + kvh) * S + chunk) * group * (HD + 2);
+    // the warps' states merged in warp order: this chunk's partial (in the
+    // scratch, or with a cluster in the ring after the warps' states), or
+    // the output
+    float* outp = P.cluster ? reinterpret_cast<float*>(smb + L::ring) + kTcWarps * 8 * (HD + 2)
+                            : P.scratch + ((size_t(i) * P.kv_heads + kvh) * S + chunk) * group * (HD + 2);
     for (int e = threadIdx.x; e < group * HD; e += kTcThreads) {
         const int h = e / HD, d = e % HD;
         const float* st = reinterpret_cast<const float*>(smb + L::ring) + h * (HD + 2);
@@ -838,6 +848,10 @@ __global__ void __launch_bounds__(kTcThreads) attention_tc_kernel(const AttnPara
         pdl_trigger();
         return;
     }
+    if (P.cluster) {
+        attn_cluster_combine<kTcThreads>(P, i, kvh, S, chunk, outp);
+        return;
+    }
     attn_combine<kTcThreads>(P, i, kvh, S);
 }
 
@@ -860,6 +874,28 @@ static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+// An attention grid (kv head, client, chunk); with `cluster` the chunks of
+// each (kv head, client) form one thread-block cluster (at most 8).
+static cudaError_t launch_attention_grid(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                                         int cluster, void** args) {
+    if (!cluster) return launch_pdl(fn, grid, block, smem, s, pdl, args);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = grid.z;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
@@ -898,9 +934,11 @@ static cudaError_t launch_attention_tc(const AttnParams& P, int n, int sms, cuda
     const int chunks = (P.context + chunk - 1) / chunk;
     AttnParams p = P;
     p.chunk = chunk;
+    // up to eight chunks of a pair form a cluster and combine on chip
+    p.cluster = chunks > 1 && chunks <= 8 ? 1 : 0;
     void* args[] = {&p};
-    return launch_pdl(reinterpret_cast<const void*>(attention_tc_kernel<HD>), dim3(P.kv_heads, n, chunks),
-                      dim3(kTcThreads), smem, s, pdl, args);
+    return launch_attention_grid(reinterpret_cast<const void*>(attention_tc_kernel<HD>),
+                                 dim3(P.kv_heads, n, chunks), dim3(kTcThreads), smem, s, pdl, p.cluster, args);
 }
 
 cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t s, bool pdl) {
@@ -944,24 +982,8 @@ cudaError_t launch_attention(const AttnParams& P, int n, cudaStream_t s, bool pd
     }
     p.chunk = chunk;
     void* args[] = {&p};
-    if (!p.cluster)
-        return launch_pdl(reinterpret_cast<const void*>(attention_kernel), dim3(P.kv_heads, n, chunks),
-                          dim3(kAttnThreads), smem, s, pdl, args);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(P.kv_heads, n, chunks);
-    cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = unsigned(chunks);
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(attention_kernel), args);
+    return launch_attention_grid(reinterpret_cast<const void*>(attention_kernel), dim3(P.kv_heads, n, chunks),
+                                 dim3(kAttnThreads), smem, s, pdl, p.cluster, args);
 }
 
 cudaError_t launch_attention_queries(const AttnParams& P, int n, cudaStream_t s) {
