@@ -12,114 +12,115 @@ __device__ __forceinline__ int32_t total_key(float f) {
     return b ^ int32_t(uint32_t(b >> 31) >> 1);
 }
 
-// One CTA.  Warp i routes client i; then the plan is built over experts.
+// One CTA.  Warp i routes client i with its probabilities in registers
+// (lane l holds experts l, l + 32, ..., NV of them); then the plan is built
+// from a bitmap of each expert's clients.
+//
+// Selection: each round every lane offers its largest untaken probability
+// (by f32::total_cmp order key, the lower id among equals), the warp agrees
+// on the largest key and then on the lowest id holding it with two
+// redux.sync reductions, and the owner marks it taken -- the same routes as a
+// scan of all experts per round, in far fewer dependent steps.
+template <int NV>
 __global__ void __launch_bounds__(256) route_kernel(const float* logits, const float* bias, int n, int E, int K,
                                                     int world, int rank, MoePlan* plan) {
-    __shared__ float prob[kMoeMaxClients][kMoeMaxExperts];
     __shared__ int32_t sel[kMoeMaxClients][kMoeMaxUsed];
-    __shared__ int32_t cnt[kMoeMaxExperts], base[kMoeMaxExperts];
-    __shared__ int32_t pos_of[kMoeMaxClients][kMoeMaxUsed];
-    pdl_wait();
+    __shared__ float psel[kMoeMaxClients][kMoeMaxUsed];
+    __shared__ uint32_t cmask[kMoeMaxExperts];  // bit i: client i routes to the expert
+    __shared__ int32_t base[kMoeMaxExperts];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cmask[e] = 0;
+    __syncthreads();
+    pdl_wait();
     if (warp < n) {
         const int i = warp;
+        float p[NV];
         // softmax: max by fold, exp(v - max), sum, divide (math.rs:23-29)
         float mx = -INFINITY;
-        for (int e = lane; e < E; e += 32) {
-            const float v = bias ? logits[i * E + e] + bias[e] : logits[i * E + e];
-            prob[i][e] = v;
-            mx = fmaxf(mx, v);
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+            const int e = lane + 32 * j;
+            p[j] = -INFINITY;
+            if (e < E) {
+                p[j] = bias ? logits[i * E + e] + bias[e] : logits[i * E + e];
+                mx = fmaxf(mx, p[j]);
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         float sum = 0.f;
-        for (int e = lane; e < E; e += 32) {
-            const float v = expf(prob[i][e] - mx);
-            prob[i][e] = v;
-            sum += v;
-        }
-        sum = warp_sum(sum);
-        __syncwarp();
-        for (int e = lane; e < E; e += 32) prob[i][e] = __fdiv_rn(prob[i][e], sum);
-        __syncwarp();
-        // top-K: largest probability first, the lower id among equals
-        uint64_t taken = 0, taken2 = 0, taken3 = 0, taken4 = 0;
-        for (int j = 0; j < K; j++) {
-            int32_t bk = INT32_MIN;
-            int bi = -1;
-            for (int e = lane; e < E; e += 32) {
-                const uint64_t bit = 1ull << (e & 63);
-                const uint64_t t = e < 64 ? taken : e < 128 ? taken2 : e < 192 ? taken3 : taken4;
-                if (t & bit) continue;
-                const int32_t k = total_key(prob[i][e]);
-                if (bi < 0 || k > bk) { bk = k; bi = e; }
-            }
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const int32_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (oi >= 0 && (bi < 0 || ok > bk || (ok == bk && oi < bi))) { bk = ok; bi = oi; }
+        for (int j = 0; j < NV; j++)
+            if (lane + 32 * j < E) {
+                p[j] = expf(p[j] - mx);
+                sum += p[j];
             }
-            const uint64_t bit = 1ull << (bi & 63);
-            if (bi < 64) taken |= bit;
-            else if (bi < 128) taken2 |= bit;
-            else if (bi < 192) taken3 |= bit;
-            else taken4 |= bit;
-            if (lane == 0) sel[i][j] = bi;
+        sum = warp_sum(sum);
+        int32_t key[NV];
+#pragma unroll
+        for (int j = 0; j < NV; j++) {
+            p[j] = __fdiv_rn(p[j], sum);
+            key[j] = lane + 32 * j < E ? total_key(p[j]) : INT32_MIN;
+        }
+        // top-K: largest probability first, the lower id among equals
+        uint32_t taken = 0;
+        float mine = 0.f;  // lane r < K: probability and expert of route r
+        int myid = 0;
+        for (int r = 0; r < K; r++) {
+            int32_t bk = INT32_MIN;
+            int bj = -1;
+#pragma unroll
+            for (int j = 0; j < NV; j++)
+                if (lane + 32 * j < E && !((taken >> j) & 1u) && (bj < 0 || key[j] > bk)) {
+                    bk = key[j];
+                    bj = j;
+                }
+            const int32_t m = __reduce_max_sync(0xffffffffu, bk);
+            const int win = __reduce_min_sync(0xffffffffu, bj >= 0 && bk == m ? lane + 32 * bj : INT32_MAX);
+            float pw = 0.f;
+            if ((win & 31) == lane) {
+                taken |= 1u << (win >> 5);
+#pragma unroll
+                for (int j = 0; j < NV; j++)
+                    if (j == (win >> 5)) pw = p[j];
+            }
+            pw = __shfl_sync(0xffffffffu, pw, win & 31);
+            if (lane == r) {
+                mine = pw;
+                myid = win;
+            }
         }
         // the largest probability left out, for the routing's margin
-        {
-            float best = -INFINITY;
-            for (int e = lane; e < E; e += 32) {
-                const uint64_t bit = 1ull << (e & 63);
-                const uint64_t t = e < 64 ? taken : e < 128 ? taken2 : e < 192 ? taken3 : taken4;
-                if (!(t & bit)) best = fmaxf(best, prob[i][e]);
-            }
+        float best = -INFINITY;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
-            __syncwarp();
-            if (lane == 0) {
-                const float pk = prob[i][sel[i][K - 1]];
-                plan->gap[i] = best == -INFINITY ? 1.0f : (pk - best) / pk;
-            }
+        for (int j = 0; j < NV; j++)
+            if (lane + 32 * j < E && !((taken >> j) & 1u)) best = fmaxf(best, p[j]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, o));
+        const float pk = __shfl_sync(0xffffffffu, mine, K - 1);
+        if (lane < K) {
+            sel[i][lane] = myid;
+            psel[i][lane] = mine;
+            atomicOr(&cmask[myid], 1u << i);
+            plan->route[i][lane] = myid;
         }
-        __syncwarp();
+        // the renormaliser, in route order (layout.rs:289-293)
+        float s = 0.f;
+        for (int r = 0; r < K; r++) s += __shfl_sync(0xffffffffu, mine, r);
         if (lane == 0) {
-            float s = 0.f;  // in route order (layout.rs:289-293)
-            for (int j = 0; j < K; j++) s += prob[i][sel[i][j]];
             plan->norm[i] = s;
-            for (int j = 0; j < K; j++) plan->route[i][j] = sel[i][j];
+            plan->gap[i] = best == -INFINITY ? 1.0f : (pk - best) / pk;
         }
     }
     __syncthreads();
     // ---- plan: active experts ascending, their clients ascending ----
-    // Every thread holds the selection table in registers (-1 beyond n
-    // clients and K routes), so the scans below run without memory waits.
-    int32_t S[kMoeMaxClients][kMoeMaxUsed];
-#pragma unroll
-    for (int i = 0; i < kMoeMaxClients; i++)
-#pragma unroll
-        for (int j = 0; j < kMoeMaxUsed; j++) S[i][j] = i < n && j < K ? sel[i][j] : -1;
-    // Thread e counts expert e's routes and records, for each of them, its
-    // position among the expert's clients (clients ascending; a client
-    // routes to an expert at most once).
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        int c = 0;
-#pragma unroll
-        for (int i = 0; i < kMoeMaxClients; i++)
-#pragma unroll
-            for (int j = 0; j < kMoeMaxUsed; j++)
-                if (S[i][j] == e) pos_of[i][j] = c++;
-        cnt[e] = c;
-    }
-    __syncthreads();
-    // active index of every expert: exclusive prefix count of cnt[e] > 0,
-    // 32 experts per step by ballot
+    // active index of every expert: exclusive prefix count of the experts
+    // with a client, 32 experts per step by ballot
     if (warp == 0) {
         int run = 0;
         for (int e0 = 0; e0 < E; e0 += 32) {
             const int e = e0 + lane;
-            const bool act = e < E && cnt[e] > 0;
+            const bool act = e < E && cmask[e] != 0;
             const uint32_t m = __ballot_sync(0xffffffffu, act);
             if (e < E) base[e] = run + __popc(m & ((1u << lane) - 1u));
             run += __popc(m);
@@ -130,7 +131,7 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
         int run = 0, local = 0;
         for (int e0 = 0; e0 < E; e0 += 32) {
             const int e = e0 + lane;
-            const bool act = e < E && cnt[e] > 0;
+            const bool act = e < E && cmask[e] != 0;
             const bool own = act && e % world == rank;
             const uint32_t ma = __ballot_sync(0xffffffffu, act), mo = __ballot_sync(0xffffffffu, own);
             if (own) plan->local[local + __popc(mo & ((1u << lane) - 1u))] = run + __popc(ma & ((1u << lane) - 1u));
@@ -141,19 +142,14 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
     }
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        if (!cnt[e]) continue;
+        uint32_t m = cmask[e];
+        if (!m) continue;
         const int a = base[e];
         plan->expert[a] = e;
-        plan->ntok[a] = cnt[e];
-        int p = 0;
-#pragma unroll
-        for (int i = 0; i < kMoeMaxClients; i++) {
-            bool hit = false;
-#pragma unroll
-            for (int j = 0; j < kMoeMaxUsed; j++) hit |= S[i][j] == e;
-            if (hit) plan->tok[a][p++] = i;
-        }
-        for (; p < kMoeMaxClients; p++) plan->tok[a][p] = 0;
+        plan->ntok[a] = __popc(m);
+        int q = 0;
+        for (; m; m &= m - 1u) plan->tok[a][q++] = __ffs(m) - 1;
+        for (; q < kMoeMaxClients; q++) plan->tok[a][q] = 0;
     }
     if (threadIdx.x < n) {
         // this client's routes in ascending expert id: route j goes to place
@@ -165,12 +161,13 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
 #pragma unroll
         for (int j = 0; j < kMoeMaxUsed; j++) {
             if (j >= K) break;
-            int rank = 0;
+            int rk = 0;
 #pragma unroll
-            for (int x = 0; x < kMoeMaxUsed; x++) rank += (x < K && ids[x] < ids[j]) ? 1 : 0;
-            plan->slot_a[i][rank] = base[ids[j]];
-            plan->slot_pos[i][rank] = pos_of[i][j];
-            plan->slot_p[i][rank] = prob[i][ids[j]];
+            for (int x = 0; x < kMoeMaxUsed; x++) rk += (x < K && ids[x] < ids[j]) ? 1 : 0;
+            plan->slot_a[i][rk] = base[ids[j]];
+            // its place among the expert's clients (clients ascending)
+            plan->slot_pos[i][rk] = __popc(cmask[ids[j]] & ((1u << i) - 1u));
+            plan->slot_p[i][rk] = psel[i][j];
         }
     }
     pdl_trigger();
@@ -295,7 +292,10 @@ cudaError_t launch_route(const float* logits, const float* bias, int n, int expe
         return cudaErrorInvalidValue;
     if (world < 1 || rank < 0 || rank >= world) return cudaErrorInvalidValue;
     void* args[] = {&logits, &bias, &n, &experts, &used, &world, &rank, &plan};
-    return launch_pdl(reinterpret_cast<const void*>(route_kernel), dim3(1), dim3(256), s, pdl, args);
+    const void* fn = experts <= 64    ? reinterpret_cast<const void*>(route_kernel<2>)
+                     : experts <= 128 ? reinterpret_cast<const void*>(route_kernel<4>)
+                                      : reinterpret_cast<const void*>(route_kernel<8>);
+    return launch_pdl(fn, dim3(1), dim3(256), s, pdl, args);
 }
 
 int combine_parts(int width, int n) { return ((width + kCombineCols - 1) / kCombineCols) * n; }
