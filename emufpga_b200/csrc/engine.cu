@@ -98,6 +98,7 @@ struct spm_session {
     int moe_max_active = 0;
     float* attn_scratch = nullptr;
     int32_t* attn_counters = nullptr;
+    uint32_t* route_counter = nullptr;  // CTAs of the router launch that have finished (zero between launches)
     int32_t* status = nullptr;         // device error word of bounded waits
     int32_t* h_status = nullptr;
     uint32_t* step = nullptr;          // steps taken (advance kernel); names the exchange rounds
@@ -848,26 +849,51 @@ void enqueue_step(spm_session* s, int n) {
         if (is_moe(c)) {
             // routed feed-forward (spm-granite-moe/src/layout.rs:188-333)
             const int E = int(c.experts), K = int(c.experts_used), eff = int(c.expert_ff);
-            GemvLaunch gr = gemv_base(m, L.router, s->states, n);
-            gr.status = s->status;
-            norm_in(gr, L.ffn_norm, 1);
-            if (dp) {
-                // every rank's rows of this layer must be in place
-                gr.world = m->world;
-                gr.ep_wait_flags = s->dp_flags;
-                gr.ep_step = s->step;
-                gr.ep_layers = int32_t(c.layers);
-                gr.ep_layer = int32_t(l);
-                gr.wait_ns = s->wait_ns;
-            }
-            add_job(gr, m, L.router, nullptr, s->moe_logits, E, nullptr, 0, EPI_STORE);
-            gemv(gr, L.router, SPM_GEMV_ROUTER, int(l), qbytes(L.router));
             MoePlan* plan = s->plans + l;
-            timed(SPM_KERNEL_ROUTE, int(l), -1, 0, [&] {
-                CUDA_OK(launch_route(s->moe_logits, L.bias >= 0 ? m->gains + L.bias : nullptr, n, E, K, m->world, m->rank,
-                                     plan, st, pdl));
-                return 0;
-            });
+            if (m->world == 1 && m->streams[L.router].pk.dtype == SPM_F32) {
+                // one GPU: the router logits and the routing are one launch
+                const Packed& rp = m->streams[L.router].pk;
+                RouterArgs ra{};
+                ra.x = s->states;
+                ra.x_stride = d;
+                ra.gain = m->gains + L.ffn_norm;
+                ra.sumsq = part[1];
+                ra.sumsq_parts = parts;
+                ra.eps = c.eps;
+                ra.w = reinterpret_cast<const float*>(m->tiles(L.router));
+                ra.cols = int(rp.cols);
+                ra.E = E;
+                ra.K = K;
+                ra.n = n;
+                ra.bias = L.bias >= 0 ? m->gains + L.bias : nullptr;
+                ra.logits = s->moe_logits;
+                ra.plan = plan;
+                ra.counter = s->route_counter;
+                timed(SPM_KERNEL_ROUTE, int(l), -1, 0, [&] {
+                    CUDA_OK(launch_router_route(ra, st, pdl));
+                    return 0;
+                });
+            } else {
+                GemvLaunch gr = gemv_base(m, L.router, s->states, n);
+                gr.status = s->status;
+                norm_in(gr, L.ffn_norm, 1);
+                if (dp) {
+                    // every rank's rows of this layer must be in place
+                    gr.world = m->world;
+                    gr.ep_wait_flags = s->dp_flags;
+                    gr.ep_step = s->step;
+                    gr.ep_layers = int32_t(c.layers);
+                    gr.ep_layer = int32_t(l);
+                    gr.wait_ns = s->wait_ns;
+                }
+                add_job(gr, m, L.router, nullptr, s->moe_logits, E, nullptr, 0, EPI_STORE);
+                gemv(gr, L.router, SPM_GEMV_ROUTER, int(l), qbytes(L.router));
+                timed(SPM_KERNEL_ROUTE, int(l), -1, 0, [&] {
+                    CUDA_OK(launch_route(s->moe_logits, L.bias >= 0 ? m->gains + L.bias : nullptr, n, E, K, m->world, m->rank,
+                                         plan, st, pdl));
+                    return 0;
+                });
+            }
             // active experts of this rank, at most; the expert launches fill
             // the SMs once and split the active experts over them (at least
             // the chunks that would give every SM two CTAs with all possible
@@ -1551,6 +1577,7 @@ spm_status spm_session_create(spm_model* m, int32_t max_clients, int32_t max_con
             if (c.expert_ff % kTileRows || c.hidden % kTileRows) fail(SPM_E_ARG, "expert rows must be whole tiles");
             s->moe_max_active = int(std::min<size_t>(c.experts, std::min<size_t>(n, kMoeMaxClients) * c.experts_used));
             s->moe_logits = s->alloc<float>(n * c.experts);
+            s->route_counter = s->alloc<uint32_t>(1);
             s->plans = s->alloc<MoePlan>(c.layers);
             s->moe_act = s->alloc<float>(size_t(s->moe_max_active) * kMoeMaxClients * c.expert_ff);
             s->moe_out = s->alloc<float>(size_t(s->moe_max_active) * kMoeMaxClients * c.hidden);

@@ -21,17 +21,25 @@ __device__ __forceinline__ int32_t total_key(float f) {
 // on the largest key and then on the lowest id holding it with two
 // redux.sync reductions, and the owner marks it taken -- the same routes as a
 // scan of all experts per round, in far fewer dependent steps.
-template <int NV>
-__global__ void __launch_bounds__(256) route_kernel(const float* logits, const float* bias, int n, int E, int K,
-                                                    int world, int rank, MoePlan* plan) {
-    __shared__ int32_t sel[kMoeMaxClients][kMoeMaxUsed];
-    __shared__ float psel[kMoeMaxClients][kMoeMaxUsed];
-    __shared__ uint32_t cmask[kMoeMaxExperts];  // bit i: client i routes to the expert
-    __shared__ int32_t base[kMoeMaxExperts];
+struct RouteSmem {
+    int32_t sel[kMoeMaxClients][kMoeMaxUsed];
+    float psel[kMoeMaxClients][kMoeMaxUsed];
+    uint32_t cmask[kMoeMaxExperts];  // bit i: client i routes to the expert
+    int32_t base[kMoeMaxExperts];
+};
+
+// The routing of all n clients by one CTA of 256 threads.  CG: the logits
+// were written by other CTAs of this launch (read past L1).
+template <int NV, bool CG>
+__device__ void route_block(const float* logits, const float* bias, int n, int E, int K, int world, int rank,
+                            MoePlan* plan, RouteSmem& S) {
+    auto& sel = S.sel;
+    auto& psel = S.psel;
+    auto& cmask = S.cmask;
+    auto& base = S.base;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int e = threadIdx.x; e < E; e += blockDim.x) cmask[e] = 0;
     __syncthreads();
-    pdl_wait();
     if (warp < n) {
         const int i = warp;
         float p[NV];
@@ -42,7 +50,8 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
             const int e = lane + 32 * j;
             p[j] = -INFINITY;
             if (e < E) {
-                p[j] = bias ? logits[i * E + e] + bias[e] : logits[i * E + e];
+                const float lg = CG ? __ldcg(logits + i * E + e) : logits[i * E + e];
+                p[j] = bias ? lg + bias[e] : lg;
                 mx = fmaxf(mx, p[j]);
             }
         }
@@ -170,6 +179,71 @@ __global__ void __launch_bounds__(256) route_kernel(const float* logits, const f
             plan->slot_p[i][rk] = psel[i][j];
         }
     }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256) route_kernel(const float* logits, const float* bias, int n, int E, int K,
+                                                    int world, int rank, MoePlan* plan) {
+    __shared__ RouteSmem S;
+    pdl_wait();
+    route_block<NV, false>(logits, bias, n, E, K, world, rank, plan, S);
+    pdl_trigger();
+}
+
+// Router logits and routing in one launch (one GPU).  CTA e computes expert
+// e's logit of every client: warp c walks client c's state, normalised on
+// load (x * gain, the RMSNorm scale applied to the sum), against row e of the
+// F32 router, lane l taking columns 4l + 128j; the warp's sum in butterfly
+// order times the scale is the logit.  The last CTA to finish (a launch
+// counter that returns to zero) routes: route_block over the logits the
+// other CTAs wrote.
+template <int NV>
+__global__ void __launch_bounds__(256) router_route_kernel(const RouterArgs A) {
+    __shared__ RouteSmem S;
+    __shared__ int last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, e = int(blockIdx.x);
+    const float* wr = A.w + size_t(e) * A.cols;
+    pdl_wait();
+    if (warp < A.n) {
+        const int c = warp;
+        // the client's RMSNorm scale from the producer's per-CTA sums of
+        // squares, added in the streaming GEMV's order
+        const float* sp = A.sumsq + c;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int p = lane;
+        for (; p + 96 < A.sumsq_parts; p += 128) {
+            a0 += sp[p * 8];
+            a1 += sp[(p + 32) * 8];
+            a2 += sp[(p + 64) * 8];
+            a3 += sp[(p + 96) * 8];
+        }
+        for (; p < A.sumsq_parts; p += 32) a0 += sp[p * 8];
+        const float ssum = warp_sum((a0 + a1) + (a2 + a3));
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssum, float(A.cols)), A.eps)));
+        const float* xr = A.x + size_t(c) * A.x_stride;
+        float acc = 0.f;
+#pragma unroll 4
+        for (int col = lane * 4; col < A.cols; col += 128) {
+            const float4 w = ldx4(wr + col), x = ldx4(xr + col), g = ldx4(A.gain + col);
+            acc = fmaf(w.x, __fmul_rn(x.x, g.x), acc);
+            acc = fmaf(w.y, __fmul_rn(x.y, g.y), acc);
+            acc = fmaf(w.z, __fmul_rn(x.z, g.z), acc);
+            acc = fmaf(w.w, __fmul_rn(x.w, g.w), acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) A.logits[c * A.E + e] = acc * scale;
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t prev = atomicAdd(A.counter, 1u);
+        last = prev + 1 == gridDim.x;
+        if (last) *A.counter = 0;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    route_block<NV, true>(A.logits, A.bias, A.n, A.E, A.K, 1, 0, A.plan, S);
     pdl_trigger();
 }
 
@@ -296,6 +370,18 @@ cudaError_t launch_route(const float* logits, const float* bias, int n, int expe
                      : experts <= 128 ? reinterpret_cast<const void*>(route_kernel<4>)
                                       : reinterpret_cast<const void*>(route_kernel<8>);
     return launch_pdl(fn, dim3(1), dim3(256), s, pdl, args);
+}
+
+cudaError_t launch_router_route(const RouterArgs& A, cudaStream_t s, bool pdl) {
+    if (A.n < 1 || A.n > kMoeMaxClients || A.E < 1 || A.E > kMoeMaxExperts || A.K < 1 || A.K > kMoeMaxUsed ||
+        A.K > A.E || A.cols < 4 || A.cols % 4)
+        return cudaErrorInvalidValue;
+    RouterArgs a = A;
+    void* args[] = {&a};
+    const void* fn = A.E <= 64    ? reinterpret_cast<const void*>(router_route_kernel<2>)
+                     : A.E <= 128 ? reinterpret_cast<const void*>(router_route_kernel<4>)
+                                  : reinterpret_cast<const void*>(router_route_kernel<8>);
+    return launch_pdl(fn, dim3(A.E), dim3(256), s, pdl, args);
 }
 
 int combine_parts(int width, int n) { return ((width + kCombineCols - 1) / kCombineCols) * n; }

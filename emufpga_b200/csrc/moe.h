@@ -37,6 +37,25 @@ struct MoePlan {
 // renormaliser, and the plan (spm-granite-moe/src/moe.rs:17-35, math.rs:23-39).
 cudaError_t launch_route(const float* logits, const float* bias, int n, int experts, int used, int world, int rank,
                          MoePlan* plan, cudaStream_t s, bool pdl);
+// Router logits and routing in one launch (one GPU): logits[c][e] =
+// s_c * sum_k W[e][k] * (x[c][k] * gain[k]) with s_c the RMSNorm scale of
+// client c from the producer's per-CTA sums of squares (sumsq[p * 8 + c],
+// p < sumsq_parts), then launch_route's softmax, top-k and plan.  W is the
+// F32 router, row-major [E][cols]; counter is zero between launches.
+struct RouterArgs {
+    const float* x;
+    int32_t x_stride;
+    const float *gain, *sumsq;
+    int32_t sumsq_parts;
+    float eps;
+    const float* w;
+    int32_t cols, E, K, n;
+    const float* bias;
+    float* logits;
+    MoePlan* plan;
+    uint32_t* counter;
+};
+cudaError_t launch_router_route(const RouterArgs& A, cudaStream_t s, bool pdl);
 // Expert parallel combine: before reading the expert outputs, wait until
 // every rank has raised its flag for this layer (flag value E = *step *
 // layers + layer + 1, in flags[(E & 1) * 64 + rank]); the outputs are in the

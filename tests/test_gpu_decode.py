@@ -128,7 +128,9 @@ def test_launch_profile_times_every_kernel_and_changes_no_result(cuda, models):
         assert np.array_equal(la.view(np.uint32), lb.view(np.uint32))
     prof = b.profile()
     kinds = [eb.Session.KERNEL_KINDS[k] for k in prof["kind"]]
-    per_step = 1 + sh.layers * 8 + 1 + 2  # embed, 8 per routed layer, head, argmax, advance
+    # embed; per routed layer QKV, attention, O, router with routing (one
+    # launch on one GPU), expert gate/up, expert down, combine; head, argmax, advance
+    per_step = 1 + sh.layers * 7 + 1 + 2
     assert len(kinds) == 2 * per_step
     assert kinds.count("attention") == 2 * sh.layers and kinds.count("gemv_head") == 2
     assert (prof["ms"] > 0).all()

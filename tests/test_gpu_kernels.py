@@ -165,3 +165,41 @@ def test_tensor_core_product_large_shape(cuda):
     got, want, scale = gemv_case(cuda, O.Q5_K, 600, 4096, 300, seed=123)
     err = np.abs(got - want)
     assert np.all(err <= 1e-5 * scale + 1e-30), float((err / (scale + 1e-30)).max())
+
+
+@pytest.mark.parametrize("dtype", [O.Q8_0, O.Q6_K, O.Q5_K, O.Q2_K])
+@pytest.mark.parametrize("positions", [1, 5, 8])
+def test_gemv_staging_worst_case(cuda, dtype, positions):
+    """Activations are staged per 32-value unit as 22-bit block fixed point
+    (a power-of-two scale below the unit's largest |x|, three int8 digit
+    planes).  Worst case for that staging: in every unit one value of order
+    100 and 31 of order 1e-4, so the small ones keep only a few significant
+    bits.  Each output must stay within the staging bound -- at most 2^-22 of
+    its unit's largest |x| per value (half a step of 2^(e-22) with
+    2^(e-1) <= max|x| < 2^e), times |w|, checked at 2^-21 -- on top of
+    the fp32 summation-order tolerance, and within 1e-3 of the largest output
+    (the logit bar).  One position runs the dp4a loop; five and eight the
+    tensor-core loops (Q8_0: codes as B; K-quants: codes as A)."""
+    import torch
+
+    rows, cols = (203, 1536) if dtype != O.Q8_0 else (203, 576)
+    rng = np.random.default_rng(1000 + dtype * 10 + positions)
+    blocks = random_matrix(dtype, rows, cols, seed=dtype * 17 + positions)
+    x = rng.normal(0, 1e-4, (positions, cols)).astype(np.float32)
+    units = cols // 32
+    big = rng.integers(0, 32, size=(positions, units)) + 32 * np.arange(units)
+    for p in range(positions):
+        x[p, big[p]] = rng.normal(0, 100, units).astype(np.float32)
+    want = O.gemv_fma(dtype, blocks, rows, cols, x, positions)
+    w = eb.Weights(dtype, rows, cols, blocks)
+    yd = torch.full((positions, rows), float("nan"), device=cuda)
+    w.gemv(torch.from_numpy(x).to(cuda), positions, yd)
+    torch.cuda.synchronize()
+    got = yd.cpu().numpy()
+    dense = np.abs(O.decode(dtype, blocks.tobytes()).reshape(rows, cols))
+    scale = np.abs(x) @ dense.T
+    umax = np.repeat(np.abs(x).reshape(positions, units, 32).max(axis=2), 32, axis=1)  # unit max per column
+    staging = umax @ dense.T * 2.0 ** -21
+    err = np.abs(got - want)
+    assert np.all(err <= 1e-5 * scale + staging + 1e-30), float((err / (1e-5 * scale + staging + 1e-30)).max())
+    assert np.all(err <= 1e-3 * np.abs(want).max(axis=1, keepdims=True))
