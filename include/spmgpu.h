@@ -257,12 +257,13 @@ spm_status spm_session_launches_per_step(spm_session* s, int32_t n, int32_t* lau
  * *count receives the number recorded. */
 enum {
     SPM_GEMV_DENSE = 0,          /* GEMV: attention q/k/v, o; dense feed-forward */
-    SPM_GEMV_ROUTER = 1,         /* GEMV: MoE router logits                   */
+    SPM_GEMV_ROUTER = 1,         /* GEMV: MoE router logits (expert parallel) */
     SPM_GEMV_EXPERT_GATE_UP = 2, /* GEMV: gate/up of the active experts       */
     SPM_GEMV_EXPERT_DOWN = 3,    /* GEMV: down projection of the active experts */
     SPM_GEMV_HEAD = 4,           /* GEMV: LM head                             */
     SPM_KERNEL_ATTENTION = 5,    /* QK-norm, RoPE, KV append, decode attention */
-    SPM_KERNEL_ROUTE = 6,        /* router softmax, top-k, expert plan         */
+    SPM_KERNEL_ROUTE = 6,        /* router softmax, top-k, expert plan; on one
+                                    GPU the router logits too (one launch)    */
     SPM_KERNEL_COMBINE = 7,      /* weighted expert combine + residual         */
     SPM_KERNEL_OTHER = 8         /* embedding gather, greedy pick, positions   */
 };
