@@ -71,6 +71,8 @@ def lib() -> C.CDLL:
         L.or_session_free.argtypes = [C.c_void_p]
         L.or_decode_step.restype = C.c_int
         L.or_decode_step.argtypes = [C.c_void_p, C.POINTER(C.c_uint32), fp, C.c_int, C.POINTER(C.c_int32)]
+        L.or_session_route_margins.restype = C.c_int
+        L.or_session_route_margins.argtypes = [C.c_void_p, fp]
         L.or_serve.restype = C.c_int
         L.or_serve.argtypes = [C.c_void_p, C.POINTER(C.c_uint32), C.POINTER(C.c_int), C.c_int, C.c_int,
                                C.POINTER(C.c_uint32), C.POINTER(C.c_int), fp, C.c_int, C.c_int]
@@ -351,3 +353,12 @@ class OracleSession:
         if rc:
             raise RuntimeError(f"oracle step failed ({rc})")
         return (logits, r) if routes else logits
+
+    def route_margins(self) -> np.ndarray:
+        """The last step's routing margin per layer and client, (p_K - p_K+1) / p_K
+        of the routing probabilities (1 for dense layers): how close each
+        client's routing came to another expert set (spm-granite-moe/src/moe.rs:17-35
+        selects by these probabilities)."""
+        out = np.empty((self.model.shape.layers, self.clients), dtype=np.float32)
+        lib().or_session_route_margins(self._h, _f(out))
+        return out

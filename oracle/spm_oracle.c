@@ -729,6 +729,7 @@ struct or_session {
     float *keys, *values;   /* [client][layer][context][kv_width] */
     float *states, *normed, *q, *k, *v, *attn, *gate, *up, *proj, *act, *combined;
     float *router, *probs;
+    float* margins;         /* [layer][client] routing margin of the last step */
 };
 
 static int load_w(or_model* m, const char* name, or_w* w, int required, char* err, int errlen) {
@@ -857,6 +858,8 @@ or_session* or_session_new(or_model* m, int clients, int context) {
     s->combined = (float*)calloc((size_t)clients * c->hidden, sizeof(float));
     s->router = (float*)calloc((size_t)clients * (c->experts ? c->experts : 1), sizeof(float));
     s->probs = (float*)calloc((size_t)clients * (c->experts ? c->experts : 1), sizeof(float));
+    s->margins = (float*)calloc((size_t)clients * c->layers, sizeof(float));
+    for (size_t i = 0; i < (size_t)clients * c->layers; i++) s->margins[i] = 1.0f;
     return s;
 }
 
@@ -864,11 +867,17 @@ void or_session_free(or_session* s) {
     if (!s) return;
     free(s->len); free(s->keys); free(s->values); free(s->states); free(s->normed); free(s->q);
     free(s->k); free(s->v); free(s->attn); free(s->gate); free(s->up); free(s->act); free(s->proj);
-    free(s->combined); free(s->router); free(s->probs);
+    free(s->combined); free(s->router); free(s->probs); free(s->margins);
     free(s);
 }
 
 int or_session_len(const or_session* s, int client) { return s->len[client]; }
+
+int or_session_route_margins(const or_session* s, float* out) {
+    const size_t count = (size_t)s->clients * s->m->cfg.layers;
+    for (size_t i = 0; i < count; i++) out[i] = s->margins[i];
+    return 0;
+}
 
 static int gemv_w(const or_w* w, uint64_t expert, const float* x, int n, float* y, int threads) {
     uint64_t bv, bb;
@@ -894,7 +903,7 @@ static void norm_rows(const or_model* m, const float* src, float* dst, const flo
  * layout.rs:244-333 (experts in ascending id, up/gate/down FMA chains,
  * combined += down * p_e / sum(p_sel)).  The router bias is this build's
  * Zipf skew, added to each logit before the softmax. */
-static void moe_half(or_session* s, const or_layer* L, int threads, int32_t* routes) {
+static void moe_half(or_session* s, const or_layer* L, int threads, int32_t* routes, float* margins) {
     or_model* m = s->m;
     const or_cfg* c = &m->cfg;
     int n = s->clients, E = (int)c->experts, K = (int)c->experts_used;
@@ -909,6 +918,19 @@ static void moe_half(or_session* s, const or_layer* L, int threads, int32_t* rou
             for (int e = 0; e < E; e++) logit[e] = logit[e] + L->router_bias[e];
         or_softmax_route(logit, E, s->probs + (size_t)i * E);
         or_top_k(s->probs + (size_t)i * E, E, K, sel + (size_t)i * K, selv + (size_t)i * K);
+        {
+            /* how close the selection came to another expert set: the K-th
+             * probability against the largest one left out (a record only) */
+            const float* pr = s->probs + (size_t)i * E;
+            float best = -1.0f;
+            for (int e = 0; e < E; e++) {
+                int taken = 0;
+                for (int j = 0; j < K; j++) taken |= sel[(size_t)i * K + j] == e;
+                if (!taken && pr[e] > best) best = pr[e];
+            }
+            const float pk = selv[(size_t)i * K + K - 1];
+            margins[i] = best < 0.0f ? 1.0f : (pk - best) / pk;
+        }
         float sum = 0.0f;
         for (int j = 0; j < K; j++) sum = sum + s->probs[(size_t)i * E + sel[(size_t)i * K + j]];
         normv[i] = sum;
@@ -1040,7 +1062,8 @@ int or_decode_step(or_session* s, const uint32_t* tokens, float* logits, int thr
         /* feed-forward half: spm-batch/src/inner.rs:40-58 */
         norm_rows(m, s->states, s->normed, L->ffn_norm, n);
         if (m->moe) {
-            moe_half(s, L, threads, routes ? routes + (size_t)l * n * c->experts_used : NULL);
+            moe_half(s, L, threads, routes ? routes + (size_t)l * n * c->experts_used : NULL,
+                     s->margins + (size_t)l * n);
         } else {
             size_t ff = c->intermediate;
             gemv_w(&L->gate, 0, s->normed, n, s->gate, threads);

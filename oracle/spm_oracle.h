@@ -98,6 +98,12 @@ void or_session_free(or_session* s);
  * layer and client, the selected expert ids (layers x clients x used). */
 int or_decode_step(or_session* s, const uint32_t* tokens, float* logits, int threads, int32_t* routes);
 int or_session_len(const or_session* s, int client);
+/* After a step: each routed layer's margin per client, layers x clients,
+ * (p_K - p_K+1) / p_K of the routing probabilities (the K-th selected and
+ * the largest left out; 1 where every expert is selected and for dense
+ * layers).  A record for the parity tests: how close the routing came to
+ * another expert set. */
+int or_session_route_margins(const or_session* s, float* out);
 
 /* The lockstep serving loop of spm-batch/examples/serve-demo.rs:59-91.
  * prompts_flat holds each prompt back to back. produced must have room for

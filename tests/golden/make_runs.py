@@ -15,6 +15,10 @@ bytes).  Per tick and client the file keeps:
   top_vals their values
   margin   largest minus second-largest logit
   maxabs   max |logit| (the tolerance scale: 1e-3 * maxabs)
+  route_margin  routed models: the smallest over the layers of the oracle's
+           routing margin (p_K - p_K+1) / p_K (1 for dense models) -- where
+           it is tiny, any other order of fp32 sums may route the client
+           through another expert set
   digest   a sampled SHA-256 of the GGUF image, so a test can check that it
            synthesised the same bytes
 
@@ -62,7 +66,7 @@ def top_k(logits: np.ndarray, k: int = TOPK):
     return out_ids, out_vals
 
 
-def run(name: str, threads: int) -> Path:
+def run(name: str, threads: int, out: Path = OUT) -> Path:
     import emufpga_b200 as eb
     from emufpga_b200 import configs
     from oracle import oracle as O
@@ -82,6 +86,7 @@ def run(name: str, threads: int) -> Path:
     top_ids = np.zeros((ticks, n, TOPK), np.int32)
     top_vals = np.zeros((ticks, n, TOPK), np.float32)
     margin = np.zeros((ticks, n), np.float32)
+    route_margin = np.ones((ticks, n), np.float32)
     maxabs = np.zeros((ticks, n), np.float32)
     tokens = [p[0] for p in prompts]
     for t in range(ticks):
@@ -92,12 +97,14 @@ def run(name: str, threads: int) -> Path:
         s = np.sort(logits, axis=1)
         margin[t] = s[:, -1] - s[:, -2]
         maxabs[t] = np.abs(logits).max(axis=1)
+        route_margin[t] = sess.route_margins().min(axis=0)
         tokens = [p[t + 1] if t + 1 < len(p) else best[i] for i, p in enumerate(prompts)]
         if t % 64 == 0:
             print(f"{name}: tick {t}/{ticks} ({time.time() - t0:.0f} s)", flush=True)
-    OUT.mkdir(exist_ok=True)
-    path = OUT / f"{name}.npz"
+    out.mkdir(parents=True, exist_ok=True)
+    path = out / f"{name}.npz"
     np.savez_compressed(path, argmax=argmax, top_ids=top_ids, top_vals=top_vals, margin=margin, maxabs=maxabs,
+                        route_margin=route_margin,
                         digest=np.array(digest), prompt_lens=np.array([len(p) for p in prompts], np.int32),
                         steps=np.array(w["steps"], np.int32))
     print(f"{name}: {ticks} ticks in {time.time() - t0:.0f} s -> {path}", flush=True)
@@ -108,10 +115,11 @@ def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("workloads", nargs="*")
     ap.add_argument("--threads", type=int, default=0)
+    ap.add_argument("--out", type=Path, default=OUT, help="directory for the .npz files")
     a = ap.parse_args()
-    names = a.workloads or [n for n in RUNS if not (OUT / f"{n}.npz").exists()]
+    names = a.workloads or [n for n in RUNS if not (a.out / f"{n}.npz").exists()]
     for name in names:
-        run(name, a.threads)
+        run(name, a.threads, a.out)
     return 0
 
 

@@ -156,3 +156,25 @@ def test_oracle_serves_a_tiny_model_deterministically():
     for i, p in enumerate(prompts):
         alone, _ = m.serve([p], 4 + len(prompts[-1]) - len(p), threads=2)
         assert alone[0][: len(a[i])] == a[i][: len(alone[0])]
+
+
+def test_oracle_records_routing_margins():
+    """The oracle's per-layer routing margin (p_K - p_K+1) / p_K of each
+    client: in [0, 1], the same on any thread count, 1 for a dense model."""
+    r = configs.TINY["olmoe-q6_k"]
+    img = eb.synth_gguf(r)
+    m = O.OracleModel(img, r.shape)
+    a, b = m.session(3, 8), m.session(3, 8)
+    for t in range(3):
+        toks = [(t * 7 + i * 5) % r.shape.vocab for i in range(3)]
+        _, ra = a.step(toks, threads=1, routes=True)
+        b.step(toks, threads=4)
+        ma, mb = a.route_margins(), b.route_margins()
+        assert ma.shape == (r.shape.layers, 3)
+        assert np.array_equal(ma, mb)
+        assert ((ma >= 0) & (ma <= 1)).all() and (ma < 1).any()
+        assert ra.shape[0] == r.shape.layers
+    d = configs.TINY["llama-q8_0"]
+    dm = O.OracleModel(eb.synth_gguf(d), d.shape).session(2, 4)
+    dm.step([1, 2])
+    assert (dm.route_margins() == 1).all()
