@@ -17,6 +17,8 @@
  *   spm_session_create    spm-batch/src/session.rs:25-34, :64-78 (Client::new, Scratch::new)
  *   spm_decode_step       spm-batch/src/step.rs:19-40 (decode_step) + the greedy pick
  *                         of spm-batch/examples/serve-demo.rs:72-90
+ *   spm_prefill           spm-batch/examples/serve-demo.rs:84-89 (prompt tokens fed one
+ *                         per tick) run as one pass, as spm-qwen3-slice/src/model.rs:10-171
  *   spm_streamed          spm-linear/src/stream.rs:31-55 (streamed) for one stream
  *   spm_dequant_rows      parity hook for the decoders above, run on the device
  *   spm_file_*            spm-file/src/read.rs:46-101 (SpmReader) over .spm files
