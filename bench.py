@@ -237,18 +237,32 @@ def cpu_baseline(recipe, img, prompts, steps, seconds: float, threads: int = 0):
                       f"(oracle, {how})"}
 
 
+def _reference_input(a) -> "np.ndarray":
+    """The workload's synthetic GGUF, written by a child process
+    (`python -m emufpga_b200.synth`) and read back here, so that this process
+    maps no library of this repository but the oracle."""
+    import numpy as np
+
+    path = f"{a.gguf_dir}/emufpga_reference_{a.workload}_{os.getpid()}.gguf"
+    try:
+        subprocess.run([sys.executable, "-m", "emufpga_b200.synth", a.workload, path], cwd=ROOT, check=True)
+        return np.fromfile(path, dtype=np.uint8)
+    finally:
+        for p in (path, path + ".part"):
+            if os.path.exists(p):
+                os.unlink(p)
+
+
 def run_reference(a, rank, world):
     """The reference arm: the CPU oracle on all host threads, in a process
-    that loads liboracle.so and the synthetic-model writer libspmsynth.so only
-    (no GPU code).  It times lockstep ticks W..W+K of the run (the first
-    ticks: a full run takes the oracle minutes to hours), each tick bounded so
-    the whole arm ends within a few minutes."""
+    that loads liboracle.so only (its input model is written by a child
+    process; no GPU code).  It times lockstep ticks W..W+K of the run (the
+    first ticks: a full run takes the oracle minutes to hours), each tick
+    bounded so the whole arm ends within a few minutes."""
     if rank != 0:
         return 0
     w, recipe, prompts = _workload(a.workload)
-    from emufpga_b200 import synth
-
-    img = synth.synth_gguf(recipe)
+    img = _reference_input(a)
     n = len(prompts)
     from oracle import oracle as O
 

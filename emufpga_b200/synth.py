@@ -1,14 +1,17 @@
 """The synthetic model writer, through libspmsynth.so (host code only).
 
 Benchmarks and tests make their seeded random-init GGUF models here.  The
-library holds only the encoders and the GGUF writer, so a process that must
-not load the GPU engine (the CPU reference arm of bench.py) can make the same
-input bytes as every other process: libspmgpu.so's spm_synth_gguf writes the
-same image for the same spec.
+library holds only the encoders and the GGUF writer, so the same input bytes
+can be made without the GPU engine: libspmgpu.so's spm_synth_gguf writes the
+same image for the same spec.  Run as a module it writes a workload's model
+to a file, which is how the CPU reference arm of bench.py gets its input
+without loading either library itself.
 """
 from __future__ import annotations
 
 import ctypes as C
+import os
+import sys
 from pathlib import Path
 
 import numpy as np
@@ -36,8 +39,8 @@ def lib() -> C.CDLL:
     return _lib
 
 
-def synth_gguf(recipe: Recipe, threads: int = 0) -> np.ndarray:
-    """A synthetic GGUF v3 image of `recipe` (uint8 array, copied out of the library's buffer)."""
+def _with_image(recipe: Recipe, threads: int, use):
+    """Calls use(image) on the library's buffer (a uint8 view), then frees it."""
     spec = recipe.spec(threads)
     out = C.POINTER(C.c_uint8)()
     n = C.c_uint64()
@@ -45,7 +48,42 @@ def synth_gguf(recipe: Recipe, threads: int = 0) -> np.ndarray:
     if status != SPM_OK:
         raise SpmError(status, lib().spm_last_error().decode(errors="replace"))
     try:
-        arr = np.ctypeslib.as_array(out, shape=(n.value,)).copy()
+        return use(np.ctypeslib.as_array(out, shape=(n.value,)))
     finally:
         lib().spm_free(C.cast(out, C.c_void_p))
-    return arr
+
+
+def synth_gguf(recipe: Recipe, threads: int = 0) -> np.ndarray:
+    """A synthetic GGUF v3 image of `recipe` (uint8 array, copied out of the library's buffer)."""
+    return _with_image(recipe, threads, lambda view: view.copy())
+
+
+def write_gguf(recipe: Recipe, path: str, threads: int = 0) -> int:
+    """Writes synth_gguf(recipe) to `path` (through `path`.part, then a
+    rename); returns its size in bytes."""
+    part = f"{path}.part"
+
+    def write(view):
+        view.tofile(part)
+        return int(view.size)
+
+    size = _with_image(recipe, threads, write)
+    os.replace(part, path)
+    return size
+
+
+def main(argv: list[str]) -> int:
+    """python -m emufpga_b200.synth WORKLOAD PATH: writes the workload's
+    synthetic GGUF to PATH, so that a process which loads neither engine
+    library can read the same bytes."""
+    from .configs import RECIPES, WORKLOADS
+
+    if len(argv) != 2 or argv[0] not in WORKLOADS:
+        print("usage: python -m emufpga_b200.synth WORKLOAD PATH", file=sys.stderr)
+        return 2
+    write_gguf(RECIPES[WORKLOADS[argv[0]]["recipe"]], argv[1])
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main(sys.argv[1:]))
