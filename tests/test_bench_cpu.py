@@ -1,6 +1,7 @@
-"""bench.py's reference arm runs on the CPU: one JSON line per run with the
-keys the driver reads (the reference arm of a workload is the CPU oracle, so
-it needs no GPU)."""
+"""bench.py on the CPU: the reference arm's JSON line with the keys the
+driver reads (the reference arm of a workload is the CPU oracle, so it needs
+no GPU), the CPU baselines, and the host-side arithmetic of the GPU arm (its
+tick plan and its roofline summary)."""
 import json
 import subprocess
 import sys
@@ -60,3 +61,55 @@ def test_reference_arm_loads_no_gpu_engine():
     out = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=600)
     assert out.returncode == 0, out.stderr[-2000:]
     assert out.stdout.strip().splitlines()[-1] == "['liboracle.so']"
+
+
+@pytest.mark.parametrize("workload", ["qwen3-30b-b8", "qwen3-8b-b1", "olmoe-q6_k-b8", "smollm2-b5"])
+@pytest.mark.parametrize("steps,warmup", [(100, 8), (20, 3), (5000, 0)])
+def test_timed_ticks_are_decode_ticks_of_the_workload(workload, steps, warmup):
+    """The bench's tick plan: at least three warm-up ticks, then K timed and K
+    end-to-end ticks and the profiled ones, all after every prompt is
+    consumed and within the workload's decode steps."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    w, _, prompts = bench._workload(workload)
+    plan = bench._plan(w, prompts, steps, warmup)
+    longest = max(len(p) for p in prompts)
+    assert plan["prompt"] == longest and plan["warm"] >= 3 and plan["k"] >= 1
+    assert plan["k"] <= steps
+    last = plan["prompt"] + plan["warm"] + 2 * plan["k"] + bench.PROFILE_TICKS
+    assert plan["ticks"] == last
+    # every tick after the prompt phase is one of the workload's greedy ticks
+    assert last - longest <= w["steps"] - 1
+    assert plan["context"] >= longest + w["steps"]
+
+
+def test_roofline_summary_from_profiled_launches():
+    """roofline.achieved = streamed weight bytes of the GEMV launches over
+    their summed device time; frac = achieved / peak; kinds split the tick."""
+    import numpy as np
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+    from emufpga_b200.engine import Session
+
+    kinds = Session.KERNEL_KINDS
+    t = bench.PROFILE_TICKS
+    # per tick: two dense GEMVs (1 MB in 0.5 ms each), one head GEMV (2 MB in
+    # 0.25 ms), one attention launch (0.25 ms, no weight bytes)
+    dense, head, attention = kinds.index("gemv_dense"), kinds.index("gemv_head"), kinds.index("attention")
+    kind = np.array([dense, dense, head, attention], np.int32)
+    prof = {"ms": np.tile(np.array([0.5, 0.5, 0.25, 0.25], np.float32), t),
+            "bytes": np.tile(np.array([1e6, 1e6, 2e6, 0], np.float64), t),
+            "kind": np.tile(kind, t)}
+    r = bench._profile_summary(prof, 1000.0, "measured", "qwen3-30b-b8")
+    gemv_s = t * 1.25e-3
+    assert r["achieved"] == pytest.approx(t * 4e6 / gemv_s / 1e9)
+    assert r["frac"] == pytest.approx(r["achieved"] / 1000.0)
+    assert r["bound"] == "hbm" and r["unit"] == "GB/s" and r["peak"] == 1000.0
+    assert r["by_kind"]["gemv_dense"]["launches_per_tick"] == 2
+    assert r["by_kind"]["attention"]["ms_per_tick"] == pytest.approx(0.25)
+    assert sum(k["share"] for k in r["by_kind"].values()) == pytest.approx(1.0)
+    ratio = bench.TRAFFIC_RATIO["qwen3-30b-b8"][0]
+    assert r["traffic"]["bytes_per_launch"] == pytest.approx(ratio * 4e6 / 3)
+    assert bench._profile_summary(prof, 1000.0, "measured", "smollm2-b5")["traffic"] is None
