@@ -24,7 +24,8 @@ replicas ("replicas only").  Routed (MoE) models over N>1 GPUs run expert
 parallel: one job of n clients, rank r running the attention block of clients
 r*n/N .. (r+1)*n/N - 1 and the experts dealt to it (round robin) for every
 client; the attention outputs, the expert outputs and the greedy picks are
-exchanged over NVLink ("scaling": "strong").
+exchanged over NVLink ("scaling": "strong": the one-GPU line of a routed
+workload is the same job, so it says "strong" too).
 
 `--workload ternary-4096-b8` times the ternary GEMV of spm-gemv-ref instead
 (one launch over a 4096 x 4096 ternary stream with one scale per column and
@@ -291,7 +292,8 @@ def run_reference(a, rank, world):
               f"clients after {first} warm-up ticks; oracle on {os.cpu_count()} host threads")
     line = {"metric": "decode tokens/s", "value": value, "unit": "tokens/s", "impl": "reference", "n_gpus": world,
             "steps": len(times), "warmup": first, "ms_per_step": 1e3 * sum(times) / len(times),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong" if recipe.shape.moe else "weak", "vs_baseline": None,
+            "dtype": "f32",
             "data": "synthetic (seeded N(0,0.02) weights quantized by this repo's encoder, uniform prompt ids)",
             "config": {"workload": a.workload, "model": w["recipe"], "clients": n, "prompts": w["prompts"],
                        "timed_ticks": [first, first + len(times) - 1]},
@@ -475,7 +477,8 @@ def run_decode(a, name, rank, world, local, pg, dev, ep_ok=True):
         line = {
             "metric": "decode tokens/s", "value": tokens_total / (job_ms / 1e3), "unit": "tokens/s",
             "n_gpus": world, "steps": K, "warmup": warm, "ms_per_step": job_ms / K,
-            "higher_is_better": True, "scaling": "strong" if ep_mode else "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong" if ep_mode or (world == 1 and recipe.shape.moe and ep_ok) else "weak",
+            "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,0.02) weights quantized by this repo's encoder, uniform prompt ids)",
             "config": {"workload": name, "model": w["recipe"], "clients": n, "prompts": w["prompts"],
                        "parallelism": (f"expert parallel x{world}" if ep_mode else f"replicas x{world}")
